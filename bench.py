@@ -1,0 +1,415 @@
+"""Benchmark of the TAGI training step (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload r18|mlp|cnn|tfm]
+                    [--impl ours|reference]
+
+Default workload: the ResNet-18 configuration (3×32×32 N(0,1) inputs, 128 per
+GPU, gain 0.1, σ_v = 0.05, one-hot labels over 10 classes), one
+``Sequential.step`` (forward + innovation + backward + capped update) per
+step, batch-sharded over N GPUs (weak scaling, one process per GPU, launched
+by torchrun for N > 1).
+
+value      samples/s over all ranks: K·B·N / (max over ranks of the summed
+           CUDA-event step times), inputs resident in HBM, L2 flushed
+           (256 MiB write) before every step outside the timed events.
+e2e        the same metric through the public API with pinned host buffers:
+           H2D of x, y and D2H of (μ, S) inside the timed events.
+roofline   the dominant moment contraction, timed with CUDA events around
+           each of its launches during the timed steps; achieved = algorithmic
+           FLOPs (6·M·N·K forward, 4·M·N·K backward/weight sums) ÷ time,
+           against the 3xTF32-effective tensor peak (measured cuBLAS TF32 ÷ 3).
+cpu_baseline  the CPU oracle (float32 PyTorch restatement of the reference's
+           equations) on the host cores, rank 0 at N = 1, bounded sample.
+--impl reference  times that CPU restatement as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT), str(ROOT / "triton-tagi_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+SIGMA_V = 0.05
+WORKLOADS = {
+    "r18": dict(batch=128, metric="TAGI ResNet-18 Sequential.step samples/sec"),
+    "mlp": dict(batch=256, metric="TAGI MLP 784-256-128-10 Sequential.step samples/sec"),
+    "cnn": dict(batch=512, metric="TAGI CNN Sequential.step samples/sec"),
+    "tfm": dict(batch=32, metric="TAGI transformer Sequential.step samples/sec"),
+}
+
+
+# ----------------------------------------------------------------------------- networks
+def build_layers(name: str, L, device):
+    d = dict(device=device)
+    if name == "mlp":
+        return [L.Linear(784, 256, **d), L.ReLU(), L.Linear(256, 128, **d), L.ReLU(),
+                L.Linear(128, 10, **d), L.Remax()]
+    if name == "cnn":
+        return [L.Conv2D(3, 32, 5, padding=2, **d), L.ReLU(), L.AvgPool2D(2),
+                L.Conv2D(32, 64, 5, padding=2, **d), L.BatchNorm2D(64, **d), L.ReLU(),
+                L.AvgPool2D(2), L.Conv2D(64, 64, 5, padding=2, **d), L.ReLU(), L.AvgPool2D(2),
+                L.Flatten(), L.Linear(1024, 256, **d), L.ReLU(), L.Linear(256, 10, **d),
+                L.Remax()]
+    if name == "r18":
+        kw = dict(gain_w=0.1, gain_b=0.1, **d)
+        return [L.Conv2D(3, 64, 3, stride=1, padding=1, **kw), L.ReLU(), L.BatchNorm2D(64, **kw),
+                L.ResBlock(64, 64, 1, **kw), L.ResBlock(64, 64, 1, **kw),
+                L.ResBlock(64, 128, 2, **kw), L.ResBlock(128, 128, 1, **kw),
+                L.ResBlock(128, 256, 2, **kw), L.ResBlock(256, 256, 1, **kw),
+                L.ResBlock(256, 512, 2, **kw), L.ResBlock(512, 512, 1, **kw),
+                L.AvgPool2D(4), L.Flatten(), L.Linear(512, 10, **kw), L.Remax()]
+    if name == "tfm":
+        V, E, H, S = 64, 512, 8, 512
+        layers = [L.Embedding(V, E, input_size=S, scale=0.25, **d), L.PositionalEncoding(E, **d)]
+        for _ in range(4):
+            layers += [L.MultiheadAttentionV2(E, H, S, bias=False, **d), L.RMSNorm(E, **d),
+                       L.Linear(E, 4 * E, **d), L.ReLU(), L.Linear(4 * E, E, **d)]
+        return layers + [L.Linear(E, V, **d)]
+    raise KeyError(name)
+
+
+def make_batch(name: str, batch: int, seed: int, device="cpu"):
+    g = torch.Generator().manual_seed(seed)
+    if name == "mlp":
+        x = torch.randn(batch, 784, generator=g)
+    elif name == "tfm":
+        x = torch.randint(0, 64, (batch, 512), generator=g).float()
+    else:
+        x = torch.randn(batch, 3, 32, 32, generator=g)
+    if name == "tfm":
+        y = torch.nn.functional.one_hot(torch.flip(x.long(), dims=[1]), 64).float()
+    else:
+        y = torch.nn.functional.one_hot(torch.randint(0, 10, (batch,), generator=g), 10).float()
+    return x.to(device), y.to(device)
+
+
+# ----------------------------------------------------------------------------- helpers
+class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.lines, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+class LaunchTimer:
+    """Times the moment-contraction launches with CUDA events (library call hook)."""
+
+    FAMILIES = {
+        "tagi_moment_forward": ("moment_forward", lambda a: 6.0 * a[17] * a[18] * a[19]),
+        "tagi_backward_delta_view": ("backward_delta", lambda a: 4.0 * a[14] * a[15] * a[16]),
+        "tagi_fused_backward_delta": ("backward_delta", lambda a: 4.0 * a[5] * a[6] * a[7]),
+        "tagi_param_grad": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
+    }
+
+    def __init__(self):
+        self.records, self._open = [], None
+
+    def __call__(self, phase, name, args):
+        fam = self.FAMILIES.get(name)
+        if fam is None:
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        if phase == "before":
+            self._open = ev
+        else:
+            self.records.append((fam[0], fam[1](args), self._open, ev))
+
+    def summary(self):
+        fam = {}
+        for name, flops, a, b in self.records:
+            t = a.elapsed_time(b) * 1e-3
+            f = fam.setdefault(name, {"launches": 0, "flops": 0.0, "seconds": 0.0})
+            f["launches"] += 1
+            f["flops"] += flops
+            f["seconds"] += t
+        return fam
+
+
+def tf32_peak_tflops(device) -> float:
+    """Burst cuBLAS TF32 throughput on an 8192³ GEMM (best of 5, CUDA events)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=device)
+        b = torch.randn(n, n, device=device)
+        for _ in range(2):
+            torch.matmul(a, b)
+        best = float("inf")
+        for _ in range(5):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(a, b)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e) * 1e-3)
+        del a, b
+        return 2.0 * n**3 / best / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            pass
+    return {}
+
+
+# ----------------------------------------------------------------------------- CPU arms
+def cpu_rate(workload: str, steps: int, warmup: int, budget_s: float) -> dict:
+    """Samples/s of the CPU oracle (float32 PyTorch on all host threads)."""
+    import oracle.net as ON
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    # size the sample so that one step takes about budget_s / (steps + warmup)
+    probe_b = 2
+    torch.manual_seed(0)
+    net = ON.Sequential(build_layers(workload, ON, "cpu"))
+    x, y = make_batch(workload, probe_b, 1)
+    t0 = time.perf_counter()
+    net.step(x, y, SIGMA_V)
+    per_sample = (time.perf_counter() - t0) / probe_b
+    target = budget_s / max(1, steps + warmup)
+    batch = int(max(2, min(WORKLOADS[workload]["batch"], target / max(per_sample, 1e-6))))
+    x, y = make_batch(workload, batch, 2)
+    for _ in range(warmup):
+        net.step(x, y, SIGMA_V)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        net.step(x, y, SIGMA_V)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return {"value": steps * batch / total, "unit": "samples/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{workload} Sequential.step at batch {batch} (of {WORKLOADS[workload]['batch']}),"
+                      f" {steps} timed steps after {warmup} warm-up, float32 oracle on "
+                      f"{torch.get_num_threads()} threads",
+            "ms_per_step": 1e3 * total / steps}
+
+
+def reference_arm(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    r = cpu_rate(args.workload, args.steps, args.warmup, budget_s=60.0)
+    line = {
+        "impl": "reference", "metric": WORKLOADS[args.workload]["metric"], "value": r["value"],
+        "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "batch_per_step": r["sample"]},
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": "samples/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def our_arm(args, rank: int, world: int, local: int) -> None:
+    import triton_tagi as TT
+    from triton_tagi._lib import kernel_launches, lib
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B = WORKLOADS[args.workload]["batch"]
+    torch.manual_seed(1234)
+    net = TT.Sequential(build_layers(args.workload, TT, dev), device=dev)
+    if world > 1:
+        from triton_tagi.distributed import DataParallel
+
+        DataParallel(net)
+    x, y = make_batch(args.workload, B, 100 + rank, dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        net.step(x, y, SIGMA_V)
+    torch.cuda.synchronize()
+
+    timer = LaunchTimer()
+    L = lib()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = kernel_launches()
+    with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        L.hook = timer
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            net.step(x, y, SIGMA_V)
+            ends[i].record()
+        L.hook = None
+        torch.cuda.synchronize()
+        barrier()
+    launches = kernel_launches() - launches0
+    step_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) * 1e-3
+    fam = timer.summary()
+
+    # end to end through the public API: pinned host inputs in, predictions out
+    xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
+    xd, yd = torch.empty_like(x), torch.empty_like(y)
+    mu_h = torch.empty(y.shape, pin_memory=True)
+    var_h = torch.empty(y.shape, pin_memory=True)
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        e_starts[i].record()
+        xd.copy_(xh, non_blocking=True)
+        yd.copy_(yh, non_blocking=True)
+        mu, var = net.step(xd, yd, SIGMA_V)
+        mu_h.copy_(mu, non_blocking=True)
+        var_h.copy_(var, non_blocking=True)
+        e_ends[i].record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)) * 1e-3
+
+    if world > 1:
+        t = torch.tensor([step_s, e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_s, e2e_s = t.tolist()
+
+    peaks = measured_peaks()
+    tf32 = tf32_peak_tflops(dev) if rank == 0 else None
+    if rank != 0:
+        return
+    value = args.steps * B * world / step_s
+    dom_name, dom = max(fam.items(), key=lambda kv: kv[1]["seconds"]) if fam else (None, None)
+    peak3 = tf32 / 3.0 if tf32 else None
+    roof = None
+    if dom is not None:
+        achieved = dom["flops"] / dom["seconds"] / 1e12
+        roof = {"bound": "tensor", "kernel": dom_name, "achieved": achieved, "peak": peak3,
+                "unit": "TFLOP/s", "frac": achieved / peak3 if peak3 else None,
+                "traffic": None,
+                "peak_source": f"measured cuBLAS TF32 burst {tf32:.0f} TF/s / 3 (3xTF32-effective)",
+                "launches": dom["launches"],
+                "share_of_step": dom["seconds"] / step_s}
+    line = {
+        "metric": WORKLOADS[args.workload]["metric"], "value": value, "unit": "samples/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * step_s / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "batch_per_gpu": B, "global_batch": B * world,
+                   "sigma_v": SIGMA_V, "parallelism": f"dp{world}",
+                   "l2": "flushed between steps (256 MiB write outside the timed events)"},
+        "e2e": {"value": args.steps * B * world / e2e_s, "unit": "samples/s",
+                "h2d_bytes_per_step": (xh.numel() + yh.numel()) * 4,
+                "d2h_bytes_per_step": (mu_h.numel() + var_h.numel()) * 4},
+        "gpu_launches": int(launches),
+        "roofline": roof,
+        "kernels": {k: {"launches": v["launches"], "ms_per_step": 1e3 * v["seconds"] / args.steps,
+                        "tflops": v["flops"] / v["seconds"] / 1e12} for k, v in fam.items()},
+        "clocks": clocks.summary(),
+        "peaks": {"tf32_cublas_tflops": tf32, "hbm_gbs": peaks.get("hbm_gbs"),
+                  "bf16_tflops": peaks.get("bf16_tflops")},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        r = cpu_rate(args.workload, steps=3, warmup=1, budget_s=20.0)
+        line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="r18")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)  # rank 0 only; no process group needed
+        return
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        our_arm(args, rank, world, local)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

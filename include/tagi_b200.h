@@ -1,0 +1,267 @@
+/*
+ * tagi_b200.h — C ABI of libtagi_b200.so, the sm_100a implementation of the
+ * TAGI moment hot path (fused mean/variance contractions, their elementwise
+ * neighbours and the capped closed-form update).
+ *
+ * Conventions
+ *   - Every entry point returns TAGI_OK (0) or a negative TAGI_E* status and
+ *     never aborts; tagi_last_error() gives a message for the calling thread.
+ *   - All tensors are float32 device pointers. Sizes and strides are int64
+ *     element counts. `stream` is a cudaStream_t passed as void* (NULL = the
+ *     legacy default stream). Work is enqueued asynchronously; nothing here
+ *     synchronises the device.
+ *   - Outputs are caller-allocated. Entry points that need scratch memory take
+ *     (workspace, workspace_bytes) and have a *_workspace_size() query.
+ *   - A "row-split" operand dimension maps an index i to the element offset
+ *       (i / div) * outer + (i % div) * stride        (div <= 0: i * stride)
+ *     which lets one GEMM view an NCHW tensor as an (N*H*W) x C matrix.
+ *
+ * Each declaration names the reference function it replaces
+ * (paths relative to the triton-tagi project root).
+ */
+#ifndef TAGI_B200_H
+#define TAGI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    TAGI_OK = 0,
+    TAGI_E_BAD_ARG = -1,      /* null pointer, negative size, inconsistent shape */
+    TAGI_E_ALIGNMENT = -2,    /* pointer/stride alignment required by a fast path */
+    TAGI_E_LAUNCH = -3,       /* CUDA launch or runtime error */
+    TAGI_E_WORKSPACE = -4,    /* workspace missing or too small */
+    TAGI_E_UNSUPPORTED = -5,  /* configuration outside what the kernels implement */
+    TAGI_E_TIMEOUT = -6       /* a bounded device-side wait ran out */
+};
+
+/* Library identification and diagnostics. */
+int tagi_version(void);                  /* (major << 16) | (minor << 8) | patch */
+const char* tagi_last_error(void);       /* message of the last failing call (this thread) */
+int tagi_device_arch(int device);        /* SM version of `device` (e.g. 100), <0 on error */
+uint64_t tagi_kernel_launches(void);     /* kernels this library has launched (process-wide) */
+
+/* ---------------------------------------------------------------------------
+ * Dense moment contractions
+ * ------------------------------------------------------------------------- */
+
+/* Sz = ma^2 @ Sw + Sa @ (mw^2 + Sw) + Sb  (Sb: N floats).
+ * Replaces triton_fused_var_forward, triton_tagi/kernels/common.py:170-210. */
+int tagi_fused_var_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
+                           const float* Sb, float* Sz, int64_t M, int64_t N, int64_t K,
+                           int64_t stride_am, int64_t stride_ak, int64_t stride_wk,
+                           int64_t stride_wn, int64_t stride_cm, int64_t stride_cn, void* stream);
+
+/* mz = ma @ mw + mb and Sz = ma^2 @ Sw + Sa @ (mw^2 + Sw) + Sb in one pass.
+ * Rows of ma/Sa and of mz/Sz are row-split views (see header comment);
+ * mw/Sw are K x N with row stride ldw; mb/Sb hold N floats (may be NULL).
+ * Replaces the mean matmul + variance kernel pair of Linear.forward
+ * (triton_tagi/layers/linear.py:95-100) and Conv2D.forward
+ * (triton_tagi/layers/conv2d.py:301-308, output written directly in NCHW). */
+int tagi_moment_forward(const float* ma, const float* Sa, int64_t a_div, int64_t a_outer,
+                        int64_t a_stride, int64_t a_kstride, const float* mw, const float* Sw,
+                        int64_t ldw, const float* mb, const float* Sb, float* mz, float* Sz,
+                        int64_t c_div, int64_t c_outer, int64_t c_stride, int64_t c_nstride,
+                        int64_t M, int64_t N, int64_t K, void* stream);
+
+/* d_ma = dmz @ mw^T, d_Sa = dSz @ (mw^2)^T.
+ * Replaces triton_fused_backward_delta, triton_tagi/kernels/common.py:287-327. */
+int tagi_fused_backward_delta(const float* dmz, const float* dSz, const float* mw, float* d_ma,
+                              float* d_Sa, int64_t M, int64_t K, int64_t N, int64_t stride_dm,
+                              int64_t stride_dn, int64_t stride_wk, int64_t stride_wn,
+                              int64_t stride_cm, int64_t stride_ck, void* stream);
+
+/* Same contraction with row-split views on dmz/dSz rows (so an NCHW delta can
+ * be read in place) and on the output rows. Used by Conv2D.backward
+ * (triton_tagi/layers/conv2d.py:338-357). */
+int tagi_backward_delta_view(const float* dmz, const float* dSz, int64_t d_div, int64_t d_outer,
+                             int64_t d_stride, int64_t d_nstride, const float* mw, int64_t ldw,
+                             float* d_ma, float* d_Sa, int64_t c_div, int64_t c_outer,
+                             int64_t c_stride, int64_t c_kstride, int64_t M, int64_t K,
+                             int64_t N, void* stream);
+
+/* grad_mw = a^T @ dmz, grad_Sw = (a^2)^T @ dSz  (K x N outputs).
+ * Replaces triton_fused_weight_grad, triton_tagi/kernels/common.py:410-451. */
+size_t tagi_fused_weight_grad_workspace_size(int64_t M, int64_t K, int64_t N);
+int tagi_fused_weight_grad(const float* a, const float* dmz, const float* dSz, float* grad_mw,
+                           float* grad_Sw, int64_t M, int64_t K, int64_t N, int64_t stride_am,
+                           int64_t stride_ak, int64_t stride_dm, int64_t stride_dn,
+                           int64_t stride_km, int64_t stride_kn, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Parameter side of Linear/Conv2D backward + update over a batch of M rows.
+ *   g_m[k,n] = sum_r a[r,k] dmz[r,n],   g_S[k,n] = sum_r a[r,k]^2 dSz[r,n]
+ *   (row k == K, when has_bias, is the bias: a == 1)
+ * a is M x K (row stride lda, contiguous columns); dmz/dSz rows are a
+ * row-split view with column stride d_nstride.
+ * mode TAGI_WGRAD_SUMS   : out_m/out_S <- raw sums, (K+has_bias) x N, row stride N
+ * mode TAGI_WGRAD_DELTAS : out_m/out_S <- Sw*g_m, Sw^2*g_S (delta_mw/delta_Sw of
+ *                          triton_tagi/layers/linear.py:138-151 and
+ *                          conv2d.py:344-354); bias deltas to out_mb/out_Sb
+ * mode TAGI_WGRAD_UPDATE : applies the capped update to mw,Sw (and mb,Sb) in
+ *                          place, as update_parameters after backward
+ *                          (triton_tagi/update/parameters.py:58-128). */
+enum { TAGI_WGRAD_SUMS = 0, TAGI_WGRAD_DELTAS = 1, TAGI_WGRAD_UPDATE = 2 };
+size_t tagi_param_grad_workspace_size(int64_t M, int64_t K, int64_t N, int has_bias);
+int tagi_param_grad(const float* a, int64_t lda, const float* dmz, const float* dSz,
+                    int64_t d_div, int64_t d_outer, int64_t d_stride, int64_t d_nstride,
+                    int64_t M, int64_t K, int64_t N, int has_bias, int mode, float* mw,
+                    float* Sw, float* mb, float* Sb, float* out_m, float* out_S, float* out_mb,
+                    float* out_Sb, float cap_factor, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Apply all-reduced raw sums (layout of TAGI_WGRAD_SUMS) as the capped update:
+ * m += cap(S*g_m), S += cap(S^2*g_S), floor 1e-5 (parameters.py:77-96). */
+int tagi_apply_param_sums(const float* g_m, const float* g_S, int64_t K, int64_t N, int has_bias,
+                          float* mw, float* Sw, float* mb, float* Sb, float cap_factor,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Batched attention products (leading dims flattened to `batch`; each operand
+ * has a batch stride and two matrix strides, so transpose views need no copy)
+ * ------------------------------------------------------------------------- */
+
+/* var[n,m,l] = scale_sq * sum_k var_a (mu_b^2 + var_b) + mu_a^2 var_b.
+ * If mean != NULL also mean[n,m,l] = scale * sum_k mu_a mu_b (fused mean).
+ * Replaces bmm_tagi_var, triton_tagi/kernels/attention.py:149-201. */
+int tagi_bmm_tagi_var(const float* mu_a, const float* var_a, const float* mu_b,
+                      const float* var_b, float* mean, float* var, int64_t batch, int64_t M,
+                      int64_t L, int64_t K, int64_t sa_n, int64_t sa_m, int64_t sa_k,
+                      int64_t sb_n, int64_t sb_k, int64_t sb_l, int64_t so_n, int64_t so_m,
+                      int64_t so_l, float scale, float scale_sq, void* stream);
+
+/* mean = scale * a_mean @ b, var = scale^2 * a_var @ b^2.
+ * Replaces bmm_shared_right, triton_tagi/kernels/attention.py:286-336
+ * (bmm_shared_left, attention.py:339-374, is the same call on transposed views). */
+int tagi_bmm_shared_right(const float* a_mean, const float* a_var, const float* b, float* mean,
+                          float* var, int64_t batch, int64_t M, int64_t L, int64_t K,
+                          int64_t sa_n, int64_t sa_m, int64_t sa_k, int64_t sb_n, int64_t sb_k,
+                          int64_t sb_l, int64_t so_n, int64_t so_m, int64_t so_l, float scale,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Elementwise / row kernels
+ * ------------------------------------------------------------------------- */
+
+/* In-place capped update. Replaces update_parameters,
+ * triton_tagi/update/parameters.py:104-128. */
+int tagi_capped_update(float* m, float* S, const float* delta_m, const float* delta_S, int64_t n,
+                       float cap_factor, void* stream);
+
+/* delta_mu = (y - mu)/(var + sv2), delta_var = -1/(var + sv2).
+ * Replaces the dense branch of compute_innovation,
+ * triton_tagi/update/observation.py:247-291. */
+int tagi_innovation(const float* y, const float* mu, const float* var, float* delta_mu,
+                    float* delta_var, int64_t n, float sigma_v_sq, void* stream);
+
+/* Rectified-Gaussian moments and Jacobian. Replaces bayesian_relu,
+ * triton_tagi/layers/relu.py:275-303. */
+int tagi_relu_forward(const float* mz, const float* Sz, float* ma, float* Sa, float* J, int64_t n,
+                      void* stream);
+
+/* out_m = dm * J, out_S = dS * J^2 (ReLU.backward relu.py:333-350,
+ * Remax.backward remax.py:538-541). */
+int tagi_jacobian_backward(const float* dm, const float* dS, const float* J, float* out_m,
+                           float* out_S, int64_t n, void* stream);
+
+/* Row-wise Remax over K classes. Replaces triton_remax,
+ * triton_tagi/layers/remax.py:475-512. */
+int tagi_remax_forward(const float* mz, const float* Sz, float* ma, float* Sa, float* J,
+                       int64_t rows, int64_t K, int64_t row_stride, void* stream);
+
+/* a_m += b_m, a_S += b_S. Replaces triton_add_shortcut / triton_delta_merge,
+ * triton_tagi/layers/resblock.py:138-175. */
+int tagi_add_inplace(float* a_m, float* a_S, const float* b_m, const float* b_S, int64_t n,
+                     void* stream);
+
+/* Average pooling with window = stride = k. Replaces the AvgPool2D kernels,
+ * triton_tagi/layers/avgpool2d.py:158-239. */
+int tagi_avgpool_forward(const float* ma, const float* Sa, float* ma_out, float* Sa_out,
+                         int64_t N, int64_t C, int64_t H, int64_t W, int64_t k, float var_scale,
+                         void* stream);
+int tagi_avgpool_backward(const float* dm, const float* dS, float* dm_out, float* dS_out,
+                          int64_t N, int64_t C, int64_t H, int64_t W, int64_t k, float var_scale,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Convolution helpers (NCHW; padding_type 2 = right/bottom only)
+ * ------------------------------------------------------------------------- */
+
+/* patches[(n,oh,ow), (c,kh,kw)] for mean and variance in one pass.
+ * Replaces _triton_im2col, triton_tagi/layers/conv2d.py:140-152, 280-297. */
+int tagi_im2col(const float* xm, const float* xS, float* pm, float* pS, int64_t N, int64_t C,
+                int64_t H, int64_t W, int64_t k, int64_t stride, int64_t padding,
+                int64_t padding_type, void* stream);
+
+/* Gather patch-space deltas back to NCHW. mode 0 reproduces the reference's
+ * gather exactly (_col2im_kernel, conv2d.py:85-132, 155-181, 361-370);
+ * mode 1 is the true adjoint of im2col. */
+int tagi_col2im(const float* cm, const float* cS, float* dm, float* dS, int64_t N, int64_t C,
+                int64_t H, int64_t W, int64_t k, int64_t stride, int64_t padding,
+                int64_t padding_type, int mode, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Normalisation
+ * ------------------------------------------------------------------------- */
+
+/* Per-channel raw sums over (N, H*W) of an NCHW tensor pair:
+ * sums[0:C] = sum mz, sums[C:2C] = sum Sz, sums[2C:3C] = sum mz^2 (float64).
+ * Replaces the three _channel_mean_kernel launches of
+ * triton_tagi/layers/batchnorm2d.py:307-339 (one pass, no mz*mz temporary). */
+int tagi_bn_channel_sums(const float* mz, const float* Sz, double* sums, int64_t N, int64_t C,
+                         int64_t HW, void* stream);
+
+/* From (possibly all-reduced) sums over `count` = N_global*H*W elements:
+ * mean, Bessel-corrected var; running-stat init (first != 0, with optional
+ * mw = sqrt(var + eps) when preserve_var) or EMA with `momentum`
+ * (batchnorm2d.py:336-355). */
+int tagi_bn_finalize(const double* sums, int64_t C, double count, float* mean, float* var,
+                     float* running_mean, float* running_var, float* mw, int first,
+                     int preserve_var, float momentum, float eps, void* stream);
+
+/* Normalise + Gaussian affine; caches m_hat (S_hat if non-NULL).
+ * Replaces _batchnorm_fwd_kernel, batchnorm2d.py:59-126, 388-431. */
+int tagi_bn_forward(const float* mz, const float* Sz, const float* mean, const float* var,
+                    const float* mg, const float* Sg, const float* mb, const float* Sb, float* ma,
+                    float* Sa, float* m_hat, float* S_hat, int64_t N, int64_t C, int64_t HW,
+                    float eps, void* stream);
+
+/* Delta propagation plus per-channel raw sums (float64)
+ * grads[0:C]=sum dma*m_hat, [C:2C]=sum dSa*m_hat^2, [2C:3C]=sum dma, [3C:4C]=sum dSa.
+ * Replaces batchnorm2d.py:436-513 (torch sums + _batchnorm_bwd_kernel). */
+int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat, const float* var,
+                     const float* mg, float* dmz, float* dSz, double* grads, int64_t N, int64_t C,
+                     int64_t HW, float eps, void* stream);
+
+/* Apply per-channel sums (tagi_bn_backward layout, possibly all-reduced):
+ * mode TAGI_WGRAD_DELTAS writes the four delta vectors, TAGI_WGRAD_UPDATE
+ * applies the capped update to (mw,Sw,mb,Sb) in place. */
+int tagi_bn_apply_grads(const double* grads, int64_t C, int mode, float* mw, float* Sw, float* mb,
+                        float* Sb, float* d_mw, float* d_Sw, float* d_mb, float* d_Sb,
+                        float cap_factor, void* stream);
+
+/* RMSNorm over the last dim (rows x ni). Replaces RMSNorm.forward/backward,
+ * triton_tagi/layers/rms_norm.py:387-428. Backward writes propagated deltas
+ * and the raw gamma sums (float64) sum_mu[ni], sum_var[ni]. */
+int tagi_rmsnorm_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
+                         float* mz, float* Sz, float* inv_rms, int64_t rows, int64_t ni,
+                         float eps, void* stream);
+int tagi_rmsnorm_backward(const float* dmz, const float* dSz, const float* ma,
+                          const float* inv_rms, const float* mw, float* dma, float* dSa,
+                          double* sums, int64_t rows, int64_t ni, void* stream);
+
+/* Capped update from float64 raw sums with a per-element prior scale:
+ * m += cap(S*g_m), S += cap(S^2*g_S). Used for RMSNorm gamma and any vector
+ * parameter whose sums were reduced in float64 (and all-reduced). */
+int tagi_apply_vector_sums(const double* g_m, const double* g_S, int64_t n, int mode, float* m,
+                           float* S, float* d_m, float* d_S, float cap_factor, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TAGI_B200_H */

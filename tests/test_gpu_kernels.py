@@ -1,0 +1,349 @@
+"""Kernel parity on the GPU: every libtagi_b200 entry point against the CPU
+oracle (float64 where the bar is relative error) and against the golden
+vectors that the reference itself produced."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.moments as F
+from _tol import MEAN_RTOL, VAR_RTOL, assert_as_accurate, assert_rel
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def g(t):
+    return torch.as_tensor(t).to(DEV, torch.float32)
+
+
+def d64(t):
+    return torch.as_tensor(t).detach().cpu().double()
+
+
+def rnd(gen, *shape, kind="n", scale=1.0, lo=0.0):
+    if kind == "n":
+        return torch.randn(*shape, generator=gen) * scale
+    return torch.rand(*shape, generator=gen) * scale + lo
+
+
+SHAPES = [(37, 27, 10), (256, 784, 256), (513, 300, 130), (8, 4608, 64), (4096, 64, 1)]
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_var_forward_and_linear_forward(M, K, N):
+    from triton_tagi.kernels.common import triton_fused_var_forward
+    from triton_tagi import Linear
+
+    gen = torch.Generator().manual_seed(M * 7 + K)
+    ma, Sa = rnd(gen, M, K), rnd(gen, M, K, kind="u", scale=1e-2, lo=1e-4)
+    mw, Sw = rnd(gen, K, N, scale=K**-0.5), rnd(gen, K, N, kind="u", scale=1.0 / K)
+    mb, Sb = rnd(gen, 1, N, scale=0.1), rnd(gen, 1, N, kind="u", scale=1e-3)
+    ref_S = F.var_forward(d64(ma), d64(Sa), d64(mw), d64(Sw), d64(Sb))
+    assert_rel(triton_fused_var_forward(g(ma), g(Sa), g(mw), g(Sw), g(Sb)), ref_S, VAR_RTOL, "Sz")
+    lin = Linear(K, N, device=DEV)
+    lin.mw, lin.Sw, lin.mb, lin.Sb = g(mw), g(Sw), g(mb), g(Sb)
+    mz, Sz = lin.forward(g(ma), g(Sa))
+    assert_rel(mz, F.mean_forward(d64(ma), d64(mw), d64(mb)), MEAN_RTOL, "mz")
+    assert_rel(Sz, ref_S, VAR_RTOL, "Sz (linear)")
+
+
+def test_var_forward_strided_views():
+    from triton_tagi.kernels.common import triton_fused_var_forward
+
+    gen = torch.Generator().manual_seed(3)
+    ma, Sa = rnd(gen, 40, 33).T, rnd(gen, 40, 33, kind="u").T   # (33, 40), column-major
+    mw, Sw = rnd(gen, 17, 40).T, rnd(gen, 17, 40, kind="u").T   # (40, 17), column-major
+    Sb = rnd(gen, 1, 17, kind="u")
+    got = triton_fused_var_forward(g(ma.T).T, g(Sa.T).T, g(mw.T).T, g(Sw.T).T, g(Sb))
+    assert_rel(got, F.var_forward(d64(ma), d64(Sa), d64(mw), d64(Sw), d64(Sb)), VAR_RTOL, "Sz")
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_backward_delta_and_weight_grad(M, K, N):
+    from triton_tagi.kernels.common import triton_fused_backward_delta, triton_fused_weight_grad
+
+    gen = torch.Generator().manual_seed(M + 11 * N)
+    a = rnd(gen, M, K)
+    mw = rnd(gen, K, N, scale=K**-0.5)
+    dmz, dSz = rnd(gen, M, N, scale=0.1), -rnd(gen, M, N, kind="u", scale=1e-2)
+    d_ma, d_Sa = triton_fused_backward_delta(g(dmz), g(dSz), g(mw))
+    r_ma, r_Sa = F.backward_delta(d64(dmz), d64(dSz), d64(mw))
+    assert_rel(d_ma, r_ma, MEAN_RTOL, "d_ma")
+    assert_rel(d_Sa, r_Sa, VAR_RTOL, "d_Sa")
+    gm, gS = triton_fused_weight_grad(g(a), g(dmz), g(dSz))
+    rm, rS = F.weight_grad(d64(a), d64(dmz), d64(dSz))
+    assert_rel(gm, rm, MEAN_RTOL, "grad_mw")
+    assert_rel(gS, rS, VAR_RTOL, "grad_Sw")
+
+
+def test_weight_grad_split_reduction_is_deterministic():
+    from triton_tagi.kernels.common import triton_fused_weight_grad
+
+    gen = torch.Generator().manual_seed(5)
+    a, dmz, dSz = rnd(gen, 50000, 27), rnd(gen, 50000, 10), rnd(gen, 50000, 10, kind="u")
+    r1 = triton_fused_weight_grad(g(a), g(dmz), g(dSz))
+    r2 = triton_fused_weight_grad(g(a), g(dmz), g(dSz))
+    assert torch.equal(r1[0], r2[0]) and torch.equal(r1[1], r2[1])
+    rm, rS = F.weight_grad(d64(a), d64(dmz), d64(dSz))
+    assert_rel(r1[0], rm, MEAN_RTOL, "gmw")
+    assert_rel(r1[1], rS, VAR_RTOL, "gSw")
+
+
+def test_golden_gemm_family(golden):
+    from triton_tagi.kernels.common import (triton_fused_backward_delta, triton_fused_var_forward,
+                                            triton_fused_weight_grad)
+
+    z = golden("kernels")
+    for tag in ("a", "b", "c"):
+        t = {k: g(z[f"gemm_{tag}_{k}"]) for k in ("ma", "Sa", "mw", "Sw", "Sb", "dmz", "dSz")}
+        assert_rel(triton_fused_var_forward(t["ma"], t["Sa"], t["mw"], t["Sw"], t["Sb"]),
+                   z[f"gemm_{tag}_Sz"], VAR_RTOL, "Sz")
+        d_ma, d_Sa = triton_fused_backward_delta(t["dmz"], t["dSz"], t["mw"])
+        assert_rel(d_ma, z[f"gemm_{tag}_d_ma"], MEAN_RTOL, "d_ma")
+        assert_rel(d_Sa, z[f"gemm_{tag}_d_Sa"], VAR_RTOL, "d_Sa")
+        gm, gS = triton_fused_weight_grad(t["ma"], t["dmz"], t["dSz"])
+        assert_rel(gm, z[f"gemm_{tag}_gmw"], MEAN_RTOL, "gmw")
+        assert_rel(gS, z[f"gemm_{tag}_gSw"], VAR_RTOL, "gSw")
+
+
+@pytest.mark.parametrize("cap", [0.1, 2.0, 3.0])
+def test_capped_update_golden(golden, cap):
+    from triton_tagi.update.parameters import update_parameters
+
+    z = golden("kernels")
+    m, S = g(z["upd_m"]), g(z["upd_S"])
+    update_parameters(m, S, g(z["upd_dm"]), g(z["upd_dS"]), cap)
+    np.testing.assert_allclose(m.cpu().numpy(), z[f"upd_cap{cap}_m"], rtol=2.5e-7, atol=0)
+    np.testing.assert_allclose(S.cpu().numpy(), z[f"upd_cap{cap}_S"], rtol=2.5e-7, atol=0)
+    # odd length and offset view take the scalar path
+    m2, S2 = g(z["upd_m"])[1:], g(z["upd_S"])[1:]
+    update_parameters(m2, S2, g(z["upd_dm"])[1:], g(z["upd_dS"])[1:], cap)
+    np.testing.assert_allclose(m2.cpu().numpy(), z[f"upd_cap{cap}_m"][1:], rtol=2.5e-7, atol=0)
+
+
+def test_innovation_golden(golden):
+    from triton_tagi.update.observation import compute_innovation
+
+    z = golden("kernels")
+    dm, dv = compute_innovation(g(z["inn_y"]), g(z["inn_mu"]), g(z["inn_var"]), 0.05)
+    np.testing.assert_allclose(dm.cpu().numpy(), z["inn_dmu"], rtol=1e-6, atol=0)
+    np.testing.assert_allclose(dv.cpu().numpy(), z["inn_dvar"], rtol=1e-6, atol=0)
+
+
+def test_relu_golden(golden):
+    from triton_tagi.layers.relu import bayesian_relu
+
+    z = golden("kernels")
+    mz, Sz = torch.from_numpy(z["relu_mz"]), torch.from_numpy(z["relu_Sz"])
+    got = bayesian_relu(g(mz), g(Sz))
+    ex = F.relu_moments(mz.double(), Sz.double())
+    for t, key, x in zip(got, ("relu_ma", "relu_Sa", "relu_J"), ex):
+        assert_as_accurate(t.cpu(), z[key], x, floor=1e-6, what=key)
+    odd = bayesian_relu(g(mz[:4093]), g(Sz[:4093]))  # scalar path
+    assert torch.equal(odd[0].cpu(), got[0][:4093].cpu())
+
+
+@pytest.mark.parametrize("tag", ["k10", "k64", "k512"])
+def test_remax_golden(golden, tag):
+    from triton_tagi.layers.remax import triton_remax
+
+    z = golden("kernels")
+    mz, Sz = torch.from_numpy(z[f"remax_{tag}_mz"]), torch.from_numpy(z[f"remax_{tag}_Sz"])
+    got = triton_remax(g(mz), g(Sz))
+    ex = F.remax(mz.double(), Sz.double())
+    # var_a = (exp(v)-1)·μ² and cov(A,M) = (exp(c)-1)·… cancel for small v, c:
+    # a 1-ulp difference between two exp implementations becomes ~1e-4 relative,
+    # so the bar is 4x the reference's own float32 error (same formula).
+    for t, nm, x in zip(got, ("ma", "Sa", "J"), ex):
+        assert_as_accurate(t.cpu(), z[f"remax_{tag}_{nm}"], x, factor=4.0, floor=1e-6,
+                           what=f"remax {nm}")
+
+
+@pytest.mark.parametrize("K", [3, 33, 200, 700])
+def test_remax_sizes(K):
+    from triton_tagi.layers.remax import triton_remax
+
+    gen = torch.Generator().manual_seed(K)
+    mz, Sz = rnd(gen, 65, K, scale=2.0), rnd(gen, 65, K, kind="u", scale=2.0, lo=1e-3)
+    got = triton_remax(g(mz), g(Sz))
+    ref32 = F.remax(mz, Sz)
+    ex = F.remax(mz.double(), Sz.double())
+    for t, r, x, nm in zip(got, ref32, ex, ("ma", "Sa", "J")):
+        assert_as_accurate(t.cpu(), r, x, factor=4.0, floor=1e-6, what=nm)
+
+
+def test_attention_products_golden(golden):
+    from triton_tagi.kernels.attention import bmm_shared_left, bmm_shared_right, bmm_tagi_var
+
+    z = golden("kernels")
+    ma, va, mb, vb = (g(z[k]) for k in ("att_ma", "att_va", "att_mb", "att_vb"))
+    tr = lambda t: t.transpose(-1, -2)  # noqa: E731
+    assert_rel(bmm_tagi_var(ma, va, tr(mb), tr(vb), 0.25), z["att_var_t"], VAR_RTOL, "var")
+    m, v = bmm_shared_right(ma, va, tr(mb), 0.5)
+    assert_rel(m, z["att_right_m"], MEAN_RTOL, "right m")
+    assert_rel(v, z["att_right_v"], VAR_RTOL, "right v")
+    m, v = bmm_shared_left(ma, g(z["att_bm"]), g(z["att_bv"]), 0.5)
+    assert_rel(m, z["att_left_m"], MEAN_RTOL, "left m")
+    assert_rel(v, z["att_left_v"], VAR_RTOL, "left v")
+    with pytest.raises(ValueError):
+        bmm_tagi_var(ma, va, mb, vb)
+
+
+def test_attention_products_fused_mean():
+    from triton_tagi.kernels.attention import bmm_tagi_moments
+
+    gen = torch.Generator().manual_seed(9)
+    ma, va = rnd(gen, 4, 8, 64, 32), rnd(gen, 4, 8, 64, 32, kind="u")
+    mb, vb = rnd(gen, 4, 8, 32, 48), rnd(gen, 4, 8, 32, 48, kind="u")
+    m, v = bmm_tagi_moments(g(ma), g(va), g(mb), g(vb), 0.125, 0.125**2)
+    assert_rel(m, 0.125 * (d64(ma) @ d64(mb)), MEAN_RTOL, "mean")
+    assert_rel(v, F.bmm_tagi_var(d64(ma), d64(va), d64(mb), d64(vb), 0.125**2), VAR_RTOL, "var")
+
+
+@pytest.mark.parametrize("tag,k,s,p", [("k3s1p1", 3, 1, 1), ("k3s2p1", 3, 2, 1),
+                                       ("k2s2p0", 2, 2, 0), ("k5s1p2", 5, 1, 2)])
+def test_im2col_col2im_golden(golden, tag, k, s, p):
+    from triton_tagi._lib import lib, stream
+
+    z = golden("kernels")
+    x = g(z["im2col_x"])
+    N, C, H, W = x.shape
+    Ho, Wo = F.conv_out_hw(H, W, k, s, p, 1)
+    pm = torch.empty(N * Ho * Wo, C * k * k, device=DEV)
+    pS = torch.empty_like(pm)
+    lib()("tagi_im2col", x.data_ptr(), x.data_ptr(), pm.data_ptr(), pS.data_ptr(), N, C, H, W, k,
+          s, p, 1, stream(x))
+    np.testing.assert_array_equal(pm.cpu().numpy(), z[f"im2col_{tag}"])
+    cols = pm * 0.5 + 1.0
+    for mode, adjoint in ((0, False), (1, True)):
+        out = torch.empty(N, C, H, W, device=DEV)
+        out2 = torch.empty_like(out)
+        lib()("tagi_col2im", cols.data_ptr(), cols.data_ptr(), out.data_ptr(), out2.data_ptr(), N,
+              C, H, W, k, s, p, 1, mode, stream(x))
+        ref = F.col2im(cols.cpu(), N, C, H, W, k, s, p, 1, adjoint=adjoint)
+        np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), rtol=1e-6, atol=1e-5)
+        if mode == 0:  # the reference's own gather
+            np.testing.assert_allclose(out.cpu().numpy(), z[f"col2im_{tag}"], rtol=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("shape,k,s,p,pt", [((2, 3, 9, 7), 3, 2, 1, 2), ((3, 4, 8, 8), 3, 1, 1, 1),
+                                            ((2, 5, 16, 16), 2, 2, 0, 1),
+                                            ((2, 3, 12, 12), 5, 1, 2, 1)])
+def test_conv_layer_against_oracle(shape, k, s, p, pt):
+    import oracle.net as ON
+    from triton_tagi import Conv2D
+
+    gen = torch.Generator().manual_seed(sum(shape) + k)
+    N, C, H, W = shape
+    Co = 6
+    ma, Sa = rnd(gen, *shape), rnd(gen, *shape, kind="u", scale=0.1)
+    torch.manual_seed(0)
+    ref = ON.Conv2D(C, Co, k, s, p, pt)
+    dev = Conv2D(C, Co, k, s, p, pt, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, g(getattr(ref, n)))
+    rm, rS = ref.forward(ma, Sa)
+    gm, gS = dev.forward(g(ma), g(Sa))
+    ex_m, ex_S, _ = F.conv_forward(ma.double(), Sa.double(), d64(ref.mw), d64(ref.Sw),
+                                   d64(ref.mb), d64(ref.Sb), k, s, p, pt)
+    assert_rel(gm, ex_m, MEAN_RTOL, "conv mz")
+    assert_rel(gS, ex_S, VAR_RTOL, "conv Sz")
+    dmz, dSz = rnd(gen, *rm.shape, scale=0.1), -rnd(gen, *rm.shape, kind="u", scale=0.01)
+    for mode in ("reference", "adjoint"):
+        dev.col2im_mode = mode
+        ref.col2im_adjoint = mode == "adjoint"
+        ref.forward(ma, Sa)
+        dev.forward(g(ma), g(Sa))
+        r_dm, r_dS = ref.backward(dmz, dSz)
+        d_dm, d_dS = dev.backward(g(dmz), g(dSz))
+        assert_rel(d_dm, r_dm, 1e-5, f"conv d_ma {mode}")
+        assert_rel(d_dS, r_dS, 1e-4, f"conv d_Sa {mode}")
+        for n in ("delta_mw", "delta_mb"):
+            assert_rel(getattr(dev, n), getattr(ref, n), 1e-5, n)
+        for n in ("delta_Sw", "delta_Sb"):
+            assert_rel(getattr(dev, n), getattr(ref, n), 1e-4, n)
+
+
+def test_batchnorm_layer_against_oracle():
+    import oracle.net as ON
+    from triton_tagi import BatchNorm2D
+
+    gen = torch.Generator().manual_seed(21)
+    N, C, H, W = 8, 16, 6, 6
+    ref, dev = ON.BatchNorm2D(C), BatchNorm2D(C, device=DEV)
+    for step in range(2):  # first call initialises running stats, second uses the EMA
+        mz, Sz = rnd(gen, N, C, H, W) + 0.3, rnd(gen, N, C, H, W, kind="u", scale=0.2)
+        rm, rS = ref.forward(mz, Sz)
+        gm, gS = dev.forward(g(mz), g(Sz))
+        assert_rel(gm, rm, 1e-5, f"bn ma {step}")
+        assert_rel(gS, rS, 1e-4, f"bn Sa {step}")
+        assert_rel(dev.running_mean, ref.running_mean, 1e-5, "running_mean")
+        assert_rel(dev.running_var, ref.running_var, 1e-5, "running_var")
+        assert_rel(dev.mw, ref.mw, 1e-6, "gamma (preserve_var)")
+        dm, dS = rnd(gen, N, C, H, W, scale=0.1), -rnd(gen, N, C, H, W, kind="u", scale=0.01)
+        r = ref.backward(dm, dS)
+        d = dev.backward(g(dm), g(dS))
+        assert_rel(d[0], r[0], 1e-5, "bn dmz")
+        assert_rel(d[1], r[1], 1e-4, "bn dSz")
+        for n, tol in (("delta_mw", 1e-5), ("delta_Sw", 1e-4), ("delta_mb", 1e-5),
+                       ("delta_Sb", 1e-4)):
+            assert_rel(getattr(dev, n), getattr(ref, n), tol, n)
+
+
+def test_avgpool_and_add():
+    from triton_tagi import AvgPool2D
+    from triton_tagi.layers.resblock import triton_add_shortcut
+
+    gen = torch.Generator().manual_seed(4)
+    for k, sc, shape in ((2, False, (3, 5, 8, 8)), (4, False, (2, 7, 4, 4)), (2, True, (2, 3, 7, 9))):
+        ma, Sa = rnd(gen, *shape), rnd(gen, *shape, kind="u")
+        pool = AvgPool2D(k, spatial_correlation=sc)
+        om, oS = pool.forward(g(ma), g(Sa))
+        rm, rS = F.avgpool_forward(ma, Sa, k, sc)
+        assert_rel(om, rm, 1e-6, "pool m")
+        assert_rel(oS, rS, 1e-6, "pool S")
+        dm, dS = rnd(gen, *om.shape), rnd(gen, *om.shape)
+        bm, bS = pool.backward(g(dm), g(dS))
+        em, eS = F.avgpool_backward(dm, dS, shape, k, sc)
+        assert_rel(bm, em, 1e-7, "pool dm")
+        assert_rel(bS, eS, 1e-7, "pool dS")
+    a, b = g(rnd(gen, 1001)), g(rnd(gen, 1001))
+    a2, b2 = a.clone(), b.clone()
+    triton_add_shortcut(a2, b2, a, b)
+    assert torch.equal(a, 2 * a2) and torch.equal(b, 2 * b2)
+
+
+def test_rmsnorm_against_oracle():
+    import oracle.net as ON
+    from triton_tagi import RMSNorm
+
+    gen = torch.Generator().manual_seed(12)
+    ref, dev = ON.RMSNorm(96), RMSNorm(96, device=DEV)
+    ref.mw = ref.mw + rnd(gen, 96, scale=0.1)
+    dev.mw = g(ref.mw)
+    ma, Sa = rnd(gen, 3, 50, 96), rnd(gen, 3, 50, 96, kind="u", scale=0.1)
+    rm, rS = ref.forward(ma, Sa)
+    gm, gS = dev.forward(g(ma), g(Sa))
+    assert_rel(gm, rm, 1e-5, "rms mz")
+    assert_rel(gS, rS, 1e-4, "rms Sz")
+    dm, dS = rnd(gen, 3, 50, 96, scale=0.1), -rnd(gen, 3, 50, 96, kind="u", scale=0.01)
+    r = ref.backward(dm, dS)
+    d = dev.backward(g(dm), g(dS))
+    assert_rel(d[0], r[0], 1e-5, "rms dma")
+    assert_rel(d[1], r[1], 1e-4, "rms dSa")
+    assert_rel(dev.delta_mw, ref.delta_mw, 1e-5, "rms delta_mw")
+    assert_rel(dev.delta_Sw, ref.delta_Sw, 1e-4, "rms delta_Sw")
+
+
+def test_empty_inputs_are_no_ops():
+    from triton_tagi.kernels.common import triton_fused_var_forward
+    from triton_tagi.update.parameters import update_parameters
+
+    z = torch.empty(0, 5, device=DEV)
+    w = torch.rand(5, 3, device=DEV)
+    assert triton_fused_var_forward(z, z, w, w, torch.zeros(1, 3, device=DEV)).shape == (0, 3)
+    e = torch.empty(0, device=DEV)
+    update_parameters(e, e, e, e, 2.0)

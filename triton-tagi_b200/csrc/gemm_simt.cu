@@ -1,0 +1,545 @@
+// Moment contractions on CUDA cores (fp32 FMA, the reference's arithmetic).
+//
+// Every contraction on the TAGI path has two accumulators over one shared
+// reduction: a mean product acc0 += x*u and a variance product acc1. Three
+// variance forms cover all of them:
+//   FULL : acc1 += x^2 v + y (u^2 + v)   Linear/Conv forward, bmm_tagi_var
+//   RSQ  : acc1 += y u^2                 backward delta, bmm_shared_right
+//   LSQ  : acc1 += x^2 v                 weight gradient, bmm_shared_left
+// The A side (x, y) is an M x Kr view whose rows may be "row-split" (NCHW
+// tensors read in place); the B side (u, v) is Kr x N whose reduction index
+// may be row-split. Squares are formed once per element while staging tiles
+// in shared memory. Large reductions with few output tiles (weight gradients
+// of convolutions) are split over the reduction and finished by a fixed-order
+// reduce kernel, so results are deterministic.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace tagi {
+namespace {
+
+enum VarMode { FULL = 0, RSQ = 1, LSQ = 2 };
+enum Epi { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_PARAM = 2 };
+
+struct ParamEpi {
+    int mode;  // TAGI_WGRAD_SUMS / DELTAS / UPDATE
+    int K, N;  // weight rows, columns; row K is the bias row when present
+    float *mw, *Sw, *mb, *Sb;
+    float *out_m, *out_S, *out_mb, *out_Sb;
+    float cap;
+};
+
+struct GemmArgs {
+    const float *x, *y;
+    RowMap arow;
+    int64_t ak;
+    int ones_row;
+    int64_t a_bs;
+    const float *u, *v;
+    RowMap brow;
+    int64_t bn;
+    int64_t b_bs;
+    float *o0, *o1;
+    RowMap orow;
+    int64_t on;
+    int64_t o_bs;
+    const float *bias0, *bias1;
+    float scale0, scale1;
+    int M, N, Kr;
+    int splits, kchunk;
+    float* ws;
+    ParamEpi pe;
+};
+
+constexpr int BM = 64, BN = 64, BK = 16, NT = 256, PAD = 4;
+
+__device__ __forceinline__ void param_epilogue(int r, int c, float g0, float g1,
+                                               const ParamEpi& p) {
+    const int64_t rc = static_cast<int64_t>(r) * p.N + c;
+    if (p.mode == TAGI_WGRAD_SUMS) {
+        p.out_m[rc] = g0;
+        p.out_S[rc] = g1;
+        return;
+    }
+    const bool bias = (r == p.K);
+    const int64_t w = bias ? c : rc;
+    float* mp = bias ? p.mb : p.mw;
+    float* Sp = bias ? p.Sb : p.Sw;
+    const float S = Sp[w];
+    const float dm = S * g0;
+    const float dS = (S * S) * g1;
+    if (p.mode == TAGI_WGRAD_DELTAS) {
+        (bias ? p.out_mb : p.out_m)[w] = dm;
+        (bias ? p.out_Sb : p.out_S)[w] = dS;
+        return;
+    }
+    float m = mp[w], Sn = S;
+    capped_pair(m, Sn, dm, dS, p.cap);
+    mp[w] = m;
+    Sp[w] = Sn;
+}
+
+template <int VM>
+struct Needs {
+    static constexpr bool y = (VM == FULL || VM == RSQ);
+    static constexpr bool v = (VM == FULL || VM == LSQ);
+    static constexpr int a_tiles = (VM == FULL) ? 3 : 2;
+    static constexpr int b_tiles = (VM == FULL) ? 3 : 2;
+};
+
+template <int VM, bool MEAN, int EPI>
+__global__ void __launch_bounds__(NT) moment_gemm_kernel(const GemmArgs g) {
+    using Nd = Needs<VM>;
+    __shared__ __align__(16) float As[Nd::a_tiles][BK][BM + PAD];
+    __shared__ __align__(16) float Bs[Nd::b_tiles][BK][BN + PAD];
+
+    const int tid = threadIdx.x;
+    const int tx = tid % 16, ty = tid / 16;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int batch = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
+    const int kbeg = split * g.kchunk;
+    const int kend = min(g.Kr, kbeg + g.kchunk);
+
+    const float* x = g.x + batch * g.a_bs;
+    const float* y = Nd::y ? g.y + batch * g.a_bs : nullptr;
+    const float* u = g.u + batch * g.b_bs;
+    const float* v = Nd::v ? g.v + batch * g.b_bs : nullptr;
+    const bool a_kcontig = (g.ak == 1);
+    const bool b_ncontig = (g.bn == 1);
+
+    int a_mm[4], a_kk[4], b_nn[4], b_kk[4];
+    int64_t a_off[4], b_col[4];
+    bool a_ok[4], a_one[4], b_ok[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int e = tid + i * NT;
+        if (a_kcontig) { a_kk[i] = e % BK; a_mm[i] = e / BK; }
+        else           { a_mm[i] = e % BM; a_kk[i] = e / BM; }
+        const int row = m0 + a_mm[i];
+        a_ok[i] = row < g.M;
+        a_one[i] = (row == g.ones_row);
+        a_off[i] = (a_ok[i] && !a_one[i]) ? g.arow.off(row) : 0;
+        if (b_ncontig) { b_nn[i] = e % BN; b_kk[i] = e / BN; }
+        else           { b_kk[i] = e % BK; b_nn[i] = e / BK; }
+        const int col = n0 + b_nn[i];
+        b_ok[i] = col < g.N;
+        b_col[i] = b_ok[i] ? static_cast<int64_t>(col) * g.bn : 0;
+    }
+
+    float rx[4], ry[4], ru[4], rv[4];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = k0 + a_kk[i];
+            const bool ok = a_ok[i] && k < kend;
+            const int64_t o = a_off[i] + static_cast<int64_t>(k) * g.ak;
+            rx[i] = ok ? (a_one[i] ? 1.f : __ldg(x + o)) : 0.f;
+            if (Nd::y) ry[i] = (ok && !a_one[i]) ? __ldg(y + o) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = k0 + b_kk[i];
+            const bool ok = b_ok[i] && k < kend;
+            const int64_t o = ok ? g.brow.off(k) + b_col[i] : 0;
+            ru[i] = ok ? __ldg(u + o) : 0.f;
+            if (Nd::v) rv[i] = ok ? __ldg(v + o) : 0.f;
+        }
+    };
+    auto store = [&]() {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            As[0][a_kk[i]][a_mm[i]] = rx[i];
+            if (VM == FULL) {
+                As[1][a_kk[i]][a_mm[i]] = rx[i] * rx[i];
+                As[2][a_kk[i]][a_mm[i]] = ry[i];
+            } else if (VM == RSQ) {
+                As[1][a_kk[i]][a_mm[i]] = ry[i];
+            } else {
+                As[1][a_kk[i]][a_mm[i]] = rx[i] * rx[i];
+            }
+            Bs[0][b_kk[i]][b_nn[i]] = ru[i];
+            if (VM == FULL) {
+                Bs[1][b_kk[i]][b_nn[i]] = rv[i];
+                Bs[2][b_kk[i]][b_nn[i]] = ru[i] * ru[i] + rv[i];
+            } else if (VM == RSQ) {
+                Bs[1][b_kk[i]][b_nn[i]] = ru[i] * ru[i];
+            } else {
+                Bs[1][b_kk[i]][b_nn[i]] = rv[i];
+            }
+        }
+    };
+
+    float acc0[4][4], acc1[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc0[i][j] = acc1[i][j] = 0.f;
+
+    if (kbeg < kend) load(kbeg);
+    for (int k0 = kbeg; k0 < kend; k0 += BK) {
+        __syncthreads();
+        store();
+        __syncthreads();
+        if (k0 + BK < kend) load(k0 + BK);
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&As[0][kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&As[1][kk][ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[0][kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[1][kk][tx * 4]);
+            const float av0[4] = {a0.x, a0.y, a0.z, a0.w}, av1[4] = {a1.x, a1.y, a1.z, a1.w};
+            const float bv0[4] = {b0.x, b0.y, b0.z, b0.w}, bv1[4] = {b1.x, b1.y, b1.z, b1.w};
+            if (VM == FULL) {
+                const float4 a2 = *reinterpret_cast<const float4*>(&As[2][kk][ty * 4]);
+                const float4 b2 = *reinterpret_cast<const float4*>(&Bs[2][kk][tx * 4]);
+                const float av2[4] = {a2.x, a2.y, a2.z, a2.w}, bv2[4] = {b2.x, b2.y, b2.z, b2.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (MEAN) acc0[i][j] = fmaf(av0[i], bv0[j], acc0[i][j]);
+                        acc1[i][j] = fmaf(av1[i], bv1[j], acc1[i][j]);
+                        acc1[i][j] = fmaf(av2[i], bv2[j], acc1[i][j]);
+                    }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (MEAN) acc0[i][j] = fmaf(av0[i], bv0[j], acc0[i][j]);
+                        acc1[i][j] = fmaf(av1[i], bv1[j], acc1[i][j]);
+                    }
+            }
+        }
+    }
+
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = m0 + ty * 4 + i;
+        if (r >= g.M) continue;
+        const int64_t ro = (EPI == EPI_STORE) ? g.orow.off(r) + batch * g.o_bs : 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = n0 + tx * 4 + j;
+            if (c >= g.N) continue;
+            if (EPI == EPI_STORE) {
+                const int64_t o = ro + static_cast<int64_t>(c) * g.on;
+                if (MEAN && g.o0) g.o0[o] = g.scale0 * acc0[i][j] + (g.bias0 ? g.bias0[c] : 0.f);
+                g.o1[o] = g.scale1 * acc1[i][j] + (g.bias1 ? g.bias1[c] : 0.f);
+            } else if (EPI == EPI_PARTIAL) {
+                const int64_t mn = static_cast<int64_t>(g.M) * g.N;
+                const int64_t o = static_cast<int64_t>(r) * g.N + c;
+                g.ws[(2 * split) * mn + o] = acc0[i][j];
+                g.ws[(2 * split + 1) * mn + o] = acc1[i][j];
+            } else {
+                param_epilogue(r, c, acc0[i][j], acc1[i][j], g.pe);
+            }
+        }
+    }
+}
+
+// Sums split-K partials in split order, then stores or applies the parameter epilogue.
+__global__ void splitk_finish_kernel(const GemmArgs g, int param) {
+    const int64_t mn = static_cast<int64_t>(g.M) * g.N;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < mn;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float g0 = 0.f, g1 = 0.f;
+        for (int s = 0; s < g.splits; ++s) {
+            g0 += g.ws[(2 * s) * mn + idx];
+            g1 += g.ws[(2 * s + 1) * mn + idx];
+        }
+        const int r = static_cast<int>(idx / g.N), c = static_cast<int>(idx % g.N);
+        if (param) {
+            param_epilogue(r, c, g0, g1, g.pe);
+        } else {
+            const int64_t o = g.orow.off(r) + static_cast<int64_t>(c) * g.on;
+            if (g.o0) g.o0[o] = g.scale0 * g0 + (g.bias0 ? g.bias0[c] : 0.f);
+            g.o1[o] = g.scale1 * g1 + (g.bias1 ? g.bias1[c] : 0.f);
+        }
+    }
+}
+
+inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// Reduction split for output grids too small to fill the GPU.
+void choose_splits(int M, int N, int Kr, int batch, int* splits, int* kchunk) {
+    int s = 1;
+    const int tiles = cdiv(M, BM) * cdiv(N, BN) * batch;
+    if (batch == 1 && tiles < 2 * kNumSMs) {
+        s = cdiv(2 * kNumSMs, tiles);
+        s = std::min(s, std::max(1, Kr / (BK * 8)));
+        s = std::min(s, 64);
+    }
+    int chunk = cdiv(cdiv(Kr, s), BK) * BK;
+    if (chunk < BK) chunk = BK;
+    *splits = cdiv(Kr, chunk);
+    if (*splits < 1) *splits = 1;
+    *kchunk = chunk;
+}
+
+template <int VM, bool MEAN, int EPI>
+int launch(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
+    if (g.M == 0 || g.N == 0) return TAGI_OK;
+    dim3 grid(cdiv(g.N, BN), cdiv(g.M, BM), batch * g.splits);
+    TAGI_REQUIRE(grid.y <= 65535 && grid.z <= 65535, TAGI_E_UNSUPPORTED, "%s: grid too large",
+                 what);
+    moment_gemm_kernel<VM, MEAN, EPI><<<grid, NT, 0, st>>>(g);
+    return check_launch(what);
+}
+
+GemmArgs blank() {
+    GemmArgs g{};
+    g.ones_row = -1;
+    g.scale0 = g.scale1 = 1.f;
+    g.splits = 1;
+    return g;
+}
+
+bool bad_size(int64_t v) { return v < 0 || v > (int64_t(1) << 31) - 1; }
+
+// Shared driver for the weight-gradient family (stores or parameter epilogue).
+int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
+              const char* what) {
+    int splits, chunk;
+    choose_splits(Mo, g.N, g.Kr, 1, &splits, &chunk);
+    g.M = Mo;
+    if (splits > 1) {
+        const size_t need = sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N;
+        TAGI_REQUIRE(ws != nullptr && ws_bytes >= need, TAGI_E_WORKSPACE,
+                     "%s: workspace of %zu bytes required, %zu given", what, need, ws_bytes);
+        g.splits = splits;
+        g.kchunk = chunk;
+        g.ws = static_cast<float*>(ws);
+        int rc = launch<LSQ, true, EPI_PARTIAL>(g, 1, st, what);
+        if (rc) return rc;
+        splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(Mo) * g.N, 256), 256, 0, st>>>(
+            g, param ? 1 : 0);
+        return check_launch(what);
+    }
+    g.splits = 1;
+    g.kchunk = g.Kr > 0 ? g.Kr : BK;
+    return param ? launch<LSQ, true, EPI_PARAM>(g, 1, st, what)
+                 : launch<LSQ, true, EPI_STORE>(g, 1, st, what);
+}
+
+size_t wgrad_ws_bytes(int Mo, int N, int Kr) {
+    int splits, chunk;
+    choose_splits(Mo, N, Kr, 1, &splits, &chunk);
+    return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * N : 0;
+}
+
+__global__ void apply_sums_kernel(const float* gm, const float* gS, ParamEpi p, int64_t total) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        param_epilogue(static_cast<int>(i / p.N), static_cast<int>(i % p.N), gm[i], gS[i], p);
+}
+
+}  // namespace
+}  // namespace tagi
+
+using namespace tagi;
+
+extern "C" int tagi_fused_var_forward(const float* ma, const float* Sa, const float* mw,
+                                      const float* Sw, const float* Sb, float* Sz, int64_t M,
+                                      int64_t N, int64_t K, int64_t stride_am, int64_t stride_ak,
+                                      int64_t stride_wk, int64_t stride_wn, int64_t stride_cm,
+                                      int64_t stride_cn, void* stream) {
+    const char* what = "tagi_fused_var_forward";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (M == 0 || N == 0) return TAGI_OK;
+    TAGI_REQUIRE(Sz && (K == 0 || (ma && Sa && mw && Sw)), TAGI_E_BAD_ARG, "%s: null pointer",
+                 what);
+    GemmArgs g = blank();
+    g.x = ma; g.y = Sa; g.arow = plain_rows(stride_am); g.ak = stride_ak;
+    g.u = mw; g.v = Sw; g.brow = plain_rows(stride_wk); g.bn = stride_wn;
+    g.o1 = Sz; g.orow = plain_rows(stride_cm); g.on = stride_cn; g.bias1 = Sb;
+    g.M = (int)M; g.N = (int)N; g.Kr = (int)K; g.kchunk = K > 0 ? (int)K : BK;
+    return launch<FULL, false, EPI_STORE>(g, 1, as_stream(stream), what);
+}
+
+extern "C" int tagi_moment_forward(const float* ma, const float* Sa, int64_t a_div,
+                                   int64_t a_outer, int64_t a_stride, int64_t a_kstride,
+                                   const float* mw, const float* Sw, int64_t ldw, const float* mb,
+                                   const float* Sb, float* mz, float* Sz, int64_t c_div,
+                                   int64_t c_outer, int64_t c_stride, int64_t c_nstride, int64_t M,
+                                   int64_t N, int64_t K, void* stream) {
+    const char* what = "tagi_moment_forward";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (M == 0 || N == 0) return TAGI_OK;
+    TAGI_REQUIRE(mz && Sz && (K == 0 || (ma && Sa && mw && Sw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = ma; g.y = Sa; g.arow = RowMap{a_div, a_outer, a_stride}; g.ak = a_kstride;
+    g.u = mw; g.v = Sw; g.brow = plain_rows(ldw); g.bn = 1;
+    g.o0 = mz; g.o1 = Sz; g.orow = RowMap{c_div, c_outer, c_stride}; g.on = c_nstride;
+    g.bias0 = mb; g.bias1 = Sb;
+    g.M = (int)M; g.N = (int)N; g.Kr = (int)K; g.kchunk = K > 0 ? (int)K : BK;
+    return launch<FULL, true, EPI_STORE>(g, 1, as_stream(stream), what);
+}
+
+extern "C" int tagi_backward_delta_view(const float* dmz, const float* dSz, int64_t d_div,
+                                        int64_t d_outer, int64_t d_stride, int64_t d_nstride,
+                                        const float* mw, int64_t ldw, float* d_ma, float* d_Sa,
+                                        int64_t c_div, int64_t c_outer, int64_t c_stride,
+                                        int64_t c_kstride, int64_t M, int64_t K, int64_t N,
+                                        void* stream) {
+    const char* what = "tagi_backward_delta_view";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (M == 0 || K == 0) return TAGI_OK;
+    TAGI_REQUIRE(d_ma && d_Sa && (N == 0 || (dmz && dSz && mw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = dmz; g.y = dSz; g.arow = RowMap{d_div, d_outer, d_stride}; g.ak = d_nstride;
+    // u[r = n, j = k] = mw[k, n]
+    g.u = mw; g.brow = plain_rows(1); g.bn = ldw;
+    g.o0 = d_ma; g.o1 = d_Sa; g.orow = RowMap{c_div, c_outer, c_stride}; g.on = c_kstride;
+    g.M = (int)M; g.N = (int)K; g.Kr = (int)N; g.kchunk = N > 0 ? (int)N : BK;
+    return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
+}
+
+extern "C" int tagi_fused_backward_delta(const float* dmz, const float* dSz, const float* mw,
+                                         float* d_ma, float* d_Sa, int64_t M, int64_t K,
+                                         int64_t N, int64_t stride_dm, int64_t stride_dn,
+                                         int64_t stride_wk, int64_t stride_wn, int64_t stride_cm,
+                                         int64_t stride_ck, void* stream) {
+    const char* what = "tagi_fused_backward_delta";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (M == 0 || K == 0) return TAGI_OK;
+    TAGI_REQUIRE(d_ma && d_Sa && (N == 0 || (dmz && dSz && mw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = dmz; g.y = dSz; g.arow = plain_rows(stride_dm); g.ak = stride_dn;
+    g.u = mw; g.brow = plain_rows(stride_wn); g.bn = stride_wk;
+    g.o0 = d_ma; g.o1 = d_Sa; g.orow = plain_rows(stride_cm); g.on = stride_ck;
+    g.M = (int)M; g.N = (int)K; g.Kr = (int)N; g.kchunk = N > 0 ? (int)N : BK;
+    return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
+}
+
+extern "C" size_t tagi_fused_weight_grad_workspace_size(int64_t M, int64_t K, int64_t N) {
+    if (bad_size(M) || bad_size(K) || bad_size(N)) return 0;
+    return wgrad_ws_bytes((int)K, (int)N, (int)M);
+}
+
+extern "C" int tagi_fused_weight_grad(const float* a, const float* dmz, const float* dSz,
+                                      float* grad_mw, float* grad_Sw, int64_t M, int64_t K,
+                                      int64_t N, int64_t stride_am, int64_t stride_ak,
+                                      int64_t stride_dm, int64_t stride_dn, int64_t stride_km,
+                                      int64_t stride_kn, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+    const char* what = "tagi_fused_weight_grad";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (K == 0 || N == 0) return TAGI_OK;
+    TAGI_REQUIRE(grad_mw && grad_Sw && (M == 0 || (a && dmz && dSz)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    // x[i = k, r = m] = a[m, k]
+    g.x = a; g.arow = plain_rows(stride_ak); g.ak = stride_am;
+    g.u = dmz; g.v = dSz; g.brow = plain_rows(stride_dm); g.bn = stride_dn;
+    g.o0 = grad_mw; g.o1 = grad_Sw; g.orow = plain_rows(stride_km); g.on = stride_kn;
+    g.N = (int)N; g.Kr = (int)M;
+    return run_wgrad(g, (int)K, workspace, workspace_bytes, false, as_stream(stream), what);
+}
+
+extern "C" size_t tagi_param_grad_workspace_size(int64_t M, int64_t K, int64_t N, int has_bias) {
+    if (bad_size(M) || bad_size(K) || bad_size(N)) return 0;
+    return wgrad_ws_bytes((int)K + (has_bias ? 1 : 0), (int)N, (int)M);
+}
+
+extern "C" int tagi_param_grad(const float* a, int64_t lda, const float* dmz, const float* dSz,
+                               int64_t d_div, int64_t d_outer, int64_t d_stride,
+                               int64_t d_nstride, int64_t M, int64_t K, int64_t N, int has_bias,
+                               int mode, float* mw, float* Sw, float* mb, float* Sb, float* out_m,
+                               float* out_S, float* out_mb, float* out_Sb, float cap_factor,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+    const char* what = "tagi_param_grad";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    TAGI_REQUIRE(M == 0 || (a && dmz && dSz), TAGI_E_BAD_ARG, "%s: null input", what);
+    if ((K + (has_bias ? 1 : 0)) == 0 || N == 0) return TAGI_OK;
+    TAGI_REQUIRE(mode >= TAGI_WGRAD_SUMS && mode <= TAGI_WGRAD_UPDATE, TAGI_E_BAD_ARG,
+                 "%s: bad mode %d", what, mode);
+    if (mode == TAGI_WGRAD_SUMS)
+        TAGI_REQUIRE(out_m && out_S, TAGI_E_BAD_ARG, "%s: sums need out_m/out_S", what);
+    if (mode != TAGI_WGRAD_SUMS) {
+        TAGI_REQUIRE(Sw && (!has_bias || Sb), TAGI_E_BAD_ARG, "%s: null variances", what);
+        TAGI_REQUIRE(cap_factor > 0.f, TAGI_E_BAD_ARG, "%s: cap_factor must be > 0", what);
+    }
+    if (mode == TAGI_WGRAD_DELTAS)
+        TAGI_REQUIRE(out_m && out_S && (!has_bias || (out_mb && out_Sb)), TAGI_E_BAD_ARG,
+                     "%s: deltas need output buffers", what);
+    if (mode == TAGI_WGRAD_UPDATE)
+        TAGI_REQUIRE(mw && (!has_bias || mb), TAGI_E_BAD_ARG, "%s: null means", what);
+    GemmArgs g = blank();
+    g.x = a; g.arow = plain_rows(1); g.ak = lda;
+    g.ones_row = has_bias ? (int)K : -1;
+    g.u = dmz; g.v = dSz; g.brow = RowMap{d_div, d_outer, d_stride}; g.bn = d_nstride;
+    g.N = (int)N; g.Kr = (int)M;
+    g.pe = ParamEpi{mode, (int)K, (int)N, mw, Sw, mb, Sb, out_m, out_S, out_mb, out_Sb,
+                    cap_factor};
+    return run_wgrad(g, (int)K + (has_bias ? 1 : 0), workspace, workspace_bytes, true,
+                     as_stream(stream), what);
+}
+
+extern "C" int tagi_apply_param_sums(const float* g_m, const float* g_S, int64_t K, int64_t N,
+                                     int has_bias, float* mw, float* Sw, float* mb, float* Sb,
+                                     float cap_factor, void* stream) {
+    const char* what = "tagi_apply_param_sums";
+    TAGI_REQUIRE(!bad_size(K) && !bad_size(N), TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    TAGI_REQUIRE(g_m && g_S && mw && Sw && (!has_bias || (mb && Sb)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    TAGI_REQUIRE(cap_factor > 0.f, TAGI_E_BAD_ARG, "%s: cap_factor must be > 0", what);
+    ParamEpi p{TAGI_WGRAD_UPDATE, (int)K, (int)N, mw, Sw, mb, Sb, nullptr, nullptr, nullptr,
+               nullptr, cap_factor};
+    const int64_t total = (K + (has_bias ? 1 : 0)) * N;
+    if (total == 0) return TAGI_OK;
+    apply_sums_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(g_m, g_S, p, total);
+    return check_launch(what);
+}
+
+extern "C" int tagi_bmm_tagi_var(const float* mu_a, const float* var_a, const float* mu_b,
+                                 const float* var_b, float* mean, float* var, int64_t batch,
+                                 int64_t M, int64_t L, int64_t K, int64_t sa_n, int64_t sa_m,
+                                 int64_t sa_k, int64_t sb_n, int64_t sb_k, int64_t sb_l,
+                                 int64_t so_n, int64_t so_m, int64_t so_l, float scale,
+                                 float scale_sq, void* stream) {
+    const char* what = "tagi_bmm_tagi_var";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(L) && !bad_size(K) && batch >= 0 && batch <= 65535,
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (batch == 0 || M == 0 || L == 0) return TAGI_OK;
+    TAGI_REQUIRE(var && (K == 0 || (mu_a && var_a && mu_b && var_b)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = mu_a; g.y = var_a; g.arow = plain_rows(sa_m); g.ak = sa_k; g.a_bs = sa_n;
+    g.u = mu_b; g.v = var_b; g.brow = plain_rows(sb_k); g.bn = sb_l; g.b_bs = sb_n;
+    g.o0 = mean; g.o1 = var; g.orow = plain_rows(so_m); g.on = so_l; g.o_bs = so_n;
+    g.scale0 = scale; g.scale1 = scale_sq;
+    g.M = (int)M; g.N = (int)L; g.Kr = (int)K; g.kchunk = K > 0 ? (int)K : BK;
+    if (mean) return launch<FULL, true, EPI_STORE>(g, (int)batch, as_stream(stream), what);
+    return launch<FULL, false, EPI_STORE>(g, (int)batch, as_stream(stream), what);
+}
+
+extern "C" int tagi_bmm_shared_right(const float* a_mean, const float* a_var, const float* b,
+                                     float* mean, float* var, int64_t batch, int64_t M, int64_t L,
+                                     int64_t K, int64_t sa_n, int64_t sa_m, int64_t sa_k,
+                                     int64_t sb_n, int64_t sb_k, int64_t sb_l, int64_t so_n,
+                                     int64_t so_m, int64_t so_l, float scale, void* stream) {
+    const char* what = "tagi_bmm_shared_right";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(L) && !bad_size(K) && batch >= 0 && batch <= 65535,
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (batch == 0 || M == 0 || L == 0) return TAGI_OK;
+    TAGI_REQUIRE(mean && var && (K == 0 || (a_mean && a_var && b)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = a_mean; g.y = a_var; g.arow = plain_rows(sa_m); g.ak = sa_k; g.a_bs = sa_n;
+    g.u = b; g.brow = plain_rows(sb_k); g.bn = sb_l; g.b_bs = sb_n;
+    g.o0 = mean; g.o1 = var; g.orow = plain_rows(so_m); g.on = so_l; g.o_bs = so_n;
+    g.scale0 = scale; g.scale1 = scale * scale;
+    g.M = (int)M; g.N = (int)L; g.Kr = (int)K; g.kchunk = K > 0 ? (int)K : BK;
+    return launch<RSQ, true, EPI_STORE>(g, (int)batch, as_stream(stream), what);
+}

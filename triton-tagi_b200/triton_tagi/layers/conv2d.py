@@ -1,0 +1,121 @@
+"""Bayesian Conv2D via patches (drop-in for triton_tagi/layers/conv2d.py).
+
+Forward (conv2d.py:254-309): one kernel extracts mean and variance patches
+(N·L, C·k·k), then the fused moment kernel computes
+    μ_z = P_μ @ μ_w + μ_b,  S_z = P_μ² @ S_w + P_S @ (μ_w² + S_w) + S_b
+and writes the result directly in NCHW (no permute copy).
+Backward (conv2d.py:314-371): the patch-space deltas δP = δμ_z @ μ_wᵀ,
+δP_S = δS_z @ (μ_w²)ᵀ read δ in NCHW in place, are folded back to the input
+by the col2im gather, and the weight sums P_μᵀ·δμ_z, (P_μ²)ᵀ·δS_z (bias as a
+row of ones) feed the parameter mode of the layer.
+
+``col2im_mode``: "reference" (default) gathers exactly as the reference's
+_col2im_kernel (conv2d.py:119-130), which for stride > 1 does not test the
+column offset for divisibility by the stride; "adjoint" is the true adjoint
+of im2col. The two agree for stride 1.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from .._lib import check_cuda_f32, lib, stream
+from ..base import LearnableLayer
+from ..param_init import init_weight_bias_conv2d
+from ._params import contiguous_params, weight_apply_sums, weight_param_backward, weight_update
+
+_COL2IM_MODES = {"reference": 0, "adjoint": 1}
+
+
+class Conv2D(LearnableLayer):
+    def __init__(self, C_in: int, C_out: int, kernel_size: int, stride: int = 1,
+                 padding: int = 0, padding_type: int = 1, device="cuda", init_method="He",
+                 gain_w: float = 1.0, gain_b: float = 1.0, col2im_mode: str = "reference") -> None:
+        if padding_type not in (1, 2):
+            raise ValueError("padding_type must be 1 (symmetric) or 2 (right/bottom)")
+        if col2im_mode not in _COL2IM_MODES:
+            raise ValueError(f"col2im_mode must be one of {sorted(_COL2IM_MODES)}")
+        self.C_in, self.C_out = C_in, C_out
+        self.kH = self.kW = kernel_size
+        self.stride, self.padding, self.padding_type = stride, padding, padding_type
+        self.col2im_mode = col2im_mode
+        self.device = torch.device(device)
+        self.mw, self.Sw, self.mb, self.Sb = init_weight_bias_conv2d(
+            kernel_size, C_in, C_out, init_method=init_method, gain_w=gain_w, gain_b=gain_b,
+            device=self.device)
+        self.has_bias = True
+        self.patches_ma = None
+        self.input_shape = None
+        self.spatial = None
+        self.delta_mw = self.delta_Sw = self.delta_mb = self.delta_Sb = None
+
+    def _out_hw(self, H: int, W: int) -> tuple[int, int]:
+        k, s, p = self.kH, self.stride, self.padding
+        if self.padding_type == 2 and p > 0:
+            return (H + p - k) // s + 1, (W + p - k) // s + 1
+        return (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+
+    def forward(self, ma: Tensor, Sa: Tensor) -> tuple[Tensor, Tensor]:
+        check_cuda_f32(ma, Sa)
+        contiguous_params(self)
+        ma, Sa = ma.contiguous(), Sa.contiguous()
+        N, C, H, W = ma.shape
+        if C != self.C_in:
+            raise ValueError(f"Conv2D expects {self.C_in} input channels, got {C}")
+        self.input_shape = (N, C, H, W)
+        Ho, Wo = self._out_hw(H, W)
+        self.spatial = (Ho, Wo)
+        L, K, Co = Ho * Wo, C * self.kH * self.kW, self.C_out
+        dev = ma.device
+        pm = torch.empty(N * L, K, device=dev)
+        pS = torch.empty(N * L, K, device=dev)
+        st = stream(ma)
+        lib()("tagi_im2col", ma.data_ptr(), Sa.data_ptr(), pm.data_ptr(), pS.data_ptr(), N, C, H,
+              W, self.kH, self.stride, self.padding, self.padding_type, st)
+        self.patches_ma = pm
+        mz = torch.empty(N, Co, Ho, Wo, device=dev)
+        Sz = torch.empty(N, Co, Ho, Wo, device=dev)
+        # output row r = (n, l) -> n*Co*L + l, column c -> c*L  (NCHW)
+        lib()("tagi_moment_forward", pm.data_ptr(), pS.data_ptr(), 0, 0, K, 1, self.mw.data_ptr(),
+              self.Sw.data_ptr(), Co, self.mb.data_ptr(), self.Sb.data_ptr(), mz.data_ptr(),
+              Sz.data_ptr(), L, Co * L, 1, L, N * L, Co, K, st)
+        return mz, Sz
+
+    def backward(self, delta_mz: Tensor, delta_Sz: Tensor) -> tuple[Tensor, Tensor]:
+        check_cuda_f32(delta_mz, delta_Sz)
+        dmz, dSz = delta_mz.contiguous(), delta_Sz.contiguous()
+        N, C, H, W = self.input_shape
+        Ho, Wo = self.spatial
+        L, K, Co = Ho * Wo, C * self.kH * self.kW, self.C_out
+        dev = dmz.device
+        st = stream(dmz)
+        d_map = (L, Co * L, 1, L)  # NCHW delta read as an (N·L) x Co matrix
+        dpm = torch.empty(N * L, K, device=dev)
+        dpS = torch.empty(N * L, K, device=dev)
+        lib()("tagi_backward_delta_view", dmz.data_ptr(), dSz.data_ptr(), *d_map,
+              self.mw.data_ptr(), Co, dpm.data_ptr(), dpS.data_ptr(), 0, 0, K, 1, N * L, K, Co, st)
+        d_ma = torch.empty(N, C, H, W, device=dev)
+        d_Sa = torch.empty(N, C, H, W, device=dev)
+        lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N,
+              C, H, W, self.kH, self.stride, self.padding, self.padding_type,
+              _COL2IM_MODES[self.col2im_mode], st)
+        weight_param_backward(self, self.patches_ma, K, (dmz, dSz), d_map, N * L, K, Co, True)
+        return d_ma, d_Sa
+
+    def update(self, cap_factor: float) -> None:
+        weight_update(self, cap_factor, True)
+
+    def _sums_numel(self) -> int:
+        return 2 * (self.C_in * self.kH * self.kW + 1) * self.C_out
+
+    def _apply_sums(self, buf: Tensor, cap: float) -> None:
+        weight_apply_sums(self, buf, self.C_in * self.kH * self.kW, self.C_out, True, cap)
+
+    @property
+    def num_parameters(self) -> int:
+        return 2 * (self.mw.numel() + self.mb.numel())
+
+    def __repr__(self):
+        return (f"Conv2D({self.C_in}, {self.C_out}, kernel={self.kH}, stride={self.stride}, "
+                f"pad={self.padding})")

@@ -1,0 +1,126 @@
+"""Sequential container (drop-in for triton_tagi/network.py).
+
+``step(x, y, σ_v)`` runs forward → innovation → backward → capped update and
+returns the pre-update predictions, exactly as the reference
+(network.py:119-152). Two differences in *how*, not *what*:
+
+* With ``fuse_update=True`` (default) each learnable layer applies its capped
+  update inside its backward, right after propagating the deltas with the
+  pre-update weights; the weight-gradient kernel then writes the parameters
+  directly and no delta tensors are allocated. Every layer's update only
+  touches its own parameters, so the result is the reference's
+  backward-then-update. ``fuse_update=False`` keeps the reference's call
+  structure (``delta_*`` tensors stored, ``update`` applied afterwards).
+* Under data parallelism (``triton_tagi.distributed``) the batch sums of every
+  layer are all-reduced before the update and the cap factor uses the global
+  batch, so every replica applies the single-batch closed form.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from .base import Layer, LearnableLayer
+from .layers.multihead_attention import MultiheadAttentionV2
+from .layers.resblock import ResBlock
+from .update.observation import compute_innovation
+from .update.parameters import get_cap_factor
+
+
+class Sequential:
+    def __init__(self, layers: list, device="cuda", fuse_update: bool = True) -> None:
+        self.device = torch.device(device)
+        self.layers = layers
+        self.fuse_update = fuse_update
+        self.reducer = None  # set by triton_tagi.distributed.DataParallel
+        for layer in self.layers:
+            if isinstance(layer, ResBlock):
+                layer.device = self.device
+                for sub in layer._learnable:
+                    self._move_layer_to_device(sub)
+            elif isinstance(layer, LearnableLayer):
+                self._move_layer_to_device(layer)
+            if hasattr(layer, "running_mean"):
+                layer.running_mean = layer.running_mean.to(self.device)
+                layer.running_var = layer.running_var.to(self.device)
+
+    def _move_layer_to_device(self, layer) -> None:
+        if isinstance(layer, MultiheadAttentionV2):
+            layer.device = self.device
+            for sub in (layer.q_proj, layer.k_proj, layer.v_proj):
+                self._move_layer_to_device(sub)
+            return
+        if getattr(layer, "mw", None) is None:
+            return
+        layer.device = self.device
+        for name in ("mw", "Sw", "mb", "Sb", "running_mean", "running_var"):
+            t = getattr(layer, name, None)
+            if t is not None:
+                setattr(layer, name, t.to(self.device))
+
+    def learnable_layers(self) -> list[LearnableLayer]:
+        return [layer for layer in self.layers if isinstance(layer, LearnableLayer)]
+
+    def leaves(self) -> list[LearnableLayer]:
+        """Learnable layers that own parameters, in network order."""
+        out = []
+        for layer in self.learnable_layers():
+            out += layer._leaves()
+        return out
+
+    def forward(self, x: Tensor) -> tuple[Tensor, Tensor]:
+        ma, Sa = x, torch.zeros_like(x)
+        for layer in self.layers:
+            if not isinstance(layer, Layer):
+                raise TypeError(f"Unknown layer type: {type(layer)}")
+            ma, Sa = layer.forward(ma, Sa)
+        return ma, Sa
+
+    def step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
+        red = self.reducer
+        global_batch = x_batch.shape[0] * (red.world_size if red is not None else 1)
+        y_pred_mu, y_pred_var = self.forward(x_batch)
+        delta_mu, delta_var = compute_innovation(y_batch, y_pred_mu, y_pred_var, sigma_v)
+        cap = get_cap_factor(global_batch)
+        mode = "sums" if red is not None else ("update" if self.fuse_update else "deltas")
+        learn = self.learnable_layers()
+        for layer in learn:
+            layer._set_param_mode(mode, cap, red)
+        try:
+            if red is not None:
+                red.begin_step()
+            for layer in reversed(self.layers):
+                delta_mu, delta_var = layer.backward(delta_mu, delta_var)
+            if red is not None:
+                red.finish_step(cap)
+            for layer in learn:
+                layer.update(cap)
+        finally:
+            for layer in learn:
+                layer._set_param_mode("deltas")
+        return y_pred_mu, y_pred_var
+
+    def train(self) -> None:
+        for layer in self.layers:
+            if hasattr(layer, "training"):
+                layer.train()
+
+    def eval(self) -> None:
+        for layer in self.layers:
+            if hasattr(layer, "training"):
+                layer.eval()
+
+    def __repr__(self):
+        lines = ["Sequential("] + [f"  ({i}): {layer}" for i, layer in enumerate(self.layers)]
+        return "\n".join(lines + [")"])
+
+    def num_parameters(self) -> int:
+        return sum(layer.num_parameters for layer in self.learnable_layers())
+
+    def get_attention_scores(self) -> dict[int, tuple[Tensor, Tensor]]:
+        out = {i: layer.get_attention_scores() for i, layer in enumerate(self.layers)
+               if isinstance(layer, MultiheadAttentionV2)}
+        if not out:
+            raise RuntimeError("No attention layers in this Sequential.")
+        return out
