@@ -3,8 +3,10 @@
 Row-wise over the last dim (remax.py:33-114): MixtureReLU moments of
 M = max(0, Z); log-normal moments of M and M̃ = ΣM; A = M/M̃ renormalised so
 Σμ_A = 1; J = cov(A, Z)/var(Z) with cov(A, Z) = cov(A, M)/Φ(α) capped by the
-Cauchy–Schwarz bound. One warp per row; rows up to 512 classes are held in
-registers. Backward: δμ·J, δS·J².
+Cauchy–Schwarz bound. One warp per row. Inputs and outputs are float32; the
+closed form is evaluated in float64 because it cancels heavily (float32
+evaluations that merely round differently disagree by up to ~1e-3 in variance
+and Jacobian, and training amplifies that). Backward: δμ·J, δS·J².
 """
 
 from __future__ import annotations
