@@ -93,6 +93,27 @@ int tagi_fused_weight_grad(const float* a, const float* dmz, const float* dSz, f
                            int64_t stride_km, int64_t stride_kn, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Same contraction and the same results as tagi_fused_weight_grad, for callers
+ * that cannot allocate device memory: a host runtime that reaches this library
+ * only through a C FFI and owns no CUDA allocator, or an application whose
+ * device memory is a fixed pool that a plugin may not grow. Instead of a caller
+ * workspace, the split-reduction partial sums go to one array of
+ * TAGI_STATIC_SCRATCH_BYTES that lives in the library's device image: every
+ * GPU that loads the library holds it until the process exits. Shapes whose
+ * split plan needs more than that return TAGI_E_WORKSPACE. The first call on a
+ * device looks up that device's copy of the array (cudaGetSymbolAddress on
+ * the current device), so make the first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU (e.g. on two
+ * streams at once) race. Nothing needs clearing between calls, because each
+ * call writes every scratch element it reads. No counterpart in the
+ * reference. */
+#define TAGI_STATIC_SCRATCH_BYTES (16u << 20)
+int tagi_fused_weight_grad_static(const float* a, const float* dmz, const float* dSz,
+                                  float* grad_mw, float* grad_Sw, int64_t M, int64_t K, int64_t N,
+                                  int64_t stride_am, int64_t stride_ak, int64_t stride_dm,
+                                  int64_t stride_dn, int64_t stride_km, int64_t stride_kn,
+                                  void* stream);
+
 /* Parameter side of Linear/Conv2D backward + update over a batch of M rows.
  *   g_m[k,n] = sum_r a[r,k] dmz[r,n],   g_S[k,n] = sum_r a[r,k]^2 dSz[r,n]
  *   (row k == K, when has_bias, is the bias: a == 1)

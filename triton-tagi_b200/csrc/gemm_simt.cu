@@ -13,6 +13,7 @@
 // of convolutions) are split over the reduction and finished by a fixed-order
 // reduce kernel, so results are deterministic.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -542,4 +543,78 @@ extern "C" int tagi_bmm_shared_right(const float* a_mean, const float* a_var, co
     g.scale0 = scale; g.scale1 = scale * scale;
     g.M = (int)M; g.N = (int)L; g.Kr = (int)K; g.kchunk = K > 0 ? (int)K : BK;
     return launch<RSQ, true, EPI_STORE>(g, (int)batch, as_stream(stream), what);
+}
+
+// ---- weight sums without a caller workspace ---------------------------------
+// The split-reduction partials of tagi_fused_weight_grad_static live in this
+// array of the device image (one copy per GPU that loads the library). Host code
+// must not pass `g_static_scratch` itself to a kernel: on the host the name
+// denotes a stand-in, not the device address. The address is looked up once per
+// device with that device current and cached.
+namespace tagi {
+namespace {
+
+constexpr size_t kStaticScratchBytes = TAGI_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) float g_static_scratch[kStaticScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+float* g_static_addr[kMaxDevices] = {};
+
+int static_scratch_address(float** out, const char* what) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        set_error("%s: no usable current device (%s)", what, cudaGetErrorString(e));
+        return TAGI_E_LAUNCH;
+    }
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            set_error("%s: cudaGetSymbolAddress failed on device %d (%s)", what, dev,
+                      cudaGetErrorString(e));
+            return TAGI_E_LAUNCH;
+        }
+        g_static_addr[dev] = static_cast<float*>(p);
+    }
+    *out = g_static_addr[dev];
+    return TAGI_OK;
+}
+
+}  // namespace
+}  // namespace tagi
+
+extern "C" int tagi_fused_weight_grad_static(const float* a, const float* dmz, const float* dSz,
+                                             float* grad_mw, float* grad_Sw, int64_t M,
+                                             int64_t K, int64_t N, int64_t stride_am,
+                                             int64_t stride_ak, int64_t stride_dm,
+                                             int64_t stride_dn, int64_t stride_km,
+                                             int64_t stride_kn, void* stream) {
+    const char* what = "tagi_fused_weight_grad_static";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (K == 0 || N == 0) return TAGI_OK;
+    TAGI_REQUIRE(grad_mw && grad_Sw && (M == 0 || (a && dmz && dSz)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    const size_t need = wgrad_ws_bytes((int)K, (int)N, (int)M);
+    TAGI_REQUIRE(need <= kStaticScratchBytes, TAGI_E_WORKSPACE,
+                 "%s: this shape needs %zu bytes of scratch, more than the library's static "
+                 "%zu-byte array; use tagi_fused_weight_grad with a workspace",
+                 what, need, kStaticScratchBytes);
+    float* scratch = nullptr;
+    if (need > 0) {
+        const int rc = static_scratch_address(&scratch, what);
+        if (rc) return rc;
+    }
+    GemmArgs g = blank();
+    g.x = a; g.arow = plain_rows(stride_ak); g.ak = stride_am;
+    g.u = dmz; g.v = dSz; g.brow = plain_rows(stride_dm); g.bn = stride_dn;
+    g.o0 = grad_mw; g.o1 = grad_Sw; g.orow = plain_rows(stride_km); g.on = stride_kn;
+    g.N = (int)N; g.Kr = (int)M;
+    return run_wgrad(g, (int)K, scratch, need > 0 ? kStaticScratchBytes : 0, false,
+                     as_stream(stream), what);
 }

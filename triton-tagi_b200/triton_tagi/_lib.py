@@ -28,6 +28,7 @@ _SIGS = {
     "tagi_backward_delta_view": "pp" + "iiii" + "pi" + "pp" + "iiii" + "iii" + "p",
     "tagi_fused_weight_grad_workspace_size": "iii",
     "tagi_fused_weight_grad": "ppppp" + "iii" + "iiiiii" + "pz" + "p",
+    "tagi_fused_weight_grad_static": "ppppp" + "iii" + "iiiiii" + "p",
     "tagi_param_grad_workspace_size": "iiin",
     "tagi_param_grad": "pipp" + "iiii" + "iii" + "nn" + "pppp" + "pppp" + "f" + "pz" + "p",
     "tagi_apply_param_sums": "pp" + "ii" + "n" + "pppp" + "f" + "p",
