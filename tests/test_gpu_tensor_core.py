@@ -1,0 +1,176 @@
+"""The tcgen05 (3xTF32) moment contractions against the float64 oracle.
+
+Shapes are chosen so that the library routes them to the tensor-core kernel
+(M ≥ 64, N ≥ 16, reduction ≥ 32 and M·N·K ≥ 4e6) and cover ragged tails in
+every dimension, the variance-only forward, row-split (NCHW) operand views,
+the split reduction of the weight sums, the fused capped update and batched
+attention products. Each test also checks that no bounded wait inside the
+kernel ran out (tagi_device_status).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import oracle.moments as F
+from _tol import MEAN_RTOL, VAR_RTOL, assert_rel
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ok():
+    from triton_tagi._lib import device_status
+
+    assert device_status(reset=True) == 0, "a tensor-core kernel wait timed out"
+
+
+def _rnd(gen, *shape, u=False, scale=1.0, lo=0.0):
+    t = torch.rand(*shape, generator=gen) if u else torch.randn(*shape, generator=gen)
+    return t * scale + lo
+
+
+def _routes_to_tc(M, N, K):
+    return M >= 64 and N >= 16 and K >= 32 and M * N * K >= 4e6
+
+
+TC_SHAPES = [(128, 64, 512), (300, 77, 200), (1000, 576, 64), (2048, 1152, 128),
+             (4099, 35, 130), (1555, 256, 17)]
+
+
+@pytest.mark.parametrize("M,K,N", TC_SHAPES)
+def test_forward_full(M, K, N):
+    from triton_tagi import Linear
+    from triton_tagi.kernels.common import triton_fused_var_forward
+
+    assert _routes_to_tc(M, N, K)
+    g = torch.Generator().manual_seed(M + K + N)
+    ma, Sa = _rnd(g, M, K), _rnd(g, M, K, u=True, scale=1e-2, lo=1e-4)
+    mw, Sw = _rnd(g, K, N, scale=K**-0.5), _rnd(g, K, N, u=True, scale=1.0 / K)
+    mb, Sb = _rnd(g, 1, N, scale=0.1), _rnd(g, 1, N, u=True, scale=1e-3)
+    lin = Linear(K, N, device=DEV)
+    lin.mw, lin.Sw, lin.mb, lin.Sb = (t.to(DEV) for t in (mw, Sw, mb, Sb))
+    mz, Sz = lin.forward(ma.to(DEV), Sa.to(DEV))
+    d = lambda t: t.double()  # noqa: E731
+    assert_rel(mz, F.mean_forward(d(ma), d(mw), d(mb)), MEAN_RTOL, "mz")
+    ref_S = F.var_forward(d(ma), d(Sa), d(mw), d(Sw), d(Sb))
+    assert_rel(Sz, ref_S, VAR_RTOL, "Sz")
+    only = triton_fused_var_forward(ma.to(DEV), Sa.to(DEV), mw.to(DEV), Sw.to(DEV), Sb.to(DEV))
+    assert_rel(only, ref_S, VAR_RTOL, "Sz (variance only)")
+    _ok()
+
+
+@pytest.mark.parametrize("M,K,N", TC_SHAPES)
+def test_backward_delta_and_weight_sums(M, K, N):
+    from triton_tagi.kernels.common import triton_fused_backward_delta, triton_fused_weight_grad
+
+    g = torch.Generator().manual_seed(3 * M + N)
+    a, mw = _rnd(g, M, K), _rnd(g, K, N, scale=K**-0.5)
+    dmz, dSz = _rnd(g, M, N, scale=0.1), -_rnd(g, M, N, u=True, scale=1e-2)
+    d_ma, d_Sa = triton_fused_backward_delta(dmz.to(DEV), dSz.to(DEV), mw.to(DEV))
+    r_ma, r_Sa = F.backward_delta(dmz.double(), dSz.double(), mw.double())
+    assert_rel(d_ma, r_ma, MEAN_RTOL, "d_ma")
+    assert_rel(d_Sa, r_Sa, VAR_RTOL, "d_Sa")
+    gm, gS = triton_fused_weight_grad(a.to(DEV), dmz.to(DEV), dSz.to(DEV))
+    rm, rS = F.weight_grad(a.double(), dmz.double(), dSz.double())
+    assert_rel(gm, rm, MEAN_RTOL, "grad_mw")
+    assert_rel(gS, rS, VAR_RTOL, "grad_Sw")
+    _ok()
+
+
+def test_weight_sums_long_reduction_split():
+    from triton_tagi.kernels.common import triton_fused_weight_grad
+
+    g = torch.Generator().manual_seed(11)
+    a, dmz, dSz = _rnd(g, 60000, 300), _rnd(g, 60000, 64), _rnd(g, 60000, 64, u=True)
+    gm, gS = triton_fused_weight_grad(a.to(DEV), dmz.to(DEV), dSz.to(DEV))
+    rm, rS = F.weight_grad(a.double(), dmz.double(), dSz.double())
+    assert_rel(gm, rm, MEAN_RTOL, "grad_mw")
+    assert_rel(gS, rS, VAR_RTOL, "grad_Sw")
+    _ok()
+
+
+@pytest.mark.parametrize("mode", ["deltas", "update"])
+def test_linear_parameter_epilogue(mode):
+    import oracle.net as ON
+    from triton_tagi import Linear
+
+    g = torch.Generator().manual_seed(5)
+    M, K, N = 512, 600, 96
+    torch.manual_seed(1)
+    ref = ON.Linear(K, N)
+    dev = Linear(K, N, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, getattr(ref, n).to(DEV))
+    ma = _rnd(g, M, K)
+    ref.forward(ma, torch.zeros_like(ma))
+    dev.forward(ma.to(DEV), torch.zeros(M, K, device=DEV))
+    dm, dS = _rnd(g, M, N, scale=0.1), -_rnd(g, M, N, u=True, scale=1e-2)
+    ref.backward(dm, dS)
+    prev_S = ref.Sw.clone()
+    dev._set_param_mode(mode, 3.0)
+    dev.backward(dm.to(DEV), dS.to(DEV))
+    if mode == "deltas":
+        assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "delta_mw")
+        assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "delta_Sw")
+        assert_rel(dev.delta_mb, ref.delta_mb, MEAN_RTOL, "delta_mb")
+    else:
+        ref.update(3.0)
+        assert_rel(dev.mw, ref.mw, MEAN_RTOL, "mw")
+        from _tol import var_update_err
+
+        assert var_update_err(dev.Sw, ref.Sw, prev_S) <= VAR_RTOL
+    dev._set_param_mode("deltas")
+    _ok()
+
+
+def test_conv_layer_nchw_views_on_tensor_cores():
+    import oracle.net as ON
+    from triton_tagi import Conv2D
+
+    g = torch.Generator().manual_seed(8)
+    N, C, H, W, Co = 8, 16, 16, 16, 32  # M = 2048, K = 144, N = 32
+    torch.manual_seed(2)
+    ref = ON.Conv2D(C, Co, 3, 1, 1, 1)
+    dev = Conv2D(C, Co, 3, 1, 1, 1, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, getattr(ref, n).to(DEV))
+    ma, Sa = _rnd(g, N, C, H, W), _rnd(g, N, C, H, W, u=True, scale=0.1)
+    rm, rS = ref.forward(ma, Sa)
+    dm_, dS_ = dev.forward(ma.to(DEV), Sa.to(DEV))
+    assert_rel(dm_, rm, MEAN_RTOL, "conv mz")
+    assert_rel(dS_, rS, VAR_RTOL, "conv Sz")
+    dmz, dSz = _rnd(g, *rm.shape, scale=0.1), -_rnd(g, *rm.shape, u=True, scale=1e-2)
+    r = ref.backward(dmz, dSz)
+    d = dev.backward(dmz.to(DEV), dSz.to(DEV))
+    assert_rel(d[0], r[0], MEAN_RTOL, "conv d_ma")
+    assert_rel(d[1], r[1], VAR_RTOL, "conv d_Sa")
+    assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "conv delta_mw")
+    assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "conv delta_Sw")
+    _ok()
+
+
+def test_batched_attention_products():
+    from triton_tagi.kernels.attention import bmm_shared_left, bmm_shared_right, bmm_tagi_moments
+
+    g = torch.Generator().manual_seed(21)
+    B, H, S, D = 2, 4, 256, 64
+    mq, Sq = _rnd(g, B, H, S, D), _rnd(g, B, H, S, D, u=True, scale=0.1)
+    mk, Sk = _rnd(g, B, H, S, D), _rnd(g, B, H, S, D, u=True, scale=0.1)
+    s = D**-0.5
+    tr = lambda t: t.transpose(-1, -2)  # noqa: E731
+    m, v = bmm_tagi_moments(mq.to(DEV), Sq.to(DEV), tr(mk.to(DEV)), tr(Sk.to(DEV)), s, s * s)
+    assert_rel(m, s * (mq.double() @ tr(mk.double())), MEAN_RTOL, "scores mean")
+    assert_rel(v, F.bmm_tagi_var(mq.double(), Sq.double(), tr(mk.double()), tr(Sk.double()), s * s),
+               VAR_RTOL, "scores var")
+    dm, dv = _rnd(g, B, H, S, S, scale=0.1), _rnd(g, B, H, S, S, u=True, scale=0.01)
+    m, v = bmm_shared_right(dm.to(DEV), dv.to(DEV), mk.to(DEV), scale=s)
+    rm, rv = F.bmm_shared_right(dm.double(), dv.double(), mk.double(), s)
+    assert_rel(m, rm, MEAN_RTOL, "shared right mean")
+    assert_rel(v, rv, VAR_RTOL, "shared right var")
+    m, v = bmm_shared_left(tr(dm.to(DEV)), mk.to(DEV), Sk.to(DEV))
+    rm, rv = F.bmm_shared_left(tr(dm.double()), mk.double(), Sk.double())
+    assert_rel(m, rm, MEAN_RTOL, "shared left mean")
+    assert_rel(v, rv, VAR_RTOL, "shared left var")
+    _ok()

@@ -50,8 +50,9 @@ def test_static_scratch_matches_workspace_entry_point_on_consecutive_calls():
     from triton_tagi.kernels.common import triton_fused_weight_grad
 
     L = lib()
-    # two calls in a row with different split plans; the second reuses the array
-    for seed, (M, K, N) in enumerate([(131072, 576, 64), (50000, 27, 10)]):
+    # two calls in a row with different split plans (the first on the tensor-core
+    # kernel, the second on CUDA cores); the second reuses the array
+    for seed, (M, K, N) in enumerate([(131072, 288, 32), (50000, 27, 10)]):
         assert 0 < L.size("tagi_fused_weight_grad_workspace_size", M, K, N) <= STATIC_BYTES
         a, dmz, dSz = _inputs(M, K, N, seed)
         ref_m, ref_S = triton_fused_weight_grad(a, dmz, dSz)

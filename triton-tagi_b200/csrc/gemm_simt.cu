@@ -16,70 +16,12 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "moment_gemm.cuh"
 
 namespace tagi {
 namespace {
 
-enum VarMode { FULL = 0, RSQ = 1, LSQ = 2 };
-enum Epi { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_PARAM = 2 };
-
-struct ParamEpi {
-    int mode;  // TAGI_WGRAD_SUMS / DELTAS / UPDATE
-    int K, N;  // weight rows, columns; row K is the bias row when present
-    float *mw, *Sw, *mb, *Sb;
-    float *out_m, *out_S, *out_mb, *out_Sb;
-    float cap;
-};
-
-struct GemmArgs {
-    const float *x, *y;
-    RowMap arow;
-    int64_t ak;
-    int ones_row;
-    int64_t a_bs;
-    const float *u, *v;
-    RowMap brow;
-    int64_t bn;
-    int64_t b_bs;
-    float *o0, *o1;
-    RowMap orow;
-    int64_t on;
-    int64_t o_bs;
-    const float *bias0, *bias1;
-    float scale0, scale1;
-    int M, N, Kr;
-    int splits, kchunk;
-    float* ws;
-    ParamEpi pe;
-};
-
 constexpr int BM = 64, BN = 64, BK = 16, NT = 256, PAD = 4;
-
-__device__ __forceinline__ void param_epilogue(int r, int c, float g0, float g1,
-                                               const ParamEpi& p) {
-    const int64_t rc = static_cast<int64_t>(r) * p.N + c;
-    if (p.mode == TAGI_WGRAD_SUMS) {
-        p.out_m[rc] = g0;
-        p.out_S[rc] = g1;
-        return;
-    }
-    const bool bias = (r == p.K);
-    const int64_t w = bias ? c : rc;
-    float* mp = bias ? p.mb : p.mw;
-    float* Sp = bias ? p.Sb : p.Sw;
-    const float S = Sp[w];
-    const float dm = S * g0;
-    const float dS = (S * S) * g1;
-    if (p.mode == TAGI_WGRAD_DELTAS) {
-        (bias ? p.out_mb : p.out_m)[w] = dm;
-        (bias ? p.out_Sb : p.out_S)[w] = dS;
-        return;
-    }
-    float m = mp[w], Sn = S;
-    capped_pair(m, Sn, dm, dS, p.cap);
-    mp[w] = m;
-    Sp[w] = Sn;
-}
 
 template <int VM>
 struct Needs {
@@ -263,10 +205,13 @@ __global__ void splitk_finish_kernel(const GemmArgs g, int param) {
 
 inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
-// Reduction split for output grids too small to fill the GPU.
-void choose_splits(int M, int N, int Kr, int batch, int* splits, int* kchunk) {
+// Reduction split for output grids too small to fill the GPU, for the kernel
+// (tensor-core or CUDA-core tiles) that will run the shape.
+void choose_splits(int M, int N, int Kr, int batch, int* splits, int* kchunk, int* bn_tc) {
+    const int tc = tc_pick(LSQ, M, N, Kr, batch);
+    const int tm = tc ? kTcBM : BM, tn = tc ? tc : BN;
     int s = 1;
-    const int tiles = cdiv(M, BM) * cdiv(N, BN) * batch;
+    const int tiles = cdiv(M, tm) * cdiv(N, tn) * batch;
     if (batch == 1 && tiles < 2 * kNumSMs) {
         s = cdiv(2 * kNumSMs, tiles);
         s = std::min(s, std::max(1, Kr / (BK * 8)));
@@ -277,16 +222,27 @@ void choose_splits(int M, int N, int Kr, int batch, int* splits, int* kchunk) {
     *splits = cdiv(Kr, chunk);
     if (*splits < 1) *splits = 1;
     *kchunk = chunk;
+    *bn_tc = tc;
 }
 
 template <int VM, bool MEAN, int EPI>
-int launch(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
+int launch_simt(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
     if (g.M == 0 || g.N == 0) return TAGI_OK;
     dim3 grid(cdiv(g.N, BN), cdiv(g.M, BM), batch * g.splits);
     TAGI_REQUIRE(grid.y <= 65535 && grid.z <= 65535, TAGI_E_UNSUPPORTED, "%s: grid too large",
                  what);
     moment_gemm_kernel<VM, MEAN, EPI><<<grid, NT, 0, st>>>(g);
     return check_launch(what);
+}
+
+// Runs a contraction on the tensor cores when the shape is large enough
+// (tc_pick), on CUDA cores otherwise. `bn_tc` forces the choice made by a
+// planner that already sized a split-K workspace for it.
+template <int VM, bool MEAN, int EPI>
+int launch(const GemmArgs& g, int batch, cudaStream_t st, const char* what, int bn_tc = -1) {
+    if (bn_tc < 0) bn_tc = tc_pick(VM, g.M, g.N, g.Kr, batch);
+    if (bn_tc > 0) return tc_launch(g, VM, MEAN, EPI, bn_tc, batch, st, what);
+    return launch_simt<VM, MEAN, EPI>(g, batch, st, what);
 }
 
 GemmArgs blank() {
@@ -302,8 +258,8 @@ bool bad_size(int64_t v) { return v < 0 || v > (int64_t(1) << 31) - 1; }
 // Shared driver for the weight-gradient family (stores or parameter epilogue).
 int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
               const char* what) {
-    int splits, chunk;
-    choose_splits(Mo, g.N, g.Kr, 1, &splits, &chunk);
+    int splits, chunk, bn_tc;
+    choose_splits(Mo, g.N, g.Kr, 1, &splits, &chunk, &bn_tc);
     g.M = Mo;
     if (splits > 1) {
         const size_t need = sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N;
@@ -312,7 +268,7 @@ int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaSt
         g.splits = splits;
         g.kchunk = chunk;
         g.ws = static_cast<float*>(ws);
-        int rc = launch<LSQ, true, EPI_PARTIAL>(g, 1, st, what);
+        int rc = launch<LSQ, true, EPI_PARTIAL>(g, 1, st, what, bn_tc);
         if (rc) return rc;
         splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(Mo) * g.N, 256), 256, 0, st>>>(
             g, param ? 1 : 0);
@@ -320,13 +276,13 @@ int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaSt
     }
     g.splits = 1;
     g.kchunk = g.Kr > 0 ? g.Kr : BK;
-    return param ? launch<LSQ, true, EPI_PARAM>(g, 1, st, what)
-                 : launch<LSQ, true, EPI_STORE>(g, 1, st, what);
+    return param ? launch<LSQ, true, EPI_PARAM>(g, 1, st, what, bn_tc)
+                 : launch<LSQ, true, EPI_STORE>(g, 1, st, what, bn_tc);
 }
 
 size_t wgrad_ws_bytes(int Mo, int N, int Kr) {
-    int splits, chunk;
-    choose_splits(Mo, N, Kr, 1, &splits, &chunk);
+    int splits, chunk, bn_tc;
+    choose_splits(Mo, N, Kr, 1, &splits, &chunk, &bn_tc);
     return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * N : 0;
 }
 

@@ -56,6 +56,7 @@ _SIGS = {
     "tagi_device_arch": "n",
     "tagi_last_error": "",
     "tagi_kernel_launches": "",
+    "tagi_device_status": "n",
 }
 _RET = {
     "tagi_fused_weight_grad_workspace_size": _Z,
@@ -111,6 +112,11 @@ def lib() -> _Lib:
     if _instance is None:
         _instance = _Lib(LIB_PATH)
     return _instance
+
+
+def device_status(reset: bool = False) -> int:
+    """0, or the code of a tensor-core kernel wait that timed out (synchronises)."""
+    return int(lib().fn["tagi_device_status"](1 if reset else 0))
 
 
 def kernel_launches() -> int:
