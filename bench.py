@@ -49,7 +49,9 @@ WORKLOADS = {
     "mlp": dict(batch=256, metric="TAGI MLP 784-256-128-10 Sequential.step samples/sec"),
     "cnn": dict(batch=512, metric="TAGI CNN Sequential.step samples/sec"),
     "tfm": dict(batch=32, metric="TAGI transformer Sequential.step samples/sec"),
+    "swp": dict(batch=8192, metric="TAGI Linear op sweep: fused mean/var moment GEMM TFLOP/s"),
 }
+SWEEP = [(m, k) for m in (256, 1024, 4096, 8192) for k in (1024, 4096)]
 
 
 # ----------------------------------------------------------------------------- networks
@@ -384,6 +386,91 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def sweep_arm(args, rank: int, world: int, local: int) -> None:
+    """Linear op sweep: forward (mean+var), backward delta and weight sums with the
+    capped update, each timed with CUDA events (L2 flushed before every launch)."""
+    import triton_tagi as TT
+    from triton_tagi._lib import kernel_launches, lib, stream
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shapes = [tuple(int(v) for v in args.shape.split(","))] if args.shape else SWEEP
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    L = lib()
+    rows, peak_tf32 = [], tf32_peak_tflops(dev)
+    launches0 = kernel_launches()
+    with ClockSampler(dev.index or 0) as clocks:
+        for M, K in shapes:
+            N = K
+            g = torch.Generator(device=dev).manual_seed(M + K)
+            ma = torch.randn(M, K, device=dev, generator=g)
+            Sa = torch.rand(M, K, device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
+            lin = TT.Linear(K, N, device=dev)
+            lin.mw = torch.randn(K, N, device=dev, generator=g) / K**0.5
+            lin.Sw = (torch.rand(K, N, device=dev, generator=g) + 0.5) / K
+            lin.mb = torch.zeros(1, N, device=dev)
+            lin.Sb = torch.full((1, N), 1e-3, device=dev)
+            dmz = torch.randn(M, N, device=dev, generator=g) * 0.1
+            dSz = -torch.rand(M, N, device=dev, generator=g) * 1e-2
+            d_ma = torch.empty(M, K, device=dev)
+            d_Sa = torch.empty(M, K, device=dev)
+
+            def fwd():
+                lin.forward(ma, Sa)
+
+            def bwd():
+                L("tagi_fused_backward_delta", dmz.data_ptr(), dSz.data_ptr(), lin.mw.data_ptr(),
+                  d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, N, 1, N, 1, K, 1, stream(dmz))
+
+            def upd():
+                from triton_tagi.layers._params import weight_param_backward
+
+                lin._set_param_mode("update", 3.0)
+                weight_param_backward(lin, ma, K, (dmz, dSz), (0, 0, N, 1), M, K, N, True)
+                lin._set_param_mode("deltas")
+
+            row = {"M": M, "K": K, "N": N}
+            for name, fn, flops in (("forward", fwd, 6.0 * M * N * K),
+                                    ("backward", bwd, 4.0 * M * N * K),
+                                    ("update", upd, 4.0 * M * N * K)):
+                for _ in range(args.warmup):
+                    fn()
+                times = []
+                for _ in range(args.steps):
+                    flush.zero_()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fn()
+                    b.record()
+                    b.synchronize()
+                    times.append(a.elapsed_time(b) * 1e-3)
+                t = statistics.median(times)
+                row[name] = {"ms": 1e3 * t, "tflops": flops / t / 1e12,
+                             "frac": flops / t / 1e12 / (peak_tf32 / 3.0),
+                             "samples_per_s": M / t}
+            rows.append(row)
+    if rank != 0:
+        return
+    top = max(rows, key=lambda r: r["M"] * r["K"])
+    step_s = sum(top[n]["ms"] for n in ("forward", "backward", "update")) * 1e-3
+    fwd = top["forward"]
+    line = {
+        "metric": WORKLOADS["swp"]["metric"], "value": fwd["tflops"], "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * step_s,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "swp", "shapes": [[r["M"], r["K"]] for r in rows],
+                   "l2": "flushed before every timed launch (256 MiB write)"},
+        "roofline": {"bound": "tensor", "kernel": "moment_forward", "achieved": fwd["tflops"],
+                     "peak": peak_tf32 / 3.0, "unit": "TFLOP/s", "frac": fwd["frac"],
+                     "traffic": None,
+                     "peak_source": f"measured cuBLAS TF32 burst {peak_tf32:.0f} TF/s / 3"},
+        "sweep": rows, "gpu_launches": int(kernel_launches() - launches0),
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -392,12 +479,16 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="r18")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default=None, help="swp workload: one 'M,K' shape (K = N)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)  # rank 0 only; no process group needed
+        return
+    if args.workload == "swp":
+        sweep_arm(args, rank, world, local)
         return
     if world > 1:
         import datetime

@@ -9,15 +9,16 @@
 // relative; the split-precision scheme of Ootomo & Yokota). Squares and mu^2 + var are formed
 // in fp32 first, as the reference does, and then split.
 //
-// Warp roles (416 threads):
-//   warps 0-3  A producers: one output row each; load 8 reduction elements of
-//              x (and y) per stage from any row-split layout, form the split
-//              operand tiles and store them in the canonical no-swizzle K-major
-//              layout (8x16-byte core matrices).
-//   warps 4-7  B producers: one output column each, same for u (and v).
-//   warp 8     allocates tensor memory; lane 0 issues the tcgen05.mma
-//              instructions and commits them to the stage's "empty" barrier.
-//   warps 9-12 accumulator warps (TMEM lane quarter warp % 4): the tensor
+// Warp roles (672 threads):
+//   warps 0-7   A producers: two threads per output row, 4 reduction elements
+//               each per stage; stage raw x (and y) from any row-split layout
+//               through a cp.async ring, form the split operand tiles and store
+//               them in the canonical no-swizzle K-major layout (8x16-byte core
+//               matrices).
+//   warps 8-15  B producers: the same for u (and v), one row per output column.
+//   warp 16     allocates tensor memory; lane 0 issues the tcgen05.mma
+//               instructions and commits them to the stage's "empty" barrier.
+//   warps 17-20 accumulator warps (TMEM lane quarter warp % 4): the tensor
 //              core's fp32 accumulation truncates, so products are accumulated
 //              in tensor memory for kChunk stages only; these warps fold each
 //              chunk into a running total with round-to-nearest adds and run the
@@ -40,8 +41,11 @@ namespace {
 
 constexpr int kStages = 4;
 constexpr int kBK = 8;  // tf32 elements per MMA along the reduction
-constexpr int kThreads = 416;  // 13 warps
+constexpr int kThreads = 672;  // 21 warps
 constexpr int kChunk = 8;      // stages accumulated in tensor memory before a fold
+constexpr int kRawStages = 4;  // depth of the cp.async ring of raw operand rows
+constexpr int kRawSlot = 2 * 256 * 32;  // two operands x 256 producer rows x 8 fp32
+enum { kScalar = 0, kRowK = 1, kKRow = 2 };
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -91,6 +95,27 @@ __device__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fl
             }
         }
     }
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+// 4-byte copy; when `ok` is false nothing is read and the destination is zeroed.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool ok) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(ok ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -189,18 +214,16 @@ __device__ __forceinline__ uint32_t tile_off(int row, int half) {
     return static_cast<uint32_t>((row >> 3) * 256 + half * 128 + (row & 7) * 16);
 }
 
-__device__ __forceinline__ void st_split(char* tile_hi, char* tile_lo, uint32_t off,
-                                         const float (&v)[8]) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        float4 hi, lo;
-        hi.x = tf32_rna(v[4 * h + 0]); lo.x = tf32_rna(v[4 * h + 0] - hi.x);
-        hi.y = tf32_rna(v[4 * h + 1]); lo.y = tf32_rna(v[4 * h + 1] - hi.y);
-        hi.z = tf32_rna(v[4 * h + 2]); lo.z = tf32_rna(v[4 * h + 2] - hi.z);
-        hi.w = tf32_rna(v[4 * h + 3]); lo.w = tf32_rna(v[4 * h + 3] - hi.w);
-        *reinterpret_cast<float4*>(tile_hi + off + h * 128) = hi;
-        *reinterpret_cast<float4*>(tile_lo + off + h * 128) = lo;
-    }
+// Split four fp32 values into tf32 hi/lo parts and store them (16 bytes each).
+__device__ __forceinline__ void st_split4(char* tile_hi, char* tile_lo, uint32_t off,
+                                          const float (&v)[4]) {
+    float4 hi, lo;
+    hi.x = tf32_rna(v[0]); lo.x = tf32_rna(v[0] - hi.x);
+    hi.y = tf32_rna(v[1]); lo.y = tf32_rna(v[1] - hi.y);
+    hi.z = tf32_rna(v[2]); lo.z = tf32_rna(v[2] - hi.z);
+    hi.w = tf32_rna(v[3]); lo.w = tf32_rna(v[3] - hi.w);
+    *reinterpret_cast<float4*>(tile_hi + off) = hi;
+    *reinterpret_cast<float4*>(tile_lo + off) = lo;
 }
 
 template <int VM>
@@ -244,9 +267,17 @@ constexpr int stage_bytes() {
     return TcTiles<VM>::na * 128 * 32 + TcTiles<VM>::nb * BN * 32;
 }
 
+// Operand stages that fit next to the raw ring in 227 KB (at most kStages).
+template <int VM, int BN>
+constexpr int op_stages() {
+    return (220 * 1024 - kRawStages * kRawSlot) / stage_bytes<VM, BN>() < kStages
+               ? (220 * 1024 - kRawStages * kRawSlot) / stage_bytes<VM, BN>()
+               : kStages;
+}
+
 template <int VM, int BN>
 constexpr int smem_bytes() {
-    return kStages * stage_bytes<VM, BN>() + 1024;
+    return op_stages<VM, BN>() * stage_bytes<VM, BN>() + kRawStages * kRawSlot + 1024;
 }
 
 
@@ -269,8 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
     constexpr int STAGE = stage_bytes<VM, BN>();
     constexpr int NP = num_p<BN>();
     constexpr int COLS = tmem_cols<BN>();
+    constexpr int OPS = op_stages<VM, BN>();
     extern __shared__ __align__(1024) char smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * STAGE);
+    char* raw = smem + OPS * STAGE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(raw + kRawStages * kRawSlot);
     uint64_t* empty = full + kStages;
     uint64_t* chunk_full = empty + kStages;   // [NP]: MMA -> accumulator warps
     uint64_t* chunk_empty = chunk_full + 2;   // [NP]: accumulator warps -> MMA
@@ -288,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 256);
+            mbar_init(&full[s], 512);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -300,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async();
     }
-    if (warp == 8) {
+    if (warp == 16) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
                      "r"(COLS));
@@ -314,10 +347,12 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
     // within each, the mean accumulator then the variance accumulator.
     const uint32_t tcol_total = 2 * BN * NP;
 
-    if (warp < 8) {
+    if (warp < 16) {
         // ---------------------------------------------------------------- producers
-        const bool is_a = warp < 4;
-        const int r = is_a ? tid : tid - 128;
+        // Two threads per tile row: `half` selects reduction elements 0-3 or 4-7.
+        const bool is_a = warp < 8;
+        const int side_tid = is_a ? tid : tid - 256;
+        const int r = side_tid & 127, half = side_tid >> 7;
         const bool active = is_a ? true : (r < BN);
         int idx;
         bool valid, one = false;
@@ -338,92 +373,165 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
             p1 = (VM == RSQ) ? nullptr : g.v + batch * g.b_bs;
         }
         const bool has1 = (p1 != nullptr);
-        const bool vec = is_a && g.ak == 1 && !one && ((base & 3) == 0) &&
-                         ((reinterpret_cast<uintptr_t>(p0) & 15) == 0) &&
-                         (!has1 || (reinterpret_cast<uintptr_t>(p1) & 15) == 0);
-
-        auto load = [&](int it, float (&v0)[8], float (&v1)[8]) {
-            const int k0 = kbeg + it * kBK;
-            if (it >= niter || !valid) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v0[j] = v1[j] = 0.f;
-                return;
+        // Staging modes of this side's operands (uniform over the side):
+        //  kRowK   each row's reduction values are contiguous and 16-byte aligned:
+        //          a thread copies its own 4-element half row as one 16-byte chunk
+        //          ([row][8] layout);
+        //  kKRow   4 consecutive rows are contiguous and aligned for every reduction
+        //          index: the side's 256 threads copy one 16-byte row chunk each into a
+        //          [k][128] layout and read it transposed after a named barrier;
+        //  kScalar element-wise 4-byte copies of the thread's own half row.
+        // Out-of-range elements are zero-filled; chunks that straddle a tile edge or
+        // the bias row fall back to element-wise copies.
+        const uintptr_t align_bits = (reinterpret_cast<uintptr_t>(p0) |
+                                      (has1 ? reinterpret_cast<uintptr_t>(p1) : 0)) & 15;
+        int mode = kScalar;
+        if (is_a) {
+            const RowMap& m = g.arow;
+            const bool rows4 = (m.div <= 0) ? (m.stride % 4 == 0)
+                                            : (m.stride % 4 == 0 && m.outer % 4 == 0);
+            if (align_bits == 0 && g.ak == 1 && rows4) {
+                mode = kRowK;
+            } else if (align_bits == 0 && m.stride == 1 && g.ak % 4 == 0 &&
+                       (m.div <= 0 || (m.div % 4 == 0 && m.outer % 4 == 0))) {
+                mode = kKRow;
             }
-            if (is_a) {
-                if (one) {
+        } else {
+            const RowMap& m = g.brow;
+            if (align_bits == 0 && m.stride == 1 && g.bn % 4 == 0 &&
+                (m.div <= 0 || (m.div % 8 == 0 && m.outer % 4 == 0))) {
+                mode = kRowK;
+            } else if (align_bits == 0 && g.bn == 1 &&
+                       ((m.div <= 0) ? (m.stride % 4 == 0)
+                                     : (m.stride % 4 == 0 && m.outer % 4 == 0))) {
+                mode = kKRow;
+            }
+        }
+        const int side_rows = is_a ? g.M : g.N;
+        const int side_row0 = is_a ? m0 : n0;
+        // region of (slot, operand) for this side: 128 rows x 8 fp32
+        auto region = [&](int slot, int o) -> char* {
+            return raw + slot * kRawSlot + ((is_a ? 0 : 2) + o) * 4096;
+        };
+        // global offset of (row, k) for this side, valid row and k < kend assumed
+        auto goff = [&](int rrow, int k) -> int64_t {
+            return is_a ? g.arow.off(rrow) + static_cast<int64_t>(k) * g.ak
+                        : static_cast<int64_t>(rrow) * g.bn + g.brow.off(k);
+        };
+        auto row_ok = [&](int rrow) -> bool {
+            return rrow < side_rows && !(is_a && rrow == g.ones_row);
+        };
+        auto issue = [&](int it) {
+            if (it >= niter) return;
+            const int k0 = kbeg + it * kBK;
+            const int slot = it % kRawStages;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        v0[j] = (k0 + j < kend) ? 1.f : 0.f;
-                        v1[j] = 0.f;
-                    }
-                } else if (vec && k0 + 8 <= kend) {
-                    const float4 a = __ldg(reinterpret_cast<const float4*>(p0 + base + k0));
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(p0 + base + k0 + 4));
-                    v0[0] = a.x; v0[1] = a.y; v0[2] = a.z; v0[3] = a.w;
-                    v0[4] = b.x; v0[5] = b.y; v0[6] = b.z; v0[7] = b.w;
-                    if (has1) {
-                        const float4 c = __ldg(reinterpret_cast<const float4*>(p1 + base + k0));
-                        const float4 d = __ldg(reinterpret_cast<const float4*>(p1 + base + k0 + 4));
-                        v1[0] = c.x; v1[1] = c.y; v1[2] = c.z; v1[3] = c.w;
-                        v1[4] = d.x; v1[5] = d.y; v1[6] = d.z; v1[7] = d.w;
-                    } else {
+            for (int o = 0; o < 2; ++o) {
+                if (o == 1 && !has1) break;
+                const float* src = o ? p1 : p0;
+                char* reg = region(slot, o);
+                if (mode == kKRow) {
+                    const int c = side_tid;  // chunk: k = c / 32, rows 4*(c % 32) .. +3
+                    const int k = k0 + c / 32, rg = c % 32;
+                    const int rrow = side_row0 + 4 * rg;
+                    char* dst = reg + (c / 32) * 512 + rg * 16;
+                    if (4 * rg < (is_a ? 128 : BN)) {
+                        if (k < kend && rrow + 3 < side_rows &&
+                            !(is_a && g.ones_row >= rrow && g.ones_row <= rrow + 3)) {
+                            cp_async16(dst, src + goff(rrow, k));
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) v1[j] = 0.f;
+                            for (int q = 0; q < 4; ++q) {
+                                const bool ok = k < kend && row_ok(rrow + q);
+                                cp_async4(dst + 4 * q, ok ? src + goff(rrow + q, k) : src, ok);
+                            }
+                        }
                     }
                 } else {
+                    if (!valid || one) continue;
+                    const int kh = k0 + 4 * half;
+                    char* dst = reg + r * 32 + half * 16;
+                    if (mode == kRowK && kh + 4 <= kend) {
+                        cp_async16(dst, src + goff(idx, kh));
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int k = k0 + j;
-                        const bool ok = k < kend;
-                        const int64_t o = base + static_cast<int64_t>(k) * g.ak;
-                        v0[j] = ok ? __ldg(p0 + o) : 0.f;
-                        v1[j] = (ok && has1) ? __ldg(p1 + o) : 0.f;
+                        for (int j = 0; j < 4; ++j) {
+                            const int k = kh + j;
+                            const bool ok = k < kend;
+                            cp_async4(dst + 4 * j, ok ? src + goff(idx, k) : src, ok);
+                        }
                     }
                 }
-            } else {
+            }
+        };
+        auto fetch = [&](int it, float (&v0)[4], float (&v1)[4]) {
+            const int kh = kbeg + it * kBK + 4 * half;
+            if (!valid) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int k = k0 + j;
-                    const bool ok = k < kend;
-                    const int64_t o = ok ? g.brow.off(k) + base : 0;
-                    v0[j] = ok ? __ldg(p0 + o) : 0.f;
-                    v1[j] = (ok && has1) ? __ldg(p1 + o) : 0.f;
+                for (int j = 0; j < 4; ++j) v0[j] = v1[j] = 0.f;
+                return;
+            }
+            if (one) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    v0[j] = (kh + j < kend) ? 1.f : 0.f;
+                    v1[j] = 0.f;
+                }
+                return;
+            }
+            const int slot = it % kRawStages;
+#pragma unroll
+            for (int o = 0; o < 2; ++o) {
+                float* v = o ? v1 : v0;
+                if (o == 1 && !has1) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[j] = 0.f;
+                    break;
+                }
+                const char* reg = region(slot, o);
+                if (mode == kKRow) {
+                    const float* f = reinterpret_cast<const float*>(reg);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[j] = f[(4 * half + j) * 128 + r];
+                } else {
+                    const float4 x = *reinterpret_cast<const float4*>(reg + r * 32 + half * 16);
+                    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
                 }
             }
         };
 
-        auto produce = [&](int it, const float (&v0)[8], const float (&v1)[8]) -> bool {
-            const int s = it % kStages;
-            if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, abort_flag, 1))
+        auto produce = [&](int it, const float (&v0)[4], const float (&v1)[4]) -> bool {
+            const int s = it % OPS;
+            if (it >= OPS && !mbar_wait(&empty[s], ((it / OPS) & 1) ^ 1, abort_flag, 1))
                 return false;
             if (active) {
                 char* st = smem + s * STAGE;
-                const uint32_t off = tile_off(r, 0);
-                float sq[8];
+                const uint32_t off = tile_off(r, half);
+                float sq[4];
                 if (is_a) {
                     char* A = st;
-                    st_split(A + 0 * A_TILE, A + 1 * A_TILE, off, v0);
+                    st_split4(A + 0 * A_TILE, A + 1 * A_TILE, off, v0);
                     if (VM == FULL || VM == LSQ) {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) sq[j] = v0[j] * v0[j];
-                        st_split(A + 2 * A_TILE, A + 3 * A_TILE, off, sq);
+                        for (int j = 0; j < 4; ++j) sq[j] = v0[j] * v0[j];
+                        st_split4(A + 2 * A_TILE, A + 3 * A_TILE, off, sq);
                     }
-                    if (VM == FULL) st_split(A + 4 * A_TILE, A + 5 * A_TILE, off, v1);
-                    if (VM == RSQ) st_split(A + 2 * A_TILE, A + 3 * A_TILE, off, v1);
+                    if (VM == FULL) st_split4(A + 4 * A_TILE, A + 5 * A_TILE, off, v1);
+                    if (VM == RSQ) st_split4(A + 2 * A_TILE, A + 3 * A_TILE, off, v1);
                 } else {
                     char* B = st + T::na * A_TILE;
-                    st_split(B + 0 * B_TILE, B + 1 * B_TILE, off, v0);
+                    st_split4(B + 0 * B_TILE, B + 1 * B_TILE, off, v0);
                     if (VM == FULL) {
-                        st_split(B + 2 * B_TILE, B + 3 * B_TILE, off, v1);
+                        st_split4(B + 2 * B_TILE, B + 3 * B_TILE, off, v1);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) sq[j] = v0[j] * v0[j] + v1[j];
-                        st_split(B + 4 * B_TILE, B + 5 * B_TILE, off, sq);
+                        for (int j = 0; j < 4; ++j) sq[j] = v0[j] * v0[j] + v1[j];
+                        st_split4(B + 4 * B_TILE, B + 5 * B_TILE, off, sq);
                     } else if (VM == RSQ) {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) sq[j] = v0[j] * v0[j];
-                        st_split(B + 2 * B_TILE, B + 3 * B_TILE, off, sq);
+                        for (int j = 0; j < 4; ++j) sq[j] = v0[j] * v0[j];
+                        st_split4(B + 2 * B_TILE, B + 3 * B_TILE, off, sq);
                     } else {
-                        st_split(B + 2 * B_TILE, B + 3 * B_TILE, off, v1);
+                        st_split4(B + 2 * B_TILE, B + 3 * B_TILE, off, v1);
                     }
                 }
                 fence_proxy_async();
@@ -432,19 +540,29 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
             return true;
         };
 
-        // two stages of loads in flight ahead of the stage being produced
-        float a0[8], a1[8], b0[8], b1[8];
-        load(0, a0, a1);
-        load(1, b0, b1);
-        for (int it = 0; it < niter; it += 2) {
-            if (!produce(it, a0, a1)) break;
-            load(it + 2, a0, a1);
-            if (it + 1 < niter) {
-                if (!produce(it + 1, b0, b1)) break;
-                load(it + 3, b0, b1);
-            }
+        // cp.async ring: kRawStages-1 stages in flight ahead of the one transformed
+        for (int i = 0; i < kRawStages - 1; ++i) {
+            issue(i);
+            cp_async_commit();
         }
-    } else if (warp == 8) {
+        float v0[4], v1[4];
+        // After an abort every thread keeps iterating without work, so that all
+        // threads of a side still reach every named barrier.
+        bool alive = true;
+        for (int it = 0; it < niter; ++it) {
+            cp_async_wait<kRawStages - 2>();
+            // rows staged by other threads of this side: wait until all copied (and
+            // until all consumed the slot that the next issue refills)
+            if (mode == kKRow) named_bar_sync(is_a ? 1 : 2, 256);
+            if (alive) {
+                fetch(it, v0, v1);
+                alive = produce(it, v0, v1);
+            }
+            if (alive) issue(it + kRawStages - 1);  // refills the slot consumed one iteration ago
+            cp_async_commit();
+        }
+        cp_async_wait<0>();
+    } else if (warp == 16) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issue
             constexpr uint32_t idesc = instr_desc(BN);
@@ -459,8 +577,8 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
                     tc_fence_after();
                     started[0] = started[1] = false;
                 }
-                const int s = it % kStages;
-                if (!mbar_wait(&full[s], (it / kStages) & 1, abort_flag, 2)) break;
+                const int s = it % OPS;
+                if (!mbar_wait(&full[s], (it / OPS) & 1, abort_flag, 2)) break;
                 tc_fence_after();
                 const uint32_t st = base + s * STAGE;
                 const uint32_t pcol = tmem + static_cast<uint32_t>(2 * BN * b);
@@ -479,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
             mma_commit(done);  // arrives once every MMA issued above has completed
         }
     } else {
-        // -------------------------------------------- accumulator warps (9-12)
+        // -------------------------------------------- accumulator warps (17-20)
         // Tensor-core accumulation truncates; each chunk of kChunk stages is
         // folded into the running total with round-to-nearest fp32 adds, and the
         // last fold feeds the epilogue directly.
@@ -537,13 +655,13 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
         }
     }
 
-    if (warp == 8) {
+    if (warp == 16) {
         // the MMAs of this CTA must be complete before their memory is released
         if (!mbar_try(done, 0)) mbar_wait(done, 0, abort_flag, 4);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == 16) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"(COLS));
