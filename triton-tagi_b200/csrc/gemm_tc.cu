@@ -42,7 +42,7 @@ namespace {
 constexpr int kStages = 4;
 constexpr int kBK = 8;  // tf32 elements per MMA along the reduction
 constexpr int kThreads = 672;  // 21 warps
-constexpr int kChunk = 8;      // stages accumulated in tensor memory before a fold
+constexpr int kChunk = 16;     // stages accumulated in tensor memory before a fold
 constexpr int kRawStages = 4;  // depth of the cp.async ring of raw operand rows
 constexpr int kRawSlot = 2 * 256 * 32;  // two operands x 256 producer rows x 8 fp32
 enum { kScalar = 0, kRowK = 1, kKRow = 2 };
@@ -158,6 +158,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive columns of this warp's 32 lanes; completes at tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -616,31 +629,45 @@ __global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g
             const uint32_t tcol = lane_base + tcol_total;
             const int64_t ro =
                 (EPI == EPI_STORE && row < g.M) ? g.orow.off(row) + batch * g.o_bs : 0;
+            // Intermediate folds: T += P, 16 columns at a time, the P and T loads of a
+            // column block issued together before one wait.
+            if (!last) {
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                float pm[16], pv[16], tm[16], tv[16];
-                if (MEAN) tmem_ld16(pcol + c0, pm);
-                tmem_ld16(pcol + BN + c0, pv);
-                if (c > 0) {
-                    if (MEAN) tmem_ld16(tcol + c0, tm);
-                    tmem_ld16(tcol + BN + c0, tv);
-                }
+                for (int c0 = 0; c0 < 2 * BN; c0 += 16) {
+                    if (!MEAN && c0 < BN) continue;
+                    uint32_t pr[16], tr[16];
+                    tmem_ld16_async(pcol + c0, pr);
+                    if (c > 0) tmem_ld16_async(tcol + c0, tr);
+                    tmem_wait_ld();
+                    float tv[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    tm[j] = MEAN ? (c > 0 ? tm[j] + pm[j] : pm[j]) : 0.f;
-                    tv[j] = c > 0 ? tv[j] + pv[j] : pv[j];
+                    for (int j = 0; j < 16; ++j)
+                        tv[j] = c > 0 ? __uint_as_float(tr[j]) + __uint_as_float(pr[j])
+                                      : __uint_as_float(pr[j]);
+                    tmem_st16(tcol + c0, tv);
                 }
-                if (!last) {
-                    if (MEAN) tmem_st16(tcol + c0, tm);
-                    tmem_st16(tcol + BN + c0, tv);
-                    continue;
-                }
-                if (row >= g.M) continue;
+            } else {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float pm[16], pv[16], tm[16], tv[16];
+                    if (MEAN) tmem_ld16(pcol + c0, pm);
+                    tmem_ld16(pcol + BN + c0, pv);
+                    if (c > 0) {
+                        if (MEAN) tmem_ld16(tcol + c0, tm);
+                        tmem_ld16(tcol + BN + c0, tv);
+                    }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int col = n0 + c0 + j;
-                    if (col >= g.N) continue;
-                    store_out<EPI, MEAN>(g, row, col, ro, split, tm[j], tv[j]);
+                    for (int j = 0; j < 16; ++j) {
+                        tm[j] = MEAN ? (c > 0 ? tm[j] + pm[j] : pm[j]) : 0.f;
+                        tv[j] = c > 0 ? tv[j] + pv[j] : pv[j];
+                    }
+                    if (row >= g.M) continue;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int col = n0 + c0 + j;
+                        if (col >= g.N) continue;
+                        store_out<EPI, MEAN>(g, row, col, ro, split, tm[j], tv[j]);
+                    }
                 }
             }
             if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
