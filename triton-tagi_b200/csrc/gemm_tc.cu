@@ -1,32 +1,45 @@
 // Moment contractions on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
-// One CTA computes a 128 x BN output tile of both accumulators (mean, variance)
-// of a moment contraction (see moment_gemm.cuh for the three variance forms).
-// Accumulators live in tensor memory (2*BN fp32 columns). Precision is 3xTF32:
-// every fp32 operand v is split into hi = tf32(v) and lo = tf32(v - hi), both
-// rounded to nearest so that the tensor core sees exact tf32 values, and each
-// product a*b is formed as hi*hi + hi*lo + lo*hi, dropping lo*lo (about 2^-22
-// relative; the split-precision scheme of Ootomo & Yokota). Squares and mu^2 + var are formed
-// in fp32 first, as the reference does, and then split.
+// Tiles. A cluster of two CTAs computes a 256 x BN tile of both accumulators
+// (mean, variance) of a moment contraction (moment_gemm.cuh has the three
+// variance forms) with 2-SM MMAs (tcgen05.mma.cta_group::2, M = 256). Each CTA
+// stages its own 128 rows of the A operands and half of the B operands (BN/2
+// rows) in shared memory and keeps the accumulator rows of its half in its own
+// tensor memory; the pair's tensor cores share B. Per 128 x 128 x 8 product an
+// SM then reads 6 KB of operands from shared memory instead of 8 KB, and that is
+// what lets the MMAs run at the tensor pipe's rate: a single-CTA 128 x 128 tile
+// is bound by shared-memory bandwidth at about three quarters of it.
 //
-// Warp roles (672 threads):
-//   warps 0-7   A producers: two threads per output row, 4 reduction elements
-//               each per stage; stage raw x (and y) from any row-split layout
-//               through a cp.async ring, form the split operand tiles and store
-//               them in the canonical no-swizzle K-major layout (8x16-byte core
-//               matrices).
-//   warps 8-15  B producers: the same for u (and v), one row per output column.
-//   warp 16     allocates tensor memory; lane 0 issues the tcgen05.mma
-//               instructions and commits them to the stage's "empty" barrier.
-//   warps 17-20 accumulator warps (TMEM lane quarter warp % 4): the tensor
-//              core's fp32 accumulation truncates, so products are accumulated
-//              in tensor memory for kChunk stages only; these warps fold each
-//              chunk into a running total with round-to-nearest adds and run the
-//              epilogue from the last fold.
-// Stages form a ring of STAGES shared-memory buffers guarded by mbarriers.
-// Every wait is bounded: on timeout the CTA records an error word
-// (tagi_device_status), stops issuing work, waits (bounded) for its MMAs and
-// frees its tensor memory before returning.
+// Precision is 3xTF32: every fp32 operand v is split into hi = tf32(v) and
+// lo = tf32(v - hi), both rounded to nearest so that the tensor core sees exact
+// tf32 values, and each product a*b is formed as hi*hi + hi*lo + lo*hi, dropping
+// lo*lo (about 2^-22 relative; the split-precision scheme of Ootomo & Yokota).
+// Squares and mu^2 + var are formed in fp32 first, as the reference does, and
+// then split. The tensor core's fp32 accumulation truncates, so products are
+// accumulated in tensor memory for kChunk stages only and each chunk is folded
+// into a running total with round-to-nearest fp32 adds.
+//
+// Warp roles (per CTA):
+//   warps 0-7     A producers in two groups of four; group g serves the stages
+//                 of parity g and each thread one tile row. A thread loads its
+//                 row's 8 reduction elements per stage from global memory
+//                 straight into registers (kDepth of its stages in flight),
+//                 splits them and stores the operand tiles in the canonical
+//                 no-swizzle K-major layout (8-row x 16-byte core matrices).
+//   next 2*BW     B producers: the same for this CTA's BN/2 rows of B.
+//   MMA warp      allocates tensor memory (both CTAs); in the leader CTA
+//                 (cluster rank 0) one thread issues the MMAs and commits them
+//                 to barriers of both CTAs (multicast commit).
+//   8 acc warps   fold chunks and run the epilogue; warp w reads tensor-memory
+//                 lane quarter w % 4 and one half of the columns.
+// The mean and variance chunks end on staggered stages: when a chunk buffer must
+// be drained before reuse, the MMA warp issues the other accumulator's products
+// of the stage first and waits for the fold only then.
+//
+// Every wait is bounded: on timeout a CTA records an error word
+// (tagi_device_status), tells its peer, stops issuing work, waits (bounded) for
+// its MMAs and frees its tensor memory before returning.
+#include <climits>
 #include <cstdlib>
 #include <mutex>
 
@@ -39,14 +52,30 @@ __device__ int g_device_error = 0;  // 0 = ok, else the code of the first timeou
 
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kBK = 8;  // tf32 elements per MMA along the reduction
-constexpr int kThreads = 672;  // 21 warps
-constexpr int kChunk = 16;     // stages accumulated in tensor memory before a fold
-constexpr int kRawStages = 4;  // depth of the cp.async ring of raw operand rows
-constexpr int kRawSlot = 2 * 256 * 32;  // two operands x 256 producer rows x 8 fp32
-enum { kScalar = 0, kRowK = 1, kKRow = 2 };
+constexpr int kBK = 8;              // tf32 elements per MMA along the reduction
+constexpr int kChunk = 16;          // stages accumulated in tensor memory before a fold
+constexpr int kDepth = 2;           // stages in flight per producer thread
+constexpr int kMaxStages = 8;       // operand stages in shared memory
+constexpr int kStageBudget = 224 * 1024;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+// Warp layout and tensor-memory plan of a CTA for a pair tile of BN columns.
+template <int BN>
+struct Roles {
+    static constexpr int NC = BN / 2;                  // B rows staged by each CTA
+    static constexpr int BW = NC >= 32 ? NC / 32 : 1;  // B producer warps per group
+    static constexpr int B_W0 = 8;
+    static constexpr int MMA_W = B_W0 + 2 * BW;
+    static constexpr int ACC_W0 = MMA_W + 1;
+    static constexpr int WARPS = ACC_W0 + 8;
+    static constexpr int THREADS = 32 * WARPS;
+    static constexpr int STAGE_ARRIVALS = 2 * (4 + BW);  // producer warps of a stage, both CTAs
+    static constexpr int NP = 6 * BN <= 512 ? 2 : 1;     // chunk buffers per accumulator
+    static constexpr int COLS = 2 * (NP + 1) * BN <= 256 ? 256 : 512;
+    // tensor-memory columns: chunk buffer b of accumulator q, running total of q
+    static constexpr uint32_t pcol(int q, int b) { return static_cast<uint32_t>((q * NP + b) * BN); }
+    static constexpr uint32_t tcol(int q) { return static_cast<uint32_t>((2 * NP + q) * BN); }
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -58,64 +87,80 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
                  : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile(
-        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(
-            smem_u32(bar))
-        : "memory");
+// Arrive on a barrier given by its cluster shared-memory address (own or peer
+// CTA), with the default release semantics at CTA scope. A cluster-scope release
+// would make the arriving warp wait for all of its global loads in flight, which
+// are the producers' prefetches of later stages.
+__device__ __forceinline__ void arrive_cluster(uint32_t addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
 
+// Test for completion of phase `parity` (default acquire semantics at CTA scope,
+// as for the other barriers of the pair); a waiting thread is suspended (it
+// takes no issue slots) until the phase completes or about kSuspendNs passed.
+constexpr uint32_t kSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`; false if the CTA aborted or timed out.
-__device__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+struct Abort {
+    volatile int* flag;  // this CTA's abort word
+    uint32_t peer;       // cluster address of the peer CTA's abort word
+};
+
+// Bounded wait (after a failed first test); false if the pair aborted or timed out.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const Abort& ab,
+                                            int code) {
     const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 0;; ++it) {
+    for (;;) {
         if (mbar_try(bar, parity)) return true;
-        if ((it & 255u) == 255u) {
-            if (*abort_flag) return false;
-            if (globaltimer() - t0 > kTimeoutNs) {
-                *abort_flag = 1;
-                atomicCAS(&g_device_error, 0, code);
-                return false;
-            }
+        if (*ab.flag) return false;
+        if (globaltimer() - t0 > kTimeoutNs) {
+            *ab.flag = 1;
+            asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ab.peer), "r"(1) : "memory");
+            atomicCAS(&g_device_error, 0, code);
+            return false;
         }
     }
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab,
+                                          int code) {
+    return mbar_try(bar, parity) || mbar_wait_slow(bar, parity, ab, code);
 }
-// 4-byte copy; when `ok` is false nothing is read and the destination is zeroed.
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool ok) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
-                 "r"(ok ? 4 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const Abort& ab,
+                                          int code) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, ab, code));
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -128,38 +173,26 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_pair_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+// Arrives on `bar` in both CTAs of the pair once all MMAs issued so far completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
     asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(bar))
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+        "[%0], %1;" ::"r"(smem_u32(bar)),
+        "h"(static_cast<unsigned short>(3))
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 16 consecutive columns of this warp's 32 lanes; completes at tmem_wait_ld().
-__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+// 16 consecutive columns of this warp's 32 lanes; complete at tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -170,6 +203,9 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
     asm volatile(
@@ -204,16 +240,19 @@ __device__ __forceinline__ void store_out(const GemmArgs& g, int row, int col, i
 // Shared-memory matrix descriptor: no swizzle, K-major, core matrices of 8 rows
 // x 16 bytes; the two 16-byte halves of a row's 8 tf32 values are 128 bytes
 // apart (leading byte offset) and consecutive 8-row groups 256 bytes apart
-// (stride byte offset). Bit 46 carries the descriptor version of sm_100.
+// (stride byte offset). Bit 46 carries the descriptor version of sm_100. The
+// start address occupies the low 14 bits (address / 16), so descriptors of tiles
+// inside one stage differ by (byte offset / 16).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
     return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
            (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor: fp32 accumulate, tf32 A and B, both K-major, M=128.
+// Instruction descriptor: fp32 accumulate, tf32 A and B, both K-major, M = 256
+// (2-SM), N = bn.
 __host__ __device__ constexpr uint32_t instr_desc(int bn) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
-           (static_cast<uint32_t>(128 >> 4) << 24);
+           (static_cast<uint32_t>(256 >> 4) << 24);
 }
 
 // Nearest tf32 value (ties away from zero): add half a tf32 ulp to the
@@ -227,16 +266,20 @@ __device__ __forceinline__ uint32_t tile_off(int row, int half) {
     return static_cast<uint32_t>((row >> 3) * 256 + half * 128 + (row & 7) * 16);
 }
 
-// Split four fp32 values into tf32 hi/lo parts and store them (16 bytes each).
-__device__ __forceinline__ void st_split4(char* tile_hi, char* tile_lo, uint32_t off,
-                                          const float (&v)[4]) {
-    float4 hi, lo;
-    hi.x = tf32_rna(v[0]); lo.x = tf32_rna(v[0] - hi.x);
-    hi.y = tf32_rna(v[1]); lo.y = tf32_rna(v[1] - hi.y);
-    hi.z = tf32_rna(v[2]); lo.z = tf32_rna(v[2] - hi.z);
-    hi.w = tf32_rna(v[3]); lo.w = tf32_rna(v[3] - hi.w);
-    *reinterpret_cast<float4*>(tile_hi + off) = hi;
-    *reinterpret_cast<float4*>(tile_lo + off) = lo;
+// Split a row's 8 fp32 values into tf32 hi/lo parts and store both tiles' rows.
+__device__ __forceinline__ void st_split8(char* tile_hi, char* tile_lo, int row,
+                                          const float (&v)[8]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        float4 hi, lo;
+        hi.x = tf32_rna(v[4 * h + 0]); lo.x = tf32_rna(v[4 * h + 0] - hi.x);
+        hi.y = tf32_rna(v[4 * h + 1]); lo.y = tf32_rna(v[4 * h + 1] - hi.y);
+        hi.z = tf32_rna(v[4 * h + 2]); lo.z = tf32_rna(v[4 * h + 2] - hi.z);
+        hi.w = tf32_rna(v[4 * h + 3]); lo.w = tf32_rna(v[4 * h + 3] - hi.w);
+        const uint32_t off = tile_off(row, h);
+        *reinterpret_cast<float4*>(tile_hi + off) = hi;
+        *reinterpret_cast<float4*>(tile_lo + off) = lo;
+    }
 }
 
 template <int VM>
@@ -277,421 +320,432 @@ __host__ __device__ constexpr int field(unsigned long long packed, int i) {
 
 template <int VM, int BN>
 constexpr int stage_bytes() {
-    return TcTiles<VM>::na * 128 * 32 + TcTiles<VM>::nb * BN * 32;
+    return TcTiles<VM>::na * 128 * 32 + TcTiles<VM>::nb * (BN / 2) * 32;
 }
 
-// Operand stages that fit next to the raw ring in 227 KB (at most kStages).
 template <int VM, int BN>
 constexpr int op_stages() {
-    return (220 * 1024 - kRawStages * kRawSlot) / stage_bytes<VM, BN>() < kStages
-               ? (220 * 1024 - kRawStages * kRawSlot) / stage_bytes<VM, BN>()
-               : kStages;
+    return kStageBudget / stage_bytes<VM, BN>() < kMaxStages ? kStageBudget / stage_bytes<VM, BN>()
+                                                             : kMaxStages;
 }
+
+constexpr int kBarrierBytes = 256;
 
 template <int VM, int BN>
 constexpr int smem_bytes() {
-    return op_stages<VM, BN>() * stage_bytes<VM, BN>() + kRawStages * kRawSlot + 1024;
+    return op_stages<VM, BN>() * stage_bytes<VM, BN>() + kBarrierBytes;
 }
 
-
-// Number of chunk accumulators P (double-buffered when tensor memory allows).
-template <int BN>
-constexpr int num_p() {
-    return 6 * BN <= 512 ? 2 : 1;
+// Issue the MMAs of accumulator Q of one stage (operand tiles at descriptor d0).
+template <int VM, int BN, int Q>
+__device__ __forceinline__ void issue_acc(uint32_t d_tmem, uint64_t d0, uint32_t accumulate) {
+    using P = TcPlan<VM>;
+    constexpr uint32_t idesc = instr_desc(BN);
+    constexpr int A_TILE = 128 * 32, B_TILE = (BN / 2) * 32;
+    constexpr int B0 = TcTiles<VM>::na * A_TILE;
+    bool first = true;
+#pragma unroll
+    for (int i = 0; i < P::n; ++i) {
+        if (field(P::acc, i) != Q) continue;
+        const uint64_t ad = d0 + static_cast<uint64_t>((field(P::a, i) * A_TILE) >> 4);
+        const uint64_t bd = d0 + static_cast<uint64_t>((B0 + field(P::b, i) * B_TILE) >> 4);
+        mma_pair_tf32(d_tmem, ad, bd, idesc, first ? accumulate : 1u);
+        first = false;
+    }
 }
 
-template <int BN>
-constexpr int tmem_cols() {
-    return (num_p<BN>() + 1) * 2 * BN <= 128 ? 128 : ((num_p<BN>() + 1) * 2 * BN <= 256 ? 256 : 512);
+// 32 bytes at a 32-byte aligned address in one 256-bit load, not kept in L1.
+// A warp of row-owning threads then reads whole 32-byte sectors; two 16-byte
+// loads per row would touch each sector twice and slow the tensor pipe, whose
+// operand reads share the SM's load/store path with these requests.
+__device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
+    asm volatile("ld.global.L1::no_allocate.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                   "=f"(v[6]), "=f"(v[7])
+                 : "l"(p));
+}
+
+// One producer thread's row of its operand side.
+struct ProdRow {
+    const float* p0;
+    const float* p1;
+    int64_t base;  // A: arow.off(row); B: row * bn
+    bool valid, one, vec;
+};
+
+// The 8 reduction elements k0..k0+7 of the thread's A row (x and, if TWO, y);
+// zeros past kend, ones (and zero y) on the bias row.
+template <bool TWO>
+__device__ __forceinline__ void load_a(const GemmArgs& g, const ProdRow& w, int k0, int kend,
+                                       float (&v)[2][8]) {
+    if (w.one) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            v[0][j] = (k0 + j < kend) ? 1.f : 0.f;
+            v[1][j] = 0.f;
+        }
+        return;
+    }
+    if (w.vec && k0 + 8 <= kend) {
+        ld8(w.p0 + w.base + k0, v[0]);
+        if (TWO) ld8(w.p1 + w.base + k0, v[1]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int k = k0 + j;
+        v[0][j] = 0.f;
+        v[1][j] = 0.f;
+        if (k < kend) {
+            const int64_t o = w.base + static_cast<int64_t>(k) * g.ak;
+            v[0][j] = __ldcg(w.p0 + o);
+            if (TWO) v[1][j] = __ldcg(w.p1 + o);
+        }
+    }
+}
+
+// The same for the thread's B row; the reduction index goes through brow.
+template <bool TWO>
+__device__ __forceinline__ void load_b(const GemmArgs& g, const ProdRow& w, int k0, int kend,
+                                       float (&v)[2][8]) {
+    const RowMap& m = g.brow;
+    if (w.vec && k0 + 8 <= kend) {
+        const int64_t o = w.base + m.off(k0);
+        ld8(w.p0 + o, v[0]);
+        if (TWO) ld8(w.p1 + o, v[1]);
+        return;
+    }
+    // offsets of k0 .. k0+7 through the row map with a single division
+    uint32_t q = 0, r = static_cast<uint32_t>(k0);
+    if (m.div > 0) {
+        q = static_cast<uint32_t>(k0) / static_cast<uint32_t>(m.div);
+        r = static_cast<uint32_t>(k0) - q * static_cast<uint32_t>(m.div);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int k = k0 + j;
+        v[0][j] = 0.f;
+        v[1][j] = 0.f;
+        if (k < kend) {
+            const int64_t o =
+                w.base + (m.div > 0 ? static_cast<int64_t>(q) * m.outer +
+                                          static_cast<int64_t>(r) * m.stride
+                                    : static_cast<int64_t>(k) * m.stride);
+            v[0][j] = __ldcg(w.p0 + o);
+            if (TWO) v[1][j] = __ldcg(w.p1 + o);
+        }
+        if (m.div > 0 && ++r == static_cast<uint32_t>(m.div)) {
+            r = 0;
+            ++q;
+        }
+    }
+}
+
+// Number of chunks and last stage of chunk c when chunk boundaries are shifted
+// by `o` stages (chunk c covers stages [c*kChunk - o, (c+1)*kChunk - o)).
+__device__ __forceinline__ int num_chunks(int niter, int o) { return (niter + o + kChunk - 1) / kChunk; }
+__device__ __forceinline__ int chunk_end(int c, int o, int niter) {
+    return min((c + 1) * kChunk - o, niter) - 1;
 }
 
 template <int VM, bool MEAN, int EPI, int BN>
-__global__ void __launch_bounds__(kThreads, 1) moment_tc_kernel(const GemmArgs g) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 1)
+    moment_tc_kernel(const GemmArgs g) {
+    using R = Roles<BN>;
     using T = TcTiles<VM>;
-    using P = TcPlan<VM>;
-    constexpr int A_TILE = 128 * 32, B_TILE = BN * 32;
+    constexpr int A_TILE = 128 * 32, B_TILE = R::NC * 32;
     constexpr int STAGE = stage_bytes<VM, BN>();
-    constexpr int NP = num_p<BN>();
-    constexpr int COLS = tmem_cols<BN>();
     constexpr int OPS = op_stages<VM, BN>();
+    constexpr int NP = R::NP;
+    constexpr int kOff1 = kChunk / 2;  // stage shift of the variance chunks
     extern __shared__ __align__(1024) char smem[];
-    char* raw = smem + OPS * STAGE;
-    uint64_t* full = reinterpret_cast<uint64_t*>(raw + kRawStages * kRawSlot);
-    uint64_t* empty = full + kStages;
-    uint64_t* chunk_full = empty + kStages;   // [NP]: MMA -> accumulator warps
-    uint64_t* chunk_empty = chunk_full + 2;   // [NP]: accumulator warps -> MMA
-    uint64_t* done = chunk_empty + 2;         // all MMAs complete
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OPS * STAGE);  // [OPS], leader only
+    uint64_t* empty = full + kMaxStages;                                // [OPS]
+    uint64_t* chunk_full = empty + kMaxStages;                          // [q*2 + b]
+    uint64_t* chunk_empty = chunk_full + 4;                             // [q*2 + b], leader
+    uint64_t* done = chunk_empty + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int m_cta = static_cast<int>(blockIdx.x >> 1) * 256 + static_cast<int>(rank) * 128;
+    const int n0 = blockIdx.y * BN;
     const int batch = blockIdx.z / g.splits, split = blockIdx.z % g.splits;
     const int kbeg = split * g.kchunk;
     const int kend = min(g.Kr, kbeg + g.kchunk);
     const int niter = kend > kbeg ? (kend - kbeg + kBK - 1) / kBK : 0;
-    const int nchunks = (niter + kChunk - 1) / kChunk;
+    const Abort ab{abort_word, map_to(smem_u32(const_cast<int*>(abort_word)), rank ^ 1u)};
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 512);
+        for (int s = 0; s < OPS; ++s) {
+            mbar_init(&full[s], R::STAGE_ARRIVALS);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&chunk_full[b], 1);
-            mbar_init(&chunk_empty[b], 128);
+        for (int i = 0; i < 4; ++i) {
+            mbar_init(&chunk_full[i], 1);
+            mbar_init(&chunk_empty[i], 16);  // 8 accumulator warps in each CTA
         }
         mbar_init(done, 1);
-        *abort_flag = 0;
+        *abort_word = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        fence_proxy_async();
     }
-    if (warp == 16) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+    if (warp == R::MMA_W) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_slot)),
-                     "r"(COLS));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+                     "r"(R::COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // columns: P buffer b at [2*BN*b, 2*BN*(b+1)), running total T after them;
-    // within each, the mean accumulator then the variance accumulator.
-    const uint32_t tcol_total = 2 * BN * NP;
 
-    if (warp < 16) {
-        // ---------------------------------------------------------------- producers
-        // Two threads per tile row: `half` selects reduction elements 0-3 or 4-7.
-        const bool is_a = warp < 8;
-        const int side_tid = is_a ? tid : tid - 256;
-        const int r = side_tid & 127, half = side_tid >> 7;
-        const bool active = is_a ? true : (r < BN);
-        int idx;
-        bool valid, one = false;
-        int64_t base = 0;
-        const float *p0, *p1;
+    if (warp < R::MMA_W) {
+        // ------------------------------------------------------------ producers
+        const bool is_a = warp < R::B_W0;
+        const int grp = is_a ? (warp >> 2) : (warp - R::B_W0) / R::BW;
+        const int r = is_a ? ((warp & 3) * 32 + lane) : (((warp - R::B_W0) % R::BW) * 32 + lane);
+        ProdRow w;
+        constexpr bool TWO_A = VM != LSQ, TWO_B = VM != RSQ;
         if (is_a) {
-            idx = m0 + r;
-            valid = idx < g.M;
-            one = (idx == g.ones_row);
-            base = (valid && !one) ? g.arow.off(idx) : 0;
-            p0 = g.x + batch * g.a_bs;
-            p1 = (VM == LSQ) ? nullptr : g.y + batch * g.a_bs;
+            const int idx = m_cta + r;
+            w.valid = idx < g.M;
+            w.one = idx == g.ones_row;
+            w.p0 = g.x + batch * g.a_bs;
+            w.p1 = TWO_A ? g.y + batch * g.a_bs : nullptr;
+            w.base = (w.valid && !w.one) ? g.arow.off(idx) : 0;
+            const uintptr_t al = (reinterpret_cast<uintptr_t>(w.p0) |
+                                  (TWO_A ? reinterpret_cast<uintptr_t>(w.p1) : 0)) & 31;
+            w.vec = al == 0 && g.ak == 1 && (w.base & 7) == 0;
         } else {
-            idx = n0 + r;
-            valid = active && idx < g.N;
-            base = valid ? static_cast<int64_t>(idx) * g.bn : 0;
-            p0 = g.u + batch * g.b_bs;
-            p1 = (VM == RSQ) ? nullptr : g.v + batch * g.b_bs;
-        }
-        const bool has1 = (p1 != nullptr);
-        // Staging modes of this side's operands (uniform over the side):
-        //  kRowK   each row's reduction values are contiguous and 16-byte aligned:
-        //          a thread copies its own 4-element half row as one 16-byte chunk
-        //          ([row][8] layout);
-        //  kKRow   4 consecutive rows are contiguous and aligned for every reduction
-        //          index: the side's 256 threads copy one 16-byte row chunk each into a
-        //          [k][128] layout and read it transposed after a named barrier;
-        //  kScalar element-wise 4-byte copies of the thread's own half row.
-        // Out-of-range elements are zero-filled; chunks that straddle a tile edge or
-        // the bias row fall back to element-wise copies.
-        const uintptr_t align_bits = (reinterpret_cast<uintptr_t>(p0) |
-                                      (has1 ? reinterpret_cast<uintptr_t>(p1) : 0)) & 15;
-        int mode = kScalar;
-        if (is_a) {
-            const RowMap& m = g.arow;
-            const bool rows4 = (m.div <= 0) ? (m.stride % 4 == 0)
-                                            : (m.stride % 4 == 0 && m.outer % 4 == 0);
-            if (align_bits == 0 && g.ak == 1 && rows4) {
-                mode = kRowK;
-            } else if (align_bits == 0 && m.stride == 1 && g.ak % 4 == 0 &&
-                       (m.div <= 0 || (m.div % 4 == 0 && m.outer % 4 == 0))) {
-                mode = kKRow;
-            }
-        } else {
+            const int idx = n0 + static_cast<int>(rank) * R::NC + r;
+            w.valid = r < R::NC && idx < g.N;
+            w.one = false;
+            w.p0 = g.u + batch * g.b_bs;
+            w.p1 = TWO_B ? g.v + batch * g.b_bs : nullptr;
+            w.base = w.valid ? static_cast<int64_t>(idx) * g.bn : 0;
             const RowMap& m = g.brow;
-            if (align_bits == 0 && m.stride == 1 && g.bn % 4 == 0 &&
-                (m.div <= 0 || (m.div % 8 == 0 && m.outer % 4 == 0))) {
-                mode = kRowK;
-            } else if (align_bits == 0 && g.bn == 1 &&
-                       ((m.div <= 0) ? (m.stride % 4 == 0)
-                                     : (m.stride % 4 == 0 && m.outer % 4 == 0))) {
-                mode = kKRow;
-            }
+            const uintptr_t al = (reinterpret_cast<uintptr_t>(w.p0) |
+                                  (TWO_B ? reinterpret_cast<uintptr_t>(w.p1) : 0)) & 31;
+            w.vec = al == 0 && m.stride == 1 && (w.base & 7) == 0 &&
+                    (m.div <= 0 || (m.div % 8 == 0 && m.outer % 8 == 0));
         }
-        const int side_rows = is_a ? g.M : g.N;
-        const int side_row0 = is_a ? m0 : n0;
-        // region of (slot, operand) for this side: 128 rows x 8 fp32
-        auto region = [&](int slot, int o) -> char* {
-            return raw + slot * kRawSlot + ((is_a ? 0 : 2) + o) * 4096;
-        };
-        // global offset of (row, k) for this side, valid row and k < kend assumed
-        auto goff = [&](int rrow, int k) -> int64_t {
-            return is_a ? g.arow.off(rrow) + static_cast<int64_t>(k) * g.ak
-                        : static_cast<int64_t>(rrow) * g.bn + g.brow.off(k);
-        };
-        auto row_ok = [&](int rrow) -> bool {
-            return rrow < side_rows && !(is_a && rrow == g.ones_row);
-        };
-        auto issue = [&](int it) {
-            if (it >= niter) return;
-            const int k0 = kbeg + it * kBK;
-            const int slot = it % kRawStages;
-#pragma unroll
-            for (int o = 0; o < 2; ++o) {
-                if (o == 1 && !has1) break;
-                const float* src = o ? p1 : p0;
-                char* reg = region(slot, o);
-                if (mode == kKRow) {
-                    const int c = side_tid;  // chunk: k = c / 32, rows 4*(c % 32) .. +3
-                    const int k = k0 + c / 32, rg = c % 32;
-                    const int rrow = side_row0 + 4 * rg;
-                    char* dst = reg + (c / 32) * 512 + rg * 16;
-                    if (4 * rg < (is_a ? 128 : BN)) {
-                        if (k < kend && rrow + 3 < side_rows &&
-                            !(is_a && g.ones_row >= rrow && g.ones_row <= rrow + 3)) {
-                            cp_async16(dst, src + goff(rrow, k));
-                        } else {
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const bool ok = k < kend && row_ok(rrow + q);
-                                cp_async4(dst + 4 * q, ok ? src + goff(rrow + q, k) : src, ok);
-                            }
-                        }
-                    }
-                } else {
-                    if (!valid || one) continue;
-                    const int kh = k0 + 4 * half;
-                    char* dst = reg + r * 32 + half * 16;
-                    if (mode == kRowK && kh + 4 <= kend) {
-                        cp_async16(dst, src + goff(idx, kh));
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const int k = kh + j;
-                            const bool ok = k < kend;
-                            cp_async4(dst + 4 * j, ok ? src + goff(idx, k) : src, ok);
-                        }
-                    }
-                }
-            }
-        };
-        auto fetch = [&](int it, float (&v0)[4], float (&v1)[4]) {
-            const int kh = kbeg + it * kBK + 4 * half;
-            if (!valid) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) v0[j] = v1[j] = 0.f;
-                return;
-            }
-            if (one) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    v0[j] = (kh + j < kend) ? 1.f : 0.f;
-                    v1[j] = 0.f;
-                }
-                return;
-            }
-            const int slot = it % kRawStages;
-#pragma unroll
-            for (int o = 0; o < 2; ++o) {
-                float* v = o ? v1 : v0;
-                if (o == 1 && !has1) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) v[j] = 0.f;
-                    break;
-                }
-                const char* reg = region(slot, o);
-                if (mode == kKRow) {
-                    const float* f = reinterpret_cast<const float*>(reg);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) v[j] = f[(4 * half + j) * 128 + r];
-                } else {
-                    const float4 x = *reinterpret_cast<const float4*>(reg + r * 32 + half * 16);
-                    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-                }
-            }
-        };
+        const uint32_t full0 = map_to(smem_u32(full), 0);  // the leader's full barriers
 
-        auto produce = [&](int it, const float (&v0)[4], const float (&v1)[4]) -> bool {
+        auto load = [&](int it, float (&v)[2][8]) {
+            if (it >= niter || !w.valid) return;
+            const int k0 = kbeg + it * kBK;
+            if (is_a) load_a<TWO_A>(g, w, k0, kend, v);
+            else load_b<TWO_B>(g, w, k0, kend, v);
+        };
+        auto produce = [&](int it, const float (&v)[2][8]) -> bool {
             const int s = it % OPS;
-            if (it >= OPS && !mbar_wait(&empty[s], ((it / OPS) & 1) ^ 1, abort_flag, 1))
-                return false;
-            if (active) {
+            if (it >= OPS && !warp_wait(&empty[s], ((it / OPS) - 1) & 1, ab, 1)) return false;
+            // Rows outside the matrix are not written: an output row (column)
+            // depends only on its own A row (B row), and those outputs are dropped.
+            if (w.valid) {
                 char* st = smem + s * STAGE;
-                const uint32_t off = tile_off(r, half);
-                float sq[4];
+                float sq[8];
                 if (is_a) {
                     char* A = st;
-                    st_split4(A + 0 * A_TILE, A + 1 * A_TILE, off, v0);
+                    st_split8(A + 0 * A_TILE, A + 1 * A_TILE, r, v[0]);
                     if (VM == FULL || VM == LSQ) {
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) sq[j] = v0[j] * v0[j];
-                        st_split4(A + 2 * A_TILE, A + 3 * A_TILE, off, sq);
+                        for (int j = 0; j < 8; ++j) sq[j] = v[0][j] * v[0][j];
+                        st_split8(A + 2 * A_TILE, A + 3 * A_TILE, r, sq);
                     }
-                    if (VM == FULL) st_split4(A + 4 * A_TILE, A + 5 * A_TILE, off, v1);
-                    if (VM == RSQ) st_split4(A + 2 * A_TILE, A + 3 * A_TILE, off, v1);
+                    if (VM == FULL) st_split8(A + 4 * A_TILE, A + 5 * A_TILE, r, v[1]);
+                    if (VM == RSQ) st_split8(A + 2 * A_TILE, A + 3 * A_TILE, r, v[1]);
                 } else {
                     char* B = st + T::na * A_TILE;
-                    st_split4(B + 0 * B_TILE, B + 1 * B_TILE, off, v0);
+                    st_split8(B + 0 * B_TILE, B + 1 * B_TILE, r, v[0]);
                     if (VM == FULL) {
-                        st_split4(B + 2 * B_TILE, B + 3 * B_TILE, off, v1);
+                        st_split8(B + 2 * B_TILE, B + 3 * B_TILE, r, v[1]);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) sq[j] = v0[j] * v0[j] + v1[j];
-                        st_split4(B + 4 * B_TILE, B + 5 * B_TILE, off, sq);
+                        for (int j = 0; j < 8; ++j) sq[j] = v[0][j] * v[0][j] + v[1][j];
+                        st_split8(B + 4 * B_TILE, B + 5 * B_TILE, r, sq);
                     } else if (VM == RSQ) {
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) sq[j] = v0[j] * v0[j];
-                        st_split4(B + 2 * B_TILE, B + 3 * B_TILE, off, sq);
+                        for (int j = 0; j < 8; ++j) sq[j] = v[0][j] * v[0][j];
+                        st_split8(B + 2 * B_TILE, B + 3 * B_TILE, r, sq);
                     } else {
-                        st_split4(B + 2 * B_TILE, B + 3 * B_TILE, off, v1);
+                        st_split8(B + 2 * B_TILE, B + 3 * B_TILE, r, v[1]);
                     }
                 }
                 fence_proxy_async();
             }
-            mbar_arrive(&full[s]);
+            __syncwarp();
+            if (lane == 0) arrive_cluster(full0 + static_cast<uint32_t>(s * 8));
             return true;
         };
 
-        // cp.async ring: kRawStages-1 stages in flight ahead of the one transformed
-        for (int i = 0; i < kRawStages - 1; ++i) {
-            issue(i);
-            cp_async_commit();
-        }
-        float v0[4], v1[4];
-        // After an abort every thread keeps iterating without work, so that all
-        // threads of a side still reach every named barrier.
-        bool alive = true;
-        for (int it = 0; it < niter; ++it) {
-            cp_async_wait<kRawStages - 2>();
-            // rows staged by other threads of this side: wait until all copied (and
-            // until all consumed the slot that the next issue refills)
-            if (mode == kKRow) named_bar_sync(is_a ? 1 : 2, 256);
-            if (alive) {
-                fetch(it, v0, v1);
-                alive = produce(it, v0, v1);
-            }
-            if (alive) issue(it + kRawStages - 1);  // refills the slot consumed one iteration ago
-            cp_async_commit();
-        }
-        cp_async_wait<0>();
-    } else if (warp == 16) {
-        if (lane == 0) {
-            // ------------------------------------------------------------ MMA issue
-            constexpr uint32_t idesc = instr_desc(BN);
-            const uint32_t base = smem_u32(smem);
-            bool started[2] = {false, false};
-            for (int it = 0; it < niter; ++it) {
-                const int c = it / kChunk, b = c % NP;
-                if (it % kChunk == 0) {
-                    // chunk c accumulates into buffer b once the fold of chunk c-NP freed it
-                    if (c >= NP && !mbar_wait(&chunk_empty[b], ((c / NP) - 1) & 1, abort_flag, 5))
-                        break;
-                    tc_fence_after();
-                    started[0] = started[1] = false;
-                }
-                const int s = it % OPS;
-                if (!mbar_wait(&full[s], (it / OPS) & 1, abort_flag, 2)) break;
-                tc_fence_after();
-                const uint32_t st = base + s * STAGE;
-                const uint32_t pcol = tmem + static_cast<uint32_t>(2 * BN * b);
+        // this group's stages grp, grp+2, ...; kDepth of them loaded ahead
+        float buf[kDepth][2][8];
 #pragma unroll
-                for (int i = 0; i < P::n; ++i) {
-                    const int acc = field(P::acc, i);
-                    if (!MEAN && acc == 0) continue;
-                    const uint64_t ad = smem_desc(st + field(P::a, i) * A_TILE);
-                    const uint64_t bd = smem_desc(st + T::na * A_TILE + field(P::b, i) * B_TILE);
-                    mma_tf32(pcol + acc * BN, ad, bd, idesc, started[acc] ? 1u : 0u);
-                    started[acc] = true;
+        for (int d = 0; d < kDepth; ++d) load(grp + 2 * d, buf[d]);
+        bool alive = true;
+        for (int it0 = grp; it0 < niter && alive; it0 += 2 * kDepth) {
+#pragma unroll
+            for (int d = 0; d < kDepth; ++d) {
+                const int it = it0 + 2 * d;
+                if (it < niter && alive) {
+                    alive = produce(it, buf[d]);
+                    load(it + 2 * kDepth, buf[d]);
                 }
-                mma_commit(&empty[s]);
-                if (it % kChunk == kChunk - 1 || it == niter - 1) mma_commit(&chunk_full[b]);
             }
-            mma_commit(done);  // arrives once every MMA issued above has completed
+        }
+    } else if (warp == R::MMA_W) {
+        // ------------------------------------------------------------ MMA issue
+        // One thread issues everything (tcgen05.mma and tcgen05.commit are
+        // single-thread instructions). The tensor pipe queues only a few MMAs, so
+        // the work between two stages' MMAs is kept to a few integer updates.
+        if (leader && lane == 0) {
+            const uint64_t d_first = smem_desc(smem_u32(smem));
+            uint64_t d0 = d_first;
+            int s = 0;
+            uint32_t ph = 0;
+            int pos0 = 0, pos1 = kOff1;  // (stage + shift) % kChunk of each accumulator
+            int c0 = 0, c1 = 0;          // chunk index of each accumulator
+            // An accumulator whose chunk buffer must first be drained by a fold
+            // goes second, so that the other one's products keep the pipe busy.
+            auto drained = [&](int q, int c) -> bool {
+                if (!mbar_wait(&chunk_empty[q * 2 + c % NP], ((c / NP) - 1) & 1, ab, 5)) return false;
+                tc_fence_after();
+                return true;
+            };
+            for (int it = 0; it < niter; ++it) {
+                if (!mbar_wait(&full[s], ph, ab, 2)) break;
+                tc_fence_after();
+                const bool first0 = pos0 == 0, first1 = it == 0 || pos1 == 0;
+                const bool last0 = it == niter - 1 || pos0 == kChunk - 1;
+                const bool last1 = it == niter - 1 || pos1 == kChunk - 1;
+                const int b0 = c0 % NP, b1 = c1 % NP;
+                const uint32_t acc0 = first0 ? 0u : 1u, acc1 = first1 ? 0u : 1u;
+                bool ok = true;
+                if (!(MEAN && first0 && c0 >= NP)) {
+                    if (MEAN) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), d0, acc0);
+                    if (first1 && c1 >= NP) ok = drained(1, c1);
+                    if (ok) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), d0, acc1);
+                } else {
+                    issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), d0, acc1);
+                    ok = drained(0, c0);
+                    if (ok) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), d0, acc0);
+                }
+                if (!ok) break;
+                mma_commit_pair(&empty[s]);
+                if (MEAN && last0) mma_commit_pair(&chunk_full[b0]);
+                if (last1) mma_commit_pair(&chunk_full[2 + b1]);
+                if (++pos0 == kChunk) { pos0 = 0; ++c0; }
+                if (++pos1 == kChunk) { pos1 = 0; ++c1; }
+                if (++s == OPS) {
+                    s = 0;
+                    ph ^= 1u;
+                    d0 = d_first;
+                } else {
+                    d0 += static_cast<uint64_t>(STAGE >> 4);
+                }
+            }
+            mma_commit_pair(done);  // arrives once every MMA issued above completed
         }
     } else {
-        // -------------------------------------------- accumulator warps (17-20)
-        // Tensor-core accumulation truncates; each chunk of kChunk stages is
-        // folded into the running total with round-to-nearest fp32 adds, and the
-        // last fold feeds the epilogue directly.
-        const int sub = warp & 3;  // TMEM lane quarter this warp may access
-        const int row = m0 + sub * 32 + lane;
+        // -------------------------------------------- accumulator warps
+        const int a = warp - R::ACC_W0;
+        const int sub = warp & 3;  // tensor-memory lane quarter this warp may access
+        constexpr int HC = BN / 2;  // columns per warp per accumulator
+        const int cbeg = (a >> 2) * HC;
+        const int row = m_cta + sub * 32 + lane;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-        bool ok = true;
-        for (int c = 0; c < nchunks && ok; ++c) {
-            const int b = c % NP;
-            ok = __all_sync(0xffffffffu, mbar_wait(&chunk_full[b], (c / NP) & 1, abort_flag, 3) &&
-                                             !*abort_flag);
+        const uint32_t ce0 = map_to(smem_u32(chunk_empty), 0);  // the leader's drain barriers
+        const int64_t ro = (EPI == EPI_STORE && row < g.M) ? g.orow.off(row) + batch * g.o_bs : 0;
+        const int nch0 = num_chunks(niter, 0), nch1 = num_chunks(niter, kOff1);
+        int c0 = MEAN ? 0 : nch0, c1 = 0;
+        bool ok = niter > 0;
+        while (ok) {
+            const bool fin0 = !MEAN || c0 == nch0 - 1;
+            const bool fin1 = c1 == nch1 - 1;
+            if (fin0 && fin1) break;
+            const int e0 = fin0 ? INT_MAX : chunk_end(c0, 0, niter);
+            const int e1 = fin1 ? INT_MAX : chunk_end(c1, kOff1, niter);
+            const int q = e0 <= e1 ? 0 : 1;
+            const int cq = q ? c1 : c0, bq = cq % NP;
+            // intermediate fold of chunk cq of accumulator q: T_q += P_q
+            ok = warp_wait(&chunk_full[q * 2 + bq], (cq / NP) & 1, ab, 3);
             if (!ok) break;
             tc_fence_after();
-            const bool last = (c == nchunks - 1);
-            const uint32_t pcol = lane_base + static_cast<uint32_t>(2 * BN * b);
-            const uint32_t tcol = lane_base + tcol_total;
-            const int64_t ro =
-                (EPI == EPI_STORE && row < g.M) ? g.orow.off(row) + batch * g.o_bs : 0;
-            // Intermediate folds: T += P, 16 columns at a time, the P and T loads of a
-            // column block issued together before one wait.
-            if (!last) {
+            const uint32_t pc = lane_base + R::pcol(q, bq) + cbeg;
+            const uint32_t tc = lane_base + R::tcol(q) + cbeg;
 #pragma unroll 1
-                for (int c0 = 0; c0 < 2 * BN; c0 += 16) {
-                    if (!MEAN && c0 < BN) continue;
-                    uint32_t pr[16], tr[16];
-                    tmem_ld16_async(pcol + c0, pr);
-                    if (c > 0) tmem_ld16_async(tcol + c0, tr);
-                    tmem_wait_ld();
-                    float tv[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        tv[j] = c > 0 ? __uint_as_float(tr[j]) + __uint_as_float(pr[j])
-                                      : __uint_as_float(pr[j]);
-                    tmem_st16(tcol + c0, tv);
+            for (int k = 0; k < HC; k += 16) {
+                uint32_t pr[16], tr[16];
+                tmem_ld16(pc + k, pr);
+                if (cq > 0) tmem_ld16(tc + k, tr);
+                tmem_wait_ld();
+                if (k + 16 >= HC) {
+                    // this warp has read all of its part of the chunk buffer
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) arrive_cluster(ce0 + static_cast<uint32_t>((q * 2 + bq) * 8));
                 }
-            } else {
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float pm[16], pv[16], tm[16], tv[16];
-                    if (MEAN) tmem_ld16(pcol + c0, pm);
-                    tmem_ld16(pcol + BN + c0, pv);
-                    if (c > 0) {
-                        if (MEAN) tmem_ld16(tcol + c0, tm);
-                        tmem_ld16(tcol + BN + c0, tv);
-                    }
+                float tv[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        tm[j] = MEAN ? (c > 0 ? tm[j] + pm[j] : pm[j]) : 0.f;
-                        tv[j] = c > 0 ? tv[j] + pv[j] : pv[j];
-                    }
+                for (int j = 0; j < 16; ++j)
+                    tv[j] = cq > 0 ? __uint_as_float(tr[j]) + __uint_as_float(pr[j])
+                                   : __uint_as_float(pr[j]);
+                tmem_st16(tc + k, tv);
+            }
+            tmem_wait_st();
+            if (q) ++c1;
+            else ++c0;
+        }
+        if (ok) {
+            // last chunks of both accumulators: fold and run the epilogue
+            const int b0 = (MEAN ? c0 : 0) % NP, b1 = c1 % NP;
+            if (MEAN) ok = warp_wait(&chunk_full[b0], (c0 / NP) & 1, ab, 3);
+            if (ok) ok = warp_wait(&chunk_full[2 + b1], (c1 / NP) & 1, ab, 3);
+            if (ok) {
+                tc_fence_after();
+#pragma unroll 1
+                for (int k = 0; k < HC; k += 16) {
+                    uint32_t pm[16], pv[16], tm[16], tv[16];
+                    if (MEAN) tmem_ld16(lane_base + R::pcol(0, b0) + cbeg + k, pm);
+                    tmem_ld16(lane_base + R::pcol(1, b1) + cbeg + k, pv);
+                    if (MEAN && c0 > 0) tmem_ld16(lane_base + R::tcol(0) + cbeg + k, tm);
+                    if (c1 > 0) tmem_ld16(lane_base + R::tcol(1) + cbeg + k, tv);
+                    tmem_wait_ld();
                     if (row >= g.M) continue;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int col = n0 + c0 + j;
+                        const int col = n0 + cbeg + k + j;
                         if (col >= g.N) continue;
-                        store_out<EPI, MEAN>(g, row, col, ro, split, tm[j], tv[j]);
+                        const float am = MEAN ? (c0 > 0 ? __uint_as_float(tm[j]) + __uint_as_float(pm[j])
+                                                        : __uint_as_float(pm[j]))
+                                              : 0.f;
+                        const float av = c1 > 0 ? __uint_as_float(tv[j]) + __uint_as_float(pv[j])
+                                                : __uint_as_float(pv[j]);
+                        store_out<EPI, MEAN>(g, row, col, ro, split, am, av);
                     }
                 }
             }
-            if (!last) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            tc_fence_before();
-            mbar_arrive(&chunk_empty[b]);
         }
-        if (nchunks == 0 && row < g.M) {
+        if (niter == 0 && row < g.M) {
             // empty reduction: outputs are the biases (or zero sums)
-            const int64_t ro = (EPI == EPI_STORE) ? g.orow.off(row) + batch * g.o_bs : 0;
-            for (int col = n0; col < min(n0 + BN, g.N); ++col)
+            for (int col = n0 + cbeg; col < min(n0 + cbeg + HC, g.N); ++col)
                 store_out<EPI, MEAN>(g, row, col, ro, split, 0.f, 0.f);
         }
     }
 
-    if (warp == 16) {
-        // the MMAs of this CTA must be complete before their memory is released
-        if (!mbar_try(done, 0)) mbar_wait(done, 0, abort_flag, 4);
+    if (warp == R::MMA_W) {
+        // the pair's MMAs read both CTAs' shared memory: wait until they are complete
+        if (!mbar_try(done, 0)) mbar_wait(done, 0, ab, 4);
     }
     tc_fence_before();
-    __syncthreads();
-    if (warp == 16) {
+    cluster_sync();  // no peer access (remote arrive, multicast commit) is still due
+    if (warp == R::MMA_W) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(COLS));
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(R::COLS));
     }
 }
 
@@ -718,10 +772,11 @@ int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
                   cudaGetErrorString(attr_err));
         return TAGI_E_LAUNCH;
     }
-    dim3 grid((g.N + BN - 1) / BN, (g.M + 127) / 128, batch * g.splits);
+    const int64_t pairs = (static_cast<int64_t>(g.M) + 255) / 256;
+    dim3 grid(static_cast<unsigned>(2 * pairs), (g.N + BN - 1) / BN, batch * g.splits);
     TAGI_REQUIRE(grid.y <= 65535 && grid.z <= 65535, TAGI_E_UNSUPPORTED, "%s: grid too large",
                  what);
-    moment_tc_kernel<VM, MEAN, EPI, BN><<<grid, kThreads, smem, st>>>(g);
+    moment_tc_kernel<VM, MEAN, EPI, BN><<<grid, Roles<BN>::THREADS, smem, st>>>(g);
     return check_launch(what);
 }
 
