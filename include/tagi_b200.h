@@ -88,6 +88,20 @@ int tagi_backward_delta_view(const float* dmz, const float* dSz, int64_t d_div, 
                              int64_t c_stride, int64_t c_kstride, int64_t M, int64_t K,
                              int64_t N, void* stream);
 
+/* Input deltas of a stride-1 Conv2D with symmetric padding p, written in NCHW.
+ * With stride 1 the reference's patch-space product followed by its col2im
+ * gather (triton_tagi/layers/conv2d.py:338-357 and _col2im_kernel,
+ * conv2d.py:119-130) sums exactly the terms of a convolution of the output
+ * deltas with the spatially reversed, transposed weights; this entry computes it
+ * as one contraction over (co, tap). pm/pS are the patches of (delta_mz,
+ * delta_Sz) taken with padding k-1-p (tagi_im2col of the N x Co x Ho x Wo
+ * deltas), rows (n, h, w) of the H x W input and columns (co, kh, kw); mw is the
+ * layer's (C*k*k) x Co weight matrix. d_ma = patches_m @ W', d_Sa = patches_S @
+ * W'^2 with W'[(co,kh,kw)][c] = mw[c*k*k + (k-1-kh)*k + (k-1-kw)][co]. */
+int tagi_conv2d_backward_delta_s1(const float* pm, const float* pS, const float* mw, float* d_ma,
+                                  float* d_Sa, int64_t N, int64_t C, int64_t H, int64_t W,
+                                  int64_t Co, int64_t k, void* stream);
+
 /* grad_mw = a^T @ dmz, grad_Sw = (a^2)^T @ dSz  (K x N outputs).
  * Replaces triton_fused_weight_grad, triton_tagi/kernels/common.py:410-451. */
 size_t tagi_fused_weight_grad_workspace_size(int64_t M, int64_t K, int64_t N);

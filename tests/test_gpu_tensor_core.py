@@ -174,3 +174,35 @@ def test_batched_attention_products():
     assert_rel(m, rm, MEAN_RTOL, "shared left mean")
     assert_rel(v, rv, VAR_RTOL, "shared left var")
     _ok()
+
+
+@pytest.mark.parametrize("C,Co,k,p", [(64, 64, 3, 1), (128, 96, 3, 1), (40, 72, 5, 2),
+                                      (64, 64, 3, 0), (96, 64, 1, 0)])
+def test_conv_stride1_input_deltas_as_one_contraction(C, Co, k, p):
+    """Stride-1 Conv2D.backward runs the deltas' patches against the reversed
+    weights (tagi_conv2d_backward_delta_s1); it must equal the reference's
+    patch-space product followed by its col2im gather."""
+    import oracle.net as ON
+    from triton_tagi import Conv2D
+
+    g = torch.Generator().manual_seed(C + Co + k)
+    N, H, W = 4, 14, 13
+    torch.manual_seed(3)
+    ref = ON.Conv2D(C, Co, k, 1, p, 1)
+    dev = Conv2D(C, Co, k, 1, p, 1, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, getattr(ref, n).to(DEV))
+    ma, Sa = _rnd(g, N, C, H, W), _rnd(g, N, C, H, W, u=True, scale=0.1)
+    rm, _ = ref.forward(ma, Sa)
+    dev.forward(ma.to(DEV), Sa.to(DEV))
+    dmz, dSz = _rnd(g, *rm.shape, scale=0.1), -_rnd(g, *rm.shape, u=True, scale=1e-2)
+    r_dm, r_dS = ref.backward(dmz, dSz)
+    d_dm, d_dS = dev.backward(dmz.to(DEV), dSz.to(DEV))
+    patches = F.im2col(ma.double(), k, 1, p, 1)
+    exact_m, exact_S = F.conv_backward(dmz.double(), dSz.double(), patches, ref.mw.double(),
+                                       (N, C, H, W), k, 1, p, 1)[:2]
+    assert_rel(d_dm, exact_m, MEAN_RTOL, "d_ma vs float64")
+    assert_rel(d_dS, exact_S, VAR_RTOL, "d_Sa vs float64")
+    assert_rel(d_dm, r_dm, MEAN_RTOL, "d_ma vs reference restatement")
+    assert_rel(d_dS, r_dS, VAR_RTOL, "d_Sa vs reference restatement")
+    _ok()

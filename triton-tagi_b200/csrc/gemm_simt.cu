@@ -358,6 +358,32 @@ extern "C" int tagi_backward_delta_view(const float* dmz, const float* dSz, int6
     return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
 }
 
+extern "C" int tagi_conv2d_backward_delta_s1(const float* pm, const float* pS, const float* mw,
+                                             float* d_ma, float* d_Sa, int64_t N, int64_t C,
+                                             int64_t H, int64_t W, int64_t Co, int64_t k,
+                                             void* stream) {
+    const char* what = "tagi_conv2d_backward_delta_s1";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1, TAGI_E_BAD_ARG,
+                 "%s: bad sizes", what);
+    const int64_t HW = H * W, kk = k * k, M = N * HW, Kr = Co * kk;
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(C) && !bad_size(Kr) && !bad_size(C * HW) &&
+                     !bad_size(C * kk * Co),
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (M == 0 || C == 0) return TAGI_OK;
+    TAGI_REQUIRE(d_ma && d_Sa && (Kr == 0 || (pm && pS && mw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    // A: delta patches, rows (n, h, w) of the input, columns (co, tap) contiguous
+    g.x = pm; g.y = pS; g.arow = plain_rows(Kr); g.ak = 1;
+    // B[c][(co, tap)] = mw[(c*kk + kk-1-tap)][co]: the taps reversed, read in place
+    // through a map of negative stride from the last tap of each channel row
+    g.u = mw + (kk - 1) * Co; g.brow = RowMap{kk, 1, -Co}; g.bn = kk * Co;
+    // outputs straight into NCHW: row (n, hw) -> n*C*HW + hw, column c -> c*HW
+    g.o0 = d_ma; g.o1 = d_Sa; g.orow = RowMap{HW, C * HW, 1}; g.on = HW;
+    g.M = (int)M; g.N = (int)C; g.Kr = (int)Kr; g.kchunk = Kr > 0 ? (int)Kr : BK;
+    return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
+}
+
 extern "C" int tagi_fused_backward_delta(const float* dmz, const float* dSz, const float* mw,
                                          float* d_ma, float* d_Sa, int64_t M, int64_t K,
                                          int64_t N, int64_t stride_dm, int64_t stride_dn,

@@ -237,22 +237,44 @@ __device__ __forceinline__ void store_out(const GemmArgs& g, int row, int col, i
     }
 }
 
-// Shared-memory matrix descriptor: no swizzle, K-major, core matrices of 8 rows
-// x 16 bytes; the two 16-byte halves of a row's 8 tf32 values are 128 bytes
-// apart (leading byte offset) and consecutive 8-row groups 256 bytes apart
-// (stride byte offset). Bit 46 carries the descriptor version of sm_100. The
-// start address occupies the low 14 bits (address / 16), so descriptors of tiles
-// inside one stage differ by (byte offset / 16).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
-           (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46);
+// Shared-memory matrix descriptors (bit 46 carries the descriptor version of
+// sm_100). An operand tile holds `rows` rows x 8 tf32 reduction elements
+// (rows * 32 bytes) in one of two canonical layouts:
+//   K-major, no swizzle: core matrices of 8 rows x 16 bytes (4 reduction
+//     elements); the two halves of a row's 8 elements are 128 bytes apart
+//     (leading byte offset) and consecutive 8-row groups 256 bytes apart (stride
+//     byte offset): byte (row/8)*256 + (k/4)*128 + (row%8)*16 + (k%4)*4.
+//   MN-major, 128-byte swizzle on a 32-byte base (the MN-major layout that tf32
+//     operands accept; layout type 1): atoms of 4 reduction rows x 128 bytes
+//     (32 tile rows), the 32-byte chunks of reduction row kr XOR-permuted by kr;
+//     atoms along the tile rows 512 bytes apart (leading byte offset), the two
+//     4-row reduction groups rows*16 bytes apart (stride byte offset). Tiles
+//     start 512-byte aligned so that the address bits the swizzle reads are the
+//     atom's own row index.
+// The start address occupies the low 14 bits (address / 16), so descriptors of
+// tiles inside one stage differ by (byte offset / 16).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, bool mn_major, int rows) {
+    const uint64_t lbo = mn_major ? 512 : 128;
+    const uint64_t sbo = mn_major ? static_cast<uint64_t>(rows) * 16 : 256;
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | ((lbo >> 4) << 16) | ((sbo >> 4) << 32) |
+           (1ull << 46) | (mn_major ? (1ull << 61) : 0ull);
+}
+__device__ __forceinline__ uint32_t tile_off_k(int row, int k) {
+    return static_cast<uint32_t>((row >> 3) * 256 + (k >> 2) * 128 + (row & 7) * 16 + (k & 3) * 4);
+}
+// MN-major byte offset of (row, k) for a tile of `rows` rows; rows 4j..4j+3 at
+// one k are 16 contiguous bytes.
+__device__ __forceinline__ uint32_t tile_off_mn(int row, int k, int rows) {
+    const int mn = row & 31, kr = k & 3;
+    return static_cast<uint32_t>((row >> 5) * 512 + (k >> 2) * rows * 16 + kr * 128 +
+                                 (((mn >> 3) ^ kr) << 5) + (mn & 7) * 4);
 }
 
-// Instruction descriptor: fp32 accumulate, tf32 A and B, both K-major, M = 256
-// (2-SM), N = bn.
-__host__ __device__ constexpr uint32_t instr_desc(int bn) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(bn >> 3) << 17) |
-           (static_cast<uint32_t>(256 >> 4) << 24);
+// Instruction descriptor: fp32 accumulate, tf32 A and B, M = 256 (2-SM),
+// N = bn; bits 15 and 16 select MN-major A and B.
+__device__ __forceinline__ uint32_t instr_desc(int bn, bool a_mn, bool b_mn) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (a_mn ? 1u << 15 : 0u) | (b_mn ? 1u << 16 : 0u) |
+           (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
 }
 
 // Nearest tf32 value (ties away from zero): add half a tf32 ulp to the
@@ -261,25 +283,17 @@ __device__ __forceinline__ float tf32_rna(float v) {
     return __uint_as_float((__float_as_uint(v) + 0x1000u) & 0xFFFFE000u);
 }
 
-// Byte offset of (row, k-half) inside a K-major no-swizzle tile of 8-element rows.
-__device__ __forceinline__ uint32_t tile_off(int row, int half) {
-    return static_cast<uint32_t>((row >> 3) * 256 + half * 128 + (row & 7) * 16);
-}
-
-// Split a row's 8 fp32 values into tf32 hi/lo parts and store both tiles' rows.
-__device__ __forceinline__ void st_split8(char* tile_hi, char* tile_lo, int row,
-                                          const float (&v)[8]) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        float4 hi, lo;
-        hi.x = tf32_rna(v[4 * h + 0]); lo.x = tf32_rna(v[4 * h + 0] - hi.x);
-        hi.y = tf32_rna(v[4 * h + 1]); lo.y = tf32_rna(v[4 * h + 1] - hi.y);
-        hi.z = tf32_rna(v[4 * h + 2]); lo.z = tf32_rna(v[4 * h + 2] - hi.z);
-        hi.w = tf32_rna(v[4 * h + 3]); lo.w = tf32_rna(v[4 * h + 3] - hi.w);
-        const uint32_t off = tile_off(row, h);
-        *reinterpret_cast<float4*>(tile_hi + off) = hi;
-        *reinterpret_cast<float4*>(tile_lo + off) = lo;
-    }
+// Split 4 fp32 values into tf32 hi/lo parts and store them (16 bytes each) at
+// byte `off` of the hi and lo tiles.
+__device__ __forceinline__ void st_split4(char* tile_hi, char* tile_lo, uint32_t off,
+                                          const float* v) {
+    float4 hi, lo;
+    hi.x = tf32_rna(v[0]); lo.x = tf32_rna(v[0] - hi.x);
+    hi.y = tf32_rna(v[1]); lo.y = tf32_rna(v[1] - hi.y);
+    hi.z = tf32_rna(v[2]); lo.z = tf32_rna(v[2] - hi.z);
+    hi.w = tf32_rna(v[3]); lo.w = tf32_rna(v[3] - hi.w);
+    *reinterpret_cast<float4*>(tile_hi + off) = hi;
+    *reinterpret_cast<float4*>(tile_lo + off) = lo;
 }
 
 template <int VM>
@@ -336,19 +350,20 @@ constexpr int smem_bytes() {
     return op_stages<VM, BN>() * stage_bytes<VM, BN>() + kBarrierBytes;
 }
 
-// Issue the MMAs of accumulator Q of one stage (operand tiles at descriptor d0).
+// Issue the MMAs of accumulator Q of one stage (A and B tiles of the stage at
+// descriptors da, db).
 template <int VM, int BN, int Q>
-__device__ __forceinline__ void issue_acc(uint32_t d_tmem, uint64_t d0, uint32_t accumulate) {
+__device__ __forceinline__ void issue_acc(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                          uint32_t idesc, uint32_t accumulate) {
     using P = TcPlan<VM>;
-    constexpr uint32_t idesc = instr_desc(BN);
     constexpr int A_TILE = 128 * 32, B_TILE = (BN / 2) * 32;
     constexpr int B0 = TcTiles<VM>::na * A_TILE;
     bool first = true;
 #pragma unroll
     for (int i = 0; i < P::n; ++i) {
         if (field(P::acc, i) != Q) continue;
-        const uint64_t ad = d0 + static_cast<uint64_t>((field(P::a, i) * A_TILE) >> 4);
-        const uint64_t bd = d0 + static_cast<uint64_t>((B0 + field(P::b, i) * B_TILE) >> 4);
+        const uint64_t ad = da + static_cast<uint64_t>((field(P::a, i) * A_TILE) >> 4);
+        const uint64_t bd = db + static_cast<uint64_t>((B0 + field(P::b, i) * B_TILE) >> 4);
         mma_pair_tf32(d_tmem, ad, bd, idesc, first ? accumulate : 1u);
         first = false;
     }
@@ -365,59 +380,67 @@ __device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
                  : "l"(p));
 }
 
-// One producer thread's row of its operand side.
-struct ProdRow {
+// Staging of one operand side (A or B) of a stage: 2 operands x rows x 8
+// reduction elements, spread over the side's threads of a producer group.
+//   row mode (K-major tiles): a thread owns one tile row and loads its 8
+//     elements, with one 256-bit load per operand when the row's elements are
+//     contiguous and 32-byte aligned, else element by element;
+//   chunk mode (MN-major tiles, 32-row multiples): when 4 consecutive rows are
+//     contiguous and 16-byte aligned at every reduction index, a thread owns
+//     chunks of (4 rows, 1 reduction index) and loads each with one 128-bit
+//     load; 8 consecutive threads cover 32 rows at one index, 128 contiguous
+//     bytes that also fill one 128-byte row of a tile atom.
+// Element (row, k) of the side lies at base(row) + koff(k): A: arow.off(row) +
+// k*ak; B: row*bn + brow.off(k).
+struct Side {
     const float* p0;
     const float* p1;
-    int64_t base;  // A: arow.off(row); B: row * bn
-    bool valid, one, vec;
+    int row0, nrows;  // first global row of the CTA's tile part; rows of the matrix
+    int ones_row;     // row of ones (A only; -1 if none)
+    bool chunk;       // chunk mode (else row mode)
+    bool vec;         // row mode: 256-bit loads
 };
 
-// The 8 reduction elements k0..k0+7 of the thread's A row (x and, if TWO, y);
-// zeros past kend, ones (and zero y) on the bias row.
-template <bool TWO>
-__device__ __forceinline__ void load_a(const GemmArgs& g, const ProdRow& w, int k0, int kend,
-                                       float (&v)[2][8]) {
-    if (w.one) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            v[0][j] = (k0 + j < kend) ? 1.f : 0.f;
-            v[1][j] = 0.f;
-        }
-        return;
-    }
-    if (w.vec && k0 + 8 <= kend) {
-        ld8(w.p0 + w.base + k0, v[0]);
-        if (TWO) ld8(w.p1 + w.base + k0, v[1]);
-        return;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int k = k0 + j;
-        v[0][j] = 0.f;
-        v[1][j] = 0.f;
-        if (k < kend) {
-            const int64_t o = w.base + static_cast<int64_t>(k) * g.ak;
-            v[0][j] = __ldcg(w.p0 + o);
-            if (TWO) v[1][j] = __ldcg(w.p1 + o);
-        }
-    }
+template <bool IS_A>
+__device__ __forceinline__ int64_t row_base(const GemmArgs& g, int row) {
+    return IS_A ? g.arow.off(row) : static_cast<int64_t>(row) * g.bn;
+}
+template <bool IS_A>
+__device__ __forceinline__ int64_t k_off(const GemmArgs& g, int k) {
+    return IS_A ? static_cast<int64_t>(k) * g.ak : g.brow.off(k);
 }
 
-// The same for the thread's B row; the reduction index goes through brow.
-template <bool TWO>
-__device__ __forceinline__ void load_b(const GemmArgs& g, const ProdRow& w, int k0, int kend,
-                                       float (&v)[2][8]) {
-    const RowMap& m = g.brow;
-    if (w.vec && k0 + 8 <= kend) {
-        const int64_t o = w.base + m.off(k0);
-        ld8(w.p0 + o, v[0]);
-        if (TWO) ld8(w.p1 + o, v[1]);
+// Element (row, k) of both operands (x and, if TWO, y); the bias row holds ones.
+template <bool IS_A, bool TWO>
+__device__ __forceinline__ void load_elem(const GemmArgs& g, const Side& sd, int row, int k,
+                                          float& x, float& y) {
+    x = 0.f;
+    y = 0.f;
+    if (row >= sd.nrows) return;
+    if (IS_A && row == sd.ones_row) {
+        x = 1.f;
         return;
     }
-    // offsets of k0 .. k0+7 through the row map with a single division
-    uint32_t q = 0, r = static_cast<uint32_t>(k0);
-    if (m.div > 0) {
+    const int64_t o = row_base<IS_A>(g, row) + k_off<IS_A>(g, k);
+    x = __ldcg(sd.p0 + o);
+    if (TWO) y = __ldcg(sd.p1 + o);
+}
+
+// Row mode: the 8 elements k0..k0+7 of `row`; zeros past kend. The reduction
+// offsets of B go through brow with a single division per stage.
+template <bool IS_A, bool TWO>
+__device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int row,
+                                         int64_t base, int k0, int kend, float (&v)[2][8]) {
+    const bool one = IS_A && row == sd.ones_row;
+    if (sd.vec && k0 + 8 <= kend && row < sd.nrows && !one) {
+        const int64_t o = base + k_off<IS_A>(g, k0);
+        ld8(sd.p0 + o, v[0]);
+        if (TWO) ld8(sd.p1 + o, v[1]);
+        return;
+    }
+    const RowMap& m = g.brow;
+    uint32_t q = 0, r = 0;
+    if (!IS_A && m.div > 0) {
         q = static_cast<uint32_t>(k0) / static_cast<uint32_t>(m.div);
         r = static_cast<uint32_t>(k0) - q * static_cast<uint32_t>(m.div);
     }
@@ -426,19 +449,109 @@ __device__ __forceinline__ void load_b(const GemmArgs& g, const ProdRow& w, int 
         const int k = k0 + j;
         v[0][j] = 0.f;
         v[1][j] = 0.f;
-        if (k < kend) {
-            const int64_t o =
-                w.base + (m.div > 0 ? static_cast<int64_t>(q) * m.outer +
-                                          static_cast<int64_t>(r) * m.stride
-                                    : static_cast<int64_t>(k) * m.stride);
-            v[0][j] = __ldcg(w.p0 + o);
-            if (TWO) v[1][j] = __ldcg(w.p1 + o);
+        if (k < kend && row < sd.nrows) {
+            if (one) {
+                v[0][j] = 1.f;
+            } else {
+                const int64_t ko =
+                    IS_A ? static_cast<int64_t>(k) * g.ak
+                         : (m.div > 0 ? static_cast<int64_t>(q) * m.outer + static_cast<int64_t>(r) * m.stride
+                                      : static_cast<int64_t>(k) * m.stride);
+                v[0][j] = __ldcg(sd.p0 + base + ko);
+                if (TWO) v[1][j] = __ldcg(sd.p1 + base + ko);
+            }
         }
-        if (m.div > 0 && ++r == static_cast<uint32_t>(m.div)) {
+        if (!IS_A && m.div > 0 && ++r == static_cast<uint32_t>(m.div)) {
             r = 0;
             ++q;
         }
     }
+}
+
+// Chunk mode: rows r..r+3 at reduction index k into v[o][4*slot .. 4*slot+3].
+template <bool IS_A, bool TWO>
+__device__ __forceinline__ void load_chunk(const GemmArgs& g, const Side& sd, int r, int k,
+                                           int kend, int slot, float (&v)[2][8]) {
+    float* x = &v[0][4 * slot];
+    float* y = &v[1][4 * slot];
+    if (k >= kend) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = y[e] = 0.f;
+        return;
+    }
+    const bool whole = r + 3 < sd.nrows && !(IS_A && sd.ones_row >= r && sd.ones_row <= r + 3);
+    if (whole) {
+        const int64_t o = row_base<IS_A>(g, r) + k_off<IS_A>(g, k);
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(sd.p0 + o));
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        if (TWO) {
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(sd.p1 + o));
+            y[0] = b.x; y[1] = b.y; y[2] = b.z; y[3] = b.w;
+        }
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) load_elem<IS_A, TWO>(g, sd, r + e, k, x[e], y[e]);
+}
+
+// Forms the operand tiles of one side from 4 values per operand (x, y) and
+// stores them at byte `off` of each tile (tile t at st + t * tile_bytes).
+template <int VM, bool IS_A>
+__device__ __forceinline__ void store_tiles(char* st, int tile_bytes, uint32_t off, const float* x,
+                                            const float* y) {
+    float sq[4];
+    char* t0 = st;
+    st_split4(t0, t0 + tile_bytes, off, x);
+    if (IS_A) {
+        if (VM == FULL || VM == LSQ) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sq[e] = x[e] * x[e];
+            st_split4(t0 + 2 * tile_bytes, t0 + 3 * tile_bytes, off, sq);
+        }
+        if (VM == FULL) st_split4(t0 + 4 * tile_bytes, t0 + 5 * tile_bytes, off, y);
+        if (VM == RSQ) st_split4(t0 + 2 * tile_bytes, t0 + 3 * tile_bytes, off, y);
+    } else {
+        if (VM == FULL) {
+            st_split4(t0 + 2 * tile_bytes, t0 + 3 * tile_bytes, off, y);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sq[e] = x[e] * x[e] + y[e];
+            st_split4(t0 + 4 * tile_bytes, t0 + 5 * tile_bytes, off, sq);
+        } else if (VM == RSQ) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sq[e] = x[e] * x[e];
+            st_split4(t0 + 2 * tile_bytes, t0 + 3 * tile_bytes, off, sq);
+        } else {
+            st_split4(t0 + 2 * tile_bytes, t0 + 3 * tile_bytes, off, y);
+        }
+    }
+}
+
+// Chunk mode is possible when 4 consecutive rows are adjacent and 16-byte
+// aligned for every reduction index.
+template <bool IS_A>
+__device__ __forceinline__ bool chunk_ok(const GemmArgs& g, const float* p0, const float* p1) {
+    const uintptr_t al = (reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1)) & 15;
+    if (al) return false;
+    if (IS_A) {
+        const RowMap& m = g.arow;
+        return m.stride == 1 && g.ak % 4 == 0 && (m.div <= 0 || (m.div % 4 == 0 && m.outer % 4 == 0));
+    }
+    const RowMap& m = g.brow;
+    return g.bn == 1 && m.stride % 4 == 0 && (m.div <= 0 || m.outer % 4 == 0);
+}
+
+// Row mode with 256-bit loads is possible when each row's reduction elements
+// are contiguous and every 8-element run starts 32-byte aligned.
+template <bool IS_A>
+__device__ __forceinline__ bool rowvec_ok(const GemmArgs& g, const float* p0, const float* p1) {
+    const uintptr_t al = (reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1)) & 31;
+    if (al) return false;
+    if (IS_A) {
+        const RowMap& m = g.arow;
+        return g.ak == 1 && m.stride % 8 == 0 && (m.div <= 0 || m.outer % 8 == 0);
+    }
+    const RowMap& m = g.brow;
+    return m.stride == 1 && g.bn % 8 == 0 && (m.div <= 0 || (m.div % 8 == 0 && m.outer % 8 == 0));
 }
 
 // Number of chunks and last stage of chunk c when chunk boundaries are shifted
@@ -446,6 +559,98 @@ __device__ __forceinline__ void load_b(const GemmArgs& g, const ProdRow& w, int 
 __device__ __forceinline__ int num_chunks(int niter, int o) { return (niter + o + kChunk - 1) / kChunk; }
 __device__ __forceinline__ int chunk_end(int c, int o, int niter) {
     return min((c + 1) * kChunk - o, niter) - 1;
+}
+
+struct ProdCtx {
+    char* smem;
+    uint64_t* empty;
+    uint32_t full0;  // cluster address of the leader CTA's full barriers
+    Abort ab;
+    int niter, kbeg, kend;
+    int grp;  // producer group: stages of parity grp
+    int t;    // thread index within the group's threads of this side
+    int lane;
+};
+
+// One side's producer thread: stages grp, grp+2, ... with kDepth of them loaded
+// ahead into registers.
+template <int VM, int BN, bool IS_A>
+__device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, const Side& sd) {
+    using R = Roles<BN>;
+    constexpr int ROWS = IS_A ? 128 : R::NC;
+    constexpr int NTH = IS_A ? 128 : 32 * R::BW;  // this side's threads in a group
+    constexpr int GROUPS = ROWS / 4;               // chunk mode: 4-row groups
+    constexpr int SLOTS = GROUPS * 8;              // (4 rows, 1 k) chunks of a stage
+    constexpr int SPT = (SLOTS + NTH - 1) / NTH;   // chunks per thread
+    static_assert(SPT >= 1 && SPT <= 2, "chunk slots per thread");
+    constexpr int TILE = ROWS * 32;
+    constexpr int STAGE = stage_bytes<VM, BN>();
+    constexpr int OPS = op_stages<VM, BN>();
+    constexpr int OFF = IS_A ? 0 : TcTiles<VM>::na * 128 * 32;  // the side's first tile
+    constexpr bool TWO = IS_A ? VM != LSQ : VM != RSQ;
+    const bool has_row = c.t < ROWS;
+    const int row = sd.row0 + c.t;
+    const bool row_in = has_row && row < sd.nrows;
+    const int64_t base = (row_in && !(IS_A && row == sd.ones_row)) ? row_base<IS_A>(g, row) : 0;
+
+    auto load = [&](int it, float (&v)[2][8]) {
+        if (it >= c.niter) return;
+        const int k0 = c.kbeg + it * kBK;
+        if (sd.chunk) {
+#pragma unroll
+            for (int j = 0; j < SPT; ++j) {
+                const int slot = c.t + j * NTH;
+                if (slot < SLOTS)
+                    load_chunk<IS_A, TWO>(g, sd, sd.row0 + (slot % GROUPS) * 4, k0 + slot / GROUPS,
+                                          c.kend, j, v);
+            }
+        } else if (has_row) {
+            load_row<IS_A, TWO>(g, sd, row, base, k0, c.kend, v);
+        }
+    };
+    auto produce = [&](int it, const float (&v)[2][8]) -> bool {
+        const int s = it % OPS;
+        if (it >= OPS && !warp_wait(&c.empty[s], ((it / OPS) - 1) & 1, c.ab, 1)) return false;
+        // Rows outside the matrix are not written: an output row (column)
+        // depends only on its own A row (B row), and those outputs are dropped.
+        char* st = c.smem + s * STAGE + OFF;
+        bool wrote = false;
+        if (sd.chunk) {
+#pragma unroll
+            for (int j = 0; j < SPT; ++j) {
+                const int slot = c.t + j * NTH;
+                const int r = (slot % GROUPS) * 4;
+                if (slot < SLOTS && sd.row0 + r < sd.nrows) {
+                    store_tiles<VM, IS_A>(st, TILE, tile_off_mn(r, slot / GROUPS, ROWS),
+                                          &v[0][4 * j], &v[1][4 * j]);
+                    wrote = true;
+                }
+            }
+        } else if (row_in) {
+            store_tiles<VM, IS_A>(st, TILE, tile_off_k(c.t, 0), &v[0][0], &v[1][0]);
+            store_tiles<VM, IS_A>(st, TILE, tile_off_k(c.t, 4), &v[0][4], &v[1][4]);
+            wrote = true;
+        }
+        if (wrote) fence_proxy_async();
+        __syncwarp();
+        if (c.lane == 0) arrive_cluster(c.full0 + static_cast<uint32_t>(s * 8));
+        return true;
+    };
+
+    float buf[kDepth][2][8];
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d) load(c.grp + 2 * d, buf[d]);
+    bool alive = true;
+    for (int it0 = c.grp; it0 < c.niter && alive; it0 += 2 * kDepth) {
+#pragma unroll
+        for (int d = 0; d < kDepth; ++d) {
+            const int it = it0 + 2 * d;
+            if (it < c.niter && alive) {
+                alive = produce(it, buf[d]);
+                load(it + 2 * kDepth, buf[d]);
+            }
+        }
+    }
 }
 
 template <int VM, bool MEAN, int EPI, int BN>
@@ -502,99 +707,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // operand sides of this CTA (uniform over the CTA)
+    constexpr bool TWO_A = VM != LSQ, TWO_B = VM != RSQ;
+    Side sa, sb;
+    sa.p0 = g.x + batch * g.a_bs;
+    sa.p1 = TWO_A ? g.y + batch * g.a_bs : sa.p0;
+    sa.row0 = m_cta;
+    sa.nrows = g.M;
+    sa.ones_row = g.ones_row;
+    sa.vec = rowvec_ok<true>(g, sa.p0, sa.p1);
+    sa.chunk = !sa.vec && chunk_ok<true>(g, sa.p0, sa.p1);
+    sb.p0 = g.u + batch * g.b_bs;
+    sb.p1 = TWO_B ? g.v + batch * g.b_bs : sb.p0;
+    sb.row0 = n0 + static_cast<int>(rank) * R::NC;
+    sb.nrows = g.N;
+    sb.ones_row = -1;
+    sb.vec = rowvec_ok<false>(g, sb.p0, sb.p1);
+    sb.chunk = R::NC % 32 == 0 && !sb.vec && chunk_ok<false>(g, sb.p0, sb.p1);
+
     if (warp < R::MMA_W) {
         // ------------------------------------------------------------ producers
         const bool is_a = warp < R::B_W0;
-        const int grp = is_a ? (warp >> 2) : (warp - R::B_W0) / R::BW;
-        const int r = is_a ? ((warp & 3) * 32 + lane) : (((warp - R::B_W0) % R::BW) * 32 + lane);
-        ProdRow w;
-        constexpr bool TWO_A = VM != LSQ, TWO_B = VM != RSQ;
+        ProdCtx c;
+        c.smem = smem;
+        c.empty = empty;
+        c.full0 = map_to(smem_u32(full), 0);  // the leader's full barriers
+        c.ab = ab;
+        c.niter = niter;
+        c.kbeg = kbeg;
+        c.kend = kend;
+        c.lane = lane;
         if (is_a) {
-            const int idx = m_cta + r;
-            w.valid = idx < g.M;
-            w.one = idx == g.ones_row;
-            w.p0 = g.x + batch * g.a_bs;
-            w.p1 = TWO_A ? g.y + batch * g.a_bs : nullptr;
-            w.base = (w.valid && !w.one) ? g.arow.off(idx) : 0;
-            const uintptr_t al = (reinterpret_cast<uintptr_t>(w.p0) |
-                                  (TWO_A ? reinterpret_cast<uintptr_t>(w.p1) : 0)) & 31;
-            w.vec = al == 0 && g.ak == 1 && (w.base & 7) == 0;
+            c.grp = warp >> 2;
+            c.t = (warp & 3) * 32 + lane;
+            producer<VM, BN, true>(g, c, sa);
         } else {
-            const int idx = n0 + static_cast<int>(rank) * R::NC + r;
-            w.valid = r < R::NC && idx < g.N;
-            w.one = false;
-            w.p0 = g.u + batch * g.b_bs;
-            w.p1 = TWO_B ? g.v + batch * g.b_bs : nullptr;
-            w.base = w.valid ? static_cast<int64_t>(idx) * g.bn : 0;
-            const RowMap& m = g.brow;
-            const uintptr_t al = (reinterpret_cast<uintptr_t>(w.p0) |
-                                  (TWO_B ? reinterpret_cast<uintptr_t>(w.p1) : 0)) & 31;
-            w.vec = al == 0 && m.stride == 1 && (w.base & 7) == 0 &&
-                    (m.div <= 0 || (m.div % 8 == 0 && m.outer % 8 == 0));
-        }
-        const uint32_t full0 = map_to(smem_u32(full), 0);  // the leader's full barriers
-
-        auto load = [&](int it, float (&v)[2][8]) {
-            if (it >= niter || !w.valid) return;
-            const int k0 = kbeg + it * kBK;
-            if (is_a) load_a<TWO_A>(g, w, k0, kend, v);
-            else load_b<TWO_B>(g, w, k0, kend, v);
-        };
-        auto produce = [&](int it, const float (&v)[2][8]) -> bool {
-            const int s = it % OPS;
-            if (it >= OPS && !warp_wait(&empty[s], ((it / OPS) - 1) & 1, ab, 1)) return false;
-            // Rows outside the matrix are not written: an output row (column)
-            // depends only on its own A row (B row), and those outputs are dropped.
-            if (w.valid) {
-                char* st = smem + s * STAGE;
-                float sq[8];
-                if (is_a) {
-                    char* A = st;
-                    st_split8(A + 0 * A_TILE, A + 1 * A_TILE, r, v[0]);
-                    if (VM == FULL || VM == LSQ) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) sq[j] = v[0][j] * v[0][j];
-                        st_split8(A + 2 * A_TILE, A + 3 * A_TILE, r, sq);
-                    }
-                    if (VM == FULL) st_split8(A + 4 * A_TILE, A + 5 * A_TILE, r, v[1]);
-                    if (VM == RSQ) st_split8(A + 2 * A_TILE, A + 3 * A_TILE, r, v[1]);
-                } else {
-                    char* B = st + T::na * A_TILE;
-                    st_split8(B + 0 * B_TILE, B + 1 * B_TILE, r, v[0]);
-                    if (VM == FULL) {
-                        st_split8(B + 2 * B_TILE, B + 3 * B_TILE, r, v[1]);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) sq[j] = v[0][j] * v[0][j] + v[1][j];
-                        st_split8(B + 4 * B_TILE, B + 5 * B_TILE, r, sq);
-                    } else if (VM == RSQ) {
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) sq[j] = v[0][j] * v[0][j];
-                        st_split8(B + 2 * B_TILE, B + 3 * B_TILE, r, sq);
-                    } else {
-                        st_split8(B + 2 * B_TILE, B + 3 * B_TILE, r, v[1]);
-                    }
-                }
-                fence_proxy_async();
-            }
-            __syncwarp();
-            if (lane == 0) arrive_cluster(full0 + static_cast<uint32_t>(s * 8));
-            return true;
-        };
-
-        // this group's stages grp, grp+2, ...; kDepth of them loaded ahead
-        float buf[kDepth][2][8];
-#pragma unroll
-        for (int d = 0; d < kDepth; ++d) load(grp + 2 * d, buf[d]);
-        bool alive = true;
-        for (int it0 = grp; it0 < niter && alive; it0 += 2 * kDepth) {
-#pragma unroll
-            for (int d = 0; d < kDepth; ++d) {
-                const int it = it0 + 2 * d;
-                if (it < niter && alive) {
-                    alive = produce(it, buf[d]);
-                    load(it + 2 * kDepth, buf[d]);
-                }
-            }
+            c.grp = (warp - R::B_W0) / R::BW;
+            c.t = ((warp - R::B_W0) % R::BW) * 32 + lane;
+            producer<VM, BN, false>(g, c, sb);
         }
     } else if (warp == R::MMA_W) {
         // ------------------------------------------------------------ MMA issue
@@ -602,8 +752,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         // single-thread instructions). The tensor pipe queues only a few MMAs, so
         // the work between two stages' MMAs is kept to a few integer updates.
         if (leader && lane == 0) {
-            const uint64_t d_first = smem_desc(smem_u32(smem));
-            uint64_t d0 = d_first;
+            const uint64_t da_first = smem_desc(smem_u32(smem), sa.chunk, 128);
+            const uint64_t db_first = smem_desc(smem_u32(smem), sb.chunk, R::NC);
+            const uint32_t idesc = instr_desc(BN, sa.chunk, sb.chunk);
+            uint64_t da = da_first, db = db_first;
             int s = 0;
             uint32_t ph = 0;
             int pos0 = 0, pos1 = kOff1;  // (stage + shift) % kChunk of each accumulator
@@ -625,13 +777,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                 const uint32_t acc0 = first0 ? 0u : 1u, acc1 = first1 ? 0u : 1u;
                 bool ok = true;
                 if (!(MEAN && first0 && c0 >= NP)) {
-                    if (MEAN) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), d0, acc0);
+                    if (MEAN) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), da, db, idesc, acc0);
                     if (first1 && c1 >= NP) ok = drained(1, c1);
-                    if (ok) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), d0, acc1);
+                    if (ok) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), da, db, idesc, acc1);
                 } else {
-                    issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), d0, acc1);
+                    issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), da, db, idesc, acc1);
                     ok = drained(0, c0);
-                    if (ok) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), d0, acc0);
+                    if (ok) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), da, db, idesc, acc0);
                 }
                 if (!ok) break;
                 mma_commit_pair(&empty[s]);
@@ -642,9 +794,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                 if (++s == OPS) {
                     s = 0;
                     ph ^= 1u;
-                    d0 = d_first;
+                    da = da_first;
+                    db = db_first;
                 } else {
-                    d0 += static_cast<uint64_t>(STAGE >> 4);
+                    da += static_cast<uint64_t>(STAGE >> 4);
+                    db += static_cast<uint64_t>(STAGE >> 4);
                 }
             }
             mma_commit_pair(done);  // arrives once every MMA issued above completed

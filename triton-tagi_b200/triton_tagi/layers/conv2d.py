@@ -7,7 +7,10 @@ and writes the result directly in NCHW (no permute copy).
 Backward (conv2d.py:314-371): the patch-space deltas δP = δμ_z @ μ_wᵀ,
 δP_S = δS_z @ (μ_w²)ᵀ read δ in NCHW in place, are folded back to the input
 by the col2im gather, and the weight sums P_μᵀ·δμ_z, (P_μ²)ᵀ·δS_z (bias as a
-row of ones) feed the parameter mode of the layer.
+row of ones) feed the parameter mode of the layer. For stride 1 with symmetric
+padding p the product and the gather together are a convolution of the deltas
+(padded by k-1-p) with the reversed weights, computed as one contraction over
+(output channel, tap) straight into NCHW (tagi_conv2d_backward_delta_s1).
 
 ``col2im_mode``: "reference" (default) gathers exactly as the reference's
 _col2im_kernel (conv2d.py:119-130), which for stride > 1 does not test the
@@ -91,15 +94,31 @@ class Conv2D(LearnableLayer):
         dev = dmz.device
         st = stream(dmz)
         d_map = (L, Co * L, 1, L)  # NCHW delta read as an (N·L) x Co matrix
-        dpm = torch.empty(N * L, K, device=dev)
-        dpS = torch.empty(N * L, K, device=dev)
-        lib()("tagi_backward_delta_view", dmz.data_ptr(), dSz.data_ptr(), *d_map,
-              self.mw.data_ptr(), Co, dpm.data_ptr(), dpS.data_ptr(), 0, 0, K, 1, N * L, K, Co, st)
         d_ma = torch.empty(N, C, H, W, device=dev)
         d_Sa = torch.empty(N, C, H, W, device=dev)
-        lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N,
-              C, H, W, self.kH, self.stride, self.padding, self.padding_type,
-              _COL2IM_MODES[self.col2im_mode], st)
+        k, p = self.kH, self.padding
+        if self.stride == 1 and (self.padding_type == 1 or p == 0) and p <= k - 1:
+            # Stride 1: the patch-space product plus the col2im gather equal a
+            # convolution of the deltas with the reversed weights (both gather
+            # modes agree here); one contraction over (co, tap), no patch-space
+            # output.
+            Kd = Co * k * k
+            qm = torch.empty(N * H * W, Kd, device=dev)
+            qS = torch.empty(N * H * W, Kd, device=dev)
+            lib()("tagi_im2col", dmz.data_ptr(), dSz.data_ptr(), qm.data_ptr(), qS.data_ptr(), N,
+                  Co, Ho, Wo, k, 1, k - 1 - p, 1, st)
+            lib()("tagi_conv2d_backward_delta_s1", qm.data_ptr(), qS.data_ptr(), self.mw.data_ptr(),
+                  d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, st)
+            del qm, qS
+        else:
+            dpm = torch.empty(N * L, K, device=dev)
+            dpS = torch.empty(N * L, K, device=dev)
+            lib()("tagi_backward_delta_view", dmz.data_ptr(), dSz.data_ptr(), *d_map,
+                  self.mw.data_ptr(), Co, dpm.data_ptr(), dpS.data_ptr(), 0, 0, K, 1, N * L, K, Co,
+                  st)
+            lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(),
+                  N, C, H, W, k, self.stride, p, self.padding_type,
+                  _COL2IM_MODES[self.col2im_mode], st)
         weight_param_backward(self, self.patches_ma, K, (dmz, dSz), d_map, N * L, K, Co, True)
         return d_ma, d_Sa
 
