@@ -153,13 +153,28 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def _conv_pixels(a) -> int:
+    """Ho*Wo of a tagi_conv2d_forward call (H, W, k, stride, padding, padding_type
+    at argument positions 10, 11, 13, 14, 15, 16)."""
+    H, W, k, s, p, pt = a[10], a[11], a[13], a[14], a[15], a[16]
+    if pt == 2 and p > 0:
+        return ((H + p - k) // s + 1) * ((W + p - k) // s + 1)
+    return ((H + 2 * p - k) // s + 1) * ((W + 2 * p - k) // s + 1)
+
+
 class LaunchTimer:
     """Times the moment-contraction launches with CUDA events (library call hook)."""
 
     FAMILIES = {
         "tagi_moment_forward": ("moment_forward", lambda a: 6.0 * a[17] * a[18] * a[19]),
+        # M = N*Ho*Wo output pixels, N = Co, reduction C*k*k
+        "tagi_conv2d_forward": ("moment_forward", lambda a: 6.0 * a[8] * _conv_pixels(a) * a[12]
+                                * a[9] * a[13] * a[13]),
         "tagi_backward_delta_view": ("backward_delta", lambda a: 4.0 * a[14] * a[15] * a[16]),
         "tagi_fused_backward_delta": ("backward_delta", lambda a: 4.0 * a[5] * a[6] * a[7]),
+        # M = N*H*W input pixels, N = C, reduction Co*k*k
+        "tagi_conv2d_backward_delta_s1": (
+            "backward_delta", lambda a: 4.0 * a[5] * a[7] * a[8] * a[6] * a[9] * a[10] * a[10]),
         "tagi_param_grad": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
     }
 

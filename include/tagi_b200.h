@@ -88,19 +88,30 @@ int tagi_backward_delta_view(const float* dmz, const float* dSz, int64_t d_div, 
                              int64_t c_stride, int64_t c_kstride, int64_t M, int64_t K,
                              int64_t N, void* stream);
 
+/* Conv2D forward without a patch matrix: the contraction gathers the patches
+ * of (ma, Sa) (N x C x H x W, NCHW) itself and writes mz, Sz (N x Co x Ho x Wo,
+ * NCHW). mw, Sw: (C*k*k) x Co with rows (c, kh, kw); mb, Sb: Co.
+ * Replaces Conv2D.forward's patch extraction and fused moment product,
+ * triton_tagi/layers/conv2d.py:254-309 (padding_type 1: symmetric padding;
+ * 2: `padding` on the right/bottom edge only). */
+int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
+                        const float* mb, const float* Sb, float* mz, float* Sz, int64_t N,
+                        int64_t C, int64_t H, int64_t W, int64_t Co, int64_t k, int64_t stride,
+                        int64_t padding, int64_t padding_type, void* stream);
+
 /* Input deltas of a stride-1 Conv2D with symmetric padding p, written in NCHW.
  * With stride 1 the reference's patch-space product followed by its col2im
  * gather (triton_tagi/layers/conv2d.py:338-357 and _col2im_kernel,
  * conv2d.py:119-130) sums exactly the terms of a convolution of the output
  * deltas with the spatially reversed, transposed weights; this entry computes it
- * as one contraction over (co, tap). pm/pS are the patches of (delta_mz,
- * delta_Sz) taken with padding k-1-p (tagi_im2col of the N x Co x Ho x Wo
- * deltas), rows (n, h, w) of the H x W input and columns (co, kh, kw); mw is the
- * layer's (C*k*k) x Co weight matrix. d_ma = patches_m @ W', d_Sa = patches_S @
- * W'^2 with W'[(co,kh,kw)][c] = mw[c*k*k + (k-1-kh)*k + (k-1-kw)][co]. */
-int tagi_conv2d_backward_delta_s1(const float* pm, const float* pS, const float* mw, float* d_ma,
-                                  float* d_Sa, int64_t N, int64_t C, int64_t H, int64_t W,
-                                  int64_t Co, int64_t k, void* stream);
+ * as one contraction over (co, tap), gathering the patches of (dmz, dSz)
+ * (N x Co x Ho x Wo, padded by k-1-p) itself. mw is the layer's (C*k*k) x Co
+ * weight matrix: d_ma = P_m @ W', d_Sa = P_S @ W'^2 with
+ * W'[(co,kh,kw)][c] = mw[c*k*k + (k-1-kh)*k + (k-1-kw)][co]. */
+int tagi_conv2d_backward_delta_s1(const float* dmz, const float* dSz, const float* mw,
+                                  float* d_ma, float* d_Sa, int64_t N, int64_t C, int64_t H,
+                                  int64_t W, int64_t Co, int64_t k, int64_t padding,
+                                  void* stream);
 
 /* grad_mw = a^T @ dmz, grad_Sw = (a^2)^T @ dSz  (K x N outputs).
  * Replaces triton_fused_weight_grad, triton_tagi/kernels/common.py:410-451. */
@@ -230,7 +241,8 @@ int tagi_avgpool_backward(const float* dm, const float* dS, float* dm_out, float
  * Convolution helpers (NCHW; padding_type 2 = right/bottom only)
  * ------------------------------------------------------------------------- */
 
-/* patches[(n,oh,ow), (c,kh,kw)] for mean and variance in one pass.
+/* patches[(n,oh,ow), (c,kh,kw)] for mean and variance in one pass (xS and pS
+ * both null: the mean patches only).
  * Replaces _triton_im2col, triton_tagi/layers/conv2d.py:140-152, 280-297. */
 int tagi_im2col(const float* xm, const float* xS, float* pm, float* pS, int64_t N, int64_t C,
                 int64_t H, int64_t W, int64_t k, int64_t stride, int64_t padding,

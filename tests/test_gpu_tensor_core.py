@@ -206,3 +206,37 @@ def test_conv_stride1_input_deltas_as_one_contraction(C, Co, k, p):
     assert_rel(d_dm, r_dm, MEAN_RTOL, "d_ma vs reference restatement")
     assert_rel(d_dS, r_dS, VAR_RTOL, "d_Sa vs reference restatement")
     _ok()
+
+
+@pytest.mark.parametrize("C,Co,k,s,p,pt", [(64, 128, 3, 2, 1, 1), (32, 64, 5, 1, 2, 2),
+                                           (48, 80, 3, 1, 1, 1), (64, 64, 1, 2, 0, 1)])
+def test_conv_layer_gathered_patches(C, Co, k, s, p, pt):
+    """Conv2D.forward gathers its patches inside the contraction
+    (tagi_conv2d_forward); forward, input deltas and weight deltas against the
+    float64 oracle, at sizes that run on the tensor cores."""
+    import oracle.net as ON
+    from triton_tagi import Conv2D
+
+    g = torch.Generator().manual_seed(C * k + Co + s)
+    N, H, W = 6, 15, 12
+    torch.manual_seed(4)
+    ref = ON.Conv2D(C, Co, k, s, p, pt)
+    dev = Conv2D(C, Co, k, s, p, pt, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, getattr(ref, n).to(DEV))
+    ma, Sa = _rnd(g, N, C, H, W), _rnd(g, N, C, H, W, u=True, scale=0.1)
+    d = lambda t: t.double()  # noqa: E731
+    ex_m, ex_S, patches = F.conv_forward(d(ma), d(Sa), d(ref.mw), d(ref.Sw), d(ref.mb), d(ref.Sb),
+                                         k, s, p, pt)
+    ref.forward(ma, Sa)
+    mz, Sz = dev.forward(ma.to(DEV), Sa.to(DEV))
+    assert_rel(mz, ex_m, MEAN_RTOL, "mz")
+    assert_rel(Sz, ex_S, VAR_RTOL, "Sz")
+    dmz, dSz = _rnd(g, *ex_m.shape, scale=0.1), -_rnd(g, *ex_m.shape, u=True, scale=1e-2)
+    r_dm, r_dS = ref.backward(dmz, dSz)
+    d_dm, d_dS = dev.backward(dmz.to(DEV), dSz.to(DEV))
+    assert_rel(d_dm, r_dm, MEAN_RTOL, "d_ma")
+    assert_rel(d_dS, r_dS, VAR_RTOL, "d_Sa")
+    assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "delta_mw")
+    assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "delta_Sw")
+    _ok()

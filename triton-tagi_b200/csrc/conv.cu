@@ -47,10 +47,10 @@ __global__ void im2col_kernel(const float* xm, const float* xS, float* pm, float
         if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
             const int64_t src = ((static_cast<int64_t>(n) * g.C + c) * g.H + ih) * g.W + iw;
             vm = xm[src];
-            vS = xS[src];
+            if (pS) vS = xS[src];
         }
         pm[i] = vm;
-        pS[i] = vS;
+        if (pS) pS[i] = vS;
     }
 }
 
@@ -108,7 +108,8 @@ extern "C" int tagi_im2col(const float* xm, const float* xS, float* pm, float* p
                  "%s: bad geometry", what);
     const int64_t total = N * g.Ho * g.Wo * C * k * k;
     if (total == 0) return TAGI_OK;
-    TAGI_REQUIRE(xm && xS && pm && pS, TAGI_E_BAD_ARG, "%s: null pointer", what);
+    TAGI_REQUIRE(xm && pm && (xS == nullptr) == (pS == nullptr), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
     im2col_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);
     return check_launch(what);
 }

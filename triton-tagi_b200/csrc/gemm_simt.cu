@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(NT) moment_gemm_kernel(const GemmArgs g) {
     int a_mm[4], a_kk[4], b_nn[4], b_kk[4];
     int64_t a_off[4], b_col[4];
     bool a_ok[4], a_one[4], b_ok[4];
+    GatherRow a_gr[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int e = tid + i * NT;
@@ -62,7 +63,8 @@ __global__ void __launch_bounds__(NT) moment_gemm_kernel(const GemmArgs g) {
         const int row = m0 + a_mm[i];
         a_ok[i] = row < g.M;
         a_one[i] = (row == g.ones_row);
-        a_off[i] = (a_ok[i] && !a_one[i]) ? g.arow.off(row) : 0;
+        a_off[i] = (a_ok[i] && !a_one[i] && !g.ga.on) ? g.arow.off(row) : 0;
+        if (g.ga.on) a_gr[i] = gather_row(g.ga, a_ok[i] ? row : 0);
         if (b_ncontig) { b_nn[i] = e % BN; b_kk[i] = e / BN; }
         else           { b_kk[i] = e % BK; b_nn[i] = e / BK; }
         const int col = n0 + b_nn[i];
@@ -75,8 +77,14 @@ __global__ void __launch_bounds__(NT) moment_gemm_kernel(const GemmArgs g) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int k = k0 + a_kk[i];
-            const bool ok = a_ok[i] && k < kend;
-            const int64_t o = a_off[i] + static_cast<int64_t>(k) * g.ak;
+            bool ok = a_ok[i] && k < kend;
+            int64_t o;
+            if (g.ga.on) {
+                o = ok ? gather_off(g.ga, a_gr[i], k) : -1;
+                ok = o >= 0;
+            } else {
+                o = a_off[i] + static_cast<int64_t>(k) * g.ak;
+            }
             rx[i] = ok ? (a_one[i] ? 1.f : __ldg(x + o)) : 0.f;
             if (Nd::y) ry[i] = (ok && !a_one[i]) ? __ldg(y + o) : 0.f;
         }
@@ -358,23 +366,77 @@ extern "C" int tagi_backward_delta_view(const float* dmz, const float* dSz, int6
     return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
 }
 
-extern "C" int tagi_conv2d_backward_delta_s1(const float* pm, const float* pS, const float* mw,
-                                             float* d_ma, float* d_Sa, int64_t N, int64_t C,
-                                             int64_t H, int64_t W, int64_t Co, int64_t k,
-                                             void* stream) {
-    const char* what = "tagi_conv2d_backward_delta_s1";
-    TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1, TAGI_E_BAD_ARG,
-                 "%s: bad sizes", what);
-    const int64_t HW = H * W, kk = k * k, M = N * HW, Kr = Co * kk;
-    TAGI_REQUIRE(!bad_size(M) && !bad_size(C) && !bad_size(Kr) && !bad_size(C * HW) &&
-                     !bad_size(C * kk * Co),
+// Output size and top/left padding of a Conv2D (padding type 1: symmetric;
+// 2: p on the right/bottom only), as triton_tagi/layers/conv2d.py computes them.
+static void conv_geometry(int64_t H, int64_t W, int64_t k, int64_t s, int64_t p, int64_t pt,
+                   int64_t* Ho, int64_t* Wo, int* top) {
+    if (pt == 2 && p > 0) {
+        *Ho = (H + p - k) / s + 1;
+        *Wo = (W + p - k) / s + 1;
+        *top = 0;
+    } else {
+        *Ho = (H + 2 * p - k) / s + 1;
+        *Wo = (W + 2 * p - k) / s + 1;
+        *top = static_cast<int>(p);
+    }
+}
+
+extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw,
+                                   const float* Sw, const float* mb, const float* Sb, float* mz,
+                                   float* Sz, int64_t N, int64_t C, int64_t H, int64_t W,
+                                   int64_t Co, int64_t k, int64_t stride, int64_t padding,
+                                   int64_t padding_type, void* stream) {
+    const char* what = "tagi_conv2d_forward";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && stride >= 1 &&
+                     padding >= 0 && (padding_type == 1 || padding_type == 2),
                  TAGI_E_BAD_ARG, "%s: bad sizes", what);
-    if (M == 0 || C == 0) return TAGI_OK;
-    TAGI_REQUIRE(d_ma && d_Sa && (Kr == 0 || (pm && pS && mw)), TAGI_E_BAD_ARG,
+    int64_t Ho, Wo;
+    int top;
+    conv_geometry(H, W, k, stride, padding, padding_type, &Ho, &Wo, &top);
+    TAGI_REQUIRE(Ho >= 1 && Wo >= 1, TAGI_E_BAD_ARG, "%s: kernel larger than the padded input",
+                 what);
+    const int64_t L = Ho * Wo, M = N * L, Kr = C * k * k;
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(Co) && !bad_size(Kr) && !bad_size(N * C * H * W) &&
+                     !bad_size(Co * L),
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (M == 0 || Co == 0) return TAGI_OK;
+    TAGI_REQUIRE(mz && Sz && mb && Sb && (Kr == 0 || (ma && Sa && mw && Sw)), TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
     GemmArgs g = blank();
-    // A: delta patches, rows (n, h, w) of the input, columns (co, tap) contiguous
-    g.x = pm; g.y = pS; g.arow = plain_rows(Kr); g.ak = 1;
+    g.x = ma; g.y = Sa;
+    g.ga = Gather{1, (int)C, (int)H, (int)W, (int)Wo, (int)L, (int)k, (int)stride, top, top};
+    g.u = mw; g.v = Sw; g.brow = plain_rows(Co); g.bn = 1;
+    g.bias0 = mb; g.bias1 = Sb;
+    // outputs straight into NCHW: row (n, l) -> n*Co*L + l, column c -> c*L
+    g.o0 = mz; g.o1 = Sz; g.orow = RowMap{L, Co * L, 1}; g.on = L;
+    g.M = (int)M; g.N = (int)Co; g.Kr = (int)Kr; g.kchunk = Kr > 0 ? (int)Kr : BK;
+    return launch<FULL, true, EPI_STORE>(g, 1, as_stream(stream), what);
+}
+
+extern "C" int tagi_conv2d_backward_delta_s1(const float* dmz, const float* dSz, const float* mw,
+                                             float* d_ma, float* d_Sa, int64_t N, int64_t C,
+                                             int64_t H, int64_t W, int64_t Co, int64_t k,
+                                             int64_t padding, void* stream) {
+    const char* what = "tagi_conv2d_backward_delta_s1";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && padding >= 0 &&
+                     padding <= k - 1,
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    const int64_t Ho = H + 2 * padding - k + 1, Wo = W + 2 * padding - k + 1;
+    TAGI_REQUIRE(Ho >= 1 && Wo >= 1, TAGI_E_BAD_ARG, "%s: kernel larger than the padded input",
+                 what);
+    const int64_t HW = H * W, kk = k * k, M = N * HW, Kr = Co * kk;
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(C) && !bad_size(Kr) && !bad_size(C * HW) &&
+                     !bad_size(N * Co * Ho * Wo) && !bad_size(C * kk * Co),
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (M == 0 || C == 0) return TAGI_OK;
+    TAGI_REQUIRE(d_ma && d_Sa && (Kr == 0 || (dmz && dSz && mw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    // A: patches of the deltas (Co x Ho x Wo per image) with padding k-1-p, gathered
+    // for rows (n, h, w) of the input, reduction (co, kh, kw)
+    const int q = static_cast<int>(k - 1 - padding);
+    g.x = dmz; g.y = dSz;
+    g.ga = Gather{1, (int)Co, (int)Ho, (int)Wo, (int)W, (int)HW, (int)k, 1, q, q};
     // B[c][(co, tap)] = mw[(c*kk + kk-1-tap)][co]: the taps reversed, read in place
     // through a map of negative stride from the last tap of each channel row
     g.u = mw + (kk - 1) * Co; g.brow = RowMap{kk, 1, -Co}; g.bn = kk * Co;

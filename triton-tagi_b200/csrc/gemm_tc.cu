@@ -399,6 +399,7 @@ struct Side {
     int ones_row;     // row of ones (A only; -1 if none)
     bool chunk;       // chunk mode (else row mode)
     bool vec;         // row mode: 256-bit loads
+    bool gather;      // A: implicit patches of an NCHW image (row mode)
 };
 
 template <bool IS_A>
@@ -430,7 +431,35 @@ __device__ __forceinline__ void load_elem(const GemmArgs& g, const Side& sd, int
 // offsets of B go through brow with a single division per stage.
 template <bool IS_A, bool TWO>
 __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int row,
-                                         int64_t base, int k0, int kend, float (&v)[2][8]) {
+                                         int64_t base, const GatherRow& gr, int k0, int kend,
+                                         float (&v)[2][8]) {
+    if (IS_A && sd.gather) {
+        // implicit patches: walk (c, kh, kw) from k0 with two divisions per stage
+        const Gather& ga = g.ga;
+        const int kk2 = ga.k * ga.k;
+        int c = k0 / kk2;
+        const int t = k0 - c * kk2;
+        int kh = t / ga.k, kw = t - kh * ga.k;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            v[0][j] = 0.f;
+            v[1][j] = 0.f;
+            const int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
+            if (k0 + j < kend && row < sd.nrows && ih >= 0 && ih < ga.H && iw >= 0 && iw < ga.W) {
+                const int64_t o = gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
+                v[0][j] = __ldcg(sd.p0 + o);
+                if (TWO) v[1][j] = __ldcg(sd.p1 + o);
+            }
+            if (++kw == ga.k) {
+                kw = 0;
+                if (++kh == ga.k) {
+                    kh = 0;
+                    ++c;
+                }
+            }
+        }
+        return;
+    }
     const bool one = IS_A && row == sd.ones_row;
     if (sd.vec && k0 + 8 <= kend && row < sd.nrows && !one) {
         const int64_t o = base + k_off<IS_A>(g, k0);
@@ -591,7 +620,10 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
     const bool has_row = c.t < ROWS;
     const int row = sd.row0 + c.t;
     const bool row_in = has_row && row < sd.nrows;
-    const int64_t base = (row_in && !(IS_A && row == sd.ones_row)) ? row_base<IS_A>(g, row) : 0;
+    const int64_t base =
+        (row_in && !(IS_A && (row == sd.ones_row || sd.gather))) ? row_base<IS_A>(g, row) : 0;
+    GatherRow gr{0, 0, 0};
+    if (IS_A && sd.gather) gr = gather_row(g.ga, row_in ? row : 0);
 
     auto load = [&](int it, float (&v)[2][8]) {
         if (it >= c.niter) return;
@@ -605,7 +637,7 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
                                           c.kend, j, v);
             }
         } else if (has_row) {
-            load_row<IS_A, TWO>(g, sd, row, base, k0, c.kend, v);
+            load_row<IS_A, TWO>(g, sd, row, base, gr, k0, c.kend, v);
         }
     };
     auto produce = [&](int it, const float (&v)[2][8]) -> bool {
@@ -715,13 +747,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     sa.row0 = m_cta;
     sa.nrows = g.M;
     sa.ones_row = g.ones_row;
-    sa.vec = rowvec_ok<true>(g, sa.p0, sa.p1);
-    sa.chunk = !sa.vec && chunk_ok<true>(g, sa.p0, sa.p1);
+    sa.gather = g.ga.on != 0;
+    sa.vec = !sa.gather && rowvec_ok<true>(g, sa.p0, sa.p1);
+    sa.chunk = !sa.gather && !sa.vec && chunk_ok<true>(g, sa.p0, sa.p1);
     sb.p0 = g.u + batch * g.b_bs;
     sb.p1 = TWO_B ? g.v + batch * g.b_bs : sb.p0;
     sb.row0 = n0 + static_cast<int>(rank) * R::NC;
     sb.nrows = g.N;
     sb.ones_row = -1;
+    sb.gather = false;
     sb.vec = rowvec_ok<false>(g, sb.p0, sb.p1);
     sb.chunk = R::NC % 32 == 0 && !sb.vec && chunk_ok<false>(g, sb.p0, sb.p1);
 

@@ -16,12 +16,46 @@ struct ParamEpi {
     float cap;
 };
 
+// Implicit patches on the A side (convolutions without a patch matrix):
+// A[m][kk] = x[n][c][oh*s - pt + kh][ow*s - pl + kw], zero outside the input,
+// for rows m = (n, oh, ow) over N x Ho x Wo and reduction kk = (c, kh, kw)
+// (the column order of triton_tagi/layers/conv2d.py:40-77).
+struct Gather {
+    int on;              // 1: A is gathered; arow and ak are unused
+    int C, H, W;         // input channels and size (NCHW)
+    int Wo, L;           // output width, output pixels per image
+    int k, s, pt, pl;    // kernel size, stride, top and left padding
+};
+
+// One output pixel's image base and input origin.
+struct GatherRow {
+    int64_t base;
+    int ih0, iw0;
+};
+
+__device__ __forceinline__ GatherRow gather_row(const Gather& ga, int m) {
+    const int n = m / ga.L, r = m - n * ga.L, oh = r / ga.Wo, ow = r - oh * ga.Wo;
+    return GatherRow{static_cast<int64_t>(n) * ga.C * ga.H * ga.W, oh * ga.s - ga.pt,
+                     ow * ga.s - ga.pl};
+}
+
+// Offset of element kk of a gathered row, or -1 where the patch lies outside
+// the input.
+__device__ __forceinline__ int64_t gather_off(const Gather& ga, const GatherRow& gr, int kk) {
+    const int kk2 = ga.k * ga.k;
+    const int c = kk / kk2, t = kk - c * kk2, kh = t / ga.k, kw = t - kh * ga.k;
+    const int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
+    if (ih < 0 || ih >= ga.H || iw < 0 || iw >= ga.W) return -1;
+    return gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
+}
+
 struct GemmArgs {
     const float *x, *y;
     RowMap arow;
     int64_t ak;
     int ones_row;
     int64_t a_bs;
+    Gather ga;
     const float *u, *v;
     RowMap brow;
     int64_t bn;

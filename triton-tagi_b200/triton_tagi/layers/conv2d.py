@@ -1,16 +1,18 @@
 """Bayesian Conv2D via patches (drop-in for triton_tagi/layers/conv2d.py).
 
-Forward (conv2d.py:254-309): one kernel extracts mean and variance patches
-(N·L, C·k·k), then the fused moment kernel computes
+Forward (conv2d.py:254-309): the fused moment contraction
     μ_z = P_μ @ μ_w + μ_b,  S_z = P_μ² @ S_w + P_S @ (μ_w² + S_w) + S_b
-and writes the result directly in NCHW (no permute copy).
+over the patches P (N·L, C·k·k) gathers them from the NCHW input itself (no
+patch matrix in memory) and writes the result directly in NCHW.
 Backward (conv2d.py:314-371): the patch-space deltas δP = δμ_z @ μ_wᵀ,
 δP_S = δS_z @ (μ_w²)ᵀ read δ in NCHW in place, are folded back to the input
 by the col2im gather, and the weight sums P_μᵀ·δμ_z, (P_μ²)ᵀ·δS_z (bias as a
-row of ones) feed the parameter mode of the layer. For stride 1 with symmetric
-padding p the product and the gather together are a convolution of the deltas
-(padded by k-1-p) with the reversed weights, computed as one contraction over
-(output channel, tap) straight into NCHW (tagi_conv2d_backward_delta_s1).
+row of ones) feed the parameter mode of the layer; the mean patches are made
+for them from the input kept by forward. For stride 1 with symmetric padding
+p the product and the gather together are a convolution of the deltas (padded
+by k-1-p) with the reversed weights, computed as one contraction over (output
+channel, tap) that gathers the delta patches itself and writes NCHW
+(tagi_conv2d_backward_delta_s1).
 
 ``col2im_mode``: "reference" (default) gathers exactly as the reference's
 _col2im_kernel (conv2d.py:119-130), which for stride > 1 does not test the
@@ -48,7 +50,7 @@ class Conv2D(LearnableLayer):
             kernel_size, C_in, C_out, init_method=init_method, gain_w=gain_w, gain_b=gain_b,
             device=self.device)
         self.has_bias = True
-        self.patches_ma = None
+        self.input_ma = None
         self.input_shape = None
         self.spatial = None
         self.delta_mw = self.delta_Sw = self.delta_mb = self.delta_Sb = None
@@ -69,20 +71,15 @@ class Conv2D(LearnableLayer):
         self.input_shape = (N, C, H, W)
         Ho, Wo = self._out_hw(H, W)
         self.spatial = (Ho, Wo)
-        L, K, Co = Ho * Wo, C * self.kH * self.kW, self.C_out
+        Co = self.C_out
         dev = ma.device
-        pm = torch.empty(N * L, K, device=dev)
-        pS = torch.empty(N * L, K, device=dev)
-        st = stream(ma)
-        lib()("tagi_im2col", ma.data_ptr(), Sa.data_ptr(), pm.data_ptr(), pS.data_ptr(), N, C, H,
-              W, self.kH, self.stride, self.padding, self.padding_type, st)
-        self.patches_ma = pm
+        self.input_ma = ma  # the weight sums of backward take their patches from it
         mz = torch.empty(N, Co, Ho, Wo, device=dev)
         Sz = torch.empty(N, Co, Ho, Wo, device=dev)
-        # output row r = (n, l) -> n*Co*L + l, column c -> c*L  (NCHW)
-        lib()("tagi_moment_forward", pm.data_ptr(), pS.data_ptr(), 0, 0, K, 1, self.mw.data_ptr(),
-              self.Sw.data_ptr(), Co, self.mb.data_ptr(), self.Sb.data_ptr(), mz.data_ptr(),
-              Sz.data_ptr(), L, Co * L, 1, L, N * L, Co, K, st)
+        lib()("tagi_conv2d_forward", ma.data_ptr(), Sa.data_ptr(), self.mw.data_ptr(),
+              self.Sw.data_ptr(), self.mb.data_ptr(), self.Sb.data_ptr(), mz.data_ptr(),
+              Sz.data_ptr(), N, C, H, W, Co, self.kH, self.stride, self.padding,
+              self.padding_type, stream(ma))
         return mz, Sz
 
     def backward(self, delta_mz: Tensor, delta_Sz: Tensor) -> tuple[Tensor, Tensor]:
@@ -100,16 +97,10 @@ class Conv2D(LearnableLayer):
         if self.stride == 1 and (self.padding_type == 1 or p == 0) and p <= k - 1:
             # Stride 1: the patch-space product plus the col2im gather equal a
             # convolution of the deltas with the reversed weights (both gather
-            # modes agree here); one contraction over (co, tap), no patch-space
+            # modes agree here): one contraction over (co, tap), no patch-space
             # output.
-            Kd = Co * k * k
-            qm = torch.empty(N * H * W, Kd, device=dev)
-            qS = torch.empty(N * H * W, Kd, device=dev)
-            lib()("tagi_im2col", dmz.data_ptr(), dSz.data_ptr(), qm.data_ptr(), qS.data_ptr(), N,
-                  Co, Ho, Wo, k, 1, k - 1 - p, 1, st)
-            lib()("tagi_conv2d_backward_delta_s1", qm.data_ptr(), qS.data_ptr(), self.mw.data_ptr(),
-                  d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, st)
-            del qm, qS
+            lib()("tagi_conv2d_backward_delta_s1", dmz.data_ptr(), dSz.data_ptr(),
+                  self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, p, st)
         else:
             dpm = torch.empty(N * L, K, device=dev)
             dpS = torch.empty(N * L, K, device=dev)
@@ -119,7 +110,10 @@ class Conv2D(LearnableLayer):
             lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(),
                   N, C, H, W, k, self.stride, p, self.padding_type,
                   _COL2IM_MODES[self.col2im_mode], st)
-        weight_param_backward(self, self.patches_ma, K, (dmz, dSz), d_map, N * L, K, Co, True)
+        pm = torch.empty(N * L, K, device=dev)
+        lib()("tagi_im2col", self.input_ma.data_ptr(), None, pm.data_ptr(), None, N, C, H, W, k,
+              self.stride, p, self.padding_type, st)
+        weight_param_backward(self, pm, K, (dmz, dSz), d_map, N * L, K, Co, True)
         return d_ma, d_Sa
 
     def update(self, cap_factor: float) -> None:
