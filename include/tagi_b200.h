@@ -104,13 +104,14 @@ int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const
  * gather (triton_tagi/layers/conv2d.py:338-357 and _col2im_kernel,
  * conv2d.py:119-130) sums exactly the terms of a convolution of the output
  * deltas with the spatially reversed, transposed weights; this entry computes it
- * as one contraction over (co, tap), gathering the patches of (dmz, dSz)
+ * as one contraction over (tap, co), gathering the patches of (dmz, dSz)
  * (N x Co x Ho x Wo, padded by k-1-p) itself. mw is the layer's (C*k*k) x Co
  * weight matrix: d_ma = P_m @ W', d_Sa = P_S @ W'^2 with
- * W'[(co,kh,kw)][c] = mw[c*k*k + (k-1-kh)*k + (k-1-kw)][co]. */
+ * W'[(kh,kw,co)][c] = mw[c*k*k + (k-1-kh)*k + (k-1-kw)][co]; W' is first written
+ * to w_rev (caller scratch of C*k*k*Co floats, one row per input channel). */
 int tagi_conv2d_backward_delta_s1(const float* dmz, const float* dSz, const float* mw,
-                                  float* d_ma, float* d_Sa, int64_t N, int64_t C, int64_t H,
-                                  int64_t W, int64_t Co, int64_t k, int64_t padding,
+                                  float* w_rev, float* d_ma, float* d_Sa, int64_t N, int64_t C,
+                                  int64_t H, int64_t W, int64_t Co, int64_t k, int64_t padding,
                                   void* stream);
 
 /* grad_mw = a^T @ dmz, grad_Sw = (a^2)^T @ dSz  (K x N outputs).

@@ -23,7 +23,7 @@
 //   warps 0-7     A producers in two groups of four; group g serves the stages
 //                 of parity g and each thread one tile row. A thread loads its
 //                 row's 8 reduction elements per stage from global memory
-//                 straight into registers (kDepth of its stages in flight),
+//                 straight into registers (its next stage in flight),
 //                 splits them and stores the operand tiles in the canonical
 //                 no-swizzle K-major layout (8-row x 16-byte core matrices).
 //   next 2*BW     B producers: the same for this CTA's BN/2 rows of B.
@@ -54,7 +54,7 @@ namespace {
 
 constexpr int kBK = 8;              // tf32 elements per MMA along the reduction
 constexpr int kChunk = 16;          // stages accumulated in tensor memory before a fold
-constexpr int kDepth = 2;           // stages in flight per producer thread
+constexpr int kDepth = 1;           // stages loaded ahead per producer thread (2 per group pair)
 constexpr int kMaxStages = 8;       // operand stages in shared memory
 constexpr int kStageBudget = 224 * 1024;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -380,6 +380,18 @@ __device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
                  : "l"(p));
 }
 
+// *p if `ok`, else 0, as one predicated load into a zeroed register: the
+// value is not consumed (no select waits on it) until the stage that uses it.
+__device__ __forceinline__ float ldg_if(const float* p, bool ok) {
+    float v;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\tmov.b32 %0, 0;\n\t"
+        "@q ld.global.cg.f32 %0, [%1];\n\t}"
+        : "=f"(v)
+        : "l"(p), "r"(static_cast<int>(ok)));
+    return v;
+}
+
 // Staging of one operand side (A or B) of a stage: 2 operands x rows x 8
 // reduction elements, spread over the side's threads of a producer group.
 //   row mode (K-major tiles): a thread owns one tile row and loads its 8
@@ -434,28 +446,31 @@ __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int 
                                          int64_t base, const GatherRow& gr, int k0, int kend,
                                          float (&v)[2][8]) {
     if (IS_A && sd.gather) {
-        // implicit patches: walk (c, kh, kw) from k0 with two divisions per stage
+        // implicit patches, reduction order (tap, c): one division per stage, then
+        // addresses a channel plane apart and a bounds test per tap
         const Gather& ga = g.ga;
-        const int kk2 = ga.k * ga.k;
-        int c = k0 / kk2;
-        const int t = k0 - c * kk2;
-        int kh = t / ga.k, kw = t - kh * ga.k;
+        const int64_t plane = static_cast<int64_t>(ga.H) * ga.W;
+        int tap = k0 / ga.C, c = k0 - tap * ga.C;
+        int kh = tap / ga.k, kw = tap - kh * ga.k;
+        int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
+        bool inside = row < sd.nrows && ih >= 0 && ih < ga.H && iw >= 0 && iw < ga.W;
+        int64_t o = gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            v[0][j] = 0.f;
-            v[1][j] = 0.f;
-            const int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
-            if (k0 + j < kend && row < sd.nrows && ih >= 0 && ih < ga.H && iw >= 0 && iw < ga.W) {
-                const int64_t o = gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
-                v[0][j] = __ldcg(sd.p0 + o);
-                if (TWO) v[1][j] = __ldcg(sd.p1 + o);
-            }
-            if (++kw == ga.k) {
-                kw = 0;
-                if (++kh == ga.k) {
-                    kh = 0;
-                    ++c;
+            const bool ok = inside && k0 + j < kend;
+            v[0][j] = ldg_if(sd.p0 + o, ok);
+            v[1][j] = TWO ? ldg_if(sd.p1 + o, ok) : 0.f;
+            o += plane;
+            if (++c == ga.C) {
+                c = 0;
+                if (++kw == ga.k) {
+                    kw = 0;
+                    ++kh;
                 }
+                ih = gr.ih0 + kh;
+                iw = gr.iw0 + kw;
+                inside = row < sd.nrows && ih >= 0 && ih < ga.H && iw >= 0 && iw < ga.W;
+                o = gr.base + static_cast<int64_t>(ih) * ga.W + iw;
             }
         }
         return;
@@ -476,20 +491,13 @@ __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int 
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int k = k0 + j;
-        v[0][j] = 0.f;
-        v[1][j] = 0.f;
-        if (k < kend && row < sd.nrows) {
-            if (one) {
-                v[0][j] = 1.f;
-            } else {
-                const int64_t ko =
-                    IS_A ? static_cast<int64_t>(k) * g.ak
-                         : (m.div > 0 ? static_cast<int64_t>(q) * m.outer + static_cast<int64_t>(r) * m.stride
-                                      : static_cast<int64_t>(k) * m.stride);
-                v[0][j] = __ldcg(sd.p0 + base + ko);
-                if (TWO) v[1][j] = __ldcg(sd.p1 + base + ko);
-            }
-        }
+        const bool in = k < kend && row < sd.nrows;
+        const int64_t ko =
+            IS_A ? static_cast<int64_t>(k) * g.ak
+                 : (m.div > 0 ? static_cast<int64_t>(q) * m.outer + static_cast<int64_t>(r) * m.stride
+                              : static_cast<int64_t>(k) * m.stride);
+        v[0][j] = one ? (in ? 1.f : 0.f) : ldg_if(sd.p0 + base + ko, in);
+        v[1][j] = (TWO && !one) ? ldg_if(sd.p1 + base + ko, in) : 0.f;
         if (!IS_A && m.div > 0 && ++r == static_cast<uint32_t>(m.div)) {
             r = 0;
             ++q;

@@ -17,9 +17,11 @@ struct ParamEpi {
 };
 
 // Implicit patches on the A side (convolutions without a patch matrix):
-// A[m][kk] = x[n][c][oh*s - pt + kh][ow*s - pl + kw], zero outside the input,
-// for rows m = (n, oh, ow) over N x Ho x Wo and reduction kk = (c, kh, kw)
-// (the column order of triton_tagi/layers/conv2d.py:40-77).
+// A[m][r] = x[n][c][oh*s - pt + kh][ow*s - pl + kw], zero outside the input,
+// for rows m = (n, oh, ow) over N x Ho x Wo and reduction index r = tap*C + c
+// with tap = kh*k + kw. Taps outermost: 8 consecutive reduction elements then
+// share one tap (for C a multiple of 8), i.e. one bounds test and 8 addresses
+// a channel plane apart. The B operand is read in the same (tap, c) order.
 struct Gather {
     int on;              // 1: A is gathered; arow and ak are unused
     int C, H, W;         // input channels and size (NCHW)
@@ -39,11 +41,10 @@ __device__ __forceinline__ GatherRow gather_row(const Gather& ga, int m) {
                      ow * ga.s - ga.pl};
 }
 
-// Offset of element kk of a gathered row, or -1 where the patch lies outside
-// the input.
-__device__ __forceinline__ int64_t gather_off(const Gather& ga, const GatherRow& gr, int kk) {
-    const int kk2 = ga.k * ga.k;
-    const int c = kk / kk2, t = kk - c * kk2, kh = t / ga.k, kw = t - kh * ga.k;
+// Offset of reduction element r of a gathered row, or -1 where the patch lies
+// outside the input.
+__device__ __forceinline__ int64_t gather_off(const Gather& ga, const GatherRow& gr, int r) {
+    const int tap = r / ga.C, c = r - tap * ga.C, kh = tap / ga.k, kw = tap - kh * ga.k;
     const int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
     if (ih < 0 || ih >= ga.H || iw < 0 || iw >= ga.W) return -1;
     return gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;

@@ -99,8 +99,10 @@ class Conv2D(LearnableLayer):
             # convolution of the deltas with the reversed weights (both gather
             # modes agree here): one contraction over (co, tap), no patch-space
             # output.
+            w_rev = torch.empty(C, Co * k * k, device=dev)
             lib()("tagi_conv2d_backward_delta_s1", dmz.data_ptr(), dSz.data_ptr(),
-                  self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, p, st)
+                  self.mw.data_ptr(), w_rev.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H,
+                  W, Co, k, p, st)
         else:
             dpm = torch.empty(N * L, K, device=dev)
             dpS = torch.empty(N * L, K, device=dev)
