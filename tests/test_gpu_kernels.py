@@ -229,6 +229,30 @@ def test_im2col_col2im_golden(golden, tag, k, s, p):
             np.testing.assert_allclose(out.cpu().numpy(), z[f"col2im_{tag}"], rtol=1e-6, atol=1e-5)
 
 
+@pytest.mark.parametrize("C,k,s,p,pt", [(4, 3, 1, 1, 1), (8, 3, 2, 1, 1), (4, 2, 2, 0, 1),
+                                       (12, 5, 1, 2, 2), (16, 1, 1, 0, 1)])
+def test_im2col_vectorised_rows(C, k, s, p, pt):
+    """Patch rows with C*k*k a multiple of 4 (16-byte stores), mean and variance
+    together and the mean alone, bit-exact against the oracle's unfold."""
+    from triton_tagi._lib import lib, stream
+
+    gen = torch.Generator().manual_seed(C * 10 + k)
+    N, H, W = 3, 11, 10
+    xm, xS = rnd(gen, N, C, H, W), rnd(gen, N, C, H, W, kind="u")
+    Ho, Wo = F.conv_out_hw(H, W, k, s, p, pt)
+    dm, dS = g(xm), g(xS)  # device copies held for the calls
+    pm = torch.empty(N * Ho * Wo, C * k * k, device=DEV)
+    pS = torch.empty_like(pm)
+    lib()("tagi_im2col", dm.data_ptr(), dS.data_ptr(), pm.data_ptr(), pS.data_ptr(), N, C, H, W,
+          k, s, p, pt, stream(pm))
+    np.testing.assert_array_equal(pm.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
+    np.testing.assert_array_equal(pS.cpu().numpy(), F.im2col(xS, k, s, p, pt).numpy())
+    only = torch.full_like(pm, 7.0)
+    lib()("tagi_im2col", dm.data_ptr(), None, only.data_ptr(), None, N, C, H, W, k, s, p, pt,
+          stream(pm))
+    np.testing.assert_array_equal(only.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
+
+
 @pytest.mark.parametrize("shape,k,s,p,pt", [((2, 3, 9, 7), 3, 2, 1, 2), ((3, 4, 8, 8), 3, 1, 1, 1),
                                             ((2, 5, 16, 16), 2, 2, 0, 1),
                                             ((2, 3, 12, 12), 5, 1, 2, 1)])
@@ -267,12 +291,14 @@ def test_conv_layer_against_oracle(shape, k, s, p, pt):
             assert_rel(getattr(dev, n), getattr(ref, n), 1e-4, n)
 
 
-def test_batchnorm_layer_against_oracle():
+@pytest.mark.parametrize("N,C,H,W", [(8, 16, 6, 6), (3, 5, 7, 5), (1, 600, 2, 2), (64, 4, 16, 16)])
+def test_batchnorm_layer_against_oracle(N, C, H, W):
+    """Covers 16-byte and element-wise channel slabs, clusters of 1 to 8 blocks per
+    channel, and fewer images than blocks in a cluster."""
     import oracle.net as ON
     from triton_tagi import BatchNorm2D
 
-    gen = torch.Generator().manual_seed(21)
-    N, C, H, W = 8, 16, 6, 6
+    gen = torch.Generator().manual_seed(21 + N + C)
     ref, dev = ON.BatchNorm2D(C), BatchNorm2D(C, device=DEV)
     for step in range(2):  # first call initialises running stats, second uses the EMA
         mz, Sz = rnd(gen, N, C, H, W) + 0.3, rnd(gen, N, C, H, W, kind="u", scale=0.2)

@@ -54,6 +54,46 @@ __global__ void im2col_kernel(const float* xm, const float* xS, float* pm, float
     }
 }
 
+// Patches with K = C*k*k a multiple of 4: one thread writes 4 consecutive
+// columns of one row with a 16-byte store (a warp covers 512 contiguous bytes of
+// the row), gathering the 4 inputs through L1; 32-bit index arithmetic.
+__global__ void im2col_v4_kernel(const float* xm, const float* xS, float* pm, float* pS,
+                                 ConvGeom g) {
+    const int kk2 = g.k * g.k, K = g.C * kk2, K4 = K / 4, L = g.Ho * g.Wo;
+    const int64_t total = static_cast<int64_t>(g.N) * L * K4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t row = i / K4;
+        const int col = static_cast<int>(i - row * K4) * 4;
+        const int n = static_cast<int>(row / L), l = static_cast<int>(row - static_cast<int64_t>(n) * L);
+        const int oh = l / g.Wo, ow = l - oh * g.Wo;
+        int c = col / kk2;
+        const int t = col - c * kk2;
+        int kh = t / g.k, kw = t - kh * g.k;
+        const int64_t img = static_cast<int64_t>(n) * g.C;
+        float vm[4], vS[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int ih = oh * g.s - g.p_tl + kh, iw = ow * g.s - g.p_tl + kw;
+            vm[e] = vS[e] = 0.f;
+            if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) {
+                const int64_t src = ((img + c) * g.H + ih) * g.W + iw;
+                vm[e] = __ldg(xm + src);
+                if (pS) vS[e] = __ldg(xS + src);
+            }
+            if (++kw == g.k) {
+                kw = 0;
+                if (++kh == g.k) {
+                    kh = 0;
+                    ++c;
+                }
+            }
+        }
+        reinterpret_cast<float4*>(pm)[i] = make_float4(vm[0], vm[1], vm[2], vm[3]);
+        if (pS) reinterpret_cast<float4*>(pS)[i] = make_float4(vS[0], vS[1], vS[2], vS[3]);
+    }
+}
+
 // One thread per input pixel; taps are visited in (kh, kw) order as the
 // reference does, so for identical patch inputs the sums are bit-identical.
 template <bool ADJOINT>
@@ -110,7 +150,12 @@ extern "C" int tagi_im2col(const float* xm, const float* xS, float* pm, float* p
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(xm && pm && (xS == nullptr) == (pS == nullptr), TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
-    im2col_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);
+    const uintptr_t al = (reinterpret_cast<uintptr_t>(pm) | reinterpret_cast<uintptr_t>(pS)) & 15;
+    if ((C * k * k) % 4 == 0 && al == 0) {
+        im2col_v4_kernel<<<grid_1d(total / 4, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);
+    } else {
+        im2col_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);
+    }
     return check_launch(what);
 }
 

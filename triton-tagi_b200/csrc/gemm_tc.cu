@@ -69,7 +69,7 @@ struct Roles {
     static constexpr int ACC_W0 = MMA_W + 1;
     static constexpr int WARPS = ACC_W0 + 8;
     static constexpr int THREADS = 32 * WARPS;
-    static constexpr int STAGE_ARRIVALS = 2 * (4 + BW);  // producer warps of a stage, both CTAs
+    static constexpr int STAGE_ARRIVALS = 2 * 2 * (4 + BW);  // producer warps of a stage: 2 groups, 2 CTAs
     static constexpr int NP = 6 * BN <= 512 ? 2 : 1;     // chunk buffers per accumulator
     static constexpr int COLS = 2 * (NP + 1) * BN <= 256 ? 256 : 512;
     // tensor-memory columns: chunk buffer b of accumulator q, running total of q
@@ -332,9 +332,18 @@ __host__ __device__ constexpr int field(unsigned long long packed, int i) {
     return static_cast<int>((packed >> (4 * i)) & 0xFull);
 }
 
+// One K-block: the operand tiles of 8 reduction elements.
+template <int VM, int BN>
+constexpr int block_bytes() {
+    return TcTiles<VM>::na * 128 * 32 + TcTiles<VM>::nb * (BN / 2) * 32;
+}
+
+// A stage holds kBlocks consecutive K-blocks (one per producer group); the MMA
+// thread waits, issues and commits once per stage.
+constexpr int kBlocks = 2;
 template <int VM, int BN>
 constexpr int stage_bytes() {
-    return TcTiles<VM>::na * 128 * 32 + TcTiles<VM>::nb * (BN / 2) * 32;
+    return kBlocks * block_bytes<VM, BN>();
 }
 
 template <int VM, int BN>
@@ -622,6 +631,7 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
     static_assert(SPT >= 1 && SPT <= 2, "chunk slots per thread");
     constexpr int TILE = ROWS * 32;
     constexpr int STAGE = stage_bytes<VM, BN>();
+    constexpr int BLOCK = block_bytes<VM, BN>();
     constexpr int OPS = op_stages<VM, BN>();
     constexpr int OFF = IS_A ? 0 : TcTiles<VM>::na * 128 * 32;  // the side's first tile
     constexpr bool TWO = IS_A ? VM != LSQ : VM != RSQ;
@@ -648,12 +658,14 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
             load_row<IS_A, TWO>(g, sd, row, base, gr, k0, c.kend, v);
         }
     };
+    // K-block `it` is block it % kBlocks of stage it / kBlocks (= this group's
+    // half of that stage's slot).
     auto produce = [&](int it, const float (&v)[2][8]) -> bool {
-        const int s = it % OPS;
-        if (it >= OPS && !warp_wait(&c.empty[s], ((it / OPS) - 1) & 1, c.ab, 1)) return false;
+        const int S = it / kBlocks, s = S % OPS;
+        if (S >= OPS && !warp_wait(&c.empty[s], ((S / OPS) - 1) & 1, c.ab, 1)) return false;
         // Rows outside the matrix are not written: an output row (column)
         // depends only on its own A row (B row), and those outputs are dropped.
-        char* st = c.smem + s * STAGE + OFF;
+        char* st = c.smem + s * STAGE + (it % kBlocks) * BLOCK + OFF;
         bool wrote = false;
         if (sd.chunk) {
 #pragma unroll
@@ -691,6 +703,15 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
             }
         }
     }
+    // An odd number of K-blocks leaves the last stage's second block empty; its
+    // group still arrives so that the stage completes.
+    if (alive && c.grp == 1 && (c.niter & 1)) {
+        const int S = c.niter / kBlocks, s = S % OPS;
+        if (S < OPS || warp_wait(&c.empty[s], ((S / OPS) - 1) & 1, c.ab, 1)) {
+            __syncwarp();
+            if (c.lane == 0) arrive_cluster(c.full0 + static_cast<uint32_t>(s * 8));
+        }
+    }
 }
 
 template <int VM, bool MEAN, int EPI, int BN>
@@ -700,6 +721,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     using T = TcTiles<VM>;
     constexpr int A_TILE = 128 * 32, B_TILE = R::NC * 32;
     constexpr int STAGE = stage_bytes<VM, BN>();
+    constexpr int BLOCK = block_bytes<VM, BN>();
     constexpr int OPS = op_stages<VM, BN>();
     constexpr int NP = R::NP;
     constexpr int kOff1 = kChunk / 2;  // stage shift of the variance chunks
@@ -809,30 +831,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                 tc_fence_after();
                 return true;
             };
-            for (int it = 0; it < niter; ++it) {
+            for (int it0 = 0; it0 < niter; it0 += kBlocks) {
                 if (!mbar_wait(&full[s], ph, ab, 2)) break;
                 tc_fence_after();
-                const bool first0 = pos0 == 0, first1 = it == 0 || pos1 == 0;
-                const bool last0 = it == niter - 1 || pos0 == kChunk - 1;
-                const bool last1 = it == niter - 1 || pos1 == kChunk - 1;
-                const int b0 = c0 % NP, b1 = c1 % NP;
-                const uint32_t acc0 = first0 ? 0u : 1u, acc1 = first1 ? 0u : 1u;
                 bool ok = true;
-                if (!(MEAN && first0 && c0 >= NP)) {
-                    if (MEAN) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), da, db, idesc, acc0);
-                    if (first1 && c1 >= NP) ok = drained(1, c1);
-                    if (ok) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), da, db, idesc, acc1);
-                } else {
-                    issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), da, db, idesc, acc1);
-                    ok = drained(0, c0);
-                    if (ok) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), da, db, idesc, acc0);
+#pragma unroll
+                for (int sub = 0; sub < kBlocks; ++sub) {
+                    const int it = it0 + sub;
+                    if (it >= niter || !ok) break;
+                    const uint64_t bda = da + static_cast<uint64_t>((sub * BLOCK) >> 4);
+                    const uint64_t bdb = db + static_cast<uint64_t>((sub * BLOCK) >> 4);
+                    const bool first0 = pos0 == 0, first1 = it == 0 || pos1 == 0;
+                    const bool last0 = it == niter - 1 || pos0 == kChunk - 1;
+                    const bool last1 = it == niter - 1 || pos1 == kChunk - 1;
+                    const int b0 = c0 % NP, b1 = c1 % NP;
+                    const uint32_t acc0 = first0 ? 0u : 1u, acc1 = first1 ? 0u : 1u;
+                    if (!(MEAN && first0 && c0 >= NP)) {
+                        if (MEAN) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), bda, bdb, idesc, acc0);
+                        if (first1 && c1 >= NP) ok = drained(1, c1);
+                        if (ok) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), bda, bdb, idesc, acc1);
+                    } else {
+                        issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), bda, bdb, idesc, acc1);
+                        ok = drained(0, c0);
+                        if (ok) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), bda, bdb, idesc, acc0);
+                    }
+                    if (!ok) break;
+                    if (MEAN && last0) mma_commit_pair(&chunk_full[b0]);
+                    if (last1) mma_commit_pair(&chunk_full[2 + b1]);
+                    if (++pos0 == kChunk) { pos0 = 0; ++c0; }
+                    if (++pos1 == kChunk) { pos1 = 0; ++c1; }
                 }
                 if (!ok) break;
                 mma_commit_pair(&empty[s]);
-                if (MEAN && last0) mma_commit_pair(&chunk_full[b0]);
-                if (last1) mma_commit_pair(&chunk_full[2 + b1]);
-                if (++pos0 == kChunk) { pos0 = 0; ++c0; }
-                if (++pos1 == kChunk) { pos1 = 0; ++c1; }
                 if (++s == OPS) {
                     s = 0;
                     ph ^= 1u;

@@ -1,59 +1,140 @@
 // BatchNorm2D and RMSNorm moment kernels.
 //
-// Channel reductions run one block per channel over the (N, H*W) slab with
-// float64 accumulation in a fixed order (deterministic, no atomics), so the
-// sums can be all-reduced across data-parallel ranks before the statistics
-// are finalised on the device.
+// Channel reductions accumulate in float64 in a fixed order (deterministic, no
+// atomics), so the sums can be all-reduced across data-parallel ranks before the
+// statistics are finalised on the device. Each channel is reduced by a
+// thread-block cluster of S = 1, 2, 4 or 8 blocks (about 512 blocks in all):
+// block j takes images j, j+S, ..., and the cluster's first block adds the S
+// partial sums from its peers' shared memory in rank order. No workspace, one
+// launch.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tagi {
 namespace {
 
-constexpr int kRedThreads = 512;
+constexpr int kBnThreads = 256;
 
+int bn_split(int64_t C, int64_t N) {
+    int s = 1;
+    while (s < 8 && C * s < 512 && s < N) s *= 2;
+    return s;
+}
+
+// Sums v over the block (fixed order), then over the cluster's blocks in rank
+// order; the totals are valid in thread 0 of cluster rank 0.
 template <int NV>
-__device__ __forceinline__ void block_sum(double (&v)[NV], double* smem) {
-    // smem: NV * (kRedThreads / 32) doubles
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nw = blockDim.x >> 5;
+__device__ __forceinline__ void cluster_channel_sum(double (&v)[NV], double* red, double* part) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
-        if (lane == 0) smem[j * 32 + warp] = v[j];
+        if (lane == 0) red[j * 32 + warp] = v[j];
     }
     __syncthreads();
-    if (warp == 0) {
+    if (threadIdx.x == 0) {
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
-            double t = lane < nw ? smem[j * 32 + lane] : 0.0;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-            v[j] = t;
+            double t = 0.0;
+            for (int w = 0; w < nw; ++w) t += red[j * 32 + w];
+            part[j] = t;
         }
     }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0 && threadIdx.x == 0) {
+#pragma unroll
+        for (int j = 0; j < NV; ++j) v[j] = 0.0;
+        for (unsigned r = 0; r < cluster.num_blocks(); ++r) {
+            const double* peer = cluster.map_shared_rank(part, r);
+#pragma unroll
+            for (int j = 0; j < NV; ++j) v[j] += peer[j];
+        }
+    }
+    cluster.sync();  // peers keep their shared memory until it has been read
 }
 
-// sums[c] = sum mz, sums[C+c] = sum Sz, sums[2C+c] = sum mz^2 over (n, hw).
-__global__ void __launch_bounds__(kRedThreads) bn_sums_kernel(const float* mz, const float* Sz,
-                                                              double* sums, int N, int C, int HW) {
-    __shared__ double smem[3 * 32];
-    const int c = blockIdx.x;
-    double v[3] = {0.0, 0.0, 0.0};
-    const int64_t per = static_cast<int64_t>(N) * HW;
-    for (int64_t t = threadIdx.x; t < per; t += blockDim.x) {
-        const int n = static_cast<int>(t / HW), hw = static_cast<int>(t % HW);
-        const int64_t o = (static_cast<int64_t>(n) * C + c) * HW + hw;
-        const double m = mz[o];
-        v[0] += m;
-        v[1] += Sz[o];
-        v[2] += m * m;
+template <typename K, typename... Args>
+int launch_cluster(K kernel, int S, int C, cudaStream_t st, const char* what, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(S), static_cast<unsigned>(C), 1);
+    cfg.blockDim = dim3(kBnThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error("%s: launch failed (%s)", what, cudaGetErrorString(e));
+        return TAGI_E_LAUNCH;
     }
-    block_sum<3>(v, smem);
-    if (threadIdx.x == 0) {
-        sums[c] = v[0];
-        sums[C + c] = v[1];
-        sums[2 * C + c] = v[2];
+    return check_launch(what);
+}
+
+// Elements of channel c handled by cluster block j of S: images j, j+S, ...,
+// visited 4 at a time along H*W when the planes allow 16-byte access.
+struct ChanSlab {
+    int n0, S, nimg, HW, C, c;
+    __device__ ChanSlab(int N, int C_, int HW_, int c_) : C(C_), HW(HW_), c(c_) {
+        n0 = blockIdx.x;
+        S = gridDim.x;
+        nimg = n0 < N ? (N - n0 + S - 1) / S : 0;
+    }
+    __device__ __forceinline__ int64_t offset(int li, int hw) const {
+        return (static_cast<int64_t>(n0 + li * S) * C + c) * HW + hw;
+    }
+};
+
+// sums[c] = sum mz, sums[C+c] = sum Sz, sums[2C+c] = sum mz^2 over (n, hw).
+template <bool V4>
+__global__ void __launch_bounds__(kBnThreads) bn_sums_kernel(const float* mz, const float* Sz,
+                                                             double* sums, int N, int C, int HW) {
+    __shared__ double red[3 * 32];
+    __shared__ double part[3];
+    const ChanSlab sl(N, C, HW, blockIdx.y);
+    double v[3] = {0.0, 0.0, 0.0};
+    if (V4) {
+        const int HW4 = HW / 4, total = sl.nimg * HW4;
+        for (int t = threadIdx.x; t < total; t += blockDim.x) {
+            const int li = t / HW4, h = (t - li * HW4) * 4;
+            const int64_t o = sl.offset(li, h);
+            const float4 m = __ldg(reinterpret_cast<const float4*>(mz + o));
+            const float4 S = __ldg(reinterpret_cast<const float4*>(Sz + o));
+            const float mm[4] = {m.x, m.y, m.z, m.w}, ss[4] = {S.x, S.y, S.z, S.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const double x = mm[e];
+                v[0] += x;
+                v[1] += ss[e];
+                v[2] += x * x;
+            }
+        }
+    } else {
+        const int total = sl.nimg * HW;
+        for (int t = threadIdx.x; t < total; t += blockDim.x) {
+            const int li = t / HW;
+            const int64_t o = sl.offset(li, t - li * HW);
+            const double x = mz[o];
+            v[0] += x;
+            v[1] += Sz[o];
+            v[2] += x * x;
+        }
+    }
+    cluster_channel_sum<3>(v, red, part);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        sums[sl.c] = v[0];
+        sums[C + sl.c] = v[1];
+        sums[2 * C + sl.c] = v[2];
     }
 }
 
@@ -103,33 +184,55 @@ __global__ void bn_forward_kernel(const float* mz, const float* Sz, const float*
     }
 }
 
-// batchnorm2d.py:134-192 plus the gamma/beta sums of 465-482, one block per channel.
-__global__ void __launch_bounds__(kRedThreads) bn_backward_kernel(
+// batchnorm2d.py:134-192 plus the gamma/beta sums of 465-482, one cluster per channel.
+template <bool V4>
+__global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     const float* dma, const float* dSa, const float* mhat, const float* var, const float* mg,
     float* dmz, float* dSz, double* grads, int N, int C, int HW, float eps) {
-    __shared__ double smem[4 * 32];
-    const int c = blockIdx.x;
-    const float g = mg[c];
-    const float rs = var[c];
+    __shared__ double red[4 * 32];
+    __shared__ double part[4];
+    const ChanSlab sl(N, C, HW, blockIdx.y);
+    const float g = mg[sl.c];
+    const float rs = var[sl.c];
     const float inv_std = 1.0f / sqrtf(rs + eps);
     const float inv_var = 1.0f / (rs + eps);
     double v[4] = {0.0, 0.0, 0.0, 0.0};
-    const int64_t per = static_cast<int64_t>(N) * HW;
-    for (int64_t t = threadIdx.x; t < per; t += blockDim.x) {
-        const int n = static_cast<int>(t / HW), hw = static_cast<int>(t % HW);
-        const int64_t o = (static_cast<int64_t>(n) * C + c) * HW + hw;
-        const float dm = dma[o], dS = dSa[o], mh = mhat[o];
+    auto one = [&](float dm, float dS, float mh, float& om, float& oS) {
         v[0] += static_cast<double>(dm * mh);
         v[1] += static_cast<double>(dS * (mh * mh));
         v[2] += dm;
         v[3] += dS;
-        dmz[o] = (dm * g) * inv_std;
-        dSz[o] = (dS * g * g) * inv_var;
+        om = (dm * g) * inv_std;
+        oS = (dS * g * g) * inv_var;
+    };
+    if (V4) {
+        const int HW4 = HW / 4, total = sl.nimg * HW4;
+        for (int t = threadIdx.x; t < total; t += blockDim.x) {
+            const int li = t / HW4, h = (t - li * HW4) * 4;
+            const int64_t o = sl.offset(li, h);
+            const float4 a = __ldg(reinterpret_cast<const float4*>(dma + o));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(dSa + o));
+            const float4 c = __ldg(reinterpret_cast<const float4*>(mhat + o));
+            float4 om, oS;
+            one(a.x, b.x, c.x, om.x, oS.x);
+            one(a.y, b.y, c.y, om.y, oS.y);
+            one(a.z, b.z, c.z, om.z, oS.z);
+            one(a.w, b.w, c.w, om.w, oS.w);
+            *reinterpret_cast<float4*>(dmz + o) = om;
+            *reinterpret_cast<float4*>(dSz + o) = oS;
+        }
+    } else {
+        const int total = sl.nimg * HW;
+        for (int t = threadIdx.x; t < total; t += blockDim.x) {
+            const int li = t / HW;
+            const int64_t o = sl.offset(li, t - li * HW);
+            one(dma[o], dSa[o], mhat[o], dmz[o], dSz[o]);
+        }
     }
-    block_sum<4>(v, smem);
-    if (threadIdx.x == 0) {
+    cluster_channel_sum<4>(v, red, part);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) grads[j * C + c] = v[j];
+        for (int j = 0; j < 4; ++j) grads[j * C + sl.c] = v[j];
     }
 }
 
@@ -242,9 +345,13 @@ extern "C" int tagi_bn_channel_sums(const float* mz, const float* Sz, double* su
     TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     if (C == 0) return TAGI_OK;
     TAGI_REQUIRE(mz && Sz && sums, TAGI_E_BAD_ARG, "%s: null pointer", what);
-    bn_sums_kernel<<<(unsigned)C, kRedThreads, 0, as_stream(stream)>>>(mz, Sz, sums, (int)N, (int)C,
-                                                                       (int)HW);
-    return check_launch(what);
+    TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    const int S = bn_split(C, N);
+    const bool v4 = HW % 4 == 0 && ((reinterpret_cast<uintptr_t>(mz) | reinterpret_cast<uintptr_t>(Sz)) & 15) == 0;
+    return v4 ? launch_cluster(bn_sums_kernel<true>, S, (int)C, as_stream(stream), what, mz, Sz,
+                               sums, (int)N, (int)C, (int)HW)
+              : launch_cluster(bn_sums_kernel<false>, S, (int)C, as_stream(stream), what, mz, Sz,
+                               sums, (int)N, (int)C, (int)HW);
 }
 
 extern "C" int tagi_bn_finalize(const double* sums, int64_t C, double count, float* mean,
@@ -287,9 +394,16 @@ extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float*
     if (C == 0) return TAGI_OK;
     TAGI_REQUIRE(dma && dSa && m_hat && var && mg && dmz && dSz && grads, TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
-    bn_backward_kernel<<<(unsigned)C, kRedThreads, 0, as_stream(stream)>>>(
-        dma, dSa, m_hat, var, mg, dmz, dSz, grads, (int)N, (int)C, (int)HW, eps);
-    return check_launch(what);
+    TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    const int S = bn_split(C, N);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(dma) | reinterpret_cast<uintptr_t>(dSa) |
+                         reinterpret_cast<uintptr_t>(m_hat) | reinterpret_cast<uintptr_t>(dmz) |
+                         reinterpret_cast<uintptr_t>(dSz);
+    const bool v4 = HW % 4 == 0 && (al & 15) == 0;
+    return v4 ? launch_cluster(bn_backward_kernel<true>, S, (int)C, as_stream(stream), what, dma,
+                               dSa, m_hat, var, mg, dmz, dSz, grads, (int)N, (int)C, (int)HW, eps)
+              : launch_cluster(bn_backward_kernel<false>, S, (int)C, as_stream(stream), what, dma,
+                               dSa, m_hat, var, mg, dmz, dSz, grads, (int)N, (int)C, (int)HW, eps);
 }
 
 extern "C" int tagi_bn_apply_grads(const double* grads, int64_t C, int mode, float* mw, float* Sw,
