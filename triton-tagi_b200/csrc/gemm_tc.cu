@@ -28,8 +28,9 @@
 //                 no-swizzle K-major layout (8-row x 16-byte core matrices).
 //   next 2*BW     B producers: the same for this CTA's BN/2 rows of B.
 //   MMA warp      allocates tensor memory (both CTAs); in the leader CTA
-//                 (cluster rank 0) one thread issues the MMAs and commits them
-//                 to barriers of both CTAs (multicast commit).
+//                 (cluster rank 0) it runs the stage loop and an elected lane
+//                 issues the MMAs and commits them to barriers of both CTAs
+//                 (multicast commit).
 //   8 acc warps   fold chunks and run the epilogue; warp w reads tensor-memory
 //                 lane quarter w % 4 and one half of the columns.
 // The mean and variance chunks end on staggered stages: when a chunk buffer must
@@ -161,6 +162,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const Abort& ab,
                                           int code) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, ab, code));
+}
+
+__device__ __forceinline__ bool elect_one() {
+    uint32_t p;
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}"
+        : "=r"(p));
+    return p != 0;
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -812,10 +821,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         }
     } else if (warp == R::MMA_W) {
         // ------------------------------------------------------------ MMA issue
-        // One thread issues everything (tcgen05.mma and tcgen05.commit are
-        // single-thread instructions). The tensor pipe queues only a few MMAs, so
-        // the work between two stages' MMAs is kept to a few integer updates.
-        if (leader && lane == 0) {
+        // The whole warp runs the loop (its state stays warp-uniform, so the
+        // descriptors live in uniform registers) and one elected lane issues the
+        // single-thread tcgen05.mma / tcgen05.commit instructions. Run by one lane
+        // alone, the same loop fed the tensor pipe at half its rate.
+        if (leader) {
+            const bool el = elect_one();
             const uint64_t da_first = smem_desc(smem_u32(smem), sa.chunk, 128);
             const uint64_t db_first = smem_desc(smem_u32(smem), sb.chunk, R::NC);
             const uint32_t idesc = instr_desc(BN, sa.chunk, sb.chunk);
@@ -827,12 +838,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
             // An accumulator whose chunk buffer must first be drained by a fold
             // goes second, so that the other one's products keep the pipe busy.
             auto drained = [&](int q, int c) -> bool {
-                if (!mbar_wait(&chunk_empty[q * 2 + c % NP], ((c / NP) - 1) & 1, ab, 5)) return false;
+                if (!warp_wait(&chunk_empty[q * 2 + c % NP], ((c / NP) - 1) & 1, ab, 5)) return false;
                 tc_fence_after();
                 return true;
             };
             for (int it0 = 0; it0 < niter; it0 += kBlocks) {
-                if (!mbar_wait(&full[s], ph, ab, 2)) break;
+                if (!warp_wait(&full[s], ph, ab, 2)) break;
                 tc_fence_after();
                 bool ok = true;
 #pragma unroll
@@ -847,22 +858,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                     const int b0 = c0 % NP, b1 = c1 % NP;
                     const uint32_t acc0 = first0 ? 0u : 1u, acc1 = first1 ? 0u : 1u;
                     if (!(MEAN && first0 && c0 >= NP)) {
-                        if (MEAN) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), bda, bdb, idesc, acc0);
+                        if (MEAN && el) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), bda, bdb, idesc, acc0);
                         if (first1 && c1 >= NP) ok = drained(1, c1);
-                        if (ok) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), bda, bdb, idesc, acc1);
+                        if (ok && el) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), bda, bdb, idesc, acc1);
                     } else {
-                        issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), bda, bdb, idesc, acc1);
+                        if (el) issue_acc<VM, BN, 1>(tmem + R::pcol(1, b1), bda, bdb, idesc, acc1);
                         ok = drained(0, c0);
-                        if (ok) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), bda, bdb, idesc, acc0);
+                        if (ok && el) issue_acc<VM, BN, 0>(tmem + R::pcol(0, b0), bda, bdb, idesc, acc0);
                     }
                     if (!ok) break;
-                    if (MEAN && last0) mma_commit_pair(&chunk_full[b0]);
-                    if (last1) mma_commit_pair(&chunk_full[2 + b1]);
+                    if (MEAN && last0 && el) mma_commit_pair(&chunk_full[b0]);
+                    if (last1 && el) mma_commit_pair(&chunk_full[2 + b1]);
                     if (++pos0 == kChunk) { pos0 = 0; ++c0; }
                     if (++pos1 == kChunk) { pos1 = 0; ++c1; }
                 }
                 if (!ok) break;
-                mma_commit_pair(&empty[s]);
+                if (el) mma_commit_pair(&empty[s]);
+                __syncwarp();
                 if (++s == OPS) {
                     s = 0;
                     ph ^= 1u;
@@ -873,7 +885,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                     db += static_cast<uint64_t>(STAGE >> 4);
                 }
             }
-            mma_commit_pair(done);  // arrives once every MMA issued above completed
+            if (el) mma_commit_pair(done);  // arrives once every MMA issued above completed
+            __syncwarp();
         }
     } else {
         // -------------------------------------------- accumulator warps
