@@ -173,9 +173,9 @@ class LaunchTimer:
         "tagi_backward_delta_view": ("backward_delta", lambda a: 4.0 * a[14] * a[15] * a[16]),
         "tagi_fused_backward_delta": ("backward_delta", lambda a: 4.0 * a[5] * a[6] * a[7]),
         # M = N*H*W input pixels, N = C, reduction Co*k*k
-        # (args: dmz, dSz, mw, w_rev, d_ma, d_Sa, N, C, H, W, Co, k, padding, stream)
-        "tagi_conv2d_backward_delta_s1": (
-            "backward_delta", lambda a: 4.0 * a[6] * a[8] * a[9] * a[7] * a[10] * a[11] * a[11]),
+        # (args: dmz, dSz, mw, d_ma, d_Sa, N, C, H, W, Co, k, stride, padding, ...)
+        "tagi_conv2d_backward_delta": (
+            "backward_delta", lambda a: 4.0 * a[5] * a[7] * a[8] * a[6] * a[9] * a[10] * a[10]),
         "tagi_param_grad": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
     }
 

@@ -99,20 +99,20 @@ int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const
                         int64_t C, int64_t H, int64_t W, int64_t Co, int64_t k, int64_t stride,
                         int64_t padding, int64_t padding_type, void* stream);
 
-/* Input deltas of a stride-1 Conv2D with symmetric padding p, written in NCHW.
- * With stride 1 the reference's patch-space product followed by its col2im
- * gather (triton_tagi/layers/conv2d.py:338-357 and _col2im_kernel,
- * conv2d.py:119-130) sums exactly the terms of a convolution of the output
- * deltas with the spatially reversed, transposed weights; this entry computes it
- * as one contraction over (tap, co), gathering the patches of (dmz, dSz)
- * (N x Co x Ho x Wo, padded by k-1-p) itself. mw is the layer's (C*k*k) x Co
- * weight matrix: d_ma = P_m @ W', d_Sa = P_S @ W'^2 with
- * W'[(kh,kw,co)][c] = mw[c*k*k + (k-1-kh)*k + (k-1-kw)][co]; W' is first written
- * to w_rev (caller scratch of C*k*k*Co floats, one row per input channel). */
-int tagi_conv2d_backward_delta_s1(const float* dmz, const float* dSz, const float* mw,
-                                  float* w_rev, float* d_ma, float* d_Sa, int64_t N, int64_t C,
-                                  int64_t H, int64_t W, int64_t Co, int64_t k, int64_t padding,
-                                  void* stream);
+/* Conv2D input deltas, written in NCHW (N x C x H x W). The reference forms the
+ * patch-space deltas dP = dmz @ mw^T, dP_S = dSz @ (mw^2)^T (rows (n, oh, ow),
+ * columns (c, kh, kw)) and folds them back with its col2im gather
+ * (triton_tagi/layers/conv2d.py:338-357, _col2im_kernel 119-130). This entry sums
+ * the same terms in one contraction over (tap, co): for input pixel (h, w) and
+ * tap (kh, kw) it gathers the deltas at the output position the gather maps to,
+ * times mw[c*k*k + tap][co]. col2im_mode 0 reproduces the reference's gather
+ * (for stride > 1 it does not test the column offset for divisibility, with
+ * truncating division); 1 is the exact adjoint of the patches. dmz, dSz:
+ * N x Co x Ho x Wo; mw: (C*k*k) x Co; padding_type as tagi_conv2d_forward. */
+int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, const float* mw, float* d_ma,
+                               float* d_Sa, int64_t N, int64_t C, int64_t H, int64_t W,
+                               int64_t Co, int64_t k, int64_t stride, int64_t padding,
+                               int64_t padding_type, int col2im_mode, void* stream);
 
 /* grad_mw = a^T @ dmz, grad_Sw = (a^2)^T @ dSz  (K x N outputs).
  * Replaces triton_fused_weight_grad, triton_tagi/kernels/common.py:410-451. */

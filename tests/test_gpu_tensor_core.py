@@ -179,9 +179,9 @@ def test_batched_attention_products():
 @pytest.mark.parametrize("C,Co,k,p", [(64, 64, 3, 1), (128, 96, 3, 1), (40, 72, 5, 2),
                                       (64, 64, 3, 0), (96, 64, 1, 0)])
 def test_conv_stride1_input_deltas_as_one_contraction(C, Co, k, p):
-    """Stride-1 Conv2D.backward runs the deltas' patches against the reversed
-    weights (tagi_conv2d_backward_delta_s1); it must equal the reference's
-    patch-space product followed by its col2im gather."""
+    """Conv2D.backward gathers the deltas as the col2im fold does inside one
+    contraction (tagi_conv2d_backward_delta); at stride 1 it must equal the
+    reference's patch-space product followed by its col2im gather."""
     import oracle.net as ON
     from triton_tagi import Conv2D
 
@@ -233,10 +233,44 @@ def test_conv_layer_gathered_patches(C, Co, k, s, p, pt):
     assert_rel(mz, ex_m, MEAN_RTOL, "mz")
     assert_rel(Sz, ex_S, VAR_RTOL, "Sz")
     dmz, dSz = _rnd(g, *ex_m.shape, scale=0.1), -_rnd(g, *ex_m.shape, u=True, scale=1e-2)
-    r_dm, r_dS = ref.backward(dmz, dSz)
-    d_dm, d_dS = dev.backward(dmz.to(DEV), dSz.to(DEV))
-    assert_rel(d_dm, r_dm, MEAN_RTOL, "d_ma")
-    assert_rel(d_dS, r_dS, VAR_RTOL, "d_Sa")
-    assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "delta_mw")
-    assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "delta_Sw")
+    for mode in ("reference", "adjoint"):  # the two col2im gathers differ for stride > 1
+        dev.col2im_mode = mode
+        ref.col2im_adjoint = mode == "adjoint"
+        ref.forward(ma, Sa)
+        dev.forward(ma.to(DEV), Sa.to(DEV))
+        r_dm, r_dS = ref.backward(dmz, dSz)
+        d_dm, d_dS = dev.backward(dmz.to(DEV), dSz.to(DEV))
+        assert_rel(d_dm, r_dm, MEAN_RTOL, f"d_ma {mode}")
+        assert_rel(d_dS, r_dS, VAR_RTOL, f"d_Sa {mode}")
+        assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "delta_mw")
+        assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "delta_Sw")
+    _ok()
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("C,Co,k,s,p,pt", [(32, 64, 3, 2, 1, 1), (16, 48, 2, 2, 0, 1),
+                                           (24, 32, 3, 2, 1, 2)])
+def test_conv_backward_delta_entry_strided_gathers(C, Co, k, s, p, pt, mode):
+    """tagi_conv2d_backward_delta with stride > 1: the reference's col2im gather
+    (mode 0, no column-divisibility test) and the adjoint (mode 1), against the
+    oracle's patch-space product followed by the same gather."""
+    from triton_tagi._lib import lib, stream
+
+    g = torch.Generator().manual_seed(C + Co + k + s + mode)
+    N, H, W = 4, 17, 14
+    mw = _rnd(g, C * k * k, Co, scale=(C * k * k) ** -0.5)
+    Ho, Wo = F.conv_out_hw(H, W, k, s, p, pt)
+    dmz, dSz = _rnd(g, N, Co, Ho, Wo, scale=0.1), -_rnd(g, N, Co, Ho, Wo, u=True, scale=1e-2)
+    d_dmz, d_dSz, d_mw = dmz.to(DEV), dSz.to(DEV), mw.to(DEV)
+    d_ma = torch.empty(N, C, H, W, device=DEV)
+    d_Sa = torch.empty_like(d_ma)
+    lib()("tagi_conv2d_backward_delta", d_dmz.data_ptr(), d_dSz.data_ptr(), d_mw.data_ptr(),
+          d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, s, p, pt, mode, stream(d_ma))
+    dm = dmz.double().permute(0, 2, 3, 1).reshape(-1, Co)
+    dS = dSz.double().permute(0, 2, 3, 1).reshape(-1, Co)
+    dpm, dpS = F.backward_delta(dm, dS, mw.double())
+    ref_m = F.col2im(dpm, N, C, H, W, k, s, p, pt, adjoint=mode == 1)
+    ref_S = F.col2im(dpS, N, C, H, W, k, s, p, pt, adjoint=mode == 1)
+    assert_rel(d_ma, ref_m, MEAN_RTOL, "d_ma")
+    assert_rel(d_Sa, ref_S, VAR_RTOL, "d_Sa")
     _ok()

@@ -294,21 +294,6 @@ size_t wgrad_ws_bytes(int Mo, int N, int Kr) {
     return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * N : 0;
 }
 
-// w_rev[c][j*Co + co] = mw[(c*kk + kk-1-j)][co]: the layer's (C*kk) x Co
-// weights with the kernel taps reversed, one row per input channel in the
-// (tap, channel) reduction order of the gathered delta patches; the B operand
-// of the stride-1 input-delta contraction.
-__global__ void reverse_taps_kernel(const float* mw, float* w_rev, int C, int Co, int kk) {
-    const int64_t total = static_cast<int64_t>(C) * Co * kk;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t c = i / (static_cast<int64_t>(Co) * kk);
-        const int r = static_cast<int>(i - c * Co * kk);
-        const int j = r / Co, co = r - j * Co;
-        w_rev[i] = mw[(c * kk + (kk - 1 - j)) * Co + co];
-    }
-}
-
 __global__ void apply_sums_kernel(const float* gm, const float* gS, ParamEpi p, int64_t total) {
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -419,7 +404,7 @@ extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float
                  "%s: null pointer", what);
     GemmArgs g = blank();
     g.x = ma; g.y = Sa;
-    g.ga = Gather{1, (int)C, (int)H, (int)W, (int)Wo, (int)L, (int)k, (int)stride, top, top};
+    g.ga = Gather{1, 0, (int)C, (int)H, (int)W, (int)Wo, (int)L, (int)k, (int)stride, top, top};
     // B[co][tap*C + c] = mw[c*kk + tap][co]: the weight rows in (tap, c) order
     g.u = mw; g.v = Sw; g.brow = RowMap{C, Co, k * k * Co}; g.bn = 1;
     g.bias0 = mb; g.bias1 = Sb;
@@ -429,15 +414,19 @@ extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float
     return launch<FULL, true, EPI_STORE>(g, 1, as_stream(stream), what);
 }
 
-extern "C" int tagi_conv2d_backward_delta_s1(const float* dmz, const float* dSz, const float* mw,
-                                             float* w_rev, float* d_ma, float* d_Sa, int64_t N,
-                                             int64_t C, int64_t H, int64_t W, int64_t Co,
-                                             int64_t k, int64_t padding, void* stream) {
-    const char* what = "tagi_conv2d_backward_delta_s1";
-    TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && padding >= 0 &&
-                     padding <= k - 1,
-                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
-    const int64_t Ho = H + 2 * padding - k + 1, Wo = W + 2 * padding - k + 1;
+extern "C" int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, const float* mw,
+                                          float* d_ma, float* d_Sa, int64_t N, int64_t C,
+                                          int64_t H, int64_t W, int64_t Co, int64_t k,
+                                          int64_t stride, int64_t padding, int64_t padding_type,
+                                          int col2im_mode, void* stream) {
+    const char* what = "tagi_conv2d_backward_delta";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && stride >= 1 &&
+                     padding >= 0 && (padding_type == 1 || padding_type == 2) &&
+                     (col2im_mode == 0 || col2im_mode == 1),
+                 TAGI_E_BAD_ARG, "%s: bad arguments", what);
+    int64_t Ho, Wo;
+    int top;
+    conv_geometry(H, W, k, stride, padding, padding_type, &Ho, &Wo, &top);
     TAGI_REQUIRE(Ho >= 1 && Wo >= 1, TAGI_E_BAD_ARG, "%s: kernel larger than the padded input",
                  what);
     const int64_t HW = H * W, kk = k * k, M = N * HW, Kr = Co * kk;
@@ -445,27 +434,21 @@ extern "C" int tagi_conv2d_backward_delta_s1(const float* dmz, const float* dSz,
                      !bad_size(N * Co * Ho * Wo) && !bad_size(C * kk * Co),
                  TAGI_E_BAD_ARG, "%s: bad sizes", what);
     if (M == 0 || C == 0) return TAGI_OK;
-    TAGI_REQUIRE(d_ma && d_Sa && (Kr == 0 || (dmz && dSz && mw && w_rev)), TAGI_E_BAD_ARG,
+    TAGI_REQUIRE(d_ma && d_Sa && (Kr == 0 || (dmz && dSz && mw)), TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
-    cudaStream_t st = as_stream(stream);
-    if (Kr > 0) {
-        reverse_taps_kernel<<<grid_1d(C * Kr, 256), 256, 0, st>>>(mw, w_rev, (int)C, (int)Co,
-                                                                  (int)kk);
-        int rc = check_launch(what);
-        if (rc) return rc;
-    }
     GemmArgs g = blank();
-    // A: patches of the deltas (Co x Ho x Wo per image) with padding k-1-p, gathered
-    // for rows (n, h, w) of the input, reduction (tap, co)
-    const int q = static_cast<int>(k - 1 - padding);
+    // A: the col2im gather of the deltas (Co x Ho x Wo per image) for rows (n, h, w)
+    // of the input, reduction (tap, co)
     g.x = dmz; g.y = dSz;
-    g.ga = Gather{1, (int)Co, (int)Ho, (int)Wo, (int)W, (int)HW, (int)k, 1, q, q};
-    // B[c][tap*Co + co] = w_rev[c][tap*Co + co]: rows contiguous along the reduction
-    g.u = w_rev; g.brow = plain_rows(1); g.bn = Kr;
+    g.ga = Gather{1, col2im_mode == 0 ? 1 : 2, (int)Co, (int)Ho, (int)Wo, (int)W, (int)HW,
+                  (int)k, (int)stride, top, top};
+    // B[c][tap*Co + co] = mw[c*kk + tap][co]: the weight matrix read in place, row c
+    // contiguous along the reduction
+    g.u = mw; g.brow = plain_rows(1); g.bn = Kr;
     // outputs straight into NCHW: row (n, hw) -> n*C*HW + hw, column c -> c*HW
     g.o0 = d_ma; g.o1 = d_Sa; g.orow = RowMap{HW, C * HW, 1}; g.on = HW;
     g.M = (int)M; g.N = (int)C; g.Kr = (int)Kr; g.kchunk = Kr > 0 ? (int)Kr : BK;
-    return launch<RSQ, true, EPI_STORE>(g, 1, st, what);
+    return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
 }
 
 extern "C" int tagi_fused_backward_delta(const float* dmz, const float* dSz, const float* mw,

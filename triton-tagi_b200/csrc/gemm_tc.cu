@@ -459,7 +459,7 @@ __device__ __forceinline__ void load_elem(const GemmArgs& g, const Side& sd, int
 
 // Row mode: the 8 elements k0..k0+7 of `row`; zeros past kend. The reduction
 // offsets of B go through brow with a single division per stage.
-template <bool IS_A, bool TWO>
+template <bool IS_A, bool TWO, int GM>
 __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int row,
                                          int64_t base, const GatherRow& gr, int k0, int kend,
                                          float (&v)[2][8]) {
@@ -470,8 +470,8 @@ __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int 
         const int64_t plane = static_cast<int64_t>(ga.H) * ga.W;
         int tap = k0 / ga.C, c = k0 - tap * ga.C;
         int kh = tap / ga.k, kw = tap - kh * ga.k;
-        int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
-        bool inside = row < sd.nrows && ih >= 0 && ih < ga.H && iw >= 0 && iw < ga.W;
+        int ih, iw;
+        bool inside = row < sd.nrows && gather_tap<GM>(ga, gr, kh, kw, &ih, &iw);
         int64_t o = gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -485,9 +485,7 @@ __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int 
                     kw = 0;
                     ++kh;
                 }
-                ih = gr.ih0 + kh;
-                iw = gr.iw0 + kw;
-                inside = row < sd.nrows && ih >= 0 && ih < ga.H && iw >= 0 && iw < ga.W;
+                inside = row < sd.nrows && gather_tap<GM>(ga, gr, kh, kw, &ih, &iw);
                 o = gr.base + static_cast<int64_t>(ih) * ga.W + iw;
             }
         }
@@ -629,7 +627,7 @@ struct ProdCtx {
 
 // One side's producer thread: stages grp, grp+2, ... with kDepth of them loaded
 // ahead into registers.
-template <int VM, int BN, bool IS_A>
+template <int VM, int BN, bool IS_A, int GM>
 __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, const Side& sd) {
     using R = Roles<BN>;
     constexpr int ROWS = IS_A ? 128 : R::NC;
@@ -664,7 +662,7 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
                                           c.kend, j, v);
             }
         } else if (has_row) {
-            load_row<IS_A, TWO>(g, sd, row, base, gr, k0, c.kend, v);
+            load_row<IS_A, TWO, GM>(g, sd, row, base, gr, k0, c.kend, v);
         }
     };
     // K-block `it` is block it % kBlocks of stage it / kBlocks (= this group's
@@ -723,7 +721,9 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
     }
 }
 
-template <int VM, bool MEAN, int EPI, int BN>
+// GM: the A gather compiled in (0 patches, 1 col2im of any stride, 2 col2im of
+// stride 1); operands that are not gathered ignore it.
+template <int VM, bool MEAN, int EPI, int BN, int GM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 1)
     moment_tc_kernel(const GemmArgs g) {
     using R = Roles<BN>;
@@ -813,11 +813,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         if (is_a) {
             c.grp = warp >> 2;
             c.t = (warp & 3) * 32 + lane;
-            producer<VM, BN, true>(g, c, sa);
+            producer<VM, BN, true, GM>(g, c, sa);
         } else {
             c.grp = (warp - R::B_W0) / R::BW;
             c.t = ((warp - R::B_W0) % R::BW) * 32 + lane;
-            producer<VM, BN, false>(g, c, sb);
+            producer<VM, BN, false, GM>(g, c, sb);
         }
     } else if (warp == R::MMA_W) {
         // ------------------------------------------------------------ MMA issue
@@ -997,13 +997,13 @@ bool tc_enabled() {
     return v == 1;
 }
 
-template <int VM, bool MEAN, int EPI, int BN>
+template <int VM, bool MEAN, int EPI, int BN, int GM>
 int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     constexpr int smem = smem_bytes<VM, BN>();
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(moment_tc_kernel<VM, MEAN, EPI, BN>,
+        attr_err = cudaFuncSetAttribute(moment_tc_kernel<VM, MEAN, EPI, BN, GM>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     if (attr_err != cudaSuccess) {
@@ -1015,16 +1015,16 @@ int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
     dim3 grid(static_cast<unsigned>(2 * pairs), (g.N + BN - 1) / BN, batch * g.splits);
     TAGI_REQUIRE(grid.y <= 65535 && grid.z <= 65535, TAGI_E_UNSUPPORTED, "%s: grid too large",
                  what);
-    moment_tc_kernel<VM, MEAN, EPI, BN><<<grid, Roles<BN>::THREADS, smem, st>>>(g);
+    moment_tc_kernel<VM, MEAN, EPI, BN, GM><<<grid, Roles<BN>::THREADS, smem, st>>>(g);
     return check_launch(what);
 }
 
-template <int VM, bool MEAN, int EPI>
+template <int VM, bool MEAN, int EPI, int GM = VM == FULL ? 0 : 1>
 int launch_bn(const GemmArgs& g, int bn, int batch, cudaStream_t st, const char* what) {
     switch (bn) {
-        case 32: return launch_tc<VM, MEAN, EPI, 32>(g, batch, st, what);
-        case 64: return launch_tc<VM, MEAN, EPI, 64>(g, batch, st, what);
-        default: return launch_tc<VM, MEAN, EPI, 128>(g, batch, st, what);
+        case 32: return launch_tc<VM, MEAN, EPI, 32, GM>(g, batch, st, what);
+        case 64: return launch_tc<VM, MEAN, EPI, 64, GM>(g, batch, st, what);
+        default: return launch_tc<VM, MEAN, EPI, 128, GM>(g, batch, st, what);
     }
 }
 
@@ -1032,12 +1032,14 @@ int launch_bn(const GemmArgs& g, int bn, int batch, cudaStream_t st, const char*
 
 int tc_pick(int vm, int M, int N, int Kr, int batch) {
     (void)vm;
-    (void)batch;
     if (!tc_enabled()) return 0;
     if (M < 64 || N < 16 || Kr < 32) return 0;
     if (static_cast<double>(M) * N * Kr < 4.0e6) return 0;
     if (N <= 32) return 32;
     if (N <= 64) return 64;
+    // 128 columns even when the grid is under one wave: 64-column tiles halve the
+    // tensor work per staged A element, and that costs more than the idle SMs.
+    (void)batch;
     return 128;
 }
 
@@ -1051,7 +1053,9 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
     }
     if (vm == RSQ) {
         if (epi != EPI_STORE || !mean) return TAGI_E_UNSUPPORTED;
-        return launch_bn<RSQ, true, EPI_STORE>(g, bn, batch, st, what);
+        // the stride-1 col2im gather compiles without divisions
+        return (g.ga.on && g.ga.s == 1) ? launch_bn<RSQ, true, EPI_STORE, 2>(g, bn, batch, st, what)
+                                        : launch_bn<RSQ, true, EPI_STORE, 1>(g, bn, batch, st, what);
     }
     if (!mean) return TAGI_E_UNSUPPORTED;
     switch (epi) {

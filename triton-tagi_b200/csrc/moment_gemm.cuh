@@ -16,37 +16,71 @@ struct ParamEpi {
     float cap;
 };
 
-// Implicit patches on the A side (convolutions without a patch matrix):
-// A[m][r] = x[n][c][oh*s - pt + kh][ow*s - pl + kw], zero outside the input,
-// for rows m = (n, oh, ow) over N x Ho x Wo and reduction index r = tap*C + c
-// with tap = kh*k + kw. Taps outermost: 8 consecutive reduction elements then
-// share one tap (for C a multiple of 8), i.e. one bounds test and 8 addresses
-// a channel plane apart. The B operand is read in the same (tap, c) order.
+// Implicit patches on the A side (convolutions without a patch matrix). Rows
+// m = (n, y, x) run over an N x (L/Wo) x Wo pixel grid, the reduction index is
+// r = tap*C + c with tap = kh*k + kw (taps outermost: 8 consecutive reduction
+// elements then share one tap for C a multiple of 8, i.e. one bounds test and
+// 8 addresses a channel plane apart). The B operand is read in the same order.
+//   mode 0, patches (Conv2D forward): A[m][r] = x[n][c][y*s - pt + kh][x*s - pl + kw]
+//     (triton_tagi/layers/conv2d.py:40-77), zero outside the input;
+//   mode 1, the reference's col2im gather (conv2d.py:119-130) of the deltas of a
+//     C x H x W output onto input pixel (y, x): tap (kh, kw) contributes
+//     x[n][c][oh][ow] with ohn = y + pt - kh, own = x + pl - kw, oh = ohn / s and
+//     ow = own / s truncating toward zero, if ohn % s == 0, 0 <= oh < H and
+//     0 <= ow < W (the column offset is not tested for divisibility);
+//   mode 2, the adjoint of the patches: mode 1 plus ohn, own >= 0 and own % s == 0.
 struct Gather {
     int on;              // 1: A is gathered; arow and ak are unused
-    int C, H, W;         // input channels and size (NCHW)
-    int Wo, L;           // output width, output pixels per image
+    int mode;            // 0 patches, 1 reference col2im gather, 2 adjoint gather
+    int C, H, W;         // gathered tensor's channels and size (NCHW)
+    int Wo, L;           // row pixel grid: width, pixels per image
     int k, s, pt, pl;    // kernel size, stride, top and left padding
 };
 
-// One output pixel's image base and input origin.
+// One row pixel's image base and origin: mode 0, the input position of tap
+// (0, 0); modes 1-2, (y + pt, x + pl).
 struct GatherRow {
     int64_t base;
     int ih0, iw0;
 };
 
 __device__ __forceinline__ GatherRow gather_row(const Gather& ga, int m) {
-    const int n = m / ga.L, r = m - n * ga.L, oh = r / ga.Wo, ow = r - oh * ga.Wo;
-    return GatherRow{static_cast<int64_t>(n) * ga.C * ga.H * ga.W, oh * ga.s - ga.pt,
-                     ow * ga.s - ga.pl};
+    const int n = m / ga.L, r = m - n * ga.L, y = r / ga.Wo, x = r - y * ga.Wo;
+    const int64_t base = static_cast<int64_t>(n) * ga.C * ga.H * ga.W;
+    if (ga.mode == 0) return GatherRow{base, y * ga.s - ga.pt, x * ga.s - ga.pl};
+    return GatherRow{base, y + ga.pt, x + ga.pl};
 }
 
-// Offset of reduction element r of a gathered row, or -1 where the patch lies
-// outside the input.
+// Position of tap (kh, kw) of a gathered row, or false where it contributes 0.
+// MODE: 0 patches, 1 either col2im gather, 2 col2im gather of stride 1, -1 read
+// from ga.mode.
+template <int MODE = -1>
+__device__ __forceinline__ bool gather_tap(const Gather& ga, const GatherRow& gr, int kh, int kw,
+                                           int* ih, int* iw) {
+    if (MODE == 0 || (MODE < 0 && ga.mode == 0)) {
+        *ih = gr.ih0 + kh;
+        *iw = gr.iw0 + kw;
+        return *ih >= 0 && *ih < ga.H && *iw >= 0 && *iw < ga.W;
+    }
+    const int ohn = gr.ih0 - kh, own = gr.iw0 - kw;
+    if (MODE == 2 || ga.s == 1) {  // both gathers are the adjoint of the patches; no division
+        *ih = ohn;
+        *iw = own;
+        return ohn >= 0 && ohn < ga.H && own >= 0 && own < ga.W;
+    }
+    const int oh = ohn / ga.s, ow = own / ga.s;  // C division truncates toward zero
+    *ih = oh;
+    *iw = ow;
+    const bool okh = (ohn % ga.s == 0) && oh >= 0 && oh < ga.H && (ga.mode == 1 || ohn >= 0);
+    const bool okw = ow >= 0 && ow < ga.W && (ga.mode == 1 || (own >= 0 && own % ga.s == 0));
+    return okh && okw;
+}
+
+// Offset of reduction element r of a gathered row, or -1 where it contributes 0.
 __device__ __forceinline__ int64_t gather_off(const Gather& ga, const GatherRow& gr, int r) {
     const int tap = r / ga.C, c = r - tap * ga.C, kh = tap / ga.k, kw = tap - kh * ga.k;
-    const int ih = gr.ih0 + kh, iw = gr.iw0 + kw;
-    if (ih < 0 || ih >= ga.H || iw < 0 || iw >= ga.W) return -1;
+    int ih, iw;
+    if (!gather_tap(ga, gr, kh, kw, &ih, &iw)) return -1;
     return gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
 }
 

@@ -26,7 +26,7 @@ _SIGS = {
     "tagi_moment_forward": "pp" + "iiii" + "ppi" + "pppp" + "iiii" + "iii" + "p",
     "tagi_fused_backward_delta": "ppppp" + "iii" + "iiiiii" + "p",
     "tagi_backward_delta_view": "pp" + "iiii" + "pi" + "pp" + "iiii" + "iii" + "p",
-    "tagi_conv2d_backward_delta_s1": "pppp" + "pp" + "iiiiiii" + "p",
+    "tagi_conv2d_backward_delta": "ppp" + "pp" + "iiiiiiiii" + "n" + "p",
     "tagi_conv2d_forward": "pppppp" + "pp" + "iiiiiiiii" + "p",
     "tagi_fused_weight_grad_workspace_size": "iii",
     "tagi_fused_weight_grad": "ppppp" + "iii" + "iiiiii" + "pz" + "p",

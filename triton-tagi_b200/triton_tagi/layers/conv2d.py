@@ -4,15 +4,16 @@ Forward (conv2d.py:254-309): the fused moment contraction
     μ_z = P_μ @ μ_w + μ_b,  S_z = P_μ² @ S_w + P_S @ (μ_w² + S_w) + S_b
 over the patches P (N·L, C·k·k) gathers them from the NCHW input itself (no
 patch matrix in memory) and writes the result directly in NCHW.
-Backward (conv2d.py:314-371): the patch-space deltas δP = δμ_z @ μ_wᵀ,
-δP_S = δS_z @ (μ_w²)ᵀ read δ in NCHW in place, are folded back to the input
-by the col2im gather, and the weight sums P_μᵀ·δμ_z, (P_μ²)ᵀ·δS_z (bias as a
-row of ones) feed the parameter mode of the layer; the mean patches are made
-for them from the input kept by forward. For stride 1 with symmetric padding
-p the product and the gather together are a convolution of the deltas (padded
-by k-1-p) with the reversed weights, computed as one contraction over (output
-channel, tap) that gathers the delta patches itself and writes NCHW
-(tagi_conv2d_backward_delta_s1).
+Backward (conv2d.py:314-371): the reference forms the patch-space deltas
+δP = δμ_z @ μ_wᵀ, δP_S = δS_z @ (μ_w²)ᵀ and folds them back to the input with
+its col2im gather. For stride 1 one contraction over (tap, output channel) sums
+the same terms: for each input pixel and tap it gathers the deltas at the output
+position the col2im gather maps to (tagi_conv2d_backward_delta), so no
+patch-space deltas exist in memory. For stride s > 1 only about 1/s² of the
+(pixel, tap) pairs contribute, so the patch-space product and the gather
+(tagi_backward_delta_view, tagi_col2im) do fewer flops and stay. The weight sums P_μᵀ·δμ_z, (P_μ²)ᵀ·δS_z
+(bias as a row of ones) feed the parameter mode of the layer; the mean patches
+are made for them from the input kept by forward.
 
 ``col2im_mode``: "reference" (default) gathers exactly as the reference's
 _col2im_kernel (conv2d.py:119-130), which for stride > 1 does not test the
@@ -94,16 +95,15 @@ class Conv2D(LearnableLayer):
         d_ma = torch.empty(N, C, H, W, device=dev)
         d_Sa = torch.empty(N, C, H, W, device=dev)
         k, p = self.kH, self.padding
-        if self.stride == 1 and (self.padding_type == 1 or p == 0) and p <= k - 1:
-            # Stride 1: the patch-space product plus the col2im gather equal a
-            # convolution of the deltas with the reversed weights (both gather
-            # modes agree here): one contraction over (co, tap), no patch-space
-            # output.
-            w_rev = torch.empty(C, Co * k * k, device=dev)
-            lib()("tagi_conv2d_backward_delta_s1", dmz.data_ptr(), dSz.data_ptr(),
-                  self.mw.data_ptr(), w_rev.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H,
-                  W, Co, k, p, st)
+        if self.stride == 1:
+            # One contraction over (tap, co) gathers the deltas as the col2im fold
+            # does (no patch-space deltas in memory).
+            lib()("tagi_conv2d_backward_delta", dmz.data_ptr(), dSz.data_ptr(),
+                  self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, 1, p,
+                  self.padding_type, _COL2IM_MODES[self.col2im_mode], st)
         else:
+            # With stride s only about 1/s² of the (pixel, tap) pairs contribute:
+            # the patch-space product plus the gather does the fewer flops.
             dpm = torch.empty(N * L, K, device=dev)
             dpS = torch.empty(N * L, K, device=dev)
             lib()("tagi_backward_delta_view", dmz.data_ptr(), dSz.data_ptr(), *d_map,
@@ -112,6 +112,7 @@ class Conv2D(LearnableLayer):
             lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(),
                   N, C, H, W, k, self.stride, p, self.padding_type,
                   _COL2IM_MODES[self.col2im_mode], st)
+            del dpm, dpS
         pm = torch.empty(N * L, K, device=dev)
         lib()("tagi_im2col", self.input_ma.data_ptr(), None, pm.data_ptr(), None, N, C, H, W, k,
               self.stride, p, self.padding_type, st)
