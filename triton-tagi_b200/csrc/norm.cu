@@ -236,6 +236,35 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     }
 }
 
+// The same, 4 elements of one channel plane per thread (H*W a multiple of 4).
+__global__ void bn_forward_v4_kernel(const float4* mz, const float4* Sz, const float* mean,
+                                     const float* var, const float* mg, const float* Sg,
+                                     const float* mb, const float* Sb, float4* ma, float4* Sa,
+                                     float4* mhat, float4* Shat, int64_t total4, int C, int HW4,
+                                     float eps) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>((i / HW4) % C);
+        const float rs = var[c], mu = mean[c];
+        const float inv_std = 1.0f / sqrtf(rs + eps);
+        const float g = mg[c], sg = Sg[c], b = mb[c], sb = Sb[c];
+        const float4 m = mz[i], S = Sz[i];
+        const float mv[4] = {m.x, m.y, m.z, m.w}, Sv[4] = {S.x, S.y, S.z, S.w};
+        float om[4], oS[4], mh[4], Sh[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            mh[e] = (mv[e] - mu) * inv_std;
+            Sh[e] = Sv[e] / (rs + eps);
+            om[e] = g * mh[e] + b;
+            oS[e] = g * g * Sh[e] + sg * mh[e] * mh[e] + sg * Sh[e] + sb;
+        }
+        ma[i] = make_float4(om[0], om[1], om[2], om[3]);
+        Sa[i] = make_float4(oS[0], oS[1], oS[2], oS[3]);
+        if (mhat) mhat[i] = make_float4(mh[0], mh[1], mh[2], mh[3]);
+        if (Shat) Shat[i] = make_float4(Sh[0], Sh[1], Sh[2], Sh[3]);
+    }
+}
+
 // Deltas S*g_m, S^2*g_S from float64 sums, written out or applied with the cap.
 __device__ __forceinline__ void vector_apply(int64_t i, double gm, double gS, int mode, float* m,
                                              float* S, float* d_m, float* d_S, float cap) {
@@ -380,8 +409,19 @@ extern "C" int tagi_bn_forward(const float* mz, const float* Sz, const float* me
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(mz && Sz && mean && var && mg && Sg && mb && Sb && ma && Sa, TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
-    bn_forward_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
-        mz, Sz, mean, var, mg, Sg, mb, Sb, ma, Sa, m_hat, S_hat, total, (int)C, (int)HW, eps);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(mz) | reinterpret_cast<uintptr_t>(Sz) |
+                         reinterpret_cast<uintptr_t>(ma) | reinterpret_cast<uintptr_t>(Sa) |
+                         reinterpret_cast<uintptr_t>(m_hat) | reinterpret_cast<uintptr_t>(S_hat);
+    if (HW % 4 == 0 && (al & 15) == 0) {
+        bn_forward_v4_kernel<<<grid_1d(total / 4, 256), 256, 0, as_stream(stream)>>>(
+            reinterpret_cast<const float4*>(mz), reinterpret_cast<const float4*>(Sz), mean, var,
+            mg, Sg, mb, Sb, reinterpret_cast<float4*>(ma), reinterpret_cast<float4*>(Sa),
+            reinterpret_cast<float4*>(m_hat), reinterpret_cast<float4*>(S_hat), total / 4, (int)C,
+            (int)(HW / 4), eps);
+    } else {
+        bn_forward_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
+            mz, Sz, mean, var, mg, Sg, mb, Sb, ma, Sa, m_hat, S_hat, total, (int)C, (int)HW, eps);
+    }
     return check_launch(what);
 }
 

@@ -43,6 +43,10 @@ class LearnableLayer(Layer):
     _param_mode: str = "deltas"
     _cap: float | None = None
     _reducer = None
+    # Set by Sequential.step on its first layer while it runs backward: the input
+    # deltas that backward returns are discarded there, so layers that honour it
+    # skip computing them (and return None) but still form their parameter sums.
+    _skip_input_delta: bool = False
     _updated_in_backward: bool = False
 
     @abstractmethod

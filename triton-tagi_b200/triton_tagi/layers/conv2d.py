@@ -92,27 +92,29 @@ class Conv2D(LearnableLayer):
         dev = dmz.device
         st = stream(dmz)
         d_map = (L, Co * L, 1, L)  # NCHW delta read as an (N·L) x Co matrix
-        d_ma = torch.empty(N, C, H, W, device=dev)
-        d_Sa = torch.empty(N, C, H, W, device=dev)
         k, p = self.kH, self.padding
-        if self.stride == 1:
-            # One contraction over (tap, co) gathers the deltas as the col2im fold
-            # does (no patch-space deltas in memory).
-            lib()("tagi_conv2d_backward_delta", dmz.data_ptr(), dSz.data_ptr(),
-                  self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, 1, p,
-                  self.padding_type, _COL2IM_MODES[self.col2im_mode], st)
-        else:
-            # With stride s only about 1/s² of the (pixel, tap) pairs contribute:
-            # the patch-space product plus the gather does the fewer flops.
-            dpm = torch.empty(N * L, K, device=dev)
-            dpS = torch.empty(N * L, K, device=dev)
-            lib()("tagi_backward_delta_view", dmz.data_ptr(), dSz.data_ptr(), *d_map,
-                  self.mw.data_ptr(), Co, dpm.data_ptr(), dpS.data_ptr(), 0, 0, K, 1, N * L, K, Co,
-                  st)
-            lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(),
-                  N, C, H, W, k, self.stride, p, self.padding_type,
-                  _COL2IM_MODES[self.col2im_mode], st)
-            del dpm, dpS
+        d_ma = d_Sa = None
+        if not self._skip_input_delta:
+            d_ma = torch.empty(N, C, H, W, device=dev)
+            d_Sa = torch.empty(N, C, H, W, device=dev)
+            if self.stride == 1:
+                # One contraction over (tap, co) gathers the deltas as the col2im fold
+                # does (no patch-space deltas in memory).
+                lib()("tagi_conv2d_backward_delta", dmz.data_ptr(), dSz.data_ptr(),
+                      self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, 1,
+                      p, self.padding_type, _COL2IM_MODES[self.col2im_mode], st)
+            else:
+                # With stride s only about 1/s² of the (pixel, tap) pairs contribute:
+                # the patch-space product plus the gather does the fewer flops.
+                dpm = torch.empty(N * L, K, device=dev)
+                dpS = torch.empty(N * L, K, device=dev)
+                lib()("tagi_backward_delta_view", dmz.data_ptr(), dSz.data_ptr(), *d_map,
+                      self.mw.data_ptr(), Co, dpm.data_ptr(), dpS.data_ptr(), 0, 0, K, 1, N * L,
+                      K, Co, st)
+                lib()("tagi_col2im", dpm.data_ptr(), dpS.data_ptr(), d_ma.data_ptr(),
+                      d_Sa.data_ptr(), N, C, H, W, k, self.stride, p, self.padding_type,
+                      _COL2IM_MODES[self.col2im_mode], st)
+                del dpm, dpS
         pm = torch.empty(N * L, K, device=dev)
         lib()("tagi_im2col", self.input_ma.data_ptr(), None, pm.data_ptr(), None, N, C, H, W, k,
               self.stride, p, self.padding_type, st)

@@ -56,11 +56,15 @@ class Linear(LearnableLayer):
         dm = delta_mz.reshape(-1, N).contiguous()
         dS = delta_Sz.reshape(-1, N).contiguous()
         M = dm.shape[0]
-        d_ma = torch.empty(M, K, device=dm.device)
-        d_Sa = torch.empty(M, K, device=dm.device)
-        lib()("tagi_fused_backward_delta", dm.data_ptr(), dS.data_ptr(), self.mw.data_ptr(),
-              d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, N, 1, N, 1, K, 1, stream(dm))
+        d_ma = d_Sa = None
+        if not self._skip_input_delta:
+            d_ma = torch.empty(M, K, device=dm.device)
+            d_Sa = torch.empty(M, K, device=dm.device)
+            lib()("tagi_fused_backward_delta", dm.data_ptr(), dS.data_ptr(), self.mw.data_ptr(),
+                  d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, N, 1, N, 1, K, 1, stream(dm))
         weight_param_backward(self, self.ma_in, K, (dm, dS), (0, 0, N, 1), M, K, N, self.has_bias)
+        if d_ma is None:
+            return None, None
         shp = (*self._input_shape[:-1], K)
         return d_ma.reshape(shp), d_Sa.reshape(shp)
 

@@ -87,9 +87,12 @@ class Sequential:
         learn = self.learnable_layers()
         for layer in learn:
             layer._set_param_mode(mode, cap, red)
+        first = self.layers[0] if self.layers else None
         try:
             if red is not None:
                 red.begin_step()
+            if isinstance(first, LearnableLayer):
+                first._skip_input_delta = True  # the input's deltas are not used
             for layer in reversed(self.layers):
                 delta_mu, delta_var = layer.backward(delta_mu, delta_var)
             if red is not None:
@@ -97,6 +100,8 @@ class Sequential:
             for layer in learn:
                 layer.update(cap)
         finally:
+            if isinstance(first, LearnableLayer):
+                first._skip_input_delta = False
             for layer in learn:
                 layer._set_param_mode("deltas")
         return y_pred_mu, y_pred_var
