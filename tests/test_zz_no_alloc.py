@@ -66,7 +66,7 @@ def test_static_scratch_refuses_shapes_beyond_its_size():
     from triton_tagi._lib import lib
 
     L = lib()
-    M, K, N = 1024, 4672, 256  # split plan needs ~19 MB of partial sums
+    M, K, N = 8192, 2304, 512  # two-way split plan: 18.9 MB of partial sums
     assert L.size("tagi_fused_weight_grad_workspace_size", M, K, N) > STATIC_BYTES
     a, dmz, dSz = _inputs(M, K, N, 7)
     with pytest.raises(RuntimeError, match="static"):

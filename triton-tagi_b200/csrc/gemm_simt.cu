@@ -217,13 +217,31 @@ inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b)
 // (tensor-core or CUDA-core tiles) that will run the shape.
 void choose_splits(int M, int N, int Kr, int batch, int* splits, int* kchunk, int* bn_tc) {
     const int tc = tc_pick(LSQ, M, N, Kr, batch);
-    const int tm = tc ? kTcBM : BM, tn = tc ? tc : BN;
     int s = 1;
-    const int tiles = cdiv(M, tm) * cdiv(N, tn) * batch;
-    if (batch == 1 && tiles < 2 * kNumSMs) {
-        s = cdiv(2 * kNumSMs, tiles);
-        s = std::min(s, std::max(1, Kr / (BK * 8)));
-        s = std::min(s, 64);
+    if (tc) {
+        // Tensor cores: CTAs come in pairs of 256 rows. Pick the split count that
+        // minimises waves x (K-blocks per CTA + the cost of one partial epilogue,
+        // about 8 K-blocks), i.e. fills the last wave without splitting needlessly.
+        const int64_t ctas = 2 * static_cast<int64_t>(cdiv(M, 256)) * cdiv(N, tc) * batch;
+        const int smax = std::min(64, std::max(1, Kr / (BK * 8)));
+        if (batch == 1 && ctas < 2 * kNumSMs) {
+            int64_t best = -1;
+            for (int t = 1; t <= smax; ++t) {
+                const int64_t waves = (ctas * t + kNumSMs - 1) / kNumSMs;
+                const int64_t cost = waves * (cdiv(Kr, t * BK) + 8);
+                if (best < 0 || cost < best) {
+                    best = cost;
+                    s = t;
+                }
+            }
+        }
+    } else {
+        const int tiles = cdiv(M, BM) * cdiv(N, BN) * batch;
+        if (batch == 1 && tiles < 2 * kNumSMs) {
+            s = cdiv(2 * kNumSMs, tiles);
+            s = std::min(s, std::max(1, Kr / (BK * 8)));
+            s = std::min(s, 64);
+        }
     }
     int chunk = cdiv(cdiv(Kr, s), BK) * BK;
     if (chunk < BK) chunk = BK;
