@@ -216,7 +216,7 @@ inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b)
 // Reduction split for output grids too small to fill the GPU, for the kernel
 // (tensor-core or CUDA-core tiles) that will run the shape.
 void choose_splits(int M, int N, int Kr, int batch, int* splits, int* kchunk, int* bn_tc) {
-    const int tc = tc_pick(LSQ, M, N, Kr, batch);
+    const int tc = tc_pick(LSQ, M, N, Kr, batch, false);  // splits fill the machine
     int s = 1;
     if (tc) {
         // Tensor cores: CTAs come in pairs of 256 rows. Pick the split count that

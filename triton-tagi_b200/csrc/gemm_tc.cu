@@ -1030,17 +1030,18 @@ int launch_bn(const GemmArgs& g, int bn, int batch, cudaStream_t st, const char*
 
 }  // namespace
 
-int tc_pick(int vm, int M, int N, int Kr, int batch) {
+int tc_pick(int vm, int M, int N, int Kr, int batch, bool fill) {
     (void)vm;
     if (!tc_enabled()) return 0;
     if (M < 64 || N < 16 || Kr < 32) return 0;
     if (static_cast<double>(M) * N * Kr < 4.0e6) return 0;
     if (N <= 32) return 32;
-    if (N <= 64) return 64;
-    // 128 columns even when the grid is under one wave: 64-column tiles halve the
-    // tensor work per staged A element, and that costs more than the idle SMs.
-    (void)batch;
-    return 128;
+    if (N <= 64 || !fill) return N <= 64 ? 64 : 128;
+    // 64-column tiles halve the tensor work per staged A element, so they pay
+    // only when 128-column tiles would leave more than half of the SMs idle.
+    const int64_t ctas = 2 * ((static_cast<int64_t>(M) + 255) / 256) * ((N + 127) / 128) *
+                         static_cast<int64_t>(batch);
+    return 2 * ctas <= kNumSMs ? 64 : 128;
 }
 
 int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, cudaStream_t st,

@@ -134,8 +134,10 @@ __device__ __forceinline__ void param_epilogue(int r, int c, float g0, float g1,
 }
 
 
-// tcgen05 path (gemm_tc.cu). tc_pick returns the N tile (0 = use CUDA cores).
-int tc_pick(int vm, int M, int N, int Kr, int batch);
+// tcgen05 path (gemm_tc.cu). tc_pick returns the N tile (0 = use CUDA cores);
+// with `fill` it narrows the tile when the grid would leave most SMs idle (for
+// launches that do not fill the machine with split reductions).
+int tc_pick(int vm, int M, int N, int Kr, int batch, bool fill = true);
 int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, cudaStream_t st,
               const char* what);
 constexpr int kTcBM = 128;
