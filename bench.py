@@ -297,7 +297,10 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     torch.cuda.set_device(dev)
     B = WORKLOADS[args.workload]["batch"]
     torch.manual_seed(1234)
-    net = TT.Sequential(build_layers(args.workload, TT, dev), device=dev)
+    # Steps of small networks are a few dozen short kernels: replay them from a
+    # CUDA graph (Sequential(cuda_graph=True); single GPU only).
+    graphed = args.workload in ("mlp", "cnn") and world == 1 and not args.no_graph
+    net = TT.Sequential(build_layers(args.workload, TT, dev), device=dev, cuda_graph=graphed)
     if world > 1:
         from triton_tagi.distributed import DataParallel
 
@@ -309,8 +312,12 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
+    per_step = None
+    for i in range(args.warmup):
+        l0 = kernel_launches()
         net.step(x, y, SIGMA_V)
+        if i == 1:
+            per_step = kernel_launches() - l0  # the captured (or eager) step's launches
     torch.cuda.synchronize()
 
     timer = LaunchTimer()
@@ -331,8 +338,20 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         torch.cuda.synchronize()
         barrier()
     launches = kernel_launches() - launches0
+    if graphed:
+        # replays launch without passing through the library's host calls
+        launches = per_step * args.steps
     step_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) * 1e-3
     fam = timer.summary()
+    if graphed:
+        # per-kernel timing of one eager step (outside the timed region)
+        net.cuda_graph = False
+        L.hook = timer
+        net.step(x, y, SIGMA_V)
+        L.hook = None
+        net.cuda_graph = True
+        torch.cuda.synchronize()
+        fam = timer.summary()
 
     # end to end through the public API: pinned host inputs in, predictions out
     xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
@@ -384,7 +403,8 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "batch_per_gpu": B, "global_batch": B * world,
                    "sigma_v": SIGMA_V, "parallelism": f"dp{world}",
-                   "l2": "flushed between steps (256 MiB write outside the timed events)"},
+                   "l2": "flushed between steps (256 MiB write outside the timed events)",
+                   "cuda_graph": graphed},
         "e2e": {"value": args.steps * B * world / e2e_s, "unit": "samples/s",
                 "h2d_bytes_per_step": (xh.numel() + yh.numel()) * 4,
                 "d2h_bytes_per_step": (mu_h.numel() + var_h.numel()) * 4},
@@ -495,6 +515,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="r18")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="mlp/cnn: run the steps eagerly instead of replaying a CUDA graph")
     ap.add_argument("--shape", default=None, help="swp workload: one 'M,K' shape (K = N)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

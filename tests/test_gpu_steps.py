@@ -134,3 +134,29 @@ def test_mlp_100_step_trajectory():
     vs_oracle = max(rel_err(a, b) for a, b in zip(pdev, p32))
     assert drift_dev <= 2 * drift_ref + 1e-4, (drift_dev, drift_ref)
     assert vs_oracle <= 1e-2, vs_oracle
+
+
+@pytest.mark.parametrize("name,batch", [("mlp", 64), ("cnn", 16)])
+def test_cuda_graph_steps_equal_eager_steps(name, batch):
+    """Sequential(cuda_graph=True) replays the eager step's kernels: predictions
+    and parameters after several steps (eager, capture + replay, replays, then a
+    new batch shape that is captured again) are bit-identical to eager steps."""
+    torch.manual_seed(7)
+    eager = build_config(name, TT, device=DEV)
+    graphed = build_config(name, TT, device=DEV)
+    copy_params(eager, graphed, DEV)
+    net_e = TT.Sequential(eager, device=DEV)
+    net_g = TT.Sequential(graphed, device=DEV, cuda_graph=True)
+    gen = torch.Generator().manual_seed(3)
+    for step, b in enumerate((batch, batch, batch, batch, batch // 2, batch // 2, batch // 2)):
+        if name == "mlp":
+            x = torch.randn(b, 784, generator=gen)
+        else:
+            x = torch.randn(b, 3, 32, 32, generator=gen)
+        y = torch.nn.functional.one_hot(torch.randint(0, 10, (b,), generator=gen), 10).float()
+        x, y = x.to(DEV), y.to(DEV)
+        mu_e, var_e = net_e.step(x, y, 0.05)
+        mu_g, var_g = net_g.step(x, y, 0.05)
+        assert torch.equal(mu_e, mu_g) and torch.equal(var_e, var_g), f"step {step}"
+    for i, (a, b) in enumerate(zip(params(eager), params(graphed))):
+        assert torch.equal(a, b), f"param {i}"

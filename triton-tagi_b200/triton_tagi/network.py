@@ -14,6 +14,13 @@ returns the pre-update predictions, exactly as the reference
 * Under data parallelism (``triton_tagi.distributed``) the batch sums of every
   layer are all-reduced before the update and the cap factor uses the global
   batch, so every replica applies the single-batch closed form.
+
+``cuda_graph=True`` replays each step from a CUDA graph: the first step with a
+new input shape (or σ_v) runs eagerly, the next one is captured on static input
+buffers and replayed, and later steps copy their inputs in and replay. A step
+of small layers is a few dozen short kernels, so launch overhead otherwise
+dominates it. The replayed kernels are the eager step's; returned predictions
+are copies. Not used under data parallelism (the step then runs eagerly).
 """
 
 from __future__ import annotations
@@ -29,10 +36,13 @@ from .update.parameters import get_cap_factor
 
 
 class Sequential:
-    def __init__(self, layers: list, device="cuda", fuse_update: bool = True) -> None:
+    def __init__(self, layers: list, device="cuda", fuse_update: bool = True,
+                 cuda_graph: bool = False) -> None:
         self.device = torch.device(device)
         self.layers = layers
         self.fuse_update = fuse_update
+        self.cuda_graph = cuda_graph
+        self._graph = None  # (key, CUDAGraph or None, static x, static y, outputs)
         self.reducer = None  # set by triton_tagi.distributed.DataParallel
         for layer in self.layers:
             if isinstance(layer, ResBlock):
@@ -78,6 +88,32 @@ class Sequential:
         return ma, Sa
 
     def step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
+        if self.cuda_graph and self.reducer is None and x_batch.is_cuda:
+            return self._graph_step(x_batch, y_batch, sigma_v)
+        return self._step(x_batch, y_batch, sigma_v)
+
+    def _graph_step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
+        key = (tuple(x_batch.shape), x_batch.dtype, tuple(y_batch.shape), y_batch.dtype,
+               float(sigma_v), x_batch.device)
+        if self._graph is None or self._graph[0] != key:
+            # first step of this shape: eager (it also leaves every layer in its
+            # steady state, e.g. BatchNorm's running statistics initialised)
+            self._graph = (key, None, None, None, None)
+            return self._step(x_batch, y_batch, sigma_v)
+        _, graph, sx, sy, out = self._graph
+        if graph is None:
+            sx, sy = x_batch.clone(), y_batch.clone()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = self._step(sx, sy, sigma_v)
+            self._graph = (key, graph, sx, sy, out)
+        else:
+            sx.copy_(x_batch)
+            sy.copy_(y_batch)
+        graph.replay()
+        return out[0].clone(), out[1].clone()
+
+    def _step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
         red = self.reducer
         global_batch = x_batch.shape[0] * (red.world_size if red is not None else 1)
         y_pred_mu, y_pred_var = self.forward(x_batch)
