@@ -97,7 +97,8 @@ int tagi_backward_delta_view(const float* dmz, const float* dSz, int64_t d_div, 
 int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
                         const float* mb, const float* Sb, float* mz, float* Sz, int64_t N,
                         int64_t C, int64_t H, int64_t W, int64_t Co, int64_t k, int64_t stride,
-                        int64_t padding, int64_t padding_type, void* stream);
+                        int64_t padding, int64_t padding_type, void* workspace,
+                        size_t workspace_bytes, void* stream);
 
 /* Conv2D input deltas, written in NCHW (N x C x H x W). The reference forms the
  * patch-space deltas dP = dmz @ mw^T, dP_S = dSz @ (mw^2)^T (rows (n, oh, ow),
@@ -112,7 +113,31 @@ int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const
 int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, const float* mw, float* d_ma,
                                float* d_Sa, int64_t N, int64_t C, int64_t H, int64_t W,
                                int64_t Co, int64_t k, int64_t stride, int64_t padding,
-                               int64_t padding_type, int col2im_mode, void* stream);
+                               int64_t padding_type, int col2im_mode, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Optional workspace of the entries above and below that write an M x N output
+ * through a reduction of length K (tagi_linear_forward: M, N, K; its backward
+ * delta: M, K, N; tagi_conv2d_forward: N*Ho*Wo, Co, C*k*k; tagi_conv2d_backward_delta:
+ * N*H*W, C, Co*k*k). When the output grid leaves SMs idle the reduction is split
+ * into partial sums there and added in split order; with less workspace (or
+ * none) the contraction runs unsplit. Host only; 0 when no split is planned. */
+size_t tagi_store_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/* Linear forward: mz = ma @ mw + mb, Sz = ma^2 @ Sw + Sa @ (mw^2 + Sw) + Sb for
+ * row-major ma, Sa (M x K), mw, Sw (K x N), mb, Sb (N); workspace as above.
+ * Replaces Linear.forward, triton_tagi/layers/linear.py:92-104. */
+int tagi_linear_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
+                        const float* mb, const float* Sb, float* mz, float* Sz, int64_t M,
+                        int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* Linear input deltas: d_ma = dmz @ mw^T, d_Sa = dSz @ (mw^2)^T for row-major dmz,
+ * dSz (M x N) and mw (K x N); workspace as above. Replaces the delta part of
+ * Linear.backward, triton_tagi/layers/linear.py:118-136. */
+int tagi_linear_backward_delta(const float* dmz, const float* dSz, const float* mw, float* d_ma,
+                               float* d_Sa, int64_t M, int64_t K, int64_t N, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* grad_mw = a^T @ dmz, grad_Sw = (a^2)^T @ dSz  (K x N outputs).
  * Replaces triton_fused_weight_grad, triton_tagi/kernels/common.py:410-451. */

@@ -91,6 +91,78 @@ def test_weight_sums_long_reduction_split():
     _ok()
 
 
+@pytest.mark.parametrize("M,K,N", [(256, 4096, 1024), (96, 3000, 600), (32, 2048, 512)])
+def test_linear_entries_split_reduction(M, K, N):
+    """tagi_linear_forward / tagi_linear_backward_delta with the workspace the
+    library asks for (the reduction split over idle SMs, partials added in split
+    order) and without one (unsplit): both against the float64 oracle. The last
+    shape runs on the CUDA-core kernel."""
+    from triton_tagi._lib import lib, stream, workspace
+
+    L = lib()
+    g = torch.Generator().manual_seed(M + 7 * K + N)
+    ma, Sa = _rnd(g, M, K), _rnd(g, M, K, u=True, scale=1e-2, lo=1e-4)
+    mw, Sw = _rnd(g, K, N, scale=K**-0.5), _rnd(g, K, N, u=True, scale=1.0 / K)
+    mb, Sb = _rnd(g, N, scale=0.1), _rnd(g, N, u=True, scale=1e-3)
+    dmz, dSz = _rnd(g, M, N, scale=0.1), -_rnd(g, M, N, u=True, scale=1e-2)
+    dv = [t.to(DEV) for t in (ma, Sa, mw, Sw, mb, Sb, dmz, dSz)]
+    d = lambda t: t.double()  # noqa: E731
+    ex_m = F.mean_forward(d(ma), d(mw), d(mb).view(1, -1))
+    ex_S = F.var_forward(d(ma), d(Sa), d(mw), d(Sw), d(Sb).view(1, -1))
+    r_ma, r_Sa = F.backward_delta(d(dmz), d(dSz), d(mw))
+    nf = L.size("tagi_store_workspace_size", M, N, K)
+    nb = L.size("tagi_store_workspace_size", M, K, N)
+    assert nf > 0 and nb > 0, "shape chosen to split the reduction"
+    for split in (True, False):
+        mz, Sz = torch.empty(M, N, device=DEV), torch.empty(M, N, device=DEV)
+        hold, wp, wn = workspace(nf if split else 0, mz)
+        L("tagi_linear_forward", *(t.data_ptr() for t in dv[:6]), mz.data_ptr(), Sz.data_ptr(),
+          M, K, N, wp, wn, stream(mz))
+        d_ma, d_Sa = torch.empty(M, K, device=DEV), torch.empty(M, K, device=DEV)
+        hold2, wp, wn = workspace(nb if split else 0, mz)
+        L("tagi_linear_backward_delta", dv[6].data_ptr(), dv[7].data_ptr(), dv[2].data_ptr(),
+          d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, wp, wn, stream(mz))
+        assert_rel(mz, ex_m, MEAN_RTOL, f"mz split={split}")
+        assert_rel(Sz, ex_S, VAR_RTOL, f"Sz split={split}")
+        assert_rel(d_ma, r_ma, MEAN_RTOL, f"d_ma split={split}")
+        assert_rel(d_Sa, r_Sa, VAR_RTOL, f"d_Sa split={split}")
+        _ok()
+
+
+def test_conv_layer_small_maps_split_reduction():
+    """A late-stage Conv2D (4x4 maps, 256 channels): the forward and stride-1
+    input-delta contractions leave SMs idle, so the layer passes the library's
+    workspace and the reduction over (tap, channel) is split."""
+    import oracle.net as ON
+    from triton_tagi import Conv2D
+    from triton_tagi._lib import lib
+
+    C = Co = 256
+    N, H, W, k = 8, 4, 4, 3
+    assert lib().size("tagi_store_workspace_size", N * H * W, Co, C * k * k) > 0
+    assert lib().size("tagi_store_workspace_size", N * H * W, C, Co * k * k) > 0
+    g = torch.Generator().manual_seed(12)
+    torch.manual_seed(6)
+    ref = ON.Conv2D(C, Co, k, 1, 1, 1)
+    dev = Conv2D(C, Co, k, 1, 1, 1, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, getattr(ref, n).to(DEV))
+    ma, Sa = _rnd(g, N, C, H, W), _rnd(g, N, C, H, W, u=True, scale=0.1)
+    d = lambda t: t.double()  # noqa: E731
+    ex_m, ex_S, _ = F.conv_forward(d(ma), d(Sa), d(ref.mw), d(ref.Sw), d(ref.mb), d(ref.Sb),
+                                   k, 1, 1, 1)
+    mz, Sz = dev.forward(ma.to(DEV), Sa.to(DEV))
+    assert_rel(mz, ex_m, MEAN_RTOL, "mz")
+    assert_rel(Sz, ex_S, VAR_RTOL, "Sz")
+    ref.forward(ma, Sa)
+    dmz, dSz = _rnd(g, *ex_m.shape, scale=0.1), -_rnd(g, *ex_m.shape, u=True, scale=1e-2)
+    r_dm, r_dS = ref.backward(dmz, dSz)
+    d_dm, d_dS = dev.backward(dmz.to(DEV), dSz.to(DEV))
+    assert_rel(d_dm, r_dm, MEAN_RTOL, "d_ma")
+    assert_rel(d_dS, r_dS, VAR_RTOL, "d_Sa")
+    _ok()
+
+
 @pytest.mark.parametrize("mode", ["deltas", "update"])
 def test_linear_parameter_epilogue(mode):
     import oracle.net as ON
@@ -265,7 +337,8 @@ def test_conv_backward_delta_entry_strided_gathers(C, Co, k, s, p, pt, mode):
     d_ma = torch.empty(N, C, H, W, device=DEV)
     d_Sa = torch.empty_like(d_ma)
     lib()("tagi_conv2d_backward_delta", d_dmz.data_ptr(), d_dSz.data_ptr(), d_mw.data_ptr(),
-          d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, s, p, pt, mode, stream(d_ma))
+          d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, s, p, pt, mode, None, 0,
+          stream(d_ma))
     dm = dmz.double().permute(0, 2, 3, 1).reshape(-1, Co)
     dS = dSz.double().permute(0, 2, 3, 1).reshape(-1, Co)
     dpm, dpS = F.backward_delta(dm, dS, mw.double())

@@ -306,6 +306,34 @@ int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaSt
                  : launch<LSQ, true, EPI_STORE>(g, 1, st, what, bn_tc);
 }
 
+// Store-epilogue contractions (forward, input deltas) whose output grid leaves
+// SMs idle: split the reduction into a caller workspace when it holds the plan,
+// else run unsplit (the workspace only buys speed).
+template <int VM>
+int run_store(GemmArgs& g, void* ws, size_t ws_bytes, cudaStream_t st, const char* what) {
+    int splits, chunk, bn_tc;
+    choose_splits(g.M, g.N, g.Kr, 1, &splits, &chunk, &bn_tc);
+    const size_t need = sizeof(float) * 2ull * splits * static_cast<size_t>(g.M) * g.N;
+    if (splits > 1 && ws != nullptr && ws_bytes >= need) {
+        g.splits = splits;
+        g.kchunk = chunk;
+        g.ws = static_cast<float*>(ws);
+        int rc = launch<VM, true, EPI_PARTIAL>(g, 1, st, what, bn_tc);
+        if (rc) return rc;
+        splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(g.M) * g.N, 256), 256, 0, st>>>(g, 0);
+        return check_launch(what);
+    }
+    g.splits = 1;
+    g.kchunk = g.Kr > 0 ? g.Kr : BK;
+    return launch<VM, true, EPI_STORE>(g, 1, st, what);
+}
+
+size_t store_ws_bytes(int M, int N, int Kr) {
+    int splits, chunk, bn_tc;
+    choose_splits(M, N, Kr, 1, &splits, &chunk, &bn_tc);
+    return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(M) * N : 0;
+}
+
 size_t wgrad_ws_bytes(int Mo, int N, int Kr) {
     int splits, chunk, bn_tc;
     choose_splits(Mo, N, Kr, 1, &splits, &chunk, &bn_tc);
@@ -403,7 +431,8 @@ extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float
                                    const float* Sw, const float* mb, const float* Sb, float* mz,
                                    float* Sz, int64_t N, int64_t C, int64_t H, int64_t W,
                                    int64_t Co, int64_t k, int64_t stride, int64_t padding,
-                                   int64_t padding_type, void* stream) {
+                                   int64_t padding_type, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
     const char* what = "tagi_conv2d_forward";
     TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && stride >= 1 &&
                      padding >= 0 && (padding_type == 1 || padding_type == 2),
@@ -428,15 +457,16 @@ extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float
     g.bias0 = mb; g.bias1 = Sb;
     // outputs straight into NCHW: row (n, l) -> n*Co*L + l, column c -> c*L
     g.o0 = mz; g.o1 = Sz; g.orow = RowMap{L, Co * L, 1}; g.on = L;
-    g.M = (int)M; g.N = (int)Co; g.Kr = (int)Kr; g.kchunk = Kr > 0 ? (int)Kr : BK;
-    return launch<FULL, true, EPI_STORE>(g, 1, as_stream(stream), what);
+    g.M = (int)M; g.N = (int)Co; g.Kr = (int)Kr;
+    return run_store<FULL>(g, workspace, workspace_bytes, as_stream(stream), what);
 }
 
 extern "C" int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, const float* mw,
                                           float* d_ma, float* d_Sa, int64_t N, int64_t C,
                                           int64_t H, int64_t W, int64_t Co, int64_t k,
                                           int64_t stride, int64_t padding, int64_t padding_type,
-                                          int col2im_mode, void* stream) {
+                                          int col2im_mode, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
     const char* what = "tagi_conv2d_backward_delta";
     TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && stride >= 1 &&
                      padding >= 0 && (padding_type == 1 || padding_type == 2) &&
@@ -465,8 +495,50 @@ extern "C" int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, co
     g.u = mw; g.brow = plain_rows(1); g.bn = Kr;
     // outputs straight into NCHW: row (n, hw) -> n*C*HW + hw, column c -> c*HW
     g.o0 = d_ma; g.o1 = d_Sa; g.orow = RowMap{HW, C * HW, 1}; g.on = HW;
-    g.M = (int)M; g.N = (int)C; g.Kr = (int)Kr; g.kchunk = Kr > 0 ? (int)Kr : BK;
-    return launch<RSQ, true, EPI_STORE>(g, 1, as_stream(stream), what);
+    g.M = (int)M; g.N = (int)C; g.Kr = (int)Kr;
+    return run_store<RSQ>(g, workspace, workspace_bytes, as_stream(stream), what);
+}
+
+extern "C" size_t tagi_store_workspace_size(int64_t M, int64_t N, int64_t K) {
+    if (bad_size(M) || bad_size(N) || bad_size(K)) return 0;
+    return store_ws_bytes((int)M, (int)N, (int)K);
+}
+
+extern "C" int tagi_linear_forward(const float* ma, const float* Sa, const float* mw,
+                                   const float* Sw, const float* mb, const float* Sb, float* mz,
+                                   float* Sz, int64_t M, int64_t K, int64_t N, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    const char* what = "tagi_linear_forward";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (M == 0 || N == 0) return TAGI_OK;
+    TAGI_REQUIRE(mz && Sz && (K == 0 || (ma && Sa && mw && Sw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = ma; g.y = Sa; g.arow = plain_rows(K); g.ak = 1;
+    g.u = mw; g.v = Sw; g.brow = plain_rows(N); g.bn = 1;
+    g.bias0 = mb; g.bias1 = Sb;
+    g.o0 = mz; g.o1 = Sz; g.orow = plain_rows(N); g.on = 1;
+    g.M = (int)M; g.N = (int)N; g.Kr = (int)K;
+    return run_store<FULL>(g, workspace, workspace_bytes, as_stream(stream), what);
+}
+
+extern "C" int tagi_linear_backward_delta(const float* dmz, const float* dSz, const float* mw,
+                                          float* d_ma, float* d_Sa, int64_t M, int64_t K,
+                                          int64_t N, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+    const char* what = "tagi_linear_backward_delta";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
+                 what);
+    if (M == 0 || K == 0) return TAGI_OK;
+    TAGI_REQUIRE(d_ma && d_Sa && (N == 0 || (dmz && dSz && mw)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = dmz; g.y = dSz; g.arow = plain_rows(N); g.ak = 1;
+    g.u = mw; g.brow = plain_rows(1); g.bn = N;  // u[r = k][j = n] = mw[k, n]
+    g.o0 = d_ma; g.o1 = d_Sa; g.orow = plain_rows(K); g.on = 1;
+    g.M = (int)M; g.N = (int)K; g.Kr = (int)N;
+    return run_store<RSQ>(g, workspace, workspace_bytes, as_stream(stream), what);
 }
 
 extern "C" int tagi_fused_backward_delta(const float* dmz, const float* dSz, const float* mw,

@@ -1048,15 +1048,20 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
               const char* what) {
     if (g.M == 0 || g.N == 0) return TAGI_OK;
     if (vm == FULL) {
+        if (epi == EPI_PARTIAL && mean) return launch_bn<FULL, true, EPI_PARTIAL>(g, bn, batch, st, what);
         if (epi != EPI_STORE) return TAGI_E_UNSUPPORTED;
         return mean ? launch_bn<FULL, true, EPI_STORE>(g, bn, batch, st, what)
                     : launch_bn<FULL, false, EPI_STORE>(g, bn, batch, st, what);
     }
     if (vm == RSQ) {
-        if (epi != EPI_STORE || !mean) return TAGI_E_UNSUPPORTED;
+        if ((epi != EPI_STORE && epi != EPI_PARTIAL) || !mean) return TAGI_E_UNSUPPORTED;
         // the stride-1 col2im gather compiles without divisions
-        return (g.ga.on && g.ga.s == 1) ? launch_bn<RSQ, true, EPI_STORE, 2>(g, bn, batch, st, what)
-                                        : launch_bn<RSQ, true, EPI_STORE, 1>(g, bn, batch, st, what);
+        const bool s1 = g.ga.on && g.ga.s == 1;
+        if (epi == EPI_PARTIAL)
+            return s1 ? launch_bn<RSQ, true, EPI_PARTIAL, 2>(g, bn, batch, st, what)
+                      : launch_bn<RSQ, true, EPI_PARTIAL, 1>(g, bn, batch, st, what);
+        return s1 ? launch_bn<RSQ, true, EPI_STORE, 2>(g, bn, batch, st, what)
+                  : launch_bn<RSQ, true, EPI_STORE, 1>(g, bn, batch, st, what);
     }
     if (!mean) return TAGI_E_UNSUPPORTED;
     switch (epi) {

@@ -26,9 +26,12 @@ _SIGS = {
     "tagi_moment_forward": "pp" + "iiii" + "ppi" + "pppp" + "iiii" + "iii" + "p",
     "tagi_fused_backward_delta": "ppppp" + "iii" + "iiiiii" + "p",
     "tagi_backward_delta_view": "pp" + "iiii" + "pi" + "pp" + "iiii" + "iii" + "p",
-    "tagi_conv2d_backward_delta": "ppp" + "pp" + "iiiiiiiii" + "n" + "p",
-    "tagi_conv2d_forward": "pppppp" + "pp" + "iiiiiiiii" + "p",
+    "tagi_conv2d_backward_delta": "ppp" + "pp" + "iiiiiiiii" + "n" + "pz" + "p",
+    "tagi_linear_forward": "pppppp" + "pp" + "iii" + "pz" + "p",
+    "tagi_linear_backward_delta": "ppp" + "pp" + "iii" + "pz" + "p",
+    "tagi_conv2d_forward": "pppppp" + "pp" + "iiiiiiiii" + "pz" + "p",
     "tagi_fused_weight_grad_workspace_size": "iii",
+    "tagi_store_workspace_size": "iii",
     "tagi_fused_weight_grad": "ppppp" + "iii" + "iiiiii" + "pz" + "p",
     "tagi_fused_weight_grad_static": "ppppp" + "iii" + "iiiiii" + "p",
     "tagi_param_grad_workspace_size": "iiin",
@@ -63,6 +66,7 @@ _SIGS = {
 _RET = {
     "tagi_fused_weight_grad_workspace_size": _Z,
     "tagi_param_grad_workspace_size": _Z,
+    "tagi_store_workspace_size": _Z,
     "tagi_last_error": ctypes.c_char_p,
     "tagi_kernel_launches": ctypes.c_uint64,
 }

@@ -26,7 +26,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
-from .._lib import check_cuda_f32, lib, stream
+from .._lib import check_cuda_f32, lib, stream, workspace
 from ..base import LearnableLayer
 from ..param_init import init_weight_bias_conv2d
 from ._params import contiguous_params, weight_apply_sums, weight_param_backward, weight_update
@@ -77,10 +77,13 @@ class Conv2D(LearnableLayer):
         self.input_ma = ma  # the weight sums of backward take their patches from it
         mz = torch.empty(N, Co, Ho, Wo, device=dev)
         Sz = torch.empty(N, Co, Ho, Wo, device=dev)
-        lib()("tagi_conv2d_forward", ma.data_ptr(), Sa.data_ptr(), self.mw.data_ptr(),
-              self.Sw.data_ptr(), self.mb.data_ptr(), self.Sb.data_ptr(), mz.data_ptr(),
-              Sz.data_ptr(), N, C, H, W, Co, self.kH, self.stride, self.padding,
-              self.padding_type, stream(ma))
+        lb = lib()
+        hold, wp, wn = workspace(
+            lb.size("tagi_store_workspace_size", N * Ho * Wo, Co, C * self.kH * self.kW), ma)
+        lb("tagi_conv2d_forward", ma.data_ptr(), Sa.data_ptr(), self.mw.data_ptr(),
+           self.Sw.data_ptr(), self.mb.data_ptr(), self.Sb.data_ptr(), mz.data_ptr(),
+           Sz.data_ptr(), N, C, H, W, Co, self.kH, self.stride, self.padding,
+           self.padding_type, wp, wn, stream(ma))
         return mz, Sz
 
     def backward(self, delta_mz: Tensor, delta_Sz: Tensor) -> tuple[Tensor, Tensor]:
@@ -100,9 +103,12 @@ class Conv2D(LearnableLayer):
             if self.stride == 1:
                 # One contraction over (tap, co) gathers the deltas as the col2im fold
                 # does (no patch-space deltas in memory).
-                lib()("tagi_conv2d_backward_delta", dmz.data_ptr(), dSz.data_ptr(),
-                      self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, 1,
-                      p, self.padding_type, _COL2IM_MODES[self.col2im_mode], st)
+                lb = lib()
+                hold, wp, wn = workspace(
+                    lb.size("tagi_store_workspace_size", N * H * W, C, Co * k * k), dmz)
+                lb("tagi_conv2d_backward_delta", dmz.data_ptr(), dSz.data_ptr(),
+                   self.mw.data_ptr(), d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, 1,
+                   p, self.padding_type, _COL2IM_MODES[self.col2im_mode], wp, wn, st)
             else:
                 # With stride s only about 1/s² of the (pixel, tap) pairs contribute:
                 # the patch-space product plus the gather does the fewer flops.

@@ -13,7 +13,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
-from .._lib import check_cuda_f32, lib, stream
+from .._lib import check_cuda_f32, lib, stream, workspace
 from ..base import LearnableLayer
 from ..param_init import init_weight_bias_linear
 from ._params import contiguous_params, weight_apply_sums, weight_param_backward, weight_update
@@ -43,10 +43,13 @@ class Linear(LearnableLayer):
         M = a.shape[0]
         mz = torch.empty(M, N, device=a.device)
         Sz = torch.empty(M, N, device=a.device)
-        lib()("tagi_moment_forward", a.data_ptr(), s.data_ptr(), 0, 0, K, 1, self.mw.data_ptr(),
-              self.Sw.data_ptr(), N, self.mb.data_ptr() if self.has_bias else None,
-              self.Sb.data_ptr() if self.has_bias else None, mz.data_ptr(), Sz.data_ptr(), 0, 0,
-              N, 1, M, N, K, stream(a))
+        L = lib()
+        # small batches split the reduction over the idle SMs (workspace sized by the library)
+        hold, wp, wn = workspace(L.size("tagi_store_workspace_size", M, N, K), a)
+        L("tagi_linear_forward", a.data_ptr(), s.data_ptr(), self.mw.data_ptr(),
+          self.Sw.data_ptr(), self.mb.data_ptr() if self.has_bias else None,
+          self.Sb.data_ptr() if self.has_bias else None, mz.data_ptr(), Sz.data_ptr(), M, K, N,
+          wp, wn, stream(a))
         out = (*self._input_shape[:-1], N)
         return mz.reshape(out), Sz.reshape(out)
 
@@ -60,8 +63,10 @@ class Linear(LearnableLayer):
         if not self._skip_input_delta:
             d_ma = torch.empty(M, K, device=dm.device)
             d_Sa = torch.empty(M, K, device=dm.device)
-            lib()("tagi_fused_backward_delta", dm.data_ptr(), dS.data_ptr(), self.mw.data_ptr(),
-                  d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, N, 1, N, 1, K, 1, stream(dm))
+            L = lib()
+            hold, wp, wn = workspace(L.size("tagi_store_workspace_size", M, K, N), dm)
+            L("tagi_linear_backward_delta", dm.data_ptr(), dS.data_ptr(), self.mw.data_ptr(),
+              d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, wp, wn, stream(dm))
         weight_param_backward(self, self.ma_in, K, (dm, dS), (0, 0, N, 1), M, K, N, self.has_bias)
         if d_ma is None:
             return None, None
