@@ -162,8 +162,42 @@ def _conv_pixels(a) -> int:
     return ((H + 2 * p - k) // s + 1) * ((W + 2 * p - k) // s + 1)
 
 
+def _out_pixels(H, W, k, s, p, pt) -> int:
+    if pt == 2 and p > 0:
+        return ((H + p - k) // s + 1) * ((W + p - k) // s + 1)
+    return ((H + 2 * p - k) // s + 1) * ((W + 2 * p - k) // s + 1)
+
+
+def _planes(*ptrs) -> int:
+    return sum(1 for q in ptrs if q)
+
+
+# Algorithmic HBM bytes of the memory-bound library entries (each input element
+# read once, each output element written once).
+ENTRY_BYTES = {
+    "tagi_relu_forward": lambda a: 20 * a[5],
+    "tagi_jacobian_backward": lambda a: 20 * a[5],
+    "tagi_innovation": lambda a: 20 * a[5],
+    "tagi_add_inplace": lambda a: 24 * a[4],
+    "tagi_capped_update": lambda a: 24 * a[4],
+    "tagi_remax_forward": lambda a: 20 * a[5] * a[6],
+    "tagi_bn_channel_sums": lambda a: 8 * a[3] * a[4] * a[5],
+    "tagi_bn_forward": lambda a: 4 * (5 + _planes(a[11])) * a[12] * a[13] * a[14],
+    "tagi_bn_backward": lambda a: 20 * a[8] * a[9] * a[10],
+    "tagi_avgpool_forward": lambda a: 8 * a[4] * a[5] * a[6] * a[7] * (1 + 1 / a[8] ** 2),
+    "tagi_avgpool_backward": lambda a: 8 * a[4] * a[5] * a[6] * a[7] * (1 + 1 / a[8] ** 2),
+    # patches written (mean, and variance if given) + image read
+    "tagi_im2col": lambda a: 4 * _planes(a[0], a[1]) * a[4] * a[5] * (
+        a[6] * a[7] + _out_pixels(a[6], a[7], a[8], a[9], a[10], a[11]) * a[8] * a[8]),
+    "tagi_col2im": lambda a: 8 * a[4] * a[5] * (
+        a[6] * a[7] + _out_pixels(a[6], a[7], a[8], a[9], a[10], a[11]) * a[8] * a[8]),
+}
+
+
 class LaunchTimer:
-    """Times the moment-contraction launches with CUDA events (library call hook)."""
+    """Times every library call with CUDA events (library call hook): the moment
+    contractions by family with their flops, the other entries by name with
+    their algorithmic bytes where known."""
 
     FAMILIES = {
         "tagi_moment_forward": ("moment_forward", lambda a: 6.0 * a[17] * a[18] * a[19]),
@@ -185,25 +219,32 @@ class LaunchTimer:
         self.records, self._open = [], None
 
     def __call__(self, phase, name, args):
-        fam = self.FAMILIES.get(name)
-        if fam is None:
-            return
         ev = torch.cuda.Event(enable_timing=True)
         ev.record()
         if phase == "before":
             self._open = ev
+            return
+        fam = self.FAMILIES.get(name)
+        if fam is not None:
+            self.records.append((fam[0], fam[1](args), None, self._open, ev))
         else:
-            self.records.append((fam[0], fam[1](args), self._open, ev))
+            nb = ENTRY_BYTES.get(name)
+            self.records.append((name, None, nb(args) if nb else None, self._open, ev))
 
     def summary(self):
-        fam = {}
-        for name, flops, a, b in self.records:
+        """(contraction families, other entries)."""
+        fam, other = {}, {}
+        for name, flops, nbytes, a, b in self.records:
             t = a.elapsed_time(b) * 1e-3
-            f = fam.setdefault(name, {"launches": 0, "flops": 0.0, "seconds": 0.0})
+            d = fam if flops is not None else other
+            f = d.setdefault(name, {"launches": 0, "flops": 0.0, "bytes": 0.0, "seconds": 0.0,
+                                    "bytes_known": True})
             f["launches"] += 1
-            f["flops"] += flops
+            f["flops"] += flops or 0.0
+            f["bytes"] += nbytes or 0.0
+            f["bytes_known"] &= nbytes is not None
             f["seconds"] += t
-        return fam
+        return fam, other
 
 
 def tf32_peak_tflops(device) -> float:
@@ -330,13 +371,11 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     torch.cuda.synchronize()
     launches0 = kernel_launches()
     with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
-        L.hook = timer
         for i in range(args.steps):
             flush.zero_()
             starts[i].record()
             net.step(x, y, SIGMA_V)
             ends[i].record()
-        L.hook = None
         torch.cuda.synchronize()
         barrier()
     launches = kernel_launches() - launches0
@@ -344,18 +383,19 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         # replays launch without passing through the library's host calls
         launches = per_step * args.steps
     step_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) * 1e-3
-    fam = timer.summary()
-    fam_steps = args.steps
-    if graphed:
-        fam_steps = 1
-        # per-kernel timing of one eager step (outside the timed region)
-        net.cuda_graph = False
+    # Per-entry timing of eager steps after the timed region (CUDA events around
+    # every library call; the timed steps carry no events of their own).
+    fam_steps = min(3, args.steps)
+    net.cuda_graph = False
+    for _ in range(fam_steps):
+        flush.zero_()
         L.hook = timer
         net.step(x, y, SIGMA_V)
         L.hook = None
-        net.cuda_graph = True
-        torch.cuda.synchronize()
-        fam = timer.summary()
+    net.cuda_graph = graphed
+    torch.cuda.synchronize()
+    barrier()
+    fam, other = timer.summary()
 
     # end to end through the public API: pinned host inputs in, predictions out
     xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
@@ -416,6 +456,14 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         "roofline": roof,
         "kernels": {k: {"launches": v["launches"], "ms_per_step": 1e3 * v["seconds"] / fam_steps,
                         "tflops": v["flops"] / v["seconds"] / 1e12} for k, v in fam.items()},
+        # every other library entry of the step (CUDA events around each call);
+        # gbs = algorithmic bytes / time, hbm_frac against the measured copy bandwidth
+        "entries": {k: {"launches": v["launches"], "ms_per_step": 1e3 * v["seconds"] / fam_steps,
+                        **({"gbs": v["bytes"] / v["seconds"] / 1e9,
+                            "hbm_frac": (v["bytes"] / v["seconds"] / 1e9 / peaks["hbm_gbs"]
+                                         if peaks.get("hbm_gbs") else None)}
+                           if v["bytes_known"] and v["bytes"] > 0 else {})}
+                    for k, v in sorted(other.items(), key=lambda kv: -kv[1]["seconds"])},
         "clocks": clocks.summary(),
         "peaks": {"tf32_cublas_tflops": tf32, "hbm_gbs": peaks.get("hbm_gbs"),
                   "bf16_tflops": peaks.get("bf16_tflops")},
@@ -454,13 +502,16 @@ def sweep_arm(args, rank: int, world: int, local: int) -> None:
             dSz = -torch.rand(M, N, device=dev, generator=g) * 1e-2
             d_ma = torch.empty(M, K, device=dev)
             d_Sa = torch.empty(M, K, device=dev)
+            ws_n = L.size("tagi_store_workspace_size", M, K, N)
+            ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
 
             def fwd():
                 lin.forward(ma, Sa)
 
             def bwd():
-                L("tagi_fused_backward_delta", dmz.data_ptr(), dSz.data_ptr(), lin.mw.data_ptr(),
-                  d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, N, 1, N, 1, K, 1, stream(dmz))
+                L("tagi_linear_backward_delta", dmz.data_ptr(), dSz.data_ptr(), lin.mw.data_ptr(),
+                  d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, ws.data_ptr() if ws_n else None,
+                  ws_n, stream(dmz))
 
             def upd():
                 from triton_tagi.layers._params import weight_param_backward

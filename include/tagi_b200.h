@@ -119,9 +119,12 @@ int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, const float* 
 /* Optional workspace of the entries above and below that write an M x N output
  * through a reduction of length K (tagi_linear_forward: M, N, K; its backward
  * delta: M, K, N; tagi_conv2d_forward: N*Ho*Wo, Co, C*k*k; tagi_conv2d_backward_delta:
- * N*H*W, C, Co*k*k). When the output grid leaves SMs idle the reduction is split
- * into partial sums there and added in split order; with less workspace (or
- * none) the contraction runs unsplit. Host only; 0 when no split is planned. */
+ * N*H*W, C, Co*k*k). It holds (1) the partial sums of a split reduction, when the
+ * output grid leaves SMs idle (added in split order), and (2) the weight-side
+ * operand prepared once per call as tf32 hi/lo tiles, which the tensor-core kernel
+ * copies with bulk asynchronous copies instead of forming them in every output
+ * tile. With less workspace the prepared tiles are dropped first, then the split;
+ * with none the contraction runs unsplit. Host only; 0 when neither applies. */
 size_t tagi_store_workspace_size(int64_t M, int64_t N, int64_t K);
 
 /* Linear forward: mz = ma @ mw + mb, Sz = ma^2 @ Sw + Sa @ (mw^2 + Sw) + Sb for

@@ -76,7 +76,11 @@ def test_workspace_queries_are_host_only():
     from triton_tagi._lib import lib
 
     L = lib()
-    # a short reduction is never split; a long one over a small output is
+    # A short reduction is never split; with 8 or more tiles of 256 weight rows
+    # the workspace holds the optional prepared tiles of the deltas (8 K-blocks x
+    # 4 tiles x 256 columns x 32 bytes); a long one over a small output is split.
     assert L.size("tagi_param_grad_workspace_size", 64, 784, 256, 1) == 0
+    assert L.size("tagi_param_grad_workspace_size", 64, 2048, 256, 1) == 8 * 4 * 256 * 32
+    assert L.size("tagi_param_grad_workspace_size", 16, 30, 20, 1) == 0  # CUDA-core path
     big = L.size("tagi_param_grad_workspace_size", 128 * 1024, 576, 64, 1)
     assert big > 0 and big % 4 == 0

@@ -53,7 +53,9 @@ def test_static_scratch_matches_workspace_entry_point_on_consecutive_calls():
     # two calls in a row with different split plans (the first on the tensor-core
     # kernel, the second on CUDA cores); the second reuses the array
     for seed, (M, K, N) in enumerate([(131072, 288, 32), (50000, 27, 10)]):
-        assert 0 < L.size("tagi_fused_weight_grad_workspace_size", M, K, N) <= STATIC_BYTES
+        # the workspace entry point gets split partials (and, on the tensor cores,
+        # room for prepared delta tiles); the static array holds the partials only
+        assert L.size("tagi_fused_weight_grad_workspace_size", M, K, N) > 0
         a, dmz, dSz = _inputs(M, K, N, seed)
         ref_m, ref_S = triton_fused_weight_grad(a, dmz, dSz)
         got_m, got_S = _static_call(a, dmz, dSz)

@@ -4,6 +4,9 @@
 // row = (n, oh, ow) and column = (c, kh, kw); images are NCHW.
 // padding_type 2 pads only the right/bottom edge by `padding`
 // (triton_tagi/layers/conv2d.py:280-291), i.e. the top-left offset is 0.
+#include <algorithm>
+#include <climits>
+
 #include "common.cuh"
 
 namespace tagi {
@@ -94,6 +97,87 @@ __global__ void im2col_v4_kernel(const float* xm, const float* xS, float* pm, fl
     }
 }
 
+// 4-byte asynchronous copy global -> shared (zero-filled when !ok): the staging
+// loads of a CTA are all in flight together and waited for once.
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool ok) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src),
+                 "r"(ok ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// q = i / d for 0 <= i < 2^22 and d >= 1, from the reciprocal r = 1/d: the
+// fraction of (i + 0.5)/d is at least 0.5/d away from an integer and the float
+// error of (i + 0.5) * r stays below that for such i.
+__device__ __forceinline__ int div_small(int i, float r) {
+    return static_cast<int>((static_cast<float>(i) + 0.5f) * r);
+}
+
+// Patches of one output image row (image n, output row oh) per CTA: the output
+// rows r = (n, oh, 0 .. Wo-1) are Wo*K contiguous floats. The k input lines each
+// channel contributes (oh*s - p + kh, all W columns) are staged in shared
+// memory with asynchronous copies spread over all threads (zeros for lines
+// outside the image), channel slice by channel slice; then each thread owns
+// patch columns (c, kh, kw) and walks ow, so that a warp stores 32 consecutive
+// columns of one patch row. Index decoding uses div_small (all indices of a CTA
+// are below 2^22: staged elements and patch columns are bounded by 32 KB and K).
+__global__ void im2col_rows_kernel(const float* xm, const float* xS, float* pm, float* pS,
+                                   ConvGeom g, int cslice) {
+    // [plane][cslice * k lines][ls]: an odd line stride puts the same column of
+    // different lines (read together by a warp) in different banks
+    extern __shared__ float lines[];
+    const int ls = g.W | 1;
+    const int n = blockIdx.x / g.Ho, oh = blockIdx.x - n * g.Ho;
+    const int kk = g.k * g.k, K = g.C * kk;
+    const int planes = pS ? 2 : 1;
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const float rW = 1.f / g.W, rk = 1.f / g.k, rkk = 1.f / kk;
+    const int64_t row0 = (static_cast<int64_t>(n) * g.Ho + oh) * g.Wo;  // first patch row
+    const int ih0 = oh * g.s - g.p_tl;
+    for (int c0 = 0; c0 < g.C; c0 += cslice) {
+        const int cs = min(cslice, g.C - c0);
+        const int nlines = cs * g.k, pstride = nlines * ls;
+        const float rn = 1.f / nlines;
+        const int ne = planes * nlines * g.W;
+        for (int e = tid; e < ne; e += nth) {
+            const int line = div_small(e, rW), w = e - line * g.W;
+            const int pl = div_small(line, rn), li = line - pl * nlines;
+            const int cl = div_small(li, rk), ih = ih0 + (li - cl * g.k);
+            const bool in = ih >= 0 && ih < g.H;
+            // rows outside the image are zero-filled (the source is not read)
+            const float* src = (pl ? xS : xm) +
+                               ((static_cast<int64_t>(n) * g.C + c0 + cl) * g.H + (in ? ih : 0)) * g.W;
+            cp_async4(lines + pl * pstride + li * ls + w, src + w, in);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+        const int ncol = cs * kk;
+        // columns per thread pass and patch rows per column
+        const int step = ncol >= nth ? 1 : nth / ncol;
+        const int j0 = ncol >= nth ? tid : tid % ncol, ow0 = ncol >= nth ? 0 : tid / ncol;
+        if (ow0 < step) {
+            for (int j = j0; j < ncol; j += (ncol >= nth ? nth : ncol)) {
+                const int cl = div_small(j, rkk), t = j - cl * kk;
+                const int kh = div_small(t, rk), kw = t - kh * g.k;
+                const float* line = lines + (cl * g.k + kh) * ls;
+                float* om = pm + row0 * K + c0 * kk + j;
+                float* oS = pS ? pS + row0 * K + c0 * kk + j : nullptr;
+                int iw = ow0 * g.s - g.p_tl + kw;
+                for (int ow = ow0; ow < g.Wo; ow += step, iw += step * g.s) {
+                    const bool in = iw >= 0 && iw < g.W;
+                    om[static_cast<int64_t>(ow) * K] = in ? line[iw] : 0.f;
+                    if (oS) oS[static_cast<int64_t>(ow) * K] = in ? line[pstride + iw] : 0.f;
+                }
+                if (ncol < nth) break;
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // One thread per input pixel; taps are visited in (kh, kw) order as the
 // reference does, so for identical patch inputs the sums are bit-identical.
 template <bool ADJOINT>
@@ -150,8 +234,15 @@ extern "C" int tagi_im2col(const float* xm, const float* xS, float* pm, float* p
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(xm && pm && (xS == nullptr) == (pS == nullptr), TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
+    // staged lines of a channel slice within 32 KB of shared memory
+    const int64_t line_bytes = (xS ? 2 : 1) * k * (W | 1) * static_cast<int64_t>(sizeof(float));
+    const int64_t cslice = std::min<int64_t>(C, (32 * 1024) / line_bytes);
     const uintptr_t al = (reinterpret_cast<uintptr_t>(pm) | reinterpret_cast<uintptr_t>(pS)) & 15;
-    if ((C * k * k) % 4 == 0 && al == 0) {
+    // div_small bounds: staged elements (<= 8192) and patch columns below 2^22
+    if (cslice >= 1 && N * g.Ho <= INT_MAX && C * k * k < (int64_t(1) << 22)) {
+        im2col_rows_kernel<<<static_cast<unsigned>(N * g.Ho), 256, cslice * line_bytes,
+                             as_stream(stream)>>>(xm, xS, pm, pS, g, static_cast<int>(cslice));
+    } else if ((C * k * k) % 4 == 0 && al == 0) {
         im2col_v4_kernel<<<grid_1d(total / 4, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);
     } else {
         im2col_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);

@@ -281,14 +281,30 @@ GemmArgs blank() {
 
 bool bad_size(int64_t v) { return v < 0 || v > (int64_t(1) << 31) - 1; }
 
+// Prepared delta tiles pay when many output tiles along M (pairs of 256 weight
+// rows) would each convert the same deltas: 8 or more.
+size_t wgrad_pack_bytes(int Mo, int N, int Kr, int bn_tc) {
+    if (bn_tc <= 0 || (Mo + 255) / 256 < 8) return 0;
+    return tc_pack_bytes(LSQ, N, Kr, bn_tc);
+}
+
 // Shared driver for the weight-gradient family (stores or parameter epilogue).
+// The workspace must hold the split-reduction partials when a split is planned;
+// room past them (256-byte aligned) takes the prepared B tiles (the deltas) of
+// the tensor-core kernel.
 int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
               const char* what) {
     int splits, chunk, bn_tc;
     choose_splits(Mo, g.N, g.Kr, 1, &splits, &chunk, &bn_tc);
     g.M = Mo;
+    const size_t need = splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N : 0;
+    const size_t pack_off = (need + 255) / 256 * 256;
+    const size_t pack = wgrad_pack_bytes(Mo, g.N, g.Kr, bn_tc);
+    if (pack > 0 && ws != nullptr && ws_bytes >= pack_off + pack) {
+        const int rc = tc_pack_b(g, LSQ, bn_tc, static_cast<char*>(ws) + pack_off, st, what);
+        if (rc) return rc;
+    }
     if (splits > 1) {
-        const size_t need = sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N;
         TAGI_REQUIRE(ws != nullptr && ws_bytes >= need, TAGI_E_WORKSPACE,
                      "%s: workspace of %zu bytes required, %zu given", what, need, ws_bytes);
         g.splits = splits;
@@ -306,38 +322,78 @@ int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaSt
                  : launch<LSQ, true, EPI_STORE>(g, 1, st, what, bn_tc);
 }
 
-// Store-epilogue contractions (forward, input deltas) whose output grid leaves
-// SMs idle: split the reduction into a caller workspace when it holds the plan,
-// else run unsplit (the workspace only buys speed).
+// Workspace of a store-epilogue contraction: split-reduction partials (when the
+// output grid leaves SMs idle), then the prepared B tiles of the tensor-core
+// kernel (sized for FULL, the larger of FULL and RSQ).
+struct StorePlan {
+    int splits, chunk, bn_split, bn_whole;
+    size_t partials, pack;
+};
+
+StorePlan store_plan(int M, int N, int Kr) {
+    StorePlan p{};
+    choose_splits(M, N, Kr, 1, &p.splits, &p.chunk, &p.bn_split);
+    p.bn_whole = tc_pick(FULL, M, N, Kr, 1);
+    p.partials = p.splits > 1 ? (sizeof(float) * 2ull * p.splits * static_cast<size_t>(M) * N + 255) /
+                                    256 * 256
+                              : 0;
+    p.pack = (p.bn_split > 0 || p.bn_whole > 0) ? tc_pack_bytes(FULL, N, Kr, 128) : 0;
+    return p;
+}
+
+size_t store_ws_bytes(int M, int N, int Kr) {
+    const StorePlan p = store_plan(M, N, Kr);
+    return p.partials + p.pack;
+}
+
+// Store-epilogue contractions (forward, input deltas). With a caller workspace
+// they split the reduction when the output grid leaves SMs idle and give the
+// tensor-core kernel prepared B tiles; a smaller workspace (or none) drops the
+// prepared tiles first, then the split (the workspace only buys speed).
 template <int VM>
 int run_store(GemmArgs& g, void* ws, size_t ws_bytes, cudaStream_t st, const char* what) {
-    int splits, chunk, bn_tc;
-    choose_splits(g.M, g.N, g.Kr, 1, &splits, &chunk, &bn_tc);
-    const size_t need = sizeof(float) * 2ull * splits * static_cast<size_t>(g.M) * g.N;
-    if (splits > 1 && ws != nullptr && ws_bytes >= need) {
-        g.splits = splits;
-        g.kchunk = chunk;
-        g.ws = static_cast<float*>(ws);
-        int rc = launch<VM, true, EPI_PARTIAL>(g, 1, st, what, bn_tc);
+    const StorePlan p = store_plan(g.M, g.N, g.Kr);
+    char* w = static_cast<char*>(ws);
+    if (w == nullptr) ws_bytes = 0;
+    const bool split = p.splits > 1 && ws_bytes >= p.partials;
+    const int bn = split ? p.bn_split : tc_pick(VM, g.M, g.N, g.Kr, 1);
+    // Prepared B tiles pay for the forward, whose weight-side producers bound the
+    // tensor-core kernel; the input-delta contraction forms its B side (the
+    // weights, read row by row) faster than a separate pass prepares it.
+    const size_t pack = (VM == FULL && bn > 0) ? tc_pack_bytes(VM, g.N, g.Kr, bn) : 0;
+    const size_t pack_off = split ? p.partials : 0;
+    if (pack > 0 && ws_bytes >= pack_off + pack) {
+        const int rc = tc_pack_b(g, VM, bn, w + pack_off, st, what);
+        if (rc) return rc;
+    }
+    if (split) {
+        g.splits = p.splits;
+        g.kchunk = p.chunk;
+        g.ws = reinterpret_cast<float*>(w);
+        int rc = launch<VM, true, EPI_PARTIAL>(g, 1, st, what, p.bn_split);
         if (rc) return rc;
         splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(g.M) * g.N, 256), 256, 0, st>>>(g, 0);
         return check_launch(what);
     }
     g.splits = 1;
     g.kchunk = g.Kr > 0 ? g.Kr : BK;
-    return launch<VM, true, EPI_STORE>(g, 1, st, what);
+    return launch<VM, true, EPI_STORE>(g, 1, st, what, bn);
 }
 
-size_t store_ws_bytes(int M, int N, int Kr) {
-    int splits, chunk, bn_tc;
-    choose_splits(M, N, Kr, 1, &splits, &chunk, &bn_tc);
-    return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(M) * N : 0;
-}
-
+// Split-reduction partials a weight-gradient call requires.
 size_t wgrad_ws_bytes(int Mo, int N, int Kr) {
     int splits, chunk, bn_tc;
     choose_splits(Mo, N, Kr, 1, &splits, &chunk, &bn_tc);
     return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * N : 0;
+}
+
+// The partials plus the optional prepared B tiles (what the size queries report).
+size_t wgrad_ws_total(int Mo, int N, int Kr) {
+    int splits, chunk, bn_tc;
+    choose_splits(Mo, N, Kr, 1, &splits, &chunk, &bn_tc);
+    const size_t need = wgrad_ws_bytes(Mo, N, Kr);
+    const size_t pack = wgrad_pack_bytes(Mo, N, Kr, bn_tc);
+    return pack > 0 ? (need + 255) / 256 * 256 + pack : need;
 }
 
 __global__ void apply_sums_kernel(const float* gm, const float* gS, ParamEpi p, int64_t total) {
@@ -562,7 +618,7 @@ extern "C" int tagi_fused_backward_delta(const float* dmz, const float* dSz, con
 
 extern "C" size_t tagi_fused_weight_grad_workspace_size(int64_t M, int64_t K, int64_t N) {
     if (bad_size(M) || bad_size(K) || bad_size(N)) return 0;
-    return wgrad_ws_bytes((int)K, (int)N, (int)M);
+    return wgrad_ws_total((int)K, (int)N, (int)M);
 }
 
 extern "C" int tagi_fused_weight_grad(const float* a, const float* dmz, const float* dSz,
@@ -588,7 +644,7 @@ extern "C" int tagi_fused_weight_grad(const float* a, const float* dmz, const fl
 
 extern "C" size_t tagi_param_grad_workspace_size(int64_t M, int64_t K, int64_t N, int has_bias) {
     if (bad_size(M) || bad_size(K) || bad_size(N)) return 0;
-    return wgrad_ws_bytes((int)K + (has_bias ? 1 : 0), (int)N, (int)M);
+    return wgrad_ws_total((int)K + (has_bias ? 1 : 0), (int)N, (int)M);
 }
 
 extern "C" int tagi_param_grad(const float* a, int64_t lda, const float* dmz, const float* dSz,

@@ -164,6 +164,35 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, ab, code));
 }
 
+// Bounded wait that ignores the abort flag: for bulk copies this warp issued,
+// which must land before the CTA may exit.
+__device__ __noinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try(bar, parity))
+        if (globaltimer() - t0 > kTimeoutNs) return false;
+    return true;
+}
+
+// Arrive on a local barrier and add `bytes` to the transactions its phase waits for.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Bulk asynchronous copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory; completes as
+// transactions on `bar`. No multicast: the source is this GPU's own memory and
+// only the issuing CTA receives it.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(dst),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ bool elect_one() {
     uint32_t p;
     asm volatile(
@@ -361,7 +390,7 @@ constexpr int op_stages() {
                                                              : kMaxStages;
 }
 
-constexpr int kBarrierBytes = 256;
+constexpr int kBarrierBytes = 512;
 
 template <int VM, int BN>
 constexpr int smem_bytes() {
@@ -617,6 +646,7 @@ __device__ __forceinline__ int chunk_end(int c, int o, int niter) {
 struct ProdCtx {
     char* smem;
     uint64_t* empty;
+    uint64_t* bfull;  // prepared-B copies of each stage slot (local)
     uint32_t full0;  // cluster address of the leader CTA's full barriers
     Abort ab;
     int niter, kbeg, kend;
@@ -721,6 +751,56 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
     }
 }
 
+// B side from prepared tiles (g.bpk), two warps per CTA:
+//   issuer (role 0): as each stage slot frees, copies the stage's K-blocks of B
+//     tiles of this CTA's NC columns (contiguous, in shared-memory byte order),
+//     one bulk copy per K-block, completing on the slot's bfull barrier;
+//   forwarder (role 1): as each stage's copies land, arrives on the leader's full
+//     barrier of the stage for the whole B side of this CTA.
+// Neither waits for the other, so copies run as far ahead as the free slots
+// allow and a landed stage is forwarded at once.
+template <int VM, int BN>
+__device__ __forceinline__ void packed_b(const GemmArgs& g, const ProdCtx& c, int chunk,
+                                         int role) {
+    using R = Roles<BN>;
+    constexpr uint32_t KB_BYTES = TcTiles<VM>::nb * R::NC * 32;
+    constexpr int STAGE = stage_bytes<VM, BN>();
+    constexpr int BLOCK = block_bytes<VM, BN>();
+    constexpr int OPS = op_stages<VM, BN>();
+    constexpr int OFF = TcTiles<VM>::na * 128 * 32;
+    const int nst = (c.niter + kBlocks - 1) / kBlocks;
+    if (role == 1) {
+        for (int F = 0; F < nst; ++F) {
+            const int f = F % OPS;
+            if (!warp_wait(&c.bfull[f], (F / OPS) & 1, c.ab, 6)) return;
+            __syncwarp();
+            if (c.lane == 0) arrive_cluster(c.full0 + static_cast<uint32_t>(f * 8));
+        }
+        return;
+    }
+    const char* src0 =
+        g.bpk + (static_cast<int64_t>(chunk) * g.bpk_nkb + c.kbeg / kBK) * KB_BYTES;
+    int issued = 0;
+    for (int S = 0; S < nst; ++S) {
+        const int s = S % OPS;
+        if (S >= OPS && !warp_wait(&c.empty[s], ((S / OPS) - 1) & 1, c.ab, 1)) break;
+        if (c.lane == 0) {
+            const int nblk = min(kBlocks, c.niter - S * kBlocks);
+            mbar_expect_tx(&c.bfull[s], nblk * KB_BYTES);
+            const uint32_t dst = smem_u32(c.smem + s * STAGE + OFF);
+            for (int sub = 0; sub < nblk; ++sub)
+                bulk_g2s(dst + sub * BLOCK, src0 + static_cast<int64_t>(S * kBlocks + sub) * KB_BYTES,
+                         KB_BYTES, &c.bfull[s]);
+        }
+        __syncwarp();
+        issued = S + 1;
+    }
+    // The copies of the last stages issued (the latest phase of each slot) must
+    // land before the CTA may exit, also after an abort.
+    for (int F = max(0, issued - OPS); F < issued; ++F)
+        mbar_drain(&c.bfull[F % OPS], (F / OPS) & 1);
+}
+
 // GM: the A gather compiled in (0 patches, 1 col2im of any stride, 2 col2im of
 // stride 1); operands that are not gathered ignore it.
 template <int VM, bool MEAN, int EPI, int BN, int GM>
@@ -740,7 +820,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     uint64_t* chunk_full = empty + kMaxStages;                          // [q*2 + b]
     uint64_t* chunk_empty = chunk_full + 4;                             // [q*2 + b], leader
     uint64_t* done = chunk_empty + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* bfull = done + 1;  // [OPS], prepared-B copies
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bfull + kMaxStages);
     volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -753,11 +834,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     const int kend = min(g.Kr, kbeg + g.kchunk);
     const int niter = kend > kbeg ? (kend - kbeg + kBK - 1) / kBK : 0;
     const Abort ab{abort_word, map_to(smem_u32(const_cast<int*>(abort_word)), rank ^ 1u)};
+    // Prepared B tiles (FULL and RSQ, unbatched): one arrival per CTA for the B side.
+    const bool packed = g.bpk != nullptr && g.bpk_nc == R::NC;
 
     if (tid == 0) {
         for (int s = 0; s < OPS; ++s) {
-            mbar_init(&full[s], R::STAGE_ARRIVALS);
+            mbar_init(&full[s], packed ? 2 * 2 * 4 + 2 : R::STAGE_ARRIVALS);
             mbar_init(&empty[s], 1);
+            mbar_init(&bfull[s], 1);
         }
         for (int i = 0; i < 4; ++i) {
             mbar_init(&chunk_full[i], 1);
@@ -814,6 +898,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
             c.grp = warp >> 2;
             c.t = (warp & 3) * 32 + lane;
             producer<VM, BN, true, GM>(g, c, sa);
+        } else if (packed) {
+            c.bfull = bfull;
+            if (warp < R::B_W0 + 2) packed_b<VM, BN>(g, c, sb.row0 / R::NC, warp - R::B_W0);
         } else {
             c.grp = (warp - R::B_W0) / R::BW;
             c.t = ((warp - R::B_W0) % R::BW) * 32 + lane;
@@ -828,8 +915,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         if (leader) {
             const bool el = elect_one();
             const uint64_t da_first = smem_desc(smem_u32(smem), sa.chunk, 128);
-            const uint64_t db_first = smem_desc(smem_u32(smem), sb.chunk, R::NC);
-            const uint32_t idesc = instr_desc(BN, sa.chunk, sb.chunk);
+            // prepared tiles: MN-major (swizzled) when NC allows it, else K-major
+            const bool b_mn = packed ? R::NC % 32 == 0 : sb.chunk;
+            const uint64_t db_first = smem_desc(smem_u32(smem), b_mn, R::NC);
+            const uint32_t idesc = instr_desc(BN, sa.chunk, b_mn);
             uint64_t da = da_first, db = db_first;
             int s = 0;
             uint32_t ph = 0;
@@ -1042,6 +1131,88 @@ int tc_pick(int vm, int M, int N, int Kr, int batch, bool fill) {
     const int64_t ctas = 2 * ((static_cast<int64_t>(M) + 255) / 256) * ((N + 127) / 128) *
                          static_cast<int64_t>(batch);
     return 2 * ctas <= kNumSMs ? 64 : 128;
+}
+
+// Prepared B tiles for N tiles of 2*nc columns: column chunk cb (nc columns)
+// holds, for each K-block kb, the nb tiles of that K-block exactly as a producer
+// stores them in shared memory (MN-major swizzled for nc a multiple of 32, else
+// K-major), so that one bulk copy moves a K-block's B side. Columns past N and
+// reduction elements past Kr are zero. One thread per (chunk, K-block, 4
+// columns, reduction element) in MN-major order, per (chunk, K-block, column)
+// in K-major order.
+template <int VM>
+__global__ void pack_b_kernel(const GemmArgs g, char* dst, int nc, int nchunk, int nkb) {
+    constexpr bool TWO = VM != RSQ;
+    constexpr int NB = TcTiles<VM>::nb;
+    const int tile = nc * 32;
+    const bool mn = nc % 32 == 0;
+    Side sd{};
+    sd.p0 = g.u;
+    sd.p1 = TWO ? g.v : g.u;
+    sd.nrows = g.N;
+    sd.ones_row = -1;
+    const int per_kb = mn ? (nc / 4) * kBK : nc;  // threads per (chunk, K-block)
+    const int64_t total = static_cast<int64_t>(nchunk) * nkb * per_kb;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t blk = i / per_kb;  // cb * nkb + kb
+        const int j = static_cast<int>(i - blk * per_kb);
+        const int cb = static_cast<int>(blk / nkb), kb = static_cast<int>(blk - int64_t(cb) * nkb);
+        char* st = dst + blk * NB * tile;
+        if (mn) {
+            const int r = (j % (nc / 4)) * 4, k = j / (nc / 4);
+            float x[4], y[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (kb * kBK + k < g.Kr)
+                    load_elem<false, TWO>(g, sd, cb * nc + r + e, kb * kBK + k, x[e], y[e]);
+                else
+                    x[e] = y[e] = 0.f;
+            }
+            store_tiles<VM, false>(st, tile, tile_off_mn(r, k, nc), x, y);
+        } else {
+            const int row = cb * nc + j;
+            const int64_t base = row < g.N ? row_base<false>(g, row) : 0;
+            float v[2][8];
+            load_row<false, TWO, 0>(g, sd, row, base, GatherRow{0, 0, 0}, kb * kBK, g.Kr, v);
+            store_tiles<VM, false>(st, tile, tile_off_k(j, 0), &v[0][0], &v[1][0]);
+            store_tiles<VM, false>(st, tile, tile_off_k(j, 4), &v[0][4], &v[1][4]);
+        }
+    }
+}
+
+size_t tc_pack_bytes(int vm, int N, int Kr, int bn) {
+    if (N <= 0 || Kr <= 0 || bn <= 0) return 0;
+    const int64_t cols = (static_cast<int64_t>(N) + bn - 1) / bn * bn;
+    const int64_t nkb = (static_cast<int64_t>(Kr) + kBK - 1) / kBK;
+    const int nb = vm == FULL ? TcTiles<FULL>::nb : TcTiles<RSQ>::nb;  // LSQ: as RSQ
+    return static_cast<size_t>(nkb * nb * cols * 32);
+}
+
+int tc_pack_b(GemmArgs& g, int vm, int bn, void* dst, cudaStream_t st, const char* what) {
+    TAGI_REQUIRE(vm == FULL || vm == RSQ || vm == LSQ, TAGI_E_UNSUPPORTED,
+                 "%s: no prepared B for mode %d", what, vm);
+    TAGI_REQUIRE(bn == 32 || bn == 64 || bn == 128, TAGI_E_UNSUPPORTED, "%s: N tile %d", what, bn);
+    TAGI_REQUIRE((reinterpret_cast<uintptr_t>(dst) & 255) == 0, TAGI_E_ALIGNMENT,
+                 "%s: prepared-B buffer not 256-byte aligned", what);
+    const int nc = bn / 2, nchunk = (g.N + bn - 1) / bn * 2, nkb = (g.Kr + kBK - 1) / kBK;
+    const int64_t per_kb = nc % 32 == 0 ? (nc / 4) * kBK : nc;
+    const int64_t total = static_cast<int64_t>(nchunk) * nkb * per_kb;
+    if (total > 0) {
+        char* d = static_cast<char*>(dst);
+        if (vm == FULL)
+            pack_b_kernel<FULL><<<grid_1d(total, 256), 256, 0, st>>>(g, d, nc, nchunk, nkb);
+        else if (vm == RSQ)
+            pack_b_kernel<RSQ><<<grid_1d(total, 256), 256, 0, st>>>(g, d, nc, nchunk, nkb);
+        else
+            pack_b_kernel<LSQ><<<grid_1d(total, 256), 256, 0, st>>>(g, d, nc, nchunk, nkb);
+        const int rc = check_launch(what);
+        if (rc) return rc;
+    }
+    g.bpk = static_cast<const char*>(dst);
+    g.bpk_nc = nc;
+    g.bpk_nkb = nkb;
+    return TAGI_OK;
 }
 
 int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, cudaStream_t st,

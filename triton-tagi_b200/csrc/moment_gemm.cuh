@@ -105,6 +105,11 @@ struct GemmArgs {
     int splits, kchunk;
     float* ws;
     ParamEpi pe;
+    // Tensor-core path only: B operand tiles prepared by tc_pack_b for an N tile
+    // of 2*bpk_nc columns (null = the kernel forms them from u, v); bpk_nkb
+    // K-blocks of 8 reduction elements per column chunk.
+    const char* bpk;
+    int bpk_nc, bpk_nkb;
 };
 
 __device__ __forceinline__ void param_epilogue(int r, int c, float g0, float g1,
@@ -140,6 +145,11 @@ __device__ __forceinline__ void param_epilogue(int r, int c, float g0, float g1,
 int tc_pick(int vm, int M, int N, int Kr, int batch, bool fill = true);
 int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, cudaStream_t st,
               const char* what);
+// Bytes of the prepared B tiles of a contraction with N output columns,
+// reduction Kr and N tile bn (bn = 128 bounds the others), and the kernel that
+// writes them into `dst` (256-byte aligned) and points g.bpk there.
+size_t tc_pack_bytes(int vm, int N, int Kr, int bn);
+int tc_pack_b(GemmArgs& g, int vm, int bn, void* dst, cudaStream_t st, const char* what);
 constexpr int kTcBM = 128;
 
 }  // namespace tagi
