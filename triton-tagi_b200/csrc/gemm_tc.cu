@@ -1034,6 +1034,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
             if (ok) ok = warp_wait(&chunk_full[2 + b1], (c1 / NP) & 1, ab, 3);
             if (ok) {
                 tc_fence_after();
+                // Outputs whose columns are contiguous (row-major stores, split
+                // partials, weight parameters) go through a per-warp transpose in
+                // shared memory (the operand stages are idle once the last MMAs
+                // completed), so that a warp touches 2 rows x 16 consecutive columns
+                // per access instead of 32 rows x 1 column. Outputs contiguous
+                // along the rows (NCHW) keep the row-per-lane order.
+                const bool transpose = EPI != EPI_STORE || g.on == 1;
+                float* eb = reinterpret_cast<float*>(smem) + a * (2 * 32 * 17);
 #pragma unroll 1
                 for (int k = 0; k < HC; k += 16) {
                     uint32_t pm[16], pv[16], tm[16], tv[16];
@@ -1042,17 +1050,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                     if (MEAN && c0 > 0) tmem_ld16(lane_base + R::tcol(0) + cbeg + k, tm);
                     if (c1 > 0) tmem_ld16(lane_base + R::tcol(1) + cbeg + k, tv);
                     tmem_wait_ld();
-                    if (row >= g.M) continue;
+                    float vm[16], vv[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int col = n0 + cbeg + k + j;
-                        if (col >= g.N) continue;
-                        const float am = MEAN ? (c0 > 0 ? __uint_as_float(tm[j]) + __uint_as_float(pm[j])
-                                                        : __uint_as_float(pm[j]))
-                                              : 0.f;
-                        const float av = c1 > 0 ? __uint_as_float(tv[j]) + __uint_as_float(pv[j])
-                                                : __uint_as_float(pv[j]);
-                        store_out<EPI, MEAN>(g, row, col, ro, split, am, av);
+                        vm[j] = MEAN ? (c0 > 0 ? __uint_as_float(tm[j]) + __uint_as_float(pm[j])
+                                               : __uint_as_float(pm[j]))
+                                     : 0.f;
+                        vv[j] = c1 > 0 ? __uint_as_float(tv[j]) + __uint_as_float(pv[j])
+                                       : __uint_as_float(pv[j]);
+                    }
+                    if (transpose) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            eb[lane * 17 + j] = vm[j];
+                            eb[32 * 17 + lane * 17 + j] = vv[j];
+                        }
+                        __syncwarp();
+                        const int cl = lane & 15, col = n0 + cbeg + k + cl;
+#pragma unroll 4
+                        for (int i = 0; i < 16; ++i) {
+                            const int rl = 2 * i + (lane >> 4);
+                            const int r = m_cta + sub * 32 + rl;
+                            if (r < g.M && col < g.N) {
+                                const int64_t rr = EPI == EPI_STORE ? g.orow.off(r) + batch * g.o_bs : 0;
+                                store_out<EPI, MEAN>(g, r, col, rr, split, eb[rl * 17 + cl],
+                                                     eb[32 * 17 + rl * 17 + cl]);
+                            }
+                        }
+                        __syncwarp();
+                    } else if (row < g.M) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int col = n0 + cbeg + k + j;
+                            if (col < g.N) store_out<EPI, MEAN>(g, row, col, ro, split, vm[j], vv[j]);
+                        }
                     }
                 }
             }
