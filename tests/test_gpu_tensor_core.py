@@ -1,8 +1,8 @@
 """The tcgen05 (3xTF32) moment contractions against the float64 oracle.
 
 Shapes are chosen so that the library routes them to the tensor-core kernel
-(M ≥ 64, N ≥ 16, reduction ≥ 32 and M·N·K ≥ 4e6) and cover ragged tails in
-every dimension, the variance-only forward, row-split (NCHW) operand views,
+(M ≥ 16, N ≥ 16, reduction ≥ 8 and M·N·K ≥ 4e6) and cover ragged tails in
+every dimension, operands narrower than one K-block or a quarter tile, the variance-only forward, row-split (NCHW) operand views,
 the split reduction of the weight sums, the fused capped update and batched
 attention products. Each test also checks that no bounded wait inside the
 kernel ran out (tagi_device_status).
@@ -32,11 +32,11 @@ def _rnd(gen, *shape, u=False, scale=1.0, lo=0.0):
 
 
 def _routes_to_tc(M, N, K):
-    return M >= 64 and N >= 16 and K >= 32 and M * N * K >= 4e6
+    return M >= 16 and N >= 16 and K >= 8 and M * N * K >= 4e6
 
 
 TC_SHAPES = [(128, 64, 512), (300, 77, 200), (1000, 576, 64), (2048, 1152, 128),
-             (4099, 35, 130), (1555, 256, 17)]
+             (4099, 35, 130), (1555, 256, 17), (131072, 27, 64), (40000, 12, 48), (24, 2048, 512)]
 
 
 @pytest.mark.parametrize("M,K,N", TC_SHAPES)

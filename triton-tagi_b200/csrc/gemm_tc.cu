@@ -55,7 +55,12 @@ namespace {
 
 constexpr int kBK = 8;              // tf32 elements per MMA along the reduction
 constexpr int kChunk = 16;          // stages accumulated in tensor memory before a fold
-constexpr int kDepth = 1;           // stages loaded ahead per producer thread (2 per group pair)
+// K-blocks loaded ahead per producer thread (each group owns every other
+// K-block). Two for the 64-column tiles of 64-channel convolutions was slower
+// than one (measured: weight sums 1.73 -> 2.04 ms, input deltas 1.44 -> 1.63 ms
+// per ResNet-18 step), so one throughout.
+template <int BN>
+constexpr int prefetch_depth() { return 1; }
 constexpr int kMaxStages = 8;       // operand stages in shared memory
 constexpr int kStageBudget = 224 * 1024;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -655,7 +660,7 @@ struct ProdCtx {
     int lane;
 };
 
-// One side's producer thread: stages grp, grp+2, ... with kDepth of them loaded
+// One side's producer thread: K-blocks grp, grp+2, ... with prefetch_depth of them loaded
 // ahead into registers.
 template <int VM, int BN, bool IS_A, int GM>
 __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, const Side& sd) {
@@ -726,6 +731,7 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
         return true;
     };
 
+    constexpr int kDepth = prefetch_depth<BN>();
     float buf[kDepth][2][8];
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) load(c.grp + 2 * d, buf[d]);
@@ -1153,7 +1159,10 @@ int launch_bn(const GemmArgs& g, int bn, int batch, cudaStream_t st, const char*
 int tc_pick(int vm, int M, int N, int Kr, int batch, bool fill) {
     (void)vm;
     if (!tc_enabled()) return 0;
-    if (M < 64 || N < 16 || Kr < 32) return 0;
+    // Narrow operands still beat the CUDA-core kernel when the work is large
+    // (the ResNet stem: reductions of 27, weight sums of 28 rows over 131072
+    // pixels); the tile's unused rows and reduction elements are zero.
+    if (M < 16 || N < 16 || Kr < 8) return 0;
     if (static_cast<double>(M) * N * Kr < 4.0e6) return 0;
     if (N <= 32) return 32;
     if (N <= 64 || !fill) return N <= 64 ? 64 : 128;
