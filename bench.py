@@ -194,6 +194,19 @@ ENTRY_BYTES = {
 }
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# contraction families, from one ncu capture of this build: 114 consecutive
+# contraction launches of two ResNet-18 steps (after 3 warm-up steps), and one
+# 4096 x 4096 x 4096 Linear forward scaled by M to the sweep's 8192-row headline
+# (A and the number of B re-reads both grow with M).
+MEASURED_TRAFFIC = {
+    ("r18", "moment_forward"): 53.5e6,
+    ("r18", "backward_delta"): 43.8e6,
+    ("r18", "param_grad"): 151.2e6,
+    ("swp", "moment_forward"): 2 * 1.822e9,
+}
+
+
 class LaunchTimer:
     """Times every library call with CUDA events (library call hook): the moment
     contractions by family with their flops, the other entries by name with
@@ -436,7 +449,8 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         achieved = dom["flops"] / dom["seconds"] / 1e12
         roof = {"bound": "tensor", "kernel": dom_name, "achieved": achieved, "peak": peak3,
                 "unit": "TFLOP/s", "frac": achieved / peak3 if peak3 else None,
-                "traffic": None,
+                "traffic": MEASURED_TRAFFIC.get((args.workload, dom_name)),
+                "traffic_unit": "bytes per launch (ncu)",
                 "peak_source": f"measured cuBLAS TF32 burst {tf32:.0f} TF/s / 3 (3xTF32-effective)",
                 "launches": dom["launches"],
                 "share_of_step": dom["seconds"] / fam_steps / (step_s / args.steps)}
@@ -554,7 +568,9 @@ def sweep_arm(args, rank: int, world: int, local: int) -> None:
                    "l2": "flushed before every timed launch (256 MiB write)"},
         "roofline": {"bound": "tensor", "kernel": "moment_forward", "achieved": fwd["tflops"],
                      "peak": peak_tf32 / 3.0, "unit": "TFLOP/s", "frac": fwd["frac"],
-                     "traffic": None,
+                     "traffic": MEASURED_TRAFFIC.get(("swp", "moment_forward"))
+                     if (top["M"], top["K"]) == (8192, 4096) else None,
+                     "traffic_unit": "bytes per launch (ncu)",
                      "peak_source": f"measured cuBLAS TF32 burst {peak_tf32:.0f} TF/s / 3"},
         "sweep": rows, "gpu_launches": int(kernel_launches() - launches0),
         "clocks": clocks.summary(),
