@@ -124,6 +124,8 @@ __device__ __forceinline__ int div_small(int i, float r) {
 // patch columns (c, kh, kw) and walks ow, so that a warp stores 32 consecutive
 // columns of one patch row. Index decoding uses div_small (all indices of a CTA
 // are below 2^22: staged elements and patch columns are bounded by 32 KB and K).
+// PLANES: 1 (means) or 2 (means and variances).
+template <int PLANES>
 __global__ void im2col_rows_kernel(const float* xm, const float* xS, float* pm, float* pS,
                                    ConvGeom g, int cslice) {
     // [plane][cslice * k lines][ls]: an odd line stride puts the same column of
@@ -132,25 +134,39 @@ __global__ void im2col_rows_kernel(const float* xm, const float* xS, float* pm, 
     const int ls = g.W | 1;
     const int n = blockIdx.x / g.Ho, oh = blockIdx.x - n * g.Ho;
     const int kk = g.k * g.k, K = g.C * kk;
-    const int planes = pS ? 2 : 1;
     const int tid = threadIdx.x, nth = blockDim.x;
     const float rW = 1.f / g.W, rk = 1.f / g.k, rkk = 1.f / kk;
     const int64_t row0 = (static_cast<int64_t>(n) * g.Ho + oh) * g.Wo;  // first patch row
     const int ih0 = oh * g.s - g.p_tl;
+    const float* img_m = xm + static_cast<int64_t>(n) * g.C * g.H * g.W;
+    const float* img_S = PLANES == 2 ? xS + static_cast<int64_t>(n) * g.C * g.H * g.W : nullptr;
     for (int c0 = 0; c0 < g.C; c0 += cslice) {
         const int cs = min(cslice, g.C - c0);
         const int nlines = cs * g.k, pstride = nlines * ls;
-        const float rn = 1.f / nlines;
-        const int ne = planes * nlines * g.W;
-        for (int e = tid; e < ne; e += nth) {
-            const int line = div_small(e, rW), w = e - line * g.W;
-            const int pl = div_small(line, rn), li = line - pl * nlines;
-            const int cl = div_small(li, rk), ih = ih0 + (li - cl * g.k);
-            const bool in = ih >= 0 && ih < g.H;
-            // rows outside the image are zero-filled (the source is not read)
-            const float* src = (pl ? xS : xm) +
-                               ((static_cast<int64_t>(n) * g.C + c0 + cl) * g.H + (in ? ih : 0)) * g.W;
-            cp_async4(lines + pl * pstride + li * ls + w, src + w, in);
+        if (g.W % 32 == 0) {
+            // a warp stages whole lines: one decode per line, lanes along the line
+            for (int l = tid >> 5; l < PLANES * nlines; l += nth >> 5) {
+                const int pl = PLANES == 2 && l >= nlines, li = pl ? l - nlines : l;
+                const int cl = div_small(li, rk), ih = ih0 + (li - cl * g.k);
+                const bool in = static_cast<unsigned>(ih) < static_cast<unsigned>(g.H);
+                const float* src = (pl ? img_S : img_m) +
+                                   (static_cast<int64_t>(c0 + cl) * g.H + (in ? ih : 0)) * g.W;
+                float* dst = lines + pl * pstride + li * ls;
+                for (int w = tid & 31; w < g.W; w += 32) cp_async4(dst + w, src + w, in);
+            }
+        } else {
+            const float rn = 1.f / nlines;
+            const int ne = PLANES * nlines * g.W;
+            for (int e = tid; e < ne; e += nth) {
+                const int line = div_small(e, rW), w = e - line * g.W;
+                const int pl = PLANES == 2 ? div_small(line, rn) : 0, li = line - pl * nlines;
+                const int cl = div_small(li, rk), ih = ih0 + (li - cl * g.k);
+                const bool in = static_cast<unsigned>(ih) < static_cast<unsigned>(g.H);
+                // rows outside the image are zero-filled (the source is not read)
+                const float* src = (pl ? img_S : img_m) +
+                                   (static_cast<int64_t>(c0 + cl) * g.H + (in ? ih : 0)) * g.W;
+                cp_async4(lines + pl * pstride + li * ls + w, src + w, in);
+            }
         }
         cp_async_wait_all();
         __syncthreads();
@@ -158,20 +174,27 @@ __global__ void im2col_rows_kernel(const float* xm, const float* xS, float* pm, 
         // columns per thread pass and patch rows per column
         const int step = ncol >= nth ? 1 : nth / ncol;
         const int j0 = ncol >= nth ? tid : tid % ncol, ow0 = ncol >= nth ? 0 : tid / ncol;
+        const int jstep = ncol >= nth ? nth : ncol;
+        const int64_t ostep = static_cast<int64_t>(step) * K;
+        const int istep = step * g.s;
         if (ow0 < step) {
-            for (int j = j0; j < ncol; j += (ncol >= nth ? nth : ncol)) {
+            for (int j = j0; j < ncol; j += jstep) {
                 const int cl = div_small(j, rkk), t = j - cl * kk;
                 const int kh = div_small(t, rk), kw = t - kh * g.k;
                 const float* line = lines + (cl * g.k + kh) * ls;
-                float* om = pm + row0 * K + c0 * kk + j;
-                float* oS = pS ? pS + row0 * K + c0 * kk + j : nullptr;
+                const int64_t o0 = (row0 + ow0) * K + c0 * kk + j;
+                float* om = pm + o0;
+                float* oS = PLANES == 2 ? pS + o0 : nullptr;
                 int iw = ow0 * g.s - g.p_tl + kw;
-                for (int ow = ow0; ow < g.Wo; ow += step, iw += step * g.s) {
-                    const bool in = iw >= 0 && iw < g.W;
-                    om[static_cast<int64_t>(ow) * K] = in ? line[iw] : 0.f;
-                    if (oS) oS[static_cast<int64_t>(ow) * K] = in ? line[pstride + iw] : 0.f;
+#pragma unroll 4
+                for (int ow = ow0; ow < g.Wo; ow += step, iw += istep, om += ostep) {
+                    const bool in = static_cast<unsigned>(iw) < static_cast<unsigned>(g.W);
+                    *om = in ? line[iw] : 0.f;
+                    if (PLANES == 2) {
+                        *oS = in ? line[pstride + iw] : 0.f;
+                        oS += ostep;
+                    }
                 }
-                if (ncol < nth) break;
             }
         }
         __syncthreads();
@@ -218,6 +241,76 @@ __global__ void col2im_kernel(const float* cm, const float* cS, float* dm, float
     }
 }
 
+// The same gather per (image, channel slice) CTA: the patch columns of the
+// slice for all L = Ho*Wo patch rows of the image (both planes) are staged in
+// shared memory with coalesced asynchronous copies (each row contributes cs*k*k
+// contiguous floats), then each thread gathers output pixels (c, h, w) from
+// shared memory, visiting taps in the same (kh, kw) order, so the sums are
+// bit-identical to col2im_kernel.
+// q / S and q % S with C semantics (truncation toward zero); S = 0 reads the
+// stride at run time, S = 2 uses shifts.
+template <int S>
+__device__ __forceinline__ void div_trunc(int q, int s, int* quo, bool* exact) {
+    if (S == 2) {
+        *quo = q >= 0 ? (q >> 1) : -((-q) >> 1);
+        *exact = (q & 1) == 0;
+    } else {
+        *quo = q / s;
+        *exact = q % s == 0;
+    }
+}
+
+template <bool ADJOINT, int S>
+__global__ void col2im_img_kernel(const float* cm, const float* cS, float* dm, float* dS,
+                                  ConvGeom g, int cslice) {
+    extern __shared__ float patch[];  // [plane][L][rs]
+    const int kk = g.k * g.k, K = g.C * kk, L = g.Ho * g.Wo;
+    const int nslice = (g.C + cslice - 1) / cslice;
+    const int n = blockIdx.x / nslice, c0 = (blockIdx.x - n * nslice) * cslice;
+    const int cs = min(cslice, g.C - c0);
+    const int q = cs * kk, rs = (cslice * kk) | 1;  // columns staged per row; odd row stride
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const float rq = 1.f / q;
+    const int64_t base = static_cast<int64_t>(n) * L * K + static_cast<int64_t>(c0) * kk;
+    for (int e = tid; e < L * q; e += nth) {
+        const int r = div_small(e, rq), j = e - r * q;
+        const int64_t src = base + static_cast<int64_t>(r) * K + j;
+        cp_async4(patch + r * rs + j, cm + src, true);
+        cp_async4(patch + (L + r) * rs + j, cS + src, true);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int hw = g.H * g.W, total = cs * hw;
+    const float rW = 1.f / g.W, rhw = 1.f / hw;
+    for (int i = tid; i < total; i += nth) {
+        const int cl = div_small(i, rhw), p = i - cl * hw;
+        const int h = div_small(p, rW), w = p - h * g.W;
+        float am = 0.f, aS = 0.f;
+        for (int kh = 0; kh < g.k; ++kh) {
+            int oh;
+            bool exh;
+            div_trunc<S>(h + g.p_tl - kh, g.s, &oh, &exh);  // truncates toward zero, as the reference
+            const bool okh = exh && oh >= 0 && oh < g.Ho && (!ADJOINT || h + g.p_tl - kh >= 0);
+            if (!okh) continue;
+            for (int kw = 0; kw < g.k; ++kw) {
+                const int own = w + g.p_tl - kw;
+                int ow;
+                bool exw;
+                div_trunc<S>(own, g.s, &ow, &exw);
+                const bool okw = ow >= 0 && ow < g.Wo && (!ADJOINT || (own >= 0 && exw));
+                if (okw) {
+                    const int o = (oh * g.Wo + ow) * rs + cl * kk + kh * g.k + kw;
+                    am += patch[o];
+                    aS += patch[L * rs + o];
+                }
+            }
+        }
+        const int64_t out = (static_cast<int64_t>(n) * g.C + c0 + cl) * hw + p;
+        dm[out] = am;
+        dS[out] = aS;
+    }
+}
+
 }  // namespace
 }  // namespace tagi
 
@@ -240,8 +333,14 @@ extern "C" int tagi_im2col(const float* xm, const float* xS, float* pm, float* p
     const uintptr_t al = (reinterpret_cast<uintptr_t>(pm) | reinterpret_cast<uintptr_t>(pS)) & 15;
     // div_small bounds: staged elements (<= 8192) and patch columns below 2^22
     if (cslice >= 1 && N * g.Ho <= INT_MAX && C * k * k < (int64_t(1) << 22)) {
-        im2col_rows_kernel<<<static_cast<unsigned>(N * g.Ho), 256, cslice * line_bytes,
-                             as_stream(stream)>>>(xm, xS, pm, pS, g, static_cast<int>(cslice));
+        const unsigned grid = static_cast<unsigned>(N * g.Ho);
+        const size_t smem = static_cast<size_t>(cslice * line_bytes);
+        if (xS)
+            im2col_rows_kernel<2><<<grid, 256, smem, as_stream(stream)>>>(
+                xm, xS, pm, pS, g, static_cast<int>(cslice));
+        else
+            im2col_rows_kernel<1><<<grid, 256, smem, as_stream(stream)>>>(
+                xm, xS, pm, pS, g, static_cast<int>(cslice));
     } else if ((C * k * k) % 4 == 0 && al == 0) {
         im2col_v4_kernel<<<grid_1d(total / 4, 256), 256, 0, as_stream(stream)>>>(xm, xS, pm, pS, g);
     } else {
@@ -261,9 +360,36 @@ extern "C" int tagi_col2im(const float* cm, const float* cS, float* dm, float* d
     const int64_t total = N * C * H * W;
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(cm && cS && dm && dS, TAGI_E_BAD_ARG, "%s: null pointer", what);
-    if (mode == 0)
+    // Staged per (image, channel slice) when one channel's patch columns for the
+    // image fit: both planes of L rows x cslice*k*k columns within 96 KB.
+    const int64_t L = static_cast<int64_t>(g.Ho) * g.Wo, kk = k * k;
+    const int64_t per_c = 2 * L * kk * static_cast<int64_t>(sizeof(float));
+    const int64_t budget = 96 * 1024;
+    int64_t cslice = per_c > 0 ? std::min<int64_t>(C, budget / per_c) : 0;
+    // the odd row stride may add one column per row
+    while (cslice >= 1 && 2 * L * ((cslice * kk) | 1) * 4 > budget) --cslice;
+    const int64_t ctas = cslice >= 1 ? N * ((C + cslice - 1) / cslice) : 0;
+    const bool small = L * C * kk < (int64_t(1) << 22) && H * W * cslice < (int64_t(1) << 22);
+    if (cslice >= 1 && ctas <= INT_MAX && small) {
+        static bool attr_set[4] = {false, false, false, false};
+        const size_t smem = static_cast<size_t>(2 * L * ((cslice * kk) | 1) * 4);
+        cudaStream_t st = as_stream(stream);
+        auto run = [&](auto kernel, int which) {
+            if (!attr_set[which]) {
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+                attr_set[which] = true;
+            }
+            kernel<<<static_cast<unsigned>(ctas), 256, smem, st>>>(cm, cS, dm, dS, g,
+                                                                  static_cast<int>(cslice));
+        };
+        if (mode == 0)
+            stride == 2 ? run(col2im_img_kernel<false, 2>, 0) : run(col2im_img_kernel<false, 0>, 1);
+        else
+            stride == 2 ? run(col2im_img_kernel<true, 2>, 2) : run(col2im_img_kernel<true, 0>, 3);
+    } else if (mode == 0) {
         col2im_kernel<false><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(cm, cS, dm, dS, g);
-    else
+    } else {
         col2im_kernel<true><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(cm, cS, dm, dS, g);
+    }
     return check_launch(what);
 }
