@@ -161,7 +161,9 @@ def _worker(rank, world, init, out_q):
         sl = slice(rank * shard, (rank + 1) * shard)
         for _ in range(2):
             dp.step(x[sl], y[sl], 0.05)
-        out_q.put((rank, [t.clone() for l in net.leaves() for t in (l.mw, l.Sw, l.mb, l.Sb)]))
+        # numpy arrays travel by value: a torch tensor would travel as a shared-memory
+        # handle that is gone if this process exits before the parent receives it
+        out_q.put((rank, [t.clone().numpy() for l in net.leaves() for t in (l.mw, l.Sw, l.mb, l.Sb)]))
     finally:
         dist.destroy_process_group()
 
@@ -215,7 +217,8 @@ def test_two_rank_step_equals_full_batch_step():
     procs = [ctx.Process(target=_worker, args=(r, 2, init, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=120) for _ in procs)
+    results = {r: [torch.from_numpy(a) for a in arrs]
+               for r, arrs in (q.get(timeout=120) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -398,3 +398,32 @@ def test_empty_inputs_are_no_ops():
     assert triton_fused_var_forward(z, z, w, w, torch.zeros(1, 3, device=DEV)).shape == (0, 3)
     e = torch.empty(0, device=DEV)
     update_parameters(e, e, e, e, 2.0)
+
+
+@pytest.mark.parametrize("N,C,H,W", [(8, 16, 6, 6), (3, 5, 7, 5), (16, 64, 8, 8)])
+def test_relu_jacobian_folded_into_batchnorm_backward(N, C, H, W):
+    """A ReLU feeding a BatchNorm2D, as containers run its backward (the ReLU's
+    Jacobian applied by the BatchNorm's backward), against the two layers' own
+    backward passes: deltas and parameter deltas."""
+    from triton_tagi import BatchNorm2D, ReLU
+
+    gen = torch.Generator().manual_seed(N * C + H)
+    mz, Sz = g(rnd(gen, N, C, H, W)), g(rnd(gen, N, C, H, W, kind="u", scale=0.5, lo=1e-3))
+    dm, dS = g(rnd(gen, N, C, H, W, scale=0.1)), g(-rnd(gen, N, C, H, W, kind="u", scale=1e-2))
+    outs = []
+    for fused in (False, True):
+        torch.manual_seed(3)
+        relu, bn = ReLU(), BatchNorm2D(C, device=DEV)
+        ma, Sa = bn.forward(*relu.forward(mz, Sz))
+        J = relu.J.clone()
+        bn._set_param_mode("deltas")
+        if fused:
+            dz, dSz = bn.backward(dm, dS, relu=relu)
+        else:
+            dz, dSz = relu.backward(*bn.backward(dm, dS))
+        outs.append((ma, Sa, J, bn.running_mean, bn.running_var, dz, dSz, bn.delta_mw,
+                     bn.delta_Sw, bn.delta_mb, bn.delta_Sb))
+    names = ("ma", "Sa", "J", "running_mean", "running_var", "d_mz", "d_Sz", "delta_mw",
+             "delta_Sw", "delta_mb", "delta_Sb")
+    for name, a, b in zip(names, *outs):
+        torch.testing.assert_close(b, a, rtol=1e-6, atol=1e-9, msg=name)

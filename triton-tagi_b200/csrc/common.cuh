@@ -43,6 +43,26 @@ __device__ __forceinline__ void capped_pair(float& m, float& S, float dm, float 
     S = S_raw <= 0.f ? 1e-5f : S_raw;
 }
 
+// Rectified-Gaussian moments of a = max(0, z), z ~ N(mz, Sz), and the Jacobian
+// J = Phi(alpha) (triton_tagi/layers/relu.py:63-86). Shared by the ReLU kernels
+// and the contraction epilogues that apply a following ReLU.
+__device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
+    constexpr float kInvSqrt2Pi = 0.3989422804014327f;
+    constexpr float kInvSqrt2 = 0.7071067811865476f;
+    const float Ss = fmaxf(Sz, 1e-30f);
+    const float sd = sqrtf(Ss);
+    const float alpha = mz / sd;
+    const float pdf = expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
+    // Below alpha = -5 the erf form cancels to 0 in fp32; the reference uses the
+    // leading asymptotic term phi(alpha)/|alpha| there.
+    const float cdf = alpha < -5.0f ? pdf / (-alpha) : 0.5f * (1.0f + erff(alpha * kInvSqrt2));
+    const float mu = sd * pdf + mz * cdf;
+    const float v = -mu * mu + 2.0f * mu * mz - mz * sd * pdf + (Ss - mz * mz) * cdf;
+    ma = mu;
+    Sa = fmaxf(v, 0.0f);
+    J = cdf;
+}
+
 constexpr int kNumSMs = 148;
 
 inline unsigned grid_1d(int64_t n, int threads, int64_t max_blocks = 148 * 16) {

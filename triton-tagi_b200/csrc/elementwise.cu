@@ -56,22 +56,7 @@ __global__ void innovation_kernel(const float* y, const float* mu, const float* 
     }
 }
 
-// ---- rectified-Gaussian moments (relu.py:63-86) -----------------------------
-__device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
-    const float Ss = fmaxf(Sz, 1e-30f);
-    const float sd = sqrtf(Ss);
-    const float alpha = mz / sd;
-    const float pdf = expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
-    // Below alpha = -5 the erf form cancels to 0 in fp32; the reference uses the
-    // leading asymptotic term phi(alpha)/|alpha| there.
-    const float cdf = alpha < -5.0f ? pdf / (-alpha) : 0.5f * (1.0f + erff(alpha * kInvSqrt2));
-    const float mu = sd * pdf + mz * cdf;
-    const float v = -mu * mu + 2.0f * mu * mz - mz * sd * pdf + (Ss - mz * mz) * cdf;
-    ma = mu;
-    Sa = fmaxf(v, 0.0f);
-    J = cdf;
-}
-
+// ---- rectified-Gaussian moments: relu_one (common.cuh) ----------------------
 __global__ void relu_v4(const float4* mz, const float4* Sz, float4* ma, float4* Sa, float4* J,
                         int64_t n4) {
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;

@@ -188,7 +188,7 @@ __global__ void bn_forward_kernel(const float* mz, const float* Sz, const float*
 template <bool V4>
 __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     const float* dma, const float* dSa, const float* mhat, const float* var, const float* mg,
-    float* dmz, float* dSz, double* grads, int N, int C, int HW, float eps) {
+    float* dmz, float* dSz, const float* rj, double* grads, int N, int C, int HW, float eps) {
     __shared__ double red[4 * 32];
     __shared__ double part[4];
     const ChanSlab sl(N, C, HW, blockIdx.y);
@@ -197,13 +197,19 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     const float inv_std = 1.0f / sqrtf(rs + eps);
     const float inv_var = 1.0f / (rs + eps);
     double v[4] = {0.0, 0.0, 0.0, 0.0};
-    auto one = [&](float dm, float dS, float mh, float& om, float& oS) {
+    // rj: Jacobian of the ReLU that produced this layer's input (NULL: none);
+    // applied to the outgoing deltas in the ReLU backward's own order.
+    auto one = [&](float dm, float dS, float mh, float j, float& om, float& oS) {
         v[0] += static_cast<double>(dm * mh);
         v[1] += static_cast<double>(dS * (mh * mh));
         v[2] += dm;
         v[3] += dS;
         om = (dm * g) * inv_std;
         oS = (dS * g * g) * inv_var;
+        if (rj) {
+            om = om * j;
+            oS = oS * j * j;
+        }
     };
     if (V4) {
         const int HW4 = HW / 4, total = sl.nimg * HW4;
@@ -213,11 +219,12 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
             const float4 a = __ldg(reinterpret_cast<const float4*>(dma + o));
             const float4 b = __ldg(reinterpret_cast<const float4*>(dSa + o));
             const float4 c = __ldg(reinterpret_cast<const float4*>(mhat + o));
+            const float4 j = rj ? __ldg(reinterpret_cast<const float4*>(rj + o)) : float4{};
             float4 om, oS;
-            one(a.x, b.x, c.x, om.x, oS.x);
-            one(a.y, b.y, c.y, om.y, oS.y);
-            one(a.z, b.z, c.z, om.z, oS.z);
-            one(a.w, b.w, c.w, om.w, oS.w);
+            one(a.x, b.x, c.x, j.x, om.x, oS.x);
+            one(a.y, b.y, c.y, j.y, om.y, oS.y);
+            one(a.z, b.z, c.z, j.z, om.z, oS.z);
+            one(a.w, b.w, c.w, j.w, om.w, oS.w);
             *reinterpret_cast<float4*>(dmz + o) = om;
             *reinterpret_cast<float4*>(dSz + o) = oS;
         }
@@ -226,7 +233,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
         for (int t = threadIdx.x; t < total; t += blockDim.x) {
             const int li = t / HW;
             const int64_t o = sl.offset(li, t - li * HW);
-            one(dma[o], dSa[o], mhat[o], dmz[o], dSz[o]);
+            one(dma[o], dSa[o], mhat[o], rj ? rj[o] : 0.f, dmz[o], dSz[o]);
         }
     }
     cluster_channel_sum<4>(v, red, part);
@@ -427,8 +434,8 @@ extern "C" int tagi_bn_forward(const float* mz, const float* Sz, const float* me
 
 extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat,
                                 const float* var, const float* mg, float* dmz, float* dSz,
-                                double* grads, int64_t N, int64_t C, int64_t HW, float eps,
-                                void* stream) {
+                                const float* relu_J, double* grads, int64_t N, int64_t C,
+                                int64_t HW, float eps, void* stream) {
     const char* what = "tagi_bn_backward";
     TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     if (C == 0) return TAGI_OK;
@@ -438,12 +445,14 @@ extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float*
     const int S = bn_split(C, N);
     const uintptr_t al = reinterpret_cast<uintptr_t>(dma) | reinterpret_cast<uintptr_t>(dSa) |
                          reinterpret_cast<uintptr_t>(m_hat) | reinterpret_cast<uintptr_t>(dmz) |
-                         reinterpret_cast<uintptr_t>(dSz);
+                         reinterpret_cast<uintptr_t>(dSz) | reinterpret_cast<uintptr_t>(relu_J);
     const bool v4 = HW % 4 == 0 && (al & 15) == 0;
     return v4 ? launch_cluster(bn_backward_kernel<true>, S, (int)C, as_stream(stream), what, dma,
-                               dSa, m_hat, var, mg, dmz, dSz, grads, (int)N, (int)C, (int)HW, eps)
+                               dSa, m_hat, var, mg, dmz, dSz, relu_J, grads, (int)N, (int)C,
+                               (int)HW, eps)
               : launch_cluster(bn_backward_kernel<false>, S, (int)C, as_stream(stream), what, dma,
-                               dSa, m_hat, var, mg, dmz, dSz, grads, (int)N, (int)C, (int)HW, eps);
+                               dSa, m_hat, var, mg, dmz, dSz, relu_J, grads, (int)N, (int)C,
+                               (int)HW, eps);
 }
 
 extern "C" int tagi_bn_apply_grads(const double* grads, int64_t C, int mode, float* mw, float* Sw,

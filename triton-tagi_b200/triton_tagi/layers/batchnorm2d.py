@@ -96,7 +96,10 @@ class BatchNorm2D(LearnableLayer):
           st)
         return ma, Sa
 
-    def backward(self, delta_ma: Tensor, delta_Sa: Tensor) -> tuple[Tensor, Tensor]:
+    def backward(self, delta_ma: Tensor, delta_Sa: Tensor, relu=None) -> tuple[Tensor, Tensor]:
+        """Input deltas and the γ/β sums; with ``relu`` (the ReLU layer that feeds
+        this one in a container) the deltas leave already multiplied by its
+        Jacobian, i.e. as ``relu.backward`` would return them."""
         check_cuda_f32(delta_ma, delta_Sa)
         dma, dSa = delta_ma.contiguous(), delta_Sa.contiguous()
         N, C, H, W = self.input_shape
@@ -108,9 +111,15 @@ class BatchNorm2D(LearnableLayer):
         mode = self._param_mode
         grads = (self._reducer.buffer(self, 4 * C, torch.float64) if mode == "sums"
                  else torch.empty(4 * C, device=dev, dtype=torch.float64))
+        rj = None
+        if relu is not None:
+            if relu.J is None or relu.J.numel() != dma.numel():
+                raise ValueError("BatchNorm2D.backward: the ReLU has no Jacobian of this size")
+            rj = relu.J.contiguous()
         L("tagi_bn_backward", dma.data_ptr(), dSa.data_ptr(), self.m_hat.data_ptr(),
           self._norm_var.data_ptr(), self.mw.data_ptr(), dmz.data_ptr(), dSz.data_ptr(),
-          grads.data_ptr(), N, C, H * W, float(self.eps), st)
+          rj.data_ptr() if rj is not None else None, grads.data_ptr(), N, C, H * W,
+          float(self.eps), st)
         if mode == "deltas":
             self.delta_mw = torch.empty(C, device=dev)
             self.delta_Sw = torch.empty(C, device=dev)

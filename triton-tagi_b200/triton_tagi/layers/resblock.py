@@ -99,22 +99,18 @@ class ResBlock(LearnableLayer):
 
     def forward(self, mu_in: Tensor, var_in: Tensor) -> tuple[Tensor, Tensor]:
         # Layers never modify their inputs, so the skip needs no copy.
-        mu_z, var_z = mu_in, var_in
-        for layer in self._main_layers:
-            mu_z, var_z = layer.forward(mu_z, var_z)
-        mu_x, var_x = mu_in, var_in
-        for layer in self._proj_layers:
-            mu_x, var_x = layer.forward(mu_x, var_x)
+        from .._chain import forward_chain
+
+        mu_z, var_z = forward_chain(self._main_layers, mu_in, var_in)
+        mu_x, var_x = forward_chain(self._proj_layers, mu_in, var_in)
         triton_add_shortcut(mu_x, var_x, mu_z, var_z)
         return mu_z, var_z
 
     def backward(self, delta_mu: Tensor, delta_var: Tensor) -> tuple[Tensor, Tensor]:
-        d_mu_main, d_var_main = delta_mu, delta_var
-        for layer in reversed(self._main_layers):
-            d_mu_main, d_var_main = layer.backward(d_mu_main, d_var_main)
-        d_mu_skip, d_var_skip = delta_mu, delta_var
-        for layer in reversed(self._proj_layers):
-            d_mu_skip, d_var_skip = layer.backward(d_mu_skip, d_var_skip)
+        from .._chain import backward_chain
+
+        d_mu_main, d_var_main = backward_chain(self._main_layers, delta_mu, delta_var)
+        d_mu_skip, d_var_skip = backward_chain(self._proj_layers, delta_mu, delta_var)
         triton_delta_merge(d_mu_skip, d_var_skip, d_mu_main, d_var_main)
         return d_mu_main, d_var_main
 

@@ -28,7 +28,8 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
-from .base import Layer, LearnableLayer
+from ._chain import backward_chain, forward_chain
+from .base import LearnableLayer
 from .layers.multihead_attention import MultiheadAttentionV2
 from .layers.resblock import ResBlock
 from .update.observation import compute_innovation
@@ -80,12 +81,7 @@ class Sequential:
         return out
 
     def forward(self, x: Tensor) -> tuple[Tensor, Tensor]:
-        ma, Sa = x, torch.zeros_like(x)
-        for layer in self.layers:
-            if not isinstance(layer, Layer):
-                raise TypeError(f"Unknown layer type: {type(layer)}")
-            ma, Sa = layer.forward(ma, Sa)
-        return ma, Sa
+        return forward_chain(self.layers, x, torch.zeros_like(x))
 
     def step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
         if self.cuda_graph and self.reducer is None and x_batch.is_cuda:
@@ -129,8 +125,7 @@ class Sequential:
                 red.begin_step()
             if isinstance(first, LearnableLayer):
                 first._skip_input_delta = True  # the input's deltas are not used
-            for layer in reversed(self.layers):
-                delta_mu, delta_var = layer.backward(delta_mu, delta_var)
+            delta_mu, delta_var = backward_chain(self.layers, delta_mu, delta_var)
             if red is not None:
                 red.finish_step(cap)
             for layer in learn:
