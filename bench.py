@@ -355,7 +355,7 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     torch.manual_seed(1234)
     # Steps of small networks are a few dozen short kernels: replay them from a
     # CUDA graph (Sequential(cuda_graph=True); single GPU only).
-    graphed = args.workload in ("mlp", "cnn") and world == 1 and not args.no_graph
+    graphed = args.workload in ("mlp", "cnn", "r18") and world == 1 and not args.no_graph
     net = TT.Sequential(build_layers(args.workload, TT, dev), device=dev, cuda_graph=graphed)
     if world > 1:
         from triton_tagi.distributed import DataParallel

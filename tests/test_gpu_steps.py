@@ -136,7 +136,7 @@ def test_mlp_100_step_trajectory():
     assert vs_oracle <= 1e-2, vs_oracle
 
 
-@pytest.mark.parametrize("name,batch", [("mlp", 64), ("cnn", 16)])
+@pytest.mark.parametrize("name,batch", [("mlp", 64), ("cnn", 16), ("r18", 8)])
 def test_cuda_graph_steps_equal_eager_steps(name, batch):
     """Sequential(cuda_graph=True) replays the eager step's kernels: predictions
     and parameters after several steps (eager, capture + replay, replays, then a
