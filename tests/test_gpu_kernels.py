@@ -162,8 +162,10 @@ def test_remax_golden(golden, tag):
                            what=f"remax {nm}")
 
 
-@pytest.mark.parametrize("K", [3, 33, 200, 700])
+@pytest.mark.parametrize("K", [3, 33, 200, 512, 700, 1100])
 def test_remax_sizes(K):
+    """Rows of every Remax kernel (registers up to 128 classes, shared memory up
+    to 1024, global recomputation beyond)."""
     from triton_tagi.layers.remax import triton_remax
 
     gen = torch.Generator().manual_seed(K)

@@ -300,6 +300,60 @@ __global__ void remax_warp_kernel(const float* mz, const float* Sz, float* ma, f
     }
 }
 
+// Rows of 128 < K <= kRemaxSmemK classes (attention scores): one warp per row;
+// each class's mixture moments (pass 1) are computed once and kept in shared
+// memory (float64) for the two later passes, where remax_warp_kernel<0>
+// recomputes them from global memory. A lane only touches its own classes
+// (j = lane mod 32), in the same order, with the same arithmetic, so the
+// results are those of remax_warp_kernel.
+constexpr int kRemaxSmemK = 1024;
+constexpr int kRemaxSmemWarps = 8;
+__global__ void __launch_bounds__(32 * kRemaxSmemWarps)
+    remax_smem_kernel(const float* mz, const float* Sz, float* ma, float* Sa, float* J,
+                      int64_t rows, int K, int64_t stride) {
+    constexpr double EPS = 1e-6;
+    extern __shared__ double remax_rs[];  // [warp][3][K]
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    double* mu_m = remax_rs + static_cast<size_t>(w) * 3 * K;
+    double* var_m = mu_m + K;
+    double* cdf = var_m + K;
+    const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+         row < rows; row += warps) {
+        const int64_t base = row * stride;
+        double s_mu = 0.0, s_var = 0.0;
+        for (int j = lane; j < K; j += 32) {
+            const RemaxLocal l = remax_mixture(mz[base + j], Sz[base + j]);
+            mu_m[j] = l.mu_m;
+            var_m[j] = l.var_m;
+            cdf[j] = l.cdf;
+            s_mu += l.mu_m;
+            s_var += l.var_m;
+        }
+        const double mu_t = fmax(warp_sum(s_mu), EPS);
+        const double var_t = fmax(warp_sum(s_var), EPS);
+        const double var_log_t = log(1.0 + var_t / (mu_t * mu_t));
+        const double mu_log_t = log(mu_t) - 0.5 * var_log_t;
+        auto local = [&](int j) {
+            RemaxLocal l;
+            l.Sz = static_cast<double>(Sz[base + j]);
+            l.mu_m = mu_m[j];
+            l.var_m = var_m[j];
+            l.cdf = cdf[j];
+            return l;
+        };
+        double s_raw = 0.0;
+        for (int j = lane; j < K; j += 32)
+            s_raw += remax_lognormal(local(j), mu_t, var_log_t, mu_log_t).mu_raw;
+        const double sum_raw = fmax(warp_sum(s_raw), EPS);
+        for (int j = lane; j < K; j += 32) {
+            const RemaxLocal l = local(j);
+            const RemaxStage2 s2 = remax_lognormal(l, mu_t, var_log_t, mu_log_t);
+            remax_finish(l, s2, sum_raw, ma[base + j], Sa[base + j], J[base + j]);
+        }
+    }
+}
+
 // ---- launch helpers ---------------------------------------------------------
 inline bool all_aligned(std::initializer_list<const void*> ps) {
     for (const void* p : ps)
@@ -433,7 +487,17 @@ extern "C" int tagi_remax_forward(const float* mz, const float* Sz, float* ma, f
         remax_warp_kernel<1><<<grid, 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
     else if (K <= 128)
         remax_warp_kernel<4><<<grid, 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
-    else
+    else if (K <= kRemaxSmemK) {
+        static bool attr = false;
+        const size_t smem = sizeof(double) * 3 * static_cast<size_t>(K) * kRemaxSmemWarps;
+        if (!attr) {
+            cudaFuncSetAttribute(remax_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(double) * 3 * kRemaxSmemK * kRemaxSmemWarps));
+            attr = true;
+        }
+        remax_smem_kernel<<<grid_1d(rows * 32, 32 * kRemaxSmemWarps), 32 * kRemaxSmemWarps, smem,
+                            st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
+    } else
         remax_warp_kernel<0><<<grid, 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
     return check_launch(what);
 }
