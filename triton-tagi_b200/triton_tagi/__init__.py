@@ -11,12 +11,13 @@ from .base import Layer, LearnableLayer
 from .layers import (Add, AvgPool2D, BatchNorm2D, Conv2D, Embedding, Flatten, Linear,
                      MultiheadAttentionV2, PositionalEncoding, ReLU, Remax, ResBlock, RMSNorm)
 from .network import Sequential
+from .checkpoint import RunDir, load_model
 from .param_init import (gaussian_param_init, he_init, init_weight_bias_conv2d,
                          init_weight_bias_linear, init_weight_bias_norm, xavier_init)
 
 __version__ = "0.1.0"
 __all__ = [
-    "Layer", "LearnableLayer", "Sequential",
+    "Layer", "LearnableLayer", "Sequential", "RunDir", "load_model",
     "Add", "AvgPool2D", "BatchNorm2D", "Conv2D", "Embedding", "Flatten", "Linear",
     "MultiheadAttentionV2", "PositionalEncoding", "RMSNorm", "ReLU", "Remax", "ResBlock",
     "he_init", "xavier_init", "gaussian_param_init", "init_weight_bias_linear",
