@@ -310,6 +310,18 @@ int tagi_bn_forward(const float* mz, const float* Sz, const float* mean, const f
                     float* Sa, float* m_hat, float* S_hat, int64_t N, int64_t C, int64_t HW,
                     float eps, void* stream);
 
+/* Training-mode forward of one process in one launch: the channel sums, the
+ * finalisation (mean, Bessel-corrected variance, running statistics and the
+ * first-call scale, as tagi_bn_finalize with count = N*H*W) and the normalised
+ * affine (as tagi_bn_forward with m_hat cached), each channel on one thread-
+ * block cluster. mean, var receive the statistics. Data-parallel SyncBN, which
+ * all-reduces the sums between the passes, uses the three entries above. */
+int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* var,
+                          float* running_mean, float* running_var, float* mg, const float* Sg,
+                          const float* mb, const float* Sb, float* ma, float* Sa, float* m_hat,
+                          int64_t N, int64_t C, int64_t HW, int first, int preserve_var,
+                          float momentum, float eps, void* stream);
+
 /* Delta propagation plus per-channel raw sums (float64)
  * grads[0:C]=sum dma*m_hat, [C:2C]=sum dSa*m_hat^2, [2C:3C]=sum dma, [3C:4C]=sum dSa.
  * relu_J (NULL: none): Jacobian of a ReLU that produced this layer's input;

@@ -361,10 +361,10 @@ extern "C" int tagi_col2im(const float* cm, const float* cS, float* dm, float* d
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(cm && cS && dm && dS, TAGI_E_BAD_ARG, "%s: null pointer", what);
     // Staged per (image, channel slice) when one channel's patch columns for the
-    // image fit: both planes of L rows x cslice*k*k columns within 96 KB.
+    // image fit: both planes of L rows x cslice*k*k columns within 48 KB.
     const int64_t L = static_cast<int64_t>(g.Ho) * g.Wo, kk = k * k;
     const int64_t per_c = 2 * L * kk * static_cast<int64_t>(sizeof(float));
-    const int64_t budget = 96 * 1024;
+    const int64_t budget = 48 * 1024;  // 4 CTAs per SM: staging overlaps gathering
     int64_t cslice = per_c > 0 ? std::min<int64_t>(C, budget / per_c) : 0;
     // the odd row stride may add one column per row
     while (cslice >= 1 && 2 * L * ((cslice * kk) | 1) * 4 > budget) --cslice;

@@ -272,6 +272,110 @@ __global__ void bn_forward_v4_kernel(const float4* mz, const float4* Sz, const f
     }
 }
 
+// Training-mode forward in one launch (single process: no all-reduce between
+// the passes): each channel's cluster sums its planes as bn_sums_kernel, rank 0
+// finalises the statistics as bn_finalize_kernel (running statistics, the
+// first-call scale) and hands mean, variance and scale to every rank through
+// distributed shared memory, and each block normalises the elements it summed
+// (read again from L2) as bn_forward_v4_kernel / bn_forward_kernel.
+template <bool V4>
+__global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
+    const float* mz, const float* Sz, float* mean, float* var, float* rmean, float* rvar,
+    float* mg, const float* Sg, const float* mb, const float* Sb, float* ma, float* Sa,
+    float* mhat, int N, int C, int HW, double count, int first, int preserve_var, float momentum,
+    float one_minus, float eps) {
+    __shared__ double red[3 * 32];
+    __shared__ double part[3];
+    __shared__ float stat[3];  // mean, variance, scale of the channel
+    const ChanSlab sl(N, C, HW, blockIdx.y);
+    double v[3] = {0.0, 0.0, 0.0};
+    const int HW4 = HW / 4;
+    const int total = V4 ? sl.nimg * HW4 : sl.nimg * HW;
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+        if (V4) {
+            const int li = t / HW4, h = (t - li * HW4) * 4;
+            const int64_t o = sl.offset(li, h);
+            const float4 m = __ldg(reinterpret_cast<const float4*>(mz + o));
+            const float4 S = __ldg(reinterpret_cast<const float4*>(Sz + o));
+            const float mm[4] = {m.x, m.y, m.z, m.w}, ss[4] = {S.x, S.y, S.z, S.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const double x = mm[e];
+                v[0] += x;
+                v[1] += ss[e];
+                v[2] += x * x;
+            }
+        } else {
+            const int li = t / HW;
+            const int64_t o = sl.offset(li, t - li * HW);
+            const double x = mz[o];
+            v[0] += x;
+            v[1] += Sz[o];
+            v[2] += x * x;
+        }
+    }
+    cluster_channel_sum<3>(v, red, part);
+    cg::cluster_group cluster = cg::this_cluster();
+    if (cluster.block_rank() == 0 && threadIdx.x == 0) {
+        const int c = sl.c;
+        const float m = static_cast<float>(v[0] / count);
+        const float mS = static_cast<float>(v[1] / count);
+        const float msq = static_cast<float>(v[2] / count);
+        const float bessel = static_cast<float>(count / (count - 1.0));
+        const float vv = (mS + msq - m * m) * bessel;
+        mean[c] = m;
+        var[c] = vv;
+        if (first) {
+            rmean[c] = m;
+            rvar[c] = vv;
+            if (preserve_var) mg[c] = sqrtf(vv + eps);
+        } else {
+            rmean[c] = one_minus * rmean[c] + momentum * m;
+            rvar[c] = one_minus * rvar[c] + momentum * vv;
+        }
+        const float g = mg[c];
+        for (unsigned r = 0; r < cluster.num_blocks(); ++r) {
+            float* peer = cluster.map_shared_rank(stat, r);
+            peer[0] = m;
+            peer[1] = vv;
+            peer[2] = g;
+        }
+    }
+    cluster.sync();
+    const int c = sl.c;
+    const float mu = stat[0], rs = stat[1], g = stat[2];
+    const float inv_std = 1.0f / sqrtf(rs + eps);
+    const float sg = Sg[c], b = mb[c], sb = Sb[c];
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+        if (V4) {
+            const int li = t / HW4, h = (t - li * HW4) * 4;
+            const int64_t o = sl.offset(li, h);
+            const float4 m = __ldg(reinterpret_cast<const float4*>(mz + o));
+            const float4 S = __ldg(reinterpret_cast<const float4*>(Sz + o));
+            const float mv[4] = {m.x, m.y, m.z, m.w}, Sv[4] = {S.x, S.y, S.z, S.w};
+            float om[4], oS[4], mh[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                mh[e] = (mv[e] - mu) * inv_std;
+                const float Sh = Sv[e] / (rs + eps);
+                om[e] = g * mh[e] + b;
+                oS[e] = g * g * Sh + sg * mh[e] * mh[e] + sg * Sh + sb;
+            }
+            *reinterpret_cast<float4*>(ma + o) = make_float4(om[0], om[1], om[2], om[3]);
+            *reinterpret_cast<float4*>(Sa + o) = make_float4(oS[0], oS[1], oS[2], oS[3]);
+            *reinterpret_cast<float4*>(mhat + o) = make_float4(mh[0], mh[1], mh[2], mh[3]);
+        } else {
+            const int li = t / HW;
+            const int64_t o = sl.offset(li, t - li * HW);
+            const float m_hat = (mz[o] - mu) * inv_std;
+            const float S_hat = Sz[o] / (rs + eps);
+            ma[o] = g * m_hat + b;
+            Sa[o] = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
+            mhat[o] = m_hat;
+        }
+    }
+}
+
 // Deltas S*g_m, S^2*g_S from float64 sums, written out or applied with the cap.
 __device__ __forceinline__ void vector_apply(int64_t i, double gm, double gS, int mode, float* m,
                                              float* S, float* d_m, float* d_S, float cap) {
@@ -430,6 +534,37 @@ extern "C" int tagi_bn_forward(const float* mz, const float* Sz, const float* me
             mz, Sz, mean, var, mg, Sg, mb, Sb, ma, Sa, m_hat, S_hat, total, (int)C, (int)HW, eps);
     }
     return check_launch(what);
+}
+
+extern "C" int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* var,
+                                     float* running_mean, float* running_var, float* mg,
+                                     const float* Sg, const float* mb, const float* Sb, float* ma,
+                                     float* Sa, float* m_hat, int64_t N, int64_t C, int64_t HW,
+                                     int first, int preserve_var, float momentum, float eps,
+                                     void* stream) {
+    const char* what = "tagi_bn_train_forward";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535, TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    const double count = static_cast<double>(N) * HW;
+    if (C == 0) return TAGI_OK;
+    TAGI_REQUIRE(count > 1.0, TAGI_E_BAD_ARG, "%s: need N*H*W > 1", what);
+    TAGI_REQUIRE(mz && Sz && mean && var && running_mean && running_var && mg && Sg && mb && Sb &&
+                     ma && Sa && m_hat,
+                 TAGI_E_BAD_ARG, "%s: null pointer", what);
+    TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    const int S = bn_split(C, N);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(mz) | reinterpret_cast<uintptr_t>(Sz) |
+                         reinterpret_cast<uintptr_t>(ma) | reinterpret_cast<uintptr_t>(Sa) |
+                         reinterpret_cast<uintptr_t>(m_hat);
+    const bool v4 = HW % 4 == 0 && (al & 15) == 0;
+    const float one_minus = static_cast<float>(1.0 - static_cast<double>(momentum));
+    return v4 ? launch_cluster(bn_train_forward_kernel<true>, S, (int)C, as_stream(stream), what,
+                               mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
+                               Sa, m_hat, (int)N, (int)C, (int)HW, count, first, preserve_var,
+                               momentum, one_minus, eps)
+              : launch_cluster(bn_train_forward_kernel<false>, S, (int)C, as_stream(stream), what,
+                               mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
+                               Sa, m_hat, (int)N, (int)C, (int)HW, count, first, preserve_var,
+                               momentum, one_minus, eps);
 }
 
 extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat,

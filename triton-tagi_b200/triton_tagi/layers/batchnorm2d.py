@@ -69,6 +69,23 @@ class BatchNorm2D(LearnableLayer):
         dev = mz.device
         st = stream(mz)
         L = lib()
+        if self.training and self._stats_allreduce is None:
+            # one launch: sums, statistics and normalisation per channel cluster
+            mean = torch.empty(C, device=dev)
+            var = torch.empty(C, device=dev)
+            ma = torch.empty_like(mz)
+            Sa = torch.empty_like(Sz)
+            self.m_hat = torch.empty_like(mz)
+            self.S_hat = None
+            L("tagi_bn_train_forward", mz.data_ptr(), Sz.data_ptr(), mean.data_ptr(),
+              var.data_ptr(), self.running_mean.data_ptr(), self.running_var.data_ptr(),
+              self.mw.data_ptr(), self.Sw.data_ptr(), self.mb.data_ptr(), self.Sb.data_ptr(),
+              ma.data_ptr(), Sa.data_ptr(), self.m_hat.data_ptr(), N, C, HW,
+              0 if self._is_initialized else 1, 1 if self.preserve_var else 0,
+              float(self.momentum), float(self.eps), st)
+            self._is_initialized = True
+            self._norm_mean, self._norm_var = mean, var
+            return ma, Sa
         if self.training:
             sums = torch.empty(3 * C, device=dev, dtype=torch.float64)
             L("tagi_bn_channel_sums", mz.data_ptr(), Sz.data_ptr(), sums.data_ptr(), N, C, HW, st)
