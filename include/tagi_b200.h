@@ -326,11 +326,15 @@ int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* 
  * grads[0:C]=sum dma*m_hat, [C:2C]=sum dSa*m_hat^2, [2C:3C]=sum dma, [3C:4C]=sum dSa.
  * relu_J (NULL: none): Jacobian of a ReLU that produced this layer's input;
  * the outgoing deltas are then multiplied by J and J^2 as the ReLU's backward
- * (triton_tagi/layers/relu.py:333-350) would.
+ * (triton_tagi/layers/relu.py:333-350) would. cap_factor > 0: the capped update
+ * of gamma (mg, Sw) and beta (mb, Sb) is also applied from the sums, as
+ * tagi_bn_apply_grads in update mode would (mg is updated in place after every
+ * block has read it); cap_factor <= 0 leaves the parameters alone.
  * Replaces batchnorm2d.py:436-513 (torch sums + _batchnorm_bwd_kernel). */
 int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat, const float* var,
-                     const float* mg, float* dmz, float* dSz, const float* relu_J, double* grads,
-                     int64_t N, int64_t C, int64_t HW, float eps, void* stream);
+                     float* mg, float* dmz, float* dSz, const float* relu_J, double* grads,
+                     int64_t N, int64_t C, int64_t HW, float eps, float* Sw, float* mb, float* Sb,
+                     float cap_factor, void* stream);
 
 /* Apply per-channel sums (tagi_bn_backward layout, possibly all-reduced):
  * mode TAGI_WGRAD_DELTAS writes the four delta vectors, TAGI_WGRAD_UPDATE

@@ -184,11 +184,29 @@ __global__ void bn_forward_kernel(const float* mz, const float* Sz, const float*
     }
 }
 
+// Deltas S*g_m, S^2*g_S from float64 sums, written out or applied with the cap.
+__device__ __forceinline__ void vector_apply(int64_t i, double gm, double gS, int mode, float* m,
+                                             float* S, float* d_m, float* d_S, float cap) {
+    const float s = S[i];
+    const float dm = s * static_cast<float>(gm);
+    const float dS = (s * s) * static_cast<float>(gS);
+    if (mode == TAGI_WGRAD_DELTAS) {
+        d_m[i] = dm;
+        d_S[i] = dS;
+    } else {
+        float mm = m[i], ss = s;
+        capped_pair(mm, ss, dm, dS, cap);
+        m[i] = mm;
+        S[i] = ss;
+    }
+}
+
 // batchnorm2d.py:134-192 plus the gamma/beta sums of 465-482, one cluster per channel.
 template <bool V4>
 __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
-    const float* dma, const float* dSa, const float* mhat, const float* var, const float* mg,
-    float* dmz, float* dSz, const float* rj, double* grads, int N, int C, int HW, float eps) {
+    const float* dma, const float* dSa, const float* mhat, const float* var, float* mg,
+    float* dmz, float* dSz, const float* rj, double* grads, int N, int C, int HW, float eps,
+    float* Sw, float* mb, float* Sb, float cap) {
     __shared__ double red[4 * 32];
     __shared__ double part[4];
     const ChanSlab sl(N, C, HW, blockIdx.y);
@@ -240,6 +258,13 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     if (blockIdx.x == 0 && threadIdx.x == 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) grads[j * C + sl.c] = v[j];
+        // cap > 0: the capped update of this channel's gamma/beta from the sums
+        // (as tagi_bn_apply_grads); every block of the cluster read gamma before
+        // the cluster-wide reduction above
+        if (cap > 0.f) {
+            vector_apply(sl.c, v[0], v[1], TAGI_WGRAD_UPDATE, mg, Sw, nullptr, nullptr, cap);
+            vector_apply(sl.c, v[2], v[3], TAGI_WGRAD_UPDATE, mb, Sb, nullptr, nullptr, cap);
+        }
     }
 }
 
@@ -373,23 +398,6 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
             Sa[o] = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
             mhat[o] = m_hat;
         }
-    }
-}
-
-// Deltas S*g_m, S^2*g_S from float64 sums, written out or applied with the cap.
-__device__ __forceinline__ void vector_apply(int64_t i, double gm, double gS, int mode, float* m,
-                                             float* S, float* d_m, float* d_S, float cap) {
-    const float s = S[i];
-    const float dm = s * static_cast<float>(gm);
-    const float dS = (s * s) * static_cast<float>(gS);
-    if (mode == TAGI_WGRAD_DELTAS) {
-        d_m[i] = dm;
-        d_S[i] = dS;
-    } else {
-        float mm = m[i], ss = s;
-        capped_pair(mm, ss, dm, dS, cap);
-        m[i] = mm;
-        S[i] = ss;
     }
 }
 
@@ -568,14 +576,17 @@ extern "C" int tagi_bn_train_forward(const float* mz, const float* Sz, float* me
 }
 
 extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat,
-                                const float* var, const float* mg, float* dmz, float* dSz,
+                                const float* var, float* mg, float* dmz, float* dSz,
                                 const float* relu_J, double* grads, int64_t N, int64_t C,
-                                int64_t HW, float eps, void* stream) {
+                                int64_t HW, float eps, float* Sw, float* mb, float* Sb,
+                                float cap_factor, void* stream) {
     const char* what = "tagi_bn_backward";
     TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     if (C == 0) return TAGI_OK;
     TAGI_REQUIRE(dma && dSa && m_hat && var && mg && dmz && dSz && grads, TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
+    TAGI_REQUIRE(cap_factor <= 0.f || (Sw && mb && Sb), TAGI_E_BAD_ARG,
+                 "%s: the update needs Sw, mb, Sb", what);
     TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     const int S = bn_split(C, N);
     const uintptr_t al = reinterpret_cast<uintptr_t>(dma) | reinterpret_cast<uintptr_t>(dSa) |
@@ -584,10 +595,10 @@ extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float*
     const bool v4 = HW % 4 == 0 && (al & 15) == 0;
     return v4 ? launch_cluster(bn_backward_kernel<true>, S, (int)C, as_stream(stream), what, dma,
                                dSa, m_hat, var, mg, dmz, dSz, relu_J, grads, (int)N, (int)C,
-                               (int)HW, eps)
+                               (int)HW, eps, Sw, mb, Sb, cap_factor)
               : launch_cluster(bn_backward_kernel<false>, S, (int)C, as_stream(stream), what, dma,
                                dSa, m_hat, var, mg, dmz, dSz, relu_J, grads, (int)N, (int)C,
-                               (int)HW, eps);
+                               (int)HW, eps, Sw, mb, Sb, cap_factor);
 }
 
 extern "C" int tagi_bn_apply_grads(const double* grads, int64_t C, int mode, float* mw, float* Sw,

@@ -133,10 +133,13 @@ class BatchNorm2D(LearnableLayer):
             if relu.J is None or relu.J.numel() != dma.numel():
                 raise ValueError("BatchNorm2D.backward: the ReLU has no Jacobian of this size")
             rj = relu.J.contiguous()
+        upd = mode == "update"  # the capped update applied by the same launch
         L("tagi_bn_backward", dma.data_ptr(), dSa.data_ptr(), self.m_hat.data_ptr(),
           self._norm_var.data_ptr(), self.mw.data_ptr(), dmz.data_ptr(), dSz.data_ptr(),
           rj.data_ptr() if rj is not None else None, grads.data_ptr(), N, C, H * W,
-          float(self.eps), st)
+          float(self.eps), self.Sw.data_ptr() if upd else None,
+          self.mb.data_ptr() if upd else None, self.Sb.data_ptr() if upd else None,
+          float(self._cap) if upd else 0.0, st)
         if mode == "deltas":
             self.delta_mw = torch.empty(C, device=dev)
             self.delta_Sw = torch.empty(C, device=dev)
@@ -146,7 +149,6 @@ class BatchNorm2D(LearnableLayer):
               None, self.Sb.data_ptr(), self.delta_mw.data_ptr(), self.delta_Sw.data_ptr(),
               self.delta_mb.data_ptr(), self.delta_Sb.data_ptr(), 1.0, st)
         elif mode == "update":
-            self._apply_sums(grads, self._cap)
             self._updated_in_backward = True
         elif mode == "sums":
             self._reducer.ready(self)
