@@ -183,7 +183,7 @@ ENTRY_BYTES = {
     "tagi_remax_forward": lambda a: 20 * a[5] * a[6],
     "tagi_bn_channel_sums": lambda a: 8 * a[3] * a[4] * a[5],
     # reads mz, Sz; writes ma, Sa, m_hat
-    "tagi_bn_train_forward": lambda a: 20 * a[13] * a[14] * a[15],
+    "tagi_bn_train_forward": lambda a: (20 + 8 * _planes(a[13])) * a[15] * a[16] * a[17],
     "tagi_bn_forward": lambda a: 4 * (5 + _planes(a[11])) * a[12] * a[13] * a[14],
     "tagi_bn_backward": lambda a: (24 if a[7] else 20) * a[9] * a[10] * a[11],
     "tagi_avgpool_forward": lambda a: 8 * a[4] * a[5] * a[6] * a[7] * (1 + 1 / a[8] ** 2),

@@ -314,13 +314,17 @@ int tagi_bn_forward(const float* mz, const float* Sz, const float* mean, const f
  * finalisation (mean, Bessel-corrected variance, running statistics and the
  * first-call scale, as tagi_bn_finalize with count = N*H*W) and the normalised
  * affine (as tagi_bn_forward with m_hat cached), each channel on one thread-
- * block cluster. mean, var receive the statistics. Data-parallel SyncBN, which
+ * block cluster. mean, var receive the statistics. add_m, add_S (both or
+ * neither; same layout as ma, Sa): a residual stream added to the outputs, as
+ * tagi_add_inplace after this layer would (the ResBlock shortcut,
+ * triton_tagi/layers/resblock.py:138-154). Data-parallel SyncBN, which
  * all-reduces the sums between the passes, uses the three entries above. */
 int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* var,
                           float* running_mean, float* running_var, float* mg, const float* Sg,
                           const float* mb, const float* Sb, float* ma, float* Sa, float* m_hat,
-                          int64_t N, int64_t C, int64_t HW, int first, int preserve_var,
-                          float momentum, float eps, void* stream);
+                          const float* add_m, const float* add_S, int64_t N, int64_t C,
+                          int64_t HW, int first, int preserve_var, float momentum, float eps,
+                          void* stream);
 
 /* Delta propagation plus per-channel raw sums (float64)
  * grads[0:C]=sum dma*m_hat, [C:2C]=sum dSa*m_hat^2, [2C:3C]=sum dma, [3C:4C]=sum dSa.

@@ -307,8 +307,8 @@ template <bool V4>
 __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     const float* mz, const float* Sz, float* mean, float* var, float* rmean, float* rvar,
     float* mg, const float* Sg, const float* mb, const float* Sb, float* ma, float* Sa,
-    float* mhat, int N, int C, int HW, double count, int first, int preserve_var, float momentum,
-    float one_minus, float eps) {
+    float* mhat, const float* add_m, const float* add_S, int N, int C, int HW, double count,
+    int first, int preserve_var, float momentum, float one_minus, float eps) {
     __shared__ double red[3 * 32];
     __shared__ double part[3];
     __shared__ float stat[3];  // mean, variance, scale of the channel
@@ -386,6 +386,12 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
                 om[e] = g * mh[e] + b;
                 oS[e] = g * g * Sh + sg * mh[e] * mh[e] + sg * Sh + sb;
             }
+            if (add_m) {  // a residual stream added to the outputs
+                const float4 am = __ldg(reinterpret_cast<const float4*>(add_m + o));
+                const float4 aS = __ldg(reinterpret_cast<const float4*>(add_S + o));
+                om[0] += am.x; om[1] += am.y; om[2] += am.z; om[3] += am.w;
+                oS[0] += aS.x; oS[1] += aS.y; oS[2] += aS.z; oS[3] += aS.w;
+            }
             *reinterpret_cast<float4*>(ma + o) = make_float4(om[0], om[1], om[2], om[3]);
             *reinterpret_cast<float4*>(Sa + o) = make_float4(oS[0], oS[1], oS[2], oS[3]);
             *reinterpret_cast<float4*>(mhat + o) = make_float4(mh[0], mh[1], mh[2], mh[3]);
@@ -394,8 +400,14 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
             const int64_t o = sl.offset(li, t - li * HW);
             const float m_hat = (mz[o] - mu) * inv_std;
             const float S_hat = Sz[o] / (rs + eps);
-            ma[o] = g * m_hat + b;
-            Sa[o] = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
+            float om = g * m_hat + b;
+            float oS = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
+            if (add_m) {
+                om += add_m[o];
+                oS += add_S[o];
+            }
+            ma[o] = om;
+            Sa[o] = oS;
             mhat[o] = m_hat;
         }
     }
@@ -547,7 +559,8 @@ extern "C" int tagi_bn_forward(const float* mz, const float* Sz, const float* me
 extern "C" int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* var,
                                      float* running_mean, float* running_var, float* mg,
                                      const float* Sg, const float* mb, const float* Sb, float* ma,
-                                     float* Sa, float* m_hat, int64_t N, int64_t C, int64_t HW,
+                                     float* Sa, float* m_hat, const float* add_m,
+                                     const float* add_S, int64_t N, int64_t C, int64_t HW,
                                      int first, int preserve_var, float momentum, float eps,
                                      void* stream) {
     const char* what = "tagi_bn_train_forward";
@@ -558,21 +571,24 @@ extern "C" int tagi_bn_train_forward(const float* mz, const float* Sz, float* me
     TAGI_REQUIRE(mz && Sz && mean && var && running_mean && running_var && mg && Sg && mb && Sb &&
                      ma && Sa && m_hat,
                  TAGI_E_BAD_ARG, "%s: null pointer", what);
+    TAGI_REQUIRE((add_m == nullptr) == (add_S == nullptr), TAGI_E_BAD_ARG,
+                 "%s: give both residual planes or neither", what);
     TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     const int S = bn_split(C, N);
     const uintptr_t al = reinterpret_cast<uintptr_t>(mz) | reinterpret_cast<uintptr_t>(Sz) |
                          reinterpret_cast<uintptr_t>(ma) | reinterpret_cast<uintptr_t>(Sa) |
-                         reinterpret_cast<uintptr_t>(m_hat);
+                         reinterpret_cast<uintptr_t>(m_hat) | reinterpret_cast<uintptr_t>(add_m) |
+                         reinterpret_cast<uintptr_t>(add_S);
     const bool v4 = HW % 4 == 0 && (al & 15) == 0;
     const float one_minus = static_cast<float>(1.0 - static_cast<double>(momentum));
     return v4 ? launch_cluster(bn_train_forward_kernel<true>, S, (int)C, as_stream(stream), what,
                                mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
-                               Sa, m_hat, (int)N, (int)C, (int)HW, count, first, preserve_var,
-                               momentum, one_minus, eps)
+                               Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
+                               preserve_var, momentum, one_minus, eps)
               : launch_cluster(bn_train_forward_kernel<false>, S, (int)C, as_stream(stream), what,
                                mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
-                               Sa, m_hat, (int)N, (int)C, (int)HW, count, first, preserve_var,
-                               momentum, one_minus, eps);
+                               Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
+                               preserve_var, momentum, one_minus, eps);
 }
 
 extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat,

@@ -59,7 +59,9 @@ class BatchNorm2D(LearnableLayer):
     def eval(self) -> None:
         self.training = False
 
-    def forward(self, mz: Tensor, Sz: Tensor) -> tuple[Tensor, Tensor]:
+    def forward(self, mz: Tensor, Sz: Tensor, residual=None) -> tuple[Tensor, Tensor]:
+        """Normalised moments; ``residual`` = (μ, S) of a stream to add to them
+        (the ResBlock shortcut), as ``triton_add_shortcut`` after this layer."""
         check_cuda_f32(mz, Sz)
         contiguous_params(self, ("mw", "Sw", "mb", "Sb", "running_mean", "running_var"))
         mz, Sz = mz.contiguous(), Sz.contiguous()
@@ -69,6 +71,11 @@ class BatchNorm2D(LearnableLayer):
         dev = mz.device
         st = stream(mz)
         L = lib()
+        if residual is not None:
+            if residual[0].shape != mz.shape or residual[1].shape != mz.shape:
+                raise ValueError("BatchNorm2D: residual shape differs from the output's")
+            check_cuda_f32(*residual)
+            residual = (residual[0].contiguous(), residual[1].contiguous())
         if self.training and self._stats_allreduce is None:
             # one launch: sums, statistics and normalisation per channel cluster
             mean = torch.empty(C, device=dev)
@@ -80,7 +87,9 @@ class BatchNorm2D(LearnableLayer):
             L("tagi_bn_train_forward", mz.data_ptr(), Sz.data_ptr(), mean.data_ptr(),
               var.data_ptr(), self.running_mean.data_ptr(), self.running_var.data_ptr(),
               self.mw.data_ptr(), self.Sw.data_ptr(), self.mb.data_ptr(), self.Sb.data_ptr(),
-              ma.data_ptr(), Sa.data_ptr(), self.m_hat.data_ptr(), N, C, HW,
+              ma.data_ptr(), Sa.data_ptr(), self.m_hat.data_ptr(),
+              residual[0].data_ptr() if residual is not None else None,
+              residual[1].data_ptr() if residual is not None else None, N, C, HW,
               0 if self._is_initialized else 1, 1 if self.preserve_var else 0,
               float(self.momentum), float(self.eps), st)
             self._is_initialized = True
@@ -111,6 +120,10 @@ class BatchNorm2D(LearnableLayer):
           self.mw.data_ptr(), self.Sw.data_ptr(), self.mb.data_ptr(), self.Sb.data_ptr(),
           ma.data_ptr(), Sa.data_ptr(), self.m_hat.data_ptr(), None, N, C, HW, float(self.eps),
           st)
+        if residual is not None:
+            from .resblock import triton_add_shortcut
+
+            triton_add_shortcut(residual[0], residual[1], ma, Sa)
         return ma, Sa
 
     def backward(self, delta_ma: Tensor, delta_Sa: Tensor, relu=None) -> tuple[Tensor, Tensor]:

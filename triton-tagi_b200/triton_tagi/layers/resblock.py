@@ -101,10 +101,10 @@ class ResBlock(LearnableLayer):
         # Layers never modify their inputs, so the skip needs no copy.
         from .._chain import forward_chain
 
-        mu_z, var_z = forward_chain(self._main_layers, mu_in, var_in)
+        # shortcut first: the main path's last BatchNorm adds it to its outputs
         mu_x, var_x = forward_chain(self._proj_layers, mu_in, var_in)
-        triton_add_shortcut(mu_x, var_x, mu_z, var_z)
-        return mu_z, var_z
+        mu_z, var_z = forward_chain(self._main_layers[:-1], mu_in, var_in)
+        return self._main_layers[-1].forward(mu_z, var_z, residual=(mu_x, var_x))
 
     def backward(self, delta_mu: Tensor, delta_var: Tensor) -> tuple[Tensor, Tensor]:
         from .._chain import backward_chain
