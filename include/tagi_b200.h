@@ -93,11 +93,14 @@ int tagi_backward_delta_view(const float* dmz, const float* dSz, int64_t d_div, 
  * NCHW). mw, Sw: (C*k*k) x Co with rows (c, kh, kw); mb, Sb: Co.
  * Replaces Conv2D.forward's patch extraction and fused moment product,
  * triton_tagi/layers/conv2d.py:254-309 (padding_type 1: symmetric padding;
- * 2: `padding` on the right/bottom edge only). */
+ * 2: `padding` on the right/bottom edge only). nhwc != 0: ma, Sa are given
+ * channels-last (N x H x W x C, e.g. from tagi_nchw_to_nhwc), which lets the
+ * contraction load a tap's channels 32 bytes at a time when C is a multiple
+ * of 8; the outputs stay NCHW. */
 int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
                         const float* mb, const float* Sb, float* mz, float* Sz, int64_t N,
                         int64_t C, int64_t H, int64_t W, int64_t Co, int64_t k, int64_t stride,
-                        int64_t padding, int64_t padding_type, void* workspace,
+                        int64_t padding, int64_t padding_type, int nhwc, void* workspace,
                         size_t workspace_bytes, void* stream);
 
 /* Conv2D input deltas, written in NCHW (N x C x H x W). The reference forms the
@@ -109,11 +112,12 @@ int tagi_conv2d_forward(const float* ma, const float* Sa, const float* mw, const
  * times mw[c*k*k + tap][co]. col2im_mode 0 reproduces the reference's gather
  * (for stride > 1 it does not test the column offset for divisibility, with
  * truncating division); 1 is the exact adjoint of the patches. dmz, dSz:
- * N x Co x Ho x Wo; mw: (C*k*k) x Co; padding_type as tagi_conv2d_forward. */
+ * N x Co x Ho x Wo (N x Ho x Wo x Co with nhwc != 0); mw: (C*k*k) x Co;
+ * padding_type as tagi_conv2d_forward. */
 int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, const float* mw, float* d_ma,
                                float* d_Sa, int64_t N, int64_t C, int64_t H, int64_t W,
                                int64_t Co, int64_t k, int64_t stride, int64_t padding,
-                               int64_t padding_type, int col2im_mode, void* workspace,
+                               int64_t padding_type, int col2im_mode, int nhwc, void* workspace,
                                size_t workspace_bytes, void* stream);
 
 /* Optional workspace of the entries above and below that write an M x N output
@@ -276,6 +280,11 @@ int tagi_avgpool_backward(const float* dm, const float* dS, float* dm_out, float
 int tagi_im2col(const float* xm, const float* xS, float* pm, float* pS, int64_t N, int64_t C,
                 int64_t H, int64_t W, int64_t k, int64_t stride, int64_t padding,
                 int64_t padding_type, void* stream);
+
+/* NCHW -> NHWC copy of a tensor pair (yS, xS may both be NULL): y[n][p][c] =
+ * x[n][c][p] for p < HW, for the channels-last gathers of the Conv2D entries. */
+int tagi_nchw_to_nhwc(const float* xm, const float* xS, float* ym, float* yS, int64_t N,
+                      int64_t C, int64_t HW, void* stream);
 
 /* Gather patch-space deltas back to NCHW. mode 0 reproduces the reference's
  * gather exactly (_col2im_kernel, conv2d.py:85-132, 155-181, 361-370);

@@ -337,7 +337,7 @@ def test_conv_backward_delta_entry_strided_gathers(C, Co, k, s, p, pt, mode):
     d_ma = torch.empty(N, C, H, W, device=DEV)
     d_Sa = torch.empty_like(d_ma)
     lib()("tagi_conv2d_backward_delta", d_dmz.data_ptr(), d_dSz.data_ptr(), d_mw.data_ptr(),
-          d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, s, p, pt, mode, None, 0,
+          d_ma.data_ptr(), d_Sa.data_ptr(), N, C, H, W, Co, k, s, p, pt, mode, 0, None, 0,
           stream(d_ma))
     dm = dmz.double().permute(0, 2, 3, 1).reshape(-1, Co)
     dS = dSz.double().permute(0, 2, 3, 1).reshape(-1, Co)
@@ -346,4 +346,45 @@ def test_conv_backward_delta_entry_strided_gathers(C, Co, k, s, p, pt, mode):
     ref_S = F.col2im(dpS, N, C, H, W, k, s, p, pt, adjoint=mode == 1)
     assert_rel(d_ma, ref_m, MEAN_RTOL, "d_ma")
     assert_rel(d_Sa, ref_S, VAR_RTOL, "d_Sa")
+    _ok()
+
+
+@pytest.mark.parametrize("C,Co", [(16, 24), (12, 20), (64, 64)])
+def test_conv_entries_channels_last_equal_nchw(C, Co):
+    """tagi_conv2d_forward / tagi_conv2d_backward_delta given the gathered
+    tensor channels-last (tagi_nchw_to_nhwc) read the same values in the same
+    order as from NCHW: bit-identical outputs, with C a multiple of 8 (one
+    32-byte load per tap and operand) and not (element by element)."""
+    from triton_tagi._lib import lib, stream
+
+    L = lib()
+    g = torch.Generator().manual_seed(C + Co)
+    N, H, W, k = 4, 12, 10, 3
+    x = [t.to(DEV) for t in (_rnd(g, N, C, H, W), _rnd(g, N, C, H, W, u=True, scale=0.1))]
+    mw = _rnd(g, C * k * k, Co, scale=(C * k * k) ** -0.5).to(DEV)
+    Sw = _rnd(g, C * k * k, Co, u=True, scale=1e-2).to(DEV)
+    mb, Sb = _rnd(g, Co, scale=0.1).to(DEV), _rnd(g, Co, u=True, scale=1e-3).to(DEV)
+    d = [t.to(DEV) for t in (_rnd(g, N, Co, H, W, scale=0.1), -_rnd(g, N, Co, H, W, u=True, scale=1e-2))]
+
+    def nhwc(a, b, c):
+        ya, yb = torch.empty(N, H, W, c, device=DEV), torch.empty(N, H, W, c, device=DEV)
+        L("tagi_nchw_to_nhwc", a.data_ptr(), b.data_ptr(), ya.data_ptr(), yb.data_ptr(), N, c,
+          H * W, stream(a))
+        assert torch.equal(ya, a.permute(0, 2, 3, 1)) and torch.equal(yb, b.permute(0, 2, 3, 1))
+        return ya, yb
+
+    outs = []
+    for last in (0, 1):
+        xm, xS = nhwc(*x, C) if last else x
+        mz, Sz = torch.empty(N, Co, H, W, device=DEV), torch.empty(N, Co, H, W, device=DEV)
+        L("tagi_conv2d_forward", xm.data_ptr(), xS.data_ptr(), mw.data_ptr(), Sw.data_ptr(),
+          mb.data_ptr(), Sb.data_ptr(), mz.data_ptr(), Sz.data_ptr(), N, C, H, W, Co, k, 1, 1, 1,
+          last, None, 0, stream(mz))
+        dm, dS = nhwc(*d, Co) if last else d
+        da, dA = torch.empty(N, C, H, W, device=DEV), torch.empty(N, C, H, W, device=DEV)
+        L("tagi_conv2d_backward_delta", dm.data_ptr(), dS.data_ptr(), mw.data_ptr(), da.data_ptr(),
+          dA.data_ptr(), N, C, H, W, Co, k, 1, 1, 1, 0, last, None, 0, stream(da))
+        outs.append((mz, Sz, da, dA))
+    for name, a, b in zip(("mz", "Sz", "d_ma", "d_Sa"), *outs):
+        assert torch.equal(a, b), name
     _ok()

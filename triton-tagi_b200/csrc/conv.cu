@@ -311,6 +311,30 @@ __global__ void col2im_img_kernel(const float* cm, const float* cS, float* dm, f
     }
 }
 
+// NCHW -> NHWC of one or two planes: 32 x 32 tiles of (channel, pixel) through
+// shared memory (padded against bank conflicts), coalesced on both sides.
+__global__ void nchw_to_nhwc_kernel(const float* xm, const float* xS, float* ym, float* yS,
+                                    int C, int HW) {
+    __shared__ float tile[2][32][33];
+    const int n = blockIdx.z, p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    const int64_t img = static_cast<int64_t>(n) * C * HW;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int c = c0 + r, p = p0 + threadIdx.x;
+        if (c < C && p < HW) {
+            tile[0][r][threadIdx.x] = xm[img + static_cast<int64_t>(c) * HW + p];
+            if (xS) tile[1][r][threadIdx.x] = xS[img + static_cast<int64_t>(c) * HW + p];
+        }
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int p = p0 + r, c = c0 + threadIdx.x;
+        if (c < C && p < HW) {
+            ym[img + static_cast<int64_t>(p) * C + c] = tile[0][threadIdx.x][r];
+            if (xS) yS[img + static_cast<int64_t>(p) * C + c] = tile[1][threadIdx.x][r];
+        }
+    }
+}
+
 }  // namespace
 }  // namespace tagi
 
@@ -391,5 +415,21 @@ extern "C" int tagi_col2im(const float* cm, const float* cS, float* dm, float* d
     } else {
         col2im_kernel<true><<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(cm, cS, dm, dS, g);
     }
+    return check_launch(what);
+}
+
+extern "C" int tagi_nchw_to_nhwc(const float* xm, const float* xS, float* ym, float* yS, int64_t N,
+                                 int64_t C, int64_t HW, void* stream) {
+    const char* what = "tagi_nchw_to_nhwc";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && N <= 65535 && C <= 65535 * 32 &&
+                     N * C * HW < (int64_t(1) << 40),
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (N == 0 || C == 0 || HW == 0) return TAGI_OK;
+    TAGI_REQUIRE(xm && ym && (xS == nullptr) == (yS == nullptr), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    const dim3 grid(static_cast<unsigned>((HW + 31) / 32), static_cast<unsigned>((C + 31) / 32),
+                    static_cast<unsigned>(N));
+    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(xm, xS, ym, yS, (int)C,
+                                                                       (int)HW);
     return check_launch(what);
 }

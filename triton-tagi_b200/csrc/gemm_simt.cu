@@ -487,8 +487,8 @@ extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float
                                    const float* Sw, const float* mb, const float* Sb, float* mz,
                                    float* Sz, int64_t N, int64_t C, int64_t H, int64_t W,
                                    int64_t Co, int64_t k, int64_t stride, int64_t padding,
-                                   int64_t padding_type, void* workspace, size_t workspace_bytes,
-                                   void* stream) {
+                                   int64_t padding_type, int nhwc, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
     const char* what = "tagi_conv2d_forward";
     TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && stride >= 1 &&
                      padding >= 0 && (padding_type == 1 || padding_type == 2),
@@ -507,7 +507,8 @@ extern "C" int tagi_conv2d_forward(const float* ma, const float* Sa, const float
                  "%s: null pointer", what);
     GemmArgs g = blank();
     g.x = ma; g.y = Sa;
-    g.ga = Gather{1, 0, (int)C, (int)H, (int)W, (int)Wo, (int)L, (int)k, (int)stride, top, top};
+    g.ga = Gather{1, 0, (int)C, (int)H, (int)W, (int)Wo, (int)L, (int)k, (int)stride, top, top,
+                  nhwc ? 1 : 0};
     // B[co][tap*C + c] = mw[c*kk + tap][co]: the weight rows in (tap, c) order
     g.u = mw; g.v = Sw; g.brow = RowMap{C, Co, k * k * Co}; g.bn = 1;
     g.bias0 = mb; g.bias1 = Sb;
@@ -521,7 +522,7 @@ extern "C" int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, co
                                           float* d_ma, float* d_Sa, int64_t N, int64_t C,
                                           int64_t H, int64_t W, int64_t Co, int64_t k,
                                           int64_t stride, int64_t padding, int64_t padding_type,
-                                          int col2im_mode, void* workspace,
+                                          int col2im_mode, int nhwc, void* workspace,
                                           size_t workspace_bytes, void* stream) {
     const char* what = "tagi_conv2d_backward_delta";
     TAGI_REQUIRE(N >= 0 && C >= 0 && H >= 0 && W >= 0 && Co >= 0 && k >= 1 && stride >= 1 &&
@@ -545,7 +546,7 @@ extern "C" int tagi_conv2d_backward_delta(const float* dmz, const float* dSz, co
     // of the input, reduction (tap, co)
     g.x = dmz; g.y = dSz;
     g.ga = Gather{1, col2im_mode == 0 ? 1 : 2, (int)Co, (int)Ho, (int)Wo, (int)W, (int)HW,
-                  (int)k, (int)stride, top, top};
+                  (int)k, (int)stride, top, top, nhwc ? 1 : 0};
     // B[c][tap*Co + co] = mw[c*kk + tap][co]: the weight matrix read in place, row c
     // contiguous along the reduction
     g.u = mw; g.brow = plain_rows(1); g.bn = Kr;

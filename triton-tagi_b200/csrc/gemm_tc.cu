@@ -432,6 +432,19 @@ __device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
                  : "l"(p));
 }
 
+// The 8 floats at a 32-byte aligned p if `ok`, else zeros (one predicated
+// 256-bit load, not kept in L1).
+__device__ __forceinline__ void ld8_if(const float* p, bool ok, float (&v)[8]) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %9, 0;\n\t"
+        "mov.b32 %0, 0;\n\tmov.b32 %1, 0;\n\tmov.b32 %2, 0;\n\tmov.b32 %3, 0;\n\t"
+        "mov.b32 %4, 0;\n\tmov.b32 %5, 0;\n\tmov.b32 %6, 0;\n\tmov.b32 %7, 0;\n\t"
+        "@q ld.global.L1::no_allocate.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t}"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+          "=f"(v[6]), "=f"(v[7])
+        : "l"(p), "r"(static_cast<int>(ok)));
+}
+
 // *p if `ok`, else 0, as one predicated load into a zeroed register: the
 // value is not consumed (no select waits on it) until the stage that uses it.
 __device__ __forceinline__ float ldg_if(const float* p, bool ok) {
@@ -506,6 +519,37 @@ __device__ __forceinline__ void load_row(const GemmArgs& g, const Side& sd, int 
         int kh = tap / ga.k, kw = tap - kh * ga.k;
         int ih, iw;
         bool inside = row < sd.nrows && gather_tap<GM>(ga, gr, kh, kw, &ih, &iw);
+        if (ga.nhwc) {
+            // channels-last: the block's 8 channels of one tap are contiguous
+            int64_t o = gr.base + (static_cast<int64_t>(ih) * ga.W + iw) * ga.C + c;
+            if (ga.C % 8 == 0 && k0 + 8 <= kend) {
+                ld8_if(sd.p0 + o, inside, v[0]);
+                if (TWO) {
+                    ld8_if(sd.p1 + o, inside, v[1]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[1][j] = 0.f;
+                }
+                return;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool ok = inside && k0 + j < kend;
+                v[0][j] = ldg_if(sd.p0 + o, ok);
+                v[1][j] = TWO ? ldg_if(sd.p1 + o, ok) : 0.f;
+                ++o;
+                if (++c == ga.C) {
+                    c = 0;
+                    if (++kw == ga.k) {
+                        kw = 0;
+                        ++kh;
+                    }
+                    inside = row < sd.nrows && gather_tap<GM>(ga, gr, kh, kw, &ih, &iw);
+                    o = gr.base + (static_cast<int64_t>(ih) * ga.W + iw) * ga.C;
+                }
+            }
+            return;
+        }
         int64_t o = gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {

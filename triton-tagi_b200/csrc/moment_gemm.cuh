@@ -29,12 +29,16 @@ struct ParamEpi {
 //     ow = own / s truncating toward zero, if ohn % s == 0, 0 <= oh < H and
 //     0 <= ow < W (the column offset is not tested for divisibility);
 //   mode 2, the adjoint of the patches: mode 1 plus ohn, own >= 0 and own % s == 0.
+// nhwc: the gathered tensor is channels-last (N x H x W x C), so the 8 channels
+// of a reduction block at one tap are 32 contiguous bytes (one 256-bit load
+// when C is a multiple of 8) instead of 8 values a channel plane apart.
 struct Gather {
     int on;              // 1: A is gathered; arow and ak are unused
     int mode;            // 0 patches, 1 reference col2im gather, 2 adjoint gather
-    int C, H, W;         // gathered tensor's channels and size (NCHW)
+    int C, H, W;         // gathered tensor's channels and size
     int Wo, L;           // row pixel grid: width, pixels per image
     int k, s, pt, pl;    // kernel size, stride, top and left padding
+    int nhwc;            // 0: NCHW, 1: NHWC
 };
 
 // One row pixel's image base and origin: mode 0, the input position of tap
@@ -81,6 +85,7 @@ __device__ __forceinline__ int64_t gather_off(const Gather& ga, const GatherRow&
     const int tap = r / ga.C, c = r - tap * ga.C, kh = tap / ga.k, kw = tap - kh * ga.k;
     int ih, iw;
     if (!gather_tap(ga, gr, kh, kw, &ih, &iw)) return -1;
+    if (ga.nhwc) return gr.base + (static_cast<int64_t>(ih) * ga.W + iw) * ga.C + c;
     return gr.base + (static_cast<int64_t>(c) * ga.H + ih) * ga.W + iw;
 }
 

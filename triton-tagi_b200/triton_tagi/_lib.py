@@ -26,10 +26,11 @@ _SIGS = {
     "tagi_moment_forward": "pp" + "iiii" + "ppi" + "pppp" + "iiii" + "iii" + "p",
     "tagi_fused_backward_delta": "ppppp" + "iii" + "iiiiii" + "p",
     "tagi_backward_delta_view": "pp" + "iiii" + "pi" + "pp" + "iiii" + "iii" + "p",
-    "tagi_conv2d_backward_delta": "ppp" + "pp" + "iiiiiiiii" + "n" + "pz" + "p",
+    "tagi_conv2d_backward_delta": "ppp" + "pp" + "iiiiiiiii" + "nn" + "pz" + "p",
     "tagi_linear_forward": "pppppp" + "pp" + "iii" + "pz" + "p",
     "tagi_linear_backward_delta": "ppp" + "pp" + "iii" + "pz" + "p",
-    "tagi_conv2d_forward": "pppppp" + "pp" + "iiiiiiiii" + "pz" + "p",
+    "tagi_conv2d_forward": "pppppp" + "pp" + "iiiiiiiii" + "n" + "pz" + "p",
+    "tagi_nchw_to_nhwc": "pppp" + "iii" + "p",
     "tagi_fused_weight_grad_workspace_size": "iii",
     "tagi_store_workspace_size": "iii",
     "tagi_fused_weight_grad": "ppppp" + "iii" + "iiiiii" + "pz" + "p",
