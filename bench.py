@@ -191,6 +191,7 @@ ENTRY_BYTES = {
     # patches written (mean, and variance if given) + image read
     "tagi_im2col": lambda a: 4 * _planes(a[0], a[1]) * a[4] * a[5] * (
         a[6] * a[7] + _out_pixels(a[6], a[7], a[8], a[9], a[10], a[11]) * a[8] * a[8]),
+    "tagi_nchw_to_nhwc": lambda a: 8 * _planes(a[0], a[1]) * a[4] * a[5] * a[6],
     "tagi_col2im": lambda a: 8 * a[4] * a[5] * (
         a[6] * a[7] + _out_pixels(a[6], a[7], a[8], a[9], a[10], a[11]) * a[8] * a[8]),
 }

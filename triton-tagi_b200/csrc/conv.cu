@@ -311,26 +311,34 @@ __global__ void col2im_img_kernel(const float* cm, const float* cS, float* dm, f
     }
 }
 
-// NCHW -> NHWC of one or two planes: 32 x 32 tiles of (channel, pixel) through
-// shared memory (padded against bank conflicts), coalesced on both sides.
+// NCHW -> NHWC of one or two planes over the flattened pixel index q = n*HW + p:
+// 32 x 32 tiles of (channel, q) through shared memory (padded against bank
+// conflicts). Reads run along q (contiguous within each image plane, so small
+// maps still fill whole tiles), writes along the channels of one pixel.
 __global__ void nchw_to_nhwc_kernel(const float* xm, const float* xS, float* ym, float* yS,
-                                    int C, int HW) {
+                                    int C, int HW, int64_t Q) {
     __shared__ float tile[2][32][33];
-    const int n = blockIdx.z, p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const int64_t img = static_cast<int64_t>(n) * C * HW;
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-        const int c = c0 + r, p = p0 + threadIdx.x;
-        if (c < C && p < HW) {
-            tile[0][r][threadIdx.x] = xm[img + static_cast<int64_t>(c) * HW + p];
-            if (xS) tile[1][r][threadIdx.x] = xS[img + static_cast<int64_t>(c) * HW + p];
+    const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int c0 = blockIdx.y * 32;
+    {
+        const int64_t q = q0 + threadIdx.x;
+        const int64_t n = q / HW, p = q - n * HW;
+        for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+            const int c = c0 + r;
+            if (c < C && q < Q) {
+                const int64_t src = (n * C + c) * HW + p;
+                tile[0][r][threadIdx.x] = xm[src];
+                if (xS) tile[1][r][threadIdx.x] = xS[src];
+            }
         }
     }
     __syncthreads();
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-        const int p = p0 + r, c = c0 + threadIdx.x;
-        if (c < C && p < HW) {
-            ym[img + static_cast<int64_t>(p) * C + c] = tile[0][threadIdx.x][r];
-            if (xS) yS[img + static_cast<int64_t>(p) * C + c] = tile[1][threadIdx.x][r];
+        const int64_t q = q0 + r;
+        const int c = c0 + threadIdx.x;
+        if (c < C && q < Q) {
+            ym[q * C + c] = tile[0][threadIdx.x][r];
+            if (xS) yS[q * C + c] = tile[1][threadIdx.x][r];
         }
     }
 }
@@ -421,15 +429,16 @@ extern "C" int tagi_col2im(const float* cm, const float* cS, float* dm, float* d
 extern "C" int tagi_nchw_to_nhwc(const float* xm, const float* xS, float* ym, float* yS, int64_t N,
                                  int64_t C, int64_t HW, void* stream) {
     const char* what = "tagi_nchw_to_nhwc";
-    TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && N <= 65535 && C <= 65535 * 32 &&
+    TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535 * 32 &&
                      N * C * HW < (int64_t(1) << 40),
                  TAGI_E_BAD_ARG, "%s: bad sizes", what);
     if (N == 0 || C == 0 || HW == 0) return TAGI_OK;
     TAGI_REQUIRE(xm && ym && (xS == nullptr) == (yS == nullptr), TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
-    const dim3 grid(static_cast<unsigned>((HW + 31) / 32), static_cast<unsigned>((C + 31) / 32),
-                    static_cast<unsigned>(N));
+    const int64_t Q = N * HW;
+    TAGI_REQUIRE((Q + 31) / 32 <= INT_MAX, TAGI_E_BAD_ARG, "%s: too many pixels", what);
+    const dim3 grid(static_cast<unsigned>((Q + 31) / 32), static_cast<unsigned>((C + 31) / 32), 1);
     nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(xm, xS, ym, yS, (int)C,
-                                                                       (int)HW);
+                                                                       (int)HW, Q);
     return check_launch(what);
 }
