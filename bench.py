@@ -339,7 +339,11 @@ def reference_arm(args, rank: int, world: int) -> None:
         "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "batch_per_step": r["sample"]},
+        # our arm's workload configuration; the bounded sample actually timed is
+        # described in cpu_baseline.sample
+        "config": {"workload": args.workload, "batch_per_gpu": WORKLOADS[args.workload]["batch"],
+                   "global_batch": WORKLOADS[args.workload]["batch"] * world,
+                   "sigma_v": SIGMA_V, "parallelism": f"dp{world}"},
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": r["value"], "unit": "samples/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
