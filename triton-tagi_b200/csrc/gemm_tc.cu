@@ -76,8 +76,15 @@ struct Roles {
     static constexpr int WARPS = ACC_W0 + 8;
     static constexpr int THREADS = 32 * WARPS;
     static constexpr int STAGE_ARRIVALS = 2 * 2 * (4 + BW);  // producer warps of a stage: 2 groups, 2 CTAs
-    static constexpr int NP = 6 * BN <= 512 ? 2 : 1;     // chunk buffers per accumulator
-    static constexpr int COLS = 2 * (NP + 1) * BN <= 256 ? 256 : 512;
+    // 64-column tiles keep the A operand in tensor memory (TA): their MMAs are
+    // bound by operand traffic in shared memory, where each 256 x 64 x 8 MMA
+    // would read a 4 KB A tile per CTA; the chunk buffers then take one slot
+    // per accumulator and the upper 256 columns hold the A stages.
+    static constexpr bool TA = BN == 64;
+    static constexpr int NP = TA ? 1 : (6 * BN <= 512 ? 2 : 1);  // chunk buffers per accumulator
+    static constexpr int ACC_COLS = 2 * (NP + 1) * BN;
+    static constexpr int COLS = (TA || ACC_COLS > 256) ? 512 : 256;
+    static constexpr uint32_t A0 = ACC_COLS;  // first tensor-memory column of the A stages (TA)
     // tensor-memory columns: chunk buffer b of accumulator q, running total of q
     static constexpr uint32_t pcol(int q, int b) { return static_cast<uint32_t>((q * NP + b) * BN); }
     static constexpr uint32_t tcol(int q) { return static_cast<uint32_t>((2 * NP + q) * BN); }
@@ -222,6 +229,27 @@ __device__ __forceinline__ void mma_pair_tf32(uint32_t d_tmem, uint64_t adesc, u
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The same with the A operand in tensor memory (column a_tmem of both CTAs).
+__device__ __forceinline__ void mma_pair_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Stores 8 consecutive 32-bit columns of this thread's lane (one warp: 32
+// lanes of its quarter) at taddr.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
         : "memory");
 }
 
@@ -375,10 +403,20 @@ __host__ __device__ constexpr int field(unsigned long long packed, int i) {
     return static_cast<int>((packed >> (4 * i)) & 0xFull);
 }
 
-// One K-block: the operand tiles of 8 reduction elements.
+// One K-block: the operand tiles of 8 reduction elements in shared memory (the
+// B tiles only when A is in tensor memory).
+template <int VM, int BN>
+constexpr int b_off() {
+    return Roles<BN>::TA ? 0 : TcTiles<VM>::na * 128 * 32;
+}
 template <int VM, int BN>
 constexpr int block_bytes() {
-    return TcTiles<VM>::na * 128 * 32 + TcTiles<VM>::nb * (BN / 2) * 32;
+    return b_off<VM, BN>() + TcTiles<VM>::nb * (BN / 2) * 32;
+}
+// Tensor-memory columns of one K-block's A tiles (8 per tile, TA only).
+template <int VM>
+constexpr int a_cols() {
+    return TcTiles<VM>::na * 8;
 }
 
 // A stage holds kBlocks consecutive K-blocks (one per producer group); the MMA
@@ -391,32 +429,51 @@ constexpr int stage_bytes() {
 
 template <int VM, int BN>
 constexpr int op_stages() {
-    return kStageBudget / stage_bytes<VM, BN>() < kMaxStages ? kStageBudget / stage_bytes<VM, BN>()
-                                                             : kMaxStages;
+    constexpr int by_smem = kStageBudget / stage_bytes<VM, BN>();
+    constexpr int by_tmem = Roles<BN>::TA ? (512 - Roles<BN>::ACC_COLS) / (kBlocks * a_cols<VM>())
+                                          : kMaxStages;
+    constexpr int n = by_smem < by_tmem ? by_smem : by_tmem;
+    return n < kMaxStages ? n : kMaxStages;
 }
 
 constexpr int kBarrierBytes = 512;
+// The epilogue's per-warp transpose buffers (8 warps x 2 x 32 x 17 floats)
+// reuse the operand stage area, which is at least this large.
+constexpr int kEpiBytes = 8 * 2 * 32 * 17 * 4;
+
+template <int VM, int BN>
+constexpr int stage_area() {
+    return op_stages<VM, BN>() * stage_bytes<VM, BN>() > kEpiBytes
+               ? op_stages<VM, BN>() * stage_bytes<VM, BN>()
+               : kEpiBytes;
+}
 
 template <int VM, int BN>
 constexpr int smem_bytes() {
-    return op_stages<VM, BN>() * stage_bytes<VM, BN>() + kBarrierBytes;
+    return stage_area<VM, BN>() + kBarrierBytes;
 }
 
-// Issue the MMAs of accumulator Q of one stage (A and B tiles of the stage at
-// descriptors da, db).
+// Issue the MMAs of accumulator Q of one K-block: A tiles at descriptor da
+// (shared memory) or, for TA tiles, at tensor-memory column da; B tiles at
+// descriptor db.
 template <int VM, int BN, int Q>
 __device__ __forceinline__ void issue_acc(uint32_t d_tmem, uint64_t da, uint64_t db,
                                           uint32_t idesc, uint32_t accumulate) {
     using P = TcPlan<VM>;
     constexpr int A_TILE = 128 * 32, B_TILE = (BN / 2) * 32;
-    constexpr int B0 = TcTiles<VM>::na * A_TILE;
+    constexpr int B0 = b_off<VM, BN>();
     bool first = true;
 #pragma unroll
     for (int i = 0; i < P::n; ++i) {
         if (field(P::acc, i) != Q) continue;
-        const uint64_t ad = da + static_cast<uint64_t>((field(P::a, i) * A_TILE) >> 4);
         const uint64_t bd = db + static_cast<uint64_t>((B0 + field(P::b, i) * B_TILE) >> 4);
-        mma_pair_tf32(d_tmem, ad, bd, idesc, first ? accumulate : 1u);
+        if (Roles<BN>::TA) {
+            mma_pair_tf32_ta(d_tmem, static_cast<uint32_t>(da) + field(P::a, i) * 8, bd, idesc,
+                             first ? accumulate : 1u);
+        } else {
+            const uint64_t ad = da + static_cast<uint64_t>((field(P::a, i) * A_TILE) >> 4);
+            mma_pair_tf32(d_tmem, ad, bd, idesc, first ? accumulate : 1u);
+        }
         first = false;
     }
 }
@@ -702,6 +759,7 @@ struct ProdCtx {
     int grp;  // producer group: stages of parity grp
     int t;    // thread index within the group's threads of this side
     int lane;
+    uint32_t tmem;  // tensor-memory base (A stages of TA tiles)
 };
 
 // One side's producer thread: K-blocks grp, grp+2, ... with prefetch_depth of them loaded
@@ -719,7 +777,8 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
     constexpr int STAGE = stage_bytes<VM, BN>();
     constexpr int BLOCK = block_bytes<VM, BN>();
     constexpr int OPS = op_stages<VM, BN>();
-    constexpr int OFF = IS_A ? 0 : TcTiles<VM>::na * 128 * 32;  // the side's first tile
+    constexpr int OFF = IS_A ? 0 : b_off<VM, BN>();  // the side's first tile
+    constexpr bool TMEM_A = IS_A && R::TA;          // A rows go to tensor memory
     constexpr bool TWO = IS_A ? VM != LSQ : VM != RSQ;
     const bool has_row = c.t < ROWS;
     const int row = sd.row0 + c.t;
@@ -751,6 +810,40 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
         if (S >= OPS && !warp_wait(&c.empty[s], ((S / OPS) - 1) & 1, c.ab, 1)) return false;
         // Rows outside the matrix are not written: an output row (column)
         // depends only on its own A row (B row), and those outputs are dropped.
+        if (TMEM_A) {
+            // this thread's row is its lane of the warp's tensor-memory quarter
+            // (warp % 4 == row / 32); the tiles' 8 reduction elements are 8
+            // consecutive columns
+            tc_fence_after();  // after the MMAs that read this slot (empty barrier)
+            // tcgen05.st is warp-collective: every lane stores; rows past M hold
+            // zeros (load_row) and their outputs are dropped
+            const uint32_t col = R::A0 + static_cast<uint32_t>(
+                                             (s * kBlocks + it % kBlocks) * a_cols<VM>());
+            const uint32_t ta = c.tmem + (static_cast<uint32_t>(c.t & ~31) << 16) + col;
+            float hi[8], lo[8], sq[8];
+            auto put = [&](int t, const float (&x)[8]) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    hi[e] = tf32_rna(x[e]);
+                    lo[e] = tf32_rna(x[e] - hi[e]);
+                }
+                tmem_st8(ta + t * 16, hi);
+                tmem_st8(ta + t * 16 + 8, lo);
+            };
+            put(0, v[0]);
+            if (VM == FULL || VM == LSQ) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) sq[e] = v[0][e] * v[0][e];
+                put(1, sq);
+            }
+            if (VM == FULL) put(2, v[1]);
+            if (VM == RSQ) put(1, v[1]);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (c.lane == 0) arrive_cluster(c.full0 + static_cast<uint32_t>(s * 8));
+            return true;
+        }
         char* st = c.smem + s * STAGE + (it % kBlocks) * BLOCK + OFF;
         bool wrote = false;
         if (sd.chunk) {
@@ -817,7 +910,7 @@ __device__ __forceinline__ void packed_b(const GemmArgs& g, const ProdCtx& c, in
     constexpr int STAGE = stage_bytes<VM, BN>();
     constexpr int BLOCK = block_bytes<VM, BN>();
     constexpr int OPS = op_stages<VM, BN>();
-    constexpr int OFF = TcTiles<VM>::na * 128 * 32;
+    constexpr int OFF = b_off<VM, BN>();
     const int nst = (c.niter + kBlocks - 1) / kBlocks;
     if (role == 1) {
         for (int F = 0; F < nst; ++F) {
@@ -865,7 +958,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     constexpr int NP = R::NP;
     constexpr int kOff1 = kChunk / 2;  // stage shift of the variance chunks
     extern __shared__ __align__(1024) char smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OPS * STAGE);  // [OPS], leader only
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + stage_area<VM, BN>());  // [OPS], leader only
     uint64_t* empty = full + kMaxStages;                                // [OPS]
     uint64_t* chunk_full = empty + kMaxStages;                          // [q*2 + b]
     uint64_t* chunk_empty = chunk_full + 4;                             // [q*2 + b], leader
@@ -922,7 +1015,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     sa.ones_row = g.ones_row;
     sa.gather = g.ga.on != 0;
     sa.vec = !sa.gather && rowvec_ok<true>(g, sa.p0, sa.p1);
-    sa.chunk = !sa.gather && !sa.vec && chunk_ok<true>(g, sa.p0, sa.p1);
+    // tensor-memory A rows are owned by one thread each: row mode
+    sa.chunk = !R::TA && !sa.gather && !sa.vec && chunk_ok<true>(g, sa.p0, sa.p1);
     sb.p0 = g.u + batch * g.b_bs;
     sb.p1 = TWO_B ? g.v + batch * g.b_bs : sb.p0;
     sb.row0 = n0 + static_cast<int>(rank) * R::NC;
@@ -944,6 +1038,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         c.kbeg = kbeg;
         c.kend = kend;
         c.lane = lane;
+        c.tmem = tmem;
         if (is_a) {
             c.grp = warp >> 2;
             c.t = (warp & 3) * 32 + lane;
@@ -964,7 +1059,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         // alone, the same loop fed the tensor pipe at half its rate.
         if (leader) {
             const bool el = elect_one();
-            const uint64_t da_first = smem_desc(smem_u32(smem), sa.chunk, 128);
+            // A of TA tiles: tensor-memory column of the stage's first tile
+            const uint64_t da_first =
+                R::TA ? static_cast<uint64_t>(tmem + R::A0) : smem_desc(smem_u32(smem), sa.chunk, 128);
+            constexpr uint64_t kDaBlock = R::TA ? a_cols<VM>() : (BLOCK >> 4);
+            constexpr uint64_t kDaStage = R::TA ? kBlocks * a_cols<VM>() : (STAGE >> 4);
             // prepared tiles: MN-major (swizzled) when NC allows it, else K-major
             const bool b_mn = packed ? R::NC % 32 == 0 : sb.chunk;
             const uint64_t db_first = smem_desc(smem_u32(smem), b_mn, R::NC);
@@ -989,7 +1088,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                 for (int sub = 0; sub < kBlocks; ++sub) {
                     const int it = it0 + sub;
                     if (it >= niter || !ok) break;
-                    const uint64_t bda = da + static_cast<uint64_t>((sub * BLOCK) >> 4);
+                    const uint64_t bda = da + sub * kDaBlock;
                     const uint64_t bdb = db + static_cast<uint64_t>((sub * BLOCK) >> 4);
                     const bool first0 = pos0 == 0, first1 = it == 0 || pos1 == 0;
                     const bool last0 = it == niter - 1 || pos0 == kChunk - 1;
@@ -1020,7 +1119,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                     da = da_first;
                     db = db_first;
                 } else {
-                    da += static_cast<uint64_t>(STAGE >> 4);
+                    da += kDaStage;
                     db += static_cast<uint64_t>(STAGE >> 4);
                 }
             }
