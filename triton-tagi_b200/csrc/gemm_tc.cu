@@ -76,11 +76,11 @@ struct Roles {
     static constexpr int WARPS = ACC_W0 + 8;
     static constexpr int THREADS = 32 * WARPS;
     static constexpr int STAGE_ARRIVALS = 2 * 2 * (4 + BW);  // producer warps of a stage: 2 groups, 2 CTAs
-    // 64-column tiles keep the A operand in tensor memory (TA): their MMAs are
-    // bound by operand traffic in shared memory, where each 256 x 64 x 8 MMA
-    // would read a 4 KB A tile per CTA; the chunk buffers then take one slot
-    // per accumulator and the upper 256 columns hold the A stages.
-    static constexpr bool TA = BN == 64;
+    // Tiles of 64 columns or fewer keep the A operand in tensor memory (TA):
+    // their MMAs are bound by operand traffic in shared memory, where each
+    // 256 x 64 x 8 MMA would read a 4 KB A tile per CTA; the chunk buffers then
+    // take one slot per accumulator and the remaining columns hold the A stages.
+    static constexpr bool TA = BN <= 64;
     static constexpr int NP = TA ? 1 : (6 * BN <= 512 ? 2 : 1);  // chunk buffers per accumulator
     static constexpr int ACC_COLS = 2 * (NP + 1) * BN;
     static constexpr int COLS = (TA || ACC_COLS > 256) ? 512 : 256;
