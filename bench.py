@@ -191,6 +191,8 @@ ENTRY_BYTES = {
     # patches written (mean, and variance if given) + image read
     "tagi_im2col": lambda a: 4 * _planes(a[0], a[1]) * a[4] * a[5] * (
         a[6] * a[7] + _out_pixels(a[6], a[7], a[8], a[9], a[10], a[11]) * a[8] * a[8]),
+    "tagi_im2col_t": lambda a: 4 * a[2] * a[3] * (
+        a[4] * a[5] + _out_pixels(a[4], a[5], a[6], a[7], a[8], a[9]) * a[6] * a[6]),
     "tagi_nchw_to_nhwc": lambda a: 8 * _planes(a[0], a[1]) * a[4] * a[5] * a[6],
     "tagi_col2im": lambda a: 8 * a[4] * a[5] * (
         a[6] * a[7] + _out_pixels(a[6], a[7], a[8], a[9], a[10], a[11]) * a[8] * a[8]),
@@ -229,6 +231,7 @@ class LaunchTimer:
         "tagi_conv2d_backward_delta": (
             "backward_delta", lambda a: 4.0 * a[5] * a[7] * a[8] * a[6] * a[9] * a[10] * a[10]),
         "tagi_param_grad": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
+        "tagi_param_grad_t": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
     }
 
     def __init__(self):

@@ -197,6 +197,16 @@ int tagi_param_grad(const float* a, int64_t lda, const float* dmz, const float* 
                     float* out_Sb, float cap_factor, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* tagi_param_grad with the activations given transposed: at is K x M (row
+ * stride ldat, the M reduction elements of each row contiguous), e.g. the
+ * transposed patches of tagi_im2col_t. Same modes, outputs and workspace. */
+int tagi_param_grad_t(const float* at, int64_t ldat, const float* dmz, const float* dSz,
+                      int64_t d_div, int64_t d_outer, int64_t d_stride, int64_t d_nstride,
+                      int64_t M, int64_t K, int64_t N, int has_bias, int mode, float* mw,
+                      float* Sw, float* mb, float* Sb, float* out_m, float* out_S, float* out_mb,
+                      float* out_Sb, float cap_factor, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /* Apply all-reduced raw sums (layout of TAGI_WGRAD_SUMS) as the capped update:
  * m += cap(S*g_m), S += cap(S^2*g_S), floor 1e-5 (parameters.py:77-96). */
 int tagi_apply_param_sums(const float* g_m, const float* g_S, int64_t K, int64_t N, int has_bias,
@@ -280,6 +290,12 @@ int tagi_avgpool_backward(const float* dm, const float* dS, float* dm_out, float
 int tagi_im2col(const float* xm, const float* xS, float* pm, float* pS, int64_t N, int64_t C,
                 int64_t H, int64_t W, int64_t k, int64_t stride, int64_t padding,
                 int64_t padding_type, void* stream);
+
+/* Transposed mean patches: pt is (C*k*k) x (N*Ho*Wo), row (c, kh, kw) holding
+ * x[n][c][oh*stride - pad + kh][ow*stride - pad + kw] (0 outside) at column
+ * (n, oh, ow); padding_type as tagi_im2col. For tagi_param_grad_t. */
+int tagi_im2col_t(const float* x, float* pt, int64_t N, int64_t C, int64_t H, int64_t W,
+                  int64_t k, int64_t stride, int64_t padding, int64_t padding_type, void* stream);
 
 /* NCHW -> NHWC copy of a tensor pair (yS, xS may both be NULL): y[n][p][c] =
  * x[n][c][p] for p < HW, for the channels-last gathers of the Conv2D entries. */

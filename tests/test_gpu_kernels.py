@@ -280,6 +280,25 @@ def test_im2col_channel_slices(C, H, W, k, s, p, pt):
     np.testing.assert_array_equal(only.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
 
 
+@pytest.mark.parametrize("C,H,W,k,s,p,pt", [(3, 11, 10, 3, 1, 1, 1), (5, 40, 36, 3, 2, 1, 2),
+                                             (4, 9, 700, 5, 1, 2, 1), (2, 5, 2100, 3, 1, 1, 1),
+                                             (6, 12, 12, 1, 1, 0, 1), (3, 30, 33, 7, 2, 3, 2)])
+def test_im2col_transposed(C, H, W, k, s, p, pt):
+    """tagi_im2col_t: one output-row band per CTA (whole maps, several bands of
+    a wide image, 128-bit stores or not) and the element-per-thread kernel of
+    images too wide to stage; bit-exact against the transposed unfold."""
+    from triton_tagi._lib import lib, stream
+
+    gen = torch.Generator().manual_seed(C * W + k)
+    N = 3
+    x = rnd(gen, N, C, H, W)
+    Ho, Wo = F.conv_out_hw(H, W, k, s, p, pt)
+    dx = g(x)
+    out = torch.full((C * k * k, N * Ho * Wo), 7.0, device=DEV)
+    lib()("tagi_im2col_t", dx.data_ptr(), out.data_ptr(), N, C, H, W, k, s, p, pt, stream(dx))
+    np.testing.assert_array_equal(out.cpu().numpy(), F.im2col(x, k, s, p, pt).t().numpy())
+
+
 @pytest.mark.parametrize("shape,k,s,p,pt", [((2, 3, 9, 7), 3, 2, 1, 2), ((3, 4, 8, 8), 3, 1, 1, 1),
                                             ((2, 5, 16, 16), 2, 2, 0, 1),
                                             ((2, 3, 12, 12), 5, 1, 2, 1)])

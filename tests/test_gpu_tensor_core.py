@@ -388,3 +388,54 @@ def test_conv_entries_channels_last_equal_nchw(C, Co):
     for name, a, b in zip(("mz", "Sz", "d_ma", "d_Sa"), *outs):
         assert torch.equal(a, b), name
     _ok()
+
+
+@pytest.mark.parametrize("C,H,W,k,s,p,pt,Co", [(64, 32, 32, 3, 1, 1, 1, 64), (3, 32, 32, 3, 1, 1, 1, 64),
+                                              (16, 17, 13, 3, 2, 1, 2, 32), (8, 20, 24, 5, 1, 2, 1, 40)])
+def test_param_grad_transposed_patches(C, H, W, k, s, p, pt, Co):
+    """tagi_im2col_t writes the transpose of tagi_im2col's patches (bit-exact
+    against the oracle's unfold), and tagi_param_grad_t on them gives the
+    weight and bias deltas of tagi_param_grad on the plain patches: the
+    same reduction in the same order, bit-identical."""
+    from triton_tagi._lib import WGRAD_DELTAS, lib, stream
+
+    L = lib()
+    g = torch.Generator().manual_seed(C * H + Co)
+    N = 8 if C > 8 else 4
+    Ho, Wo = F.conv_out_hw(H, W, k, s, p, pt)
+    M, K = N * Ho * Wo, C * k * k
+    assert M % 8 == 0
+    x = _rnd(g, N, C, H, W)
+    xd = x.to(DEV)
+    pm = torch.empty(M, K, device=DEV)
+    L("tagi_im2col", xd.data_ptr(), None, pm.data_ptr(), None, N, C, H, W, k, s, p, pt, stream(xd))
+    ptr = torch.full((K, M), 7.0, device=DEV)
+    L("tagi_im2col_t", xd.data_ptr(), ptr.data_ptr(), N, C, H, W, k, s, p, pt, stream(xd))
+    ref = F.im2col(x, k, s, p, pt)
+    assert torch.equal(ptr.cpu(), ref.t().contiguous())
+    assert torch.equal(pm.cpu(), ref)
+    dmz = _rnd(g, N, Co, Ho, Wo, scale=0.1).to(DEV)
+    dSz = -_rnd(g, N, Co, Ho, Wo, u=True, scale=1e-2).to(DEV)
+    Sw = _rnd(g, K, Co, u=True, scale=1e-2).to(DEV)
+    Sb = _rnd(g, 1, Co, u=True, scale=1e-3).to(DEV)
+    d_map = (Ho * Wo, Co * Ho * Wo, 1, Ho * Wo)
+    ws = torch.empty(max(L.size("tagi_param_grad_workspace_size", M, K, Co, 1), 1),
+                     dtype=torch.uint8, device=DEV)
+    outs = []
+    for entry, a, lda in (("tagi_param_grad", pm, K), ("tagi_param_grad_t", ptr, M)):
+        o = [torch.empty(K, Co, device=DEV), torch.empty(K, Co, device=DEV),
+             torch.empty(1, Co, device=DEV), torch.empty(1, Co, device=DEV)]
+        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, Co, 1,
+          WGRAD_DELTAS, None, Sw.data_ptr(), None, Sb.data_ptr(), *(t.data_ptr() for t in o), 1.0,
+          ws.data_ptr(), ws.numel(), stream(a))
+        outs.append(o)
+    for name, a, b in zip(("delta_mw", "delta_Sw", "delta_mb", "delta_Sb"), *outs):
+        assert torch.equal(a, b), name
+    # and against the float64 oracle
+    d = lambda t: t.double().cpu()  # noqa: E731
+    P = d(ref)
+    Dm = d(dmz).permute(0, 2, 3, 1).reshape(M, Co)
+    DS = d(dSz).permute(0, 2, 3, 1).reshape(M, Co)
+    assert_rel(outs[1][0], d(Sw) * (P.t() @ Dm), MEAN_RTOL, "delta_mw")
+    assert_rel(outs[1][1], d(Sw) ** 2 * ((P * P).t() @ DS), VAR_RTOL, "delta_Sw")
+    _ok()

@@ -343,6 +343,80 @@ __global__ void nchw_to_nhwc_kernel(const float* xm, const float* xS, float* ym,
     }
 }
 
+// Transposed mean patches: row i = (c, kh, kw) of PT holds, for every output
+// pixel q = (n, oh, ow), x[n][c][oh*s - p + kh][ow*s - p + kw] (0 outside the
+// image). One CTA per (n, c, band of TH output rows): the band's input rows
+// ((TH-1)*s + k of them, one contiguous range of the plane; rows outside the
+// image staged as zeros) go to shared memory, then each of the k*k patch rows
+// of the band is written as one contiguous run of TH*Wo pixels, four per thread
+// and 128-bit store when V4 (Wo and Q multiples of 4).
+template <bool V4>
+__global__ void __launch_bounds__(256) im2col_t_band_kernel(const float* x, float* pt, ConvGeom g,
+                                                            int64_t Q, int TH, int bands) {
+    extern __shared__ float sx[];
+    const int band = static_cast<int>(blockIdx.x % bands);
+    const int64_t nc = blockIdx.x / bands;
+    const int n = static_cast<int>(nc / g.C), c = static_cast<int>(nc - static_cast<int64_t>(n) * g.C);
+    const int oh0 = band * TH, th = min(TH, g.Ho - oh0);
+    const int rows_in = (th - 1) * g.s + g.k;
+    const int64_t plane_len = static_cast<int64_t>(g.H) * g.W;
+    const float* plane = x + nc * plane_len;
+    const int64_t first = static_cast<int64_t>(oh0 * g.s - g.p_tl) * g.W;  // may be negative
+    const int staged = rows_in * g.W;
+    for (int i = threadIdx.x; i < staged; i += blockDim.x) {
+        const int64_t o = first + i;
+        sx[i] = (o >= 0 && o < plane_len) ? __ldg(plane + o) : 0.f;
+    }
+    __syncthreads();
+    const int cnt = th * g.Wo, kk = g.k * g.k;
+    const float rWo = 1.f / g.Wo;
+    const int64_t col0 = static_cast<int64_t>(n) * g.Ho * g.Wo + static_cast<int64_t>(oh0) * g.Wo;
+    for (int t = 0; t < kk; ++t) {
+        const int kh = t / g.k, kw = t - kh * g.k;
+        float* out = pt + (static_cast<int64_t>(c) * kk + t) * Q + col0;
+        if (V4) {
+            for (int j = 4 * threadIdx.x; j < cnt; j += 4 * blockDim.x) {
+                const int ol = div_small(j, rWo), ow = j - ol * g.Wo;  // 4 pixels of one row
+                const float* row = sx + (ol * g.s + kh) * g.W;
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int iw = (ow + e) * g.s - g.p_tl + kw;
+                    v[e] = static_cast<unsigned>(iw) < static_cast<unsigned>(g.W) ? row[iw] : 0.f;
+                }
+                *reinterpret_cast<float4*>(out + j) = make_float4(v[0], v[1], v[2], v[3]);
+            }
+        } else {
+            for (int j = threadIdx.x; j < cnt; j += blockDim.x) {
+                const int ol = div_small(j, rWo), ow = j - ol * g.Wo;
+                const int iw = ow * g.s - g.p_tl + kw;
+                out[j] = static_cast<unsigned>(iw) < static_cast<unsigned>(g.W)
+                             ? sx[(ol * g.s + kh) * g.W + iw]
+                             : 0.f;
+            }
+        }
+    }
+}
+
+// The same patches one element per thread, for images too wide to stage k rows
+// (grid row = patch row i).
+__global__ void im2col_t_kernel(const float* x, float* pt, ConvGeom g, int64_t Q) {
+    const int i = blockIdx.y;
+    const int kk = g.k * g.k, c = i / kk, t = i - c * kk, kh = t / g.k, kw = t - kh * g.k;
+    const int64_t L = static_cast<int64_t>(g.Ho) * g.Wo;
+    float* out = pt + static_cast<int64_t>(i) * Q;
+    const int64_t plane = static_cast<int64_t>(g.H) * g.W;
+    for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < Q;
+         q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t n = q / L;
+        const int l = static_cast<int>(q - n * L), oh = l / g.Wo, ow = l - oh * g.Wo;
+        const int ih = oh * g.s - g.p_tl + kh, iw = ow * g.s - g.p_tl + kw;
+        const bool in = static_cast<unsigned>(ih) < static_cast<unsigned>(g.H) &&
+                        static_cast<unsigned>(iw) < static_cast<unsigned>(g.W);
+        out[q] = in ? __ldg(x + (n * g.C + c) * plane + static_cast<int64_t>(ih) * g.W + iw) : 0.f;
+    }
+}
+
 }  // namespace
 }  // namespace tagi
 
@@ -440,5 +514,40 @@ extern "C" int tagi_nchw_to_nhwc(const float* xm, const float* xS, float* ym, fl
     const dim3 grid(static_cast<unsigned>((Q + 31) / 32), static_cast<unsigned>((C + 31) / 32), 1);
     nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(xm, xS, ym, yS, (int)C,
                                                                        (int)HW, Q);
+    return check_launch(what);
+}
+
+extern "C" int tagi_im2col_t(const float* x, float* pt, int64_t N, int64_t C, int64_t H,
+                             int64_t W, int64_t k, int64_t stride, int64_t padding,
+                             int64_t padding_type, void* stream) {
+    const char* what = "tagi_im2col_t";
+    ConvGeom g;
+    TAGI_REQUIRE(make_geom(N, C, H, W, k, stride, padding, padding_type, &g), TAGI_E_BAD_ARG,
+                 "%s: bad geometry", what);
+    const int64_t Q = N * g.Ho * g.Wo, rows = C * k * k;
+    if (Q == 0 || rows == 0) return TAGI_OK;
+    TAGI_REQUIRE(x && pt, TAGI_E_BAD_ARG, "%s: null pointer", what);
+    // band kernel: staged rows within 24 KB, band pixels (div_small) below 2^22
+    constexpr int64_t kStage = 24 * 1024 / sizeof(float);
+    const int64_t rows_max = kStage / W;
+    if (rows_max >= k) {
+        const int64_t TH = std::min<int64_t>({static_cast<int64_t>(g.Ho), (rows_max - k) / stride + 1,
+                                              ((int64_t(1) << 22) - 1) / g.Wo});
+        const int64_t bands = (g.Ho + TH - 1) / TH;
+        const size_t smem = static_cast<size_t>(((TH - 1) * stride + k) * W) * sizeof(float);
+        const bool v4 = g.Wo % 4 == 0 && Q % 4 == 0 && (reinterpret_cast<uintptr_t>(pt) & 15) == 0;
+        const int64_t blocks = N * C * bands;
+        TAGI_REQUIRE(blocks <= INT_MAX, TAGI_E_UNSUPPORTED, "%s: too many planes", what);
+        if (v4)
+            im2col_t_band_kernel<true><<<static_cast<unsigned>(blocks), 256, smem, as_stream(stream)>>>(
+                x, pt, g, Q, static_cast<int>(TH), static_cast<int>(bands));
+        else
+            im2col_t_band_kernel<false><<<static_cast<unsigned>(blocks), 256, smem, as_stream(stream)>>>(
+                x, pt, g, Q, static_cast<int>(TH), static_cast<int>(bands));
+        return check_launch(what);
+    }
+    TAGI_REQUIRE(rows <= 65535, TAGI_E_UNSUPPORTED, "%s: too many patch rows", what);
+    const unsigned bx = static_cast<unsigned>(std::min<int64_t>((Q + 255) / 256, 4096));
+    im2col_t_kernel<<<dim3(bx, static_cast<unsigned>(rows)), 256, 0, as_stream(stream)>>>(x, pt, g, Q);
     return check_launch(what);
 }

@@ -648,13 +648,17 @@ extern "C" size_t tagi_param_grad_workspace_size(int64_t M, int64_t K, int64_t N
     return wgrad_ws_total((int)K + (has_bias ? 1 : 0), (int)N, (int)M);
 }
 
-extern "C" int tagi_param_grad(const float* a, int64_t lda, const float* dmz, const float* dSz,
-                               int64_t d_div, int64_t d_outer, int64_t d_stride,
-                               int64_t d_nstride, int64_t M, int64_t K, int64_t N, int has_bias,
-                               int mode, float* mw, float* Sw, float* mb, float* Sb, float* out_m,
-                               float* out_S, float* out_mb, float* out_Sb, float cap_factor,
-                               void* workspace, size_t workspace_bytes, void* stream) {
-    const char* what = "tagi_param_grad";
+namespace tagi {
+namespace {
+// The weight-gradient family with the activations given either as a (M x K,
+// row stride lda: a_rows = 1, a_k = lda) or transposed (K x M: a_rows = lda,
+// a_k = 1).
+int param_grad(const char* what, const float* a, int64_t a_rows, int64_t a_k, const float* dmz,
+               const float* dSz, int64_t d_div, int64_t d_outer, int64_t d_stride,
+               int64_t d_nstride, int64_t M, int64_t K, int64_t N, int has_bias, int mode,
+               float* mw, float* Sw, float* mb, float* Sb, float* out_m, float* out_S,
+               float* out_mb, float* out_Sb, float cap_factor, void* workspace,
+               size_t workspace_bytes, void* stream) {
     TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
                  what);
     TAGI_REQUIRE(M == 0 || (a && dmz && dSz), TAGI_E_BAD_ARG, "%s: null input", what);
@@ -673,7 +677,7 @@ extern "C" int tagi_param_grad(const float* a, int64_t lda, const float* dmz, co
     if (mode == TAGI_WGRAD_UPDATE)
         TAGI_REQUIRE(mw && (!has_bias || mb), TAGI_E_BAD_ARG, "%s: null means", what);
     GemmArgs g = blank();
-    g.x = a; g.arow = plain_rows(1); g.ak = lda;
+    g.x = a; g.arow = plain_rows(a_rows); g.ak = a_k;
     g.ones_row = has_bias ? (int)K : -1;
     g.u = dmz; g.v = dSz; g.brow = RowMap{d_div, d_outer, d_stride}; g.bn = d_nstride;
     g.N = (int)N; g.Kr = (int)M;
@@ -681,6 +685,31 @@ extern "C" int tagi_param_grad(const float* a, int64_t lda, const float* dmz, co
                     cap_factor};
     return run_wgrad(g, (int)K + (has_bias ? 1 : 0), workspace, workspace_bytes, true,
                      as_stream(stream), what);
+}
+}  // namespace
+}  // namespace tagi
+
+extern "C" int tagi_param_grad(const float* a, int64_t lda, const float* dmz, const float* dSz,
+                               int64_t d_div, int64_t d_outer, int64_t d_stride,
+                               int64_t d_nstride, int64_t M, int64_t K, int64_t N, int has_bias,
+                               int mode, float* mw, float* Sw, float* mb, float* Sb, float* out_m,
+                               float* out_S, float* out_mb, float* out_Sb, float cap_factor,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+    return param_grad("tagi_param_grad", a, 1, lda, dmz, dSz, d_div, d_outer, d_stride, d_nstride,
+                      M, K, N, has_bias, mode, mw, Sw, mb, Sb, out_m, out_S, out_mb, out_Sb,
+                      cap_factor, workspace, workspace_bytes, stream);
+}
+
+extern "C" int tagi_param_grad_t(const float* at, int64_t ldat, const float* dmz, const float* dSz,
+                                 int64_t d_div, int64_t d_outer, int64_t d_stride,
+                                 int64_t d_nstride, int64_t M, int64_t K, int64_t N, int has_bias,
+                                 int mode, float* mw, float* Sw, float* mb, float* Sb,
+                                 float* out_m, float* out_S, float* out_mb, float* out_Sb,
+                                 float cap_factor, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    return param_grad("tagi_param_grad_t", at, ldat, 1, dmz, dSz, d_div, d_outer, d_stride,
+                      d_nstride, M, K, N, has_bias, mode, mw, Sw, mb, Sb, out_m, out_S, out_mb,
+                      out_Sb, cap_factor, workspace, workspace_bytes, stream);
 }
 
 extern "C" int tagi_apply_param_sums(const float* g_m, const float* g_S, int64_t K, int64_t N,

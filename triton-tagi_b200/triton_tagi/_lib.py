@@ -37,6 +37,7 @@ _SIGS = {
     "tagi_fused_weight_grad_static": "ppppp" + "iii" + "iiiiii" + "p",
     "tagi_param_grad_workspace_size": "iiin",
     "tagi_param_grad": "pipp" + "iiii" + "iii" + "nn" + "pppp" + "pppp" + "f" + "pz" + "p",
+    "tagi_param_grad_t": "pipp" + "iiii" + "iii" + "nn" + "pppp" + "pppp" + "f" + "pz" + "p",
     "tagi_apply_param_sums": "pp" + "ii" + "n" + "pppp" + "f" + "p",
     "tagi_bmm_tagi_var": "pppppp" + "iiii" + "iiiiiiiii" + "ff" + "p",
     "tagi_bmm_shared_right": "ppppp" + "iiii" + "iiiiiiiii" + "f" + "p",
@@ -49,6 +50,7 @@ _SIGS = {
     "tagi_avgpool_forward": "pppp" + "iiiii" + "f" + "p",
     "tagi_avgpool_backward": "pppp" + "iiiii" + "f" + "p",
     "tagi_im2col": "pppp" + "iiiiiiii" + "p",
+    "tagi_im2col_t": "pp" + "iiiiiiii" + "p",
     "tagi_col2im": "pppp" + "iiiiiiii" + "n" + "p",
     "tagi_bn_channel_sums": "ppp" + "iii" + "p",
     "tagi_bn_finalize": "p" + "i" + "d" + "ppppp" + "nn" + "ff" + "p",

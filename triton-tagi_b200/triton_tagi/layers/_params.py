@@ -27,16 +27,19 @@ def sums_numel(K: int, N: int, has_bias: bool) -> int:
     return 2 * (K + (1 if has_bias else 0)) * N
 
 
-def weight_param_backward(layer, a, lda, dm, d_map, M, K, N, has_bias) -> None:
+def weight_param_backward(layer, a, lda, dm, d_map, M, K, N, has_bias,
+                          transposed: bool = False) -> None:
     """Parameter side of backward for a (K x N) weight and optional (1 x N) bias.
 
-    a: activation matrix (M x K, row stride lda); dm = (dmz, dSz) with row map
+    a: activation matrix (M x K, row stride lda), or with ``transposed`` its
+    transpose (K x M, row stride lda); dm = (dmz, dSz) with row map
     d_map = (div, outer, stride, col_stride).
     """
     contiguous_params(layer)
     dmz, dSz = dm
     mode = layer._param_mode
     L = lib()
+    entry = "tagi_param_grad_t" if transposed else "tagi_param_grad"
     hb = 1 if has_bias else 0
     hold, wp, wn = workspace(L.size("tagi_param_grad_workspace_size", M, K, N, hb), a)
     null4 = (None, None, None, None)
@@ -50,11 +53,11 @@ def weight_param_backward(layer, a, lda, dm, d_map, M, K, N, has_bias) -> None:
         outs = (layer.delta_mw.data_ptr(), layer.delta_Sw.data_ptr(),
                 layer.delta_mb.data_ptr() if has_bias else None,
                 layer.delta_Sb.data_ptr() if has_bias else None)
-        L("tagi_param_grad", a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
+        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
           hb, WGRAD_DELTAS, None, layer.Sw.data_ptr(), None,
           layer.Sb.data_ptr() if has_bias else None, *outs, 1.0, wp, wn, stream(a))
     elif mode == "update":
-        L("tagi_param_grad", a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
+        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
           hb, WGRAD_UPDATE, layer.mw.data_ptr(), layer.Sw.data_ptr(),
           layer.mb.data_ptr() if has_bias else None, layer.Sb.data_ptr() if has_bias else None,
           *null4, float(layer._cap), wp, wn, stream(a))
@@ -62,7 +65,7 @@ def weight_param_backward(layer, a, lda, dm, d_map, M, K, N, has_bias) -> None:
     elif mode == "sums":
         buf = layer._reducer.buffer(layer, sums_numel(K, N, has_bias), torch.float32)
         half = buf.numel() // 2
-        L("tagi_param_grad", a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
+        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
           hb, WGRAD_SUMS, None, None, None, None, buf.data_ptr(), buf[half:].data_ptr(), None,
           None, 1.0, wp, wn, stream(a))
         layer._reducer.ready(layer)

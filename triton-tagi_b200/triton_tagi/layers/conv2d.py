@@ -136,10 +136,20 @@ class Conv2D(LearnableLayer):
                       d_Sa.data_ptr(), N, C, H, W, k, self.stride, p, self.padding_type,
                       _COL2IM_MODES[self.col2im_mode], st)
                 del dpm, dpS
-        pm = torch.empty(N * L, K, device=dev)
-        lib()("tagi_im2col", self.input_ma.data_ptr(), None, pm.data_ptr(), None, N, C, H, W, k,
-              self.stride, p, self.padding_type, st)
-        weight_param_backward(self, pm, K, (dmz, dSz), d_map, N * L, K, Co, True)
+        if Co <= 64 and (N * L) % 8 == 0:
+            # Up to 64 output channels the weight-sum tiles stage each patch
+            # column (c, kh, kw) as one thread's row: the transposed patches give
+            # it contiguous pixels.
+            pt = torch.empty(K, N * L, device=dev)
+            lib()("tagi_im2col_t", self.input_ma.data_ptr(), pt.data_ptr(), N, C, H, W, k,
+                  self.stride, p, self.padding_type, st)
+            weight_param_backward(self, pt, N * L, (dmz, dSz), d_map, N * L, K, Co, True,
+                                  transposed=True)
+        else:
+            pm = torch.empty(N * L, K, device=dev)
+            lib()("tagi_im2col", self.input_ma.data_ptr(), None, pm.data_ptr(), None, N, C, H,
+                  W, k, self.stride, p, self.padding_type, st)
+            weight_param_backward(self, pm, K, (dmz, dSz), d_map, N * L, K, Co, True)
         return d_ma, d_Sa
 
     def update(self, cap_factor: float) -> None:
