@@ -280,6 +280,24 @@ def test_im2col_channel_slices(C, H, W, k, s, p, pt):
     np.testing.assert_array_equal(only.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
 
 
+@pytest.mark.parametrize("N,C,HW", [(3, 6, 7), (4, 64, 1024), (2, 36, 49), (5, 520, 16),
+                                    (3, 12, 20), (1, 100, 4), (2, 8, 1)])
+def test_nchw_to_nhwc(N, C, HW):
+    """Channels-last copies, one plane and two: the 128-bit tile kernel (C and
+    HW multiples of 4) and the general one; exact."""
+    from triton_tagi._lib import lib, stream
+
+    gen = torch.Generator().manual_seed(N * C + HW)
+    a, b = g(rnd(gen, N, C, HW)), g(rnd(gen, N, C, HW))
+    ya, yb = torch.full((N, HW, C), 7.0, device=DEV), torch.full((N, HW, C), 7.0, device=DEV)
+    lib()("tagi_nchw_to_nhwc", a.data_ptr(), b.data_ptr(), ya.data_ptr(), yb.data_ptr(), N, C, HW,
+          stream(a))
+    assert torch.equal(ya, a.permute(0, 2, 1)) and torch.equal(yb, b.permute(0, 2, 1))
+    only = torch.full((N, HW, C), 7.0, device=DEV)
+    lib()("tagi_nchw_to_nhwc", b.data_ptr(), None, only.data_ptr(), None, N, C, HW, stream(a))
+    assert torch.equal(only, b.permute(0, 2, 1))
+
+
 @pytest.mark.parametrize("C,H,W,k,s,p,pt", [(3, 11, 10, 3, 1, 1, 1), (5, 40, 36, 3, 2, 1, 2),
                                              (4, 9, 700, 5, 1, 2, 1), (2, 5, 2100, 3, 1, 1, 1),
                                              (6, 12, 12, 1, 1, 0, 1), (3, 30, 33, 7, 2, 3, 2)])

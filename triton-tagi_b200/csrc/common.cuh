@@ -49,13 +49,18 @@ __device__ __forceinline__ void capped_pair(float& m, float& S, float dm, float 
 __device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
     constexpr float kInvSqrt2Pi = 0.3989422804014327f;
     constexpr float kInvSqrt2 = 0.7071067811865476f;
+    // The kernel is bound by instruction issue, so the square root, the two
+    // divisions and the exponential use the hardware approximations (a few
+    // ulp, as the reference's fast sqrt, division and exp).
     const float Ss = fmaxf(Sz, 1e-30f);
-    const float sd = sqrtf(Ss);
-    const float alpha = mz / sd;
-    const float pdf = expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
+    const float rs = rsqrtf(Ss);
+    const float sd = Ss * rs;
+    const float alpha = mz * rs;
+    const float pdf = __expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
     // Below alpha = -5 the erf form cancels to 0 in fp32; the reference uses the
     // leading asymptotic term phi(alpha)/|alpha| there.
-    const float cdf = alpha < -5.0f ? pdf / (-alpha) : 0.5f * (1.0f + erff(alpha * kInvSqrt2));
+    const float cdf =
+        alpha < -5.0f ? __fdividef(pdf, -alpha) : 0.5f * (1.0f + erff(alpha * kInvSqrt2));
     const float mu = sd * pdf + mz * cdf;
     const float v = -mu * mu + 2.0f * mu * mz - mz * sd * pdf + (Ss - mz * mz) * cdf;
     ma = mu;
