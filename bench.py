@@ -205,10 +205,10 @@ ENTRY_BYTES = {
 # 4096 x 4096 x 4096 Linear forward scaled by M to the sweep's 8192-row headline
 # (A and the number of B re-reads both grow with M).
 MEASURED_TRAFFIC = {
-    ("r18", "moment_forward"): 53.5e6,
-    ("r18", "backward_delta"): 43.8e6,
-    ("r18", "param_grad"): 151.2e6,
-    ("swp", "moment_forward"): 2 * 1.822e9,
+    ("r18", "moment_forward"): 53.2e6,
+    ("r18", "backward_delta"): 43.6e6,
+    ("r18", "param_grad"): 150.8e6,
+    ("swp", "moment_forward"): 2 * 1.833e9,
 }
 
 

@@ -175,7 +175,7 @@ __global__ void bn_forward_kernel(const float* mz, const float* Sz, const float*
         const float rs = var[c];
         const float inv_std = 1.0f / sqrtf(rs + eps);
         const float m_hat = (mz[i] - mean[c]) * inv_std;
-        const float S_hat = Sz[i] / (rs + eps);
+        const float S_hat = Sz[i] * (1.0f / (rs + eps));
         const float g = mg[c], sg = Sg[c];
         ma[i] = g * m_hat + mb[c];
         Sa[i] = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + Sb[c];
@@ -279,6 +279,7 @@ __global__ void bn_forward_v4_kernel(const float4* mz, const float4* Sz, const f
         const int c = static_cast<int>((i / HW4) % C);
         const float rs = var[c], mu = mean[c];
         const float inv_std = 1.0f / sqrtf(rs + eps);
+        const float inv_var = 1.0f / (rs + eps);
         const float g = mg[c], sg = Sg[c], b = mb[c], sb = Sb[c];
         const float4 m = mz[i], S = Sz[i];
         const float mv[4] = {m.x, m.y, m.z, m.w}, Sv[4] = {S.x, S.y, S.z, S.w};
@@ -286,7 +287,7 @@ __global__ void bn_forward_v4_kernel(const float4* mz, const float4* Sz, const f
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             mh[e] = (mv[e] - mu) * inv_std;
-            Sh[e] = Sv[e] / (rs + eps);
+            Sh[e] = Sv[e] * inv_var;
             om[e] = g * mh[e] + b;
             oS[e] = g * g * Sh[e] + sg * mh[e] * mh[e] + sg * Sh[e] + sb;
         }
@@ -370,6 +371,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     const int c = sl.c;
     const float mu = stat[0], rs = stat[1], g = stat[2];
     const float inv_std = 1.0f / sqrtf(rs + eps);
+    const float inv_var = 1.0f / (rs + eps);
     const float sg = Sg[c], b = mb[c], sb = Sb[c];
     for (int t = threadIdx.x; t < total; t += blockDim.x) {
         if (V4) {
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 mh[e] = (mv[e] - mu) * inv_std;
-                const float Sh = Sv[e] / (rs + eps);
+                const float Sh = Sv[e] * inv_var;
                 om[e] = g * mh[e] + b;
                 oS[e] = g * g * Sh + sg * mh[e] * mh[e] + sg * Sh + sb;
             }
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
             const int li = t / HW;
             const int64_t o = sl.offset(li, t - li * HW);
             const float m_hat = (mz[o] - mu) * inv_std;
-            const float S_hat = Sz[o] / (rs + eps);
+            const float S_hat = Sz[o] * inv_var;
             float om = g * m_hat + b;
             float oS = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
             if (add_m) {
