@@ -277,6 +277,11 @@ def test_conv_stride1_input_deltas_as_one_contraction(C, Co, k, p):
     assert_rel(d_dS, exact_S, VAR_RTOL, "d_Sa vs float64")
     assert_rel(d_dm, r_dm, MEAN_RTOL, "d_ma vs reference restatement")
     assert_rel(d_dS, r_dS, VAR_RTOL, "d_Sa vs reference restatement")
+    # weight deltas from the channels-last copy of the deltas (Co % 8 == 0)
+    assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "delta_mw")
+    assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "delta_Sw")
+    assert_rel(dev.delta_mb, ref.delta_mb, MEAN_RTOL, "delta_mb")
+    assert_rel(dev.delta_Sb, ref.delta_Sb, VAR_RTOL, "delta_Sb")
     _ok()
 
 

@@ -230,21 +230,36 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
         }
     };
     if (V4) {
+        // two float4 runs per thread and iteration, loaded before either is
+        // used (the same summation order as one at a time)
         const int HW4 = HW / 4, total = sl.nimg * HW4;
-        for (int t = threadIdx.x; t < total; t += blockDim.x) {
-            const int li = t / HW4, h = (t - li * HW4) * 4;
-            const int64_t o = sl.offset(li, h);
-            const float4 a = __ldg(reinterpret_cast<const float4*>(dma + o));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(dSa + o));
-            const float4 c = __ldg(reinterpret_cast<const float4*>(mhat + o));
-            const float4 j = rj ? __ldg(reinterpret_cast<const float4*>(rj + o)) : float4{};
-            float4 om, oS;
-            one(a.x, b.x, c.x, j.x, om.x, oS.x);
-            one(a.y, b.y, c.y, j.y, om.y, oS.y);
-            one(a.z, b.z, c.z, j.z, om.z, oS.z);
-            one(a.w, b.w, c.w, j.w, om.w, oS.w);
-            *reinterpret_cast<float4*>(dmz + o) = om;
-            *reinterpret_cast<float4*>(dSz + o) = oS;
+        auto off4 = [&](int t) {
+            const int li = t / HW4;
+            return sl.offset(li, (t - li * HW4) * 4);
+        };
+        for (int t = threadIdx.x; t < total; t += 2 * blockDim.x) {
+            const int t1 = t + blockDim.x;
+            const bool two = t1 < total;
+            const int64_t o[2] = {off4(t), two ? off4(t1) : off4(t)};
+            float4 a[2], b[2], c[2], j[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                a[u] = __ldg(reinterpret_cast<const float4*>(dma + o[u]));
+                b[u] = __ldg(reinterpret_cast<const float4*>(dSa + o[u]));
+                c[u] = __ldg(reinterpret_cast<const float4*>(mhat + o[u]));
+                j[u] = rj ? __ldg(reinterpret_cast<const float4*>(rj + o[u])) : float4{};
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (u == 1 && !two) break;
+                float4 om, oS;
+                one(a[u].x, b[u].x, c[u].x, j[u].x, om.x, oS.x);
+                one(a[u].y, b[u].y, c[u].y, j[u].y, om.y, oS.y);
+                one(a[u].z, b[u].z, c[u].z, j[u].z, om.z, oS.z);
+                one(a[u].w, b[u].w, c[u].w, j[u].w, om.w, oS.w);
+                *reinterpret_cast<float4*>(dmz + o[u]) = om;
+                *reinterpret_cast<float4*>(dSz + o[u]) = oS;
+            }
         }
     } else {
         const int total = sl.nimg * HW;
@@ -317,13 +332,26 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     double v[3] = {0.0, 0.0, 0.0};
     const int HW4 = HW / 4;
     const int total = V4 ? sl.nimg * HW4 : sl.nimg * HW;
-    for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        if (V4) {
-            const int li = t / HW4, h = (t - li * HW4) * 4;
-            const int64_t o = sl.offset(li, h);
-            const float4 m = __ldg(reinterpret_cast<const float4*>(mz + o));
-            const float4 S = __ldg(reinterpret_cast<const float4*>(Sz + o));
-            const float mm[4] = {m.x, m.y, m.z, m.w}, ss[4] = {S.x, S.y, S.z, S.w};
+    // float4 runs: two per thread and iteration, loaded before either is summed
+    // (the same summation order as one at a time)
+    auto off4 = [&](int t) {
+        const int li = t / HW4;
+        return sl.offset(li, (t - li * HW4) * 4);
+    };
+    for (int t = threadIdx.x; V4 && t < total; t += 2 * blockDim.x) {
+        const int t1 = t + blockDim.x;
+        const bool two = t1 < total;
+        const int64_t o0 = off4(t), o1 = two ? off4(t1) : o0;
+        float4 m[2], S[2];
+        m[0] = __ldg(reinterpret_cast<const float4*>(mz + o0));
+        S[0] = __ldg(reinterpret_cast<const float4*>(Sz + o0));
+        m[1] = __ldg(reinterpret_cast<const float4*>(mz + o1));
+        S[1] = __ldg(reinterpret_cast<const float4*>(Sz + o1));
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (u == 1 && !two) break;
+            const float mm[4] = {m[u].x, m[u].y, m[u].z, m[u].w};
+            const float ss[4] = {S[u].x, S[u].y, S[u].z, S[u].w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const double x = mm[e];
@@ -331,7 +359,10 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
                 v[1] += ss[e];
                 v[2] += x * x;
             }
-        } else {
+        }
+    }
+    for (int t = threadIdx.x; !V4 && t < total; t += blockDim.x) {
+        {
             const int li = t / HW;
             const int64_t o = sl.offset(li, t - li * HW);
             const double x = mz[o];
@@ -373,13 +404,25 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     const float inv_std = 1.0f / sqrtf(rs + eps);
     const float inv_var = 1.0f / (rs + eps);
     const float sg = Sg[c], b = mb[c], sb = Sb[c];
-    for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        if (V4) {
-            const int li = t / HW4, h = (t - li * HW4) * 4;
-            const int64_t o = sl.offset(li, h);
-            const float4 m = __ldg(reinterpret_cast<const float4*>(mz + o));
-            const float4 S = __ldg(reinterpret_cast<const float4*>(Sz + o));
-            const float mv[4] = {m.x, m.y, m.z, m.w}, Sv[4] = {S.x, S.y, S.z, S.w};
+    for (int t = threadIdx.x; V4 && t < total; t += 2 * blockDim.x) {
+        const int t1 = t + blockDim.x;
+        const bool two = t1 < total;
+        const int64_t o[2] = {off4(t), two ? off4(t1) : off4(t)};
+        float4 m[2], S[2], am[2], aS[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            m[u] = __ldg(reinterpret_cast<const float4*>(mz + o[u]));
+            S[u] = __ldg(reinterpret_cast<const float4*>(Sz + o[u]));
+            if (add_m) {  // a residual stream added to the outputs
+                am[u] = __ldg(reinterpret_cast<const float4*>(add_m + o[u]));
+                aS[u] = __ldg(reinterpret_cast<const float4*>(add_S + o[u]));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (u == 1 && !two) break;
+            const float mv[4] = {m[u].x, m[u].y, m[u].z, m[u].w};
+            const float Sv[4] = {S[u].x, S[u].y, S[u].z, S[u].w};
             float om[4], oS[4], mh[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -388,16 +431,17 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
                 om[e] = g * mh[e] + b;
                 oS[e] = g * g * Sh + sg * mh[e] * mh[e] + sg * Sh + sb;
             }
-            if (add_m) {  // a residual stream added to the outputs
-                const float4 am = __ldg(reinterpret_cast<const float4*>(add_m + o));
-                const float4 aS = __ldg(reinterpret_cast<const float4*>(add_S + o));
-                om[0] += am.x; om[1] += am.y; om[2] += am.z; om[3] += am.w;
-                oS[0] += aS.x; oS[1] += aS.y; oS[2] += aS.z; oS[3] += aS.w;
+            if (add_m) {
+                om[0] += am[u].x; om[1] += am[u].y; om[2] += am[u].z; om[3] += am[u].w;
+                oS[0] += aS[u].x; oS[1] += aS[u].y; oS[2] += aS[u].z; oS[3] += aS[u].w;
             }
-            *reinterpret_cast<float4*>(ma + o) = make_float4(om[0], om[1], om[2], om[3]);
-            *reinterpret_cast<float4*>(Sa + o) = make_float4(oS[0], oS[1], oS[2], oS[3]);
-            *reinterpret_cast<float4*>(mhat + o) = make_float4(mh[0], mh[1], mh[2], mh[3]);
-        } else {
+            *reinterpret_cast<float4*>(ma + o[u]) = make_float4(om[0], om[1], om[2], om[3]);
+            *reinterpret_cast<float4*>(Sa + o[u]) = make_float4(oS[0], oS[1], oS[2], oS[3]);
+            *reinterpret_cast<float4*>(mhat + o[u]) = make_float4(mh[0], mh[1], mh[2], mh[3]);
+        }
+    }
+    for (int t = threadIdx.x; !V4 && t < total; t += blockDim.x) {
+        {
             const int li = t / HW;
             const int64_t o = sl.offset(li, t - li * HW);
             const float m_hat = (mz[o] - mu) * inv_std;
