@@ -300,11 +300,14 @@ def test_nchw_to_nhwc(N, C, HW):
 
 @pytest.mark.parametrize("C,H,W,k,s,p,pt", [(3, 11, 10, 3, 1, 1, 1), (5, 40, 36, 3, 2, 1, 2),
                                              (4, 9, 700, 5, 1, 2, 1), (2, 5, 2100, 3, 1, 1, 1),
-                                             (6, 12, 12, 1, 1, 0, 1), (3, 30, 33, 7, 2, 3, 2)])
+                                             (6, 12, 12, 1, 1, 0, 1), (3, 30, 33, 7, 2, 3, 2),
+                                             (4, 16, 21, 3, 1, 1, 2), (2, 7, 10, 5, 1, 1, 1),
+                                             (3, 6, 1500, 3, 1, 1, 1), (2, 9, 14, 3, 1, 0, 1)])
 def test_im2col_transposed(C, H, W, k, s, p, pt):
-    """tagi_im2col_t: one output-row band per CTA (whole maps, several bands of
-    a wide image, 128-bit stores or not) and the element-per-thread kernel of
-    images too wide to stage; bit-exact against the transposed unfold."""
+    """tagi_im2col_t: the stride-1 kernel (k = 1, 3, 5, zero-padded rows, one or
+    several bands), the general band kernel (128-bit stores or not) and the
+    element-per-thread kernel of images too wide to stage; bit-exact against the
+    transposed unfold."""
     from triton_tagi._lib import lib, stream
 
     gen = torch.Generator().manual_seed(C * W + k)

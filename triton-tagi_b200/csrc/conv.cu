@@ -439,6 +439,54 @@ __global__ void __launch_bounds__(256) im2col_t_band_kernel(const float* x, floa
     }
 }
 
+// Stride-1 transposed patches for k = K <= 5 with Wo a multiple of 4: the band's
+// input rows are staged zero-padded (padded column x = input column + p_tl, row
+// pitch Wo + 4), so that the K taps of a row, for 4 consecutive output pixels
+// ow..ow+3, are padded columns ow+kw .. ow+kw+3: two aligned 128-bit shared
+// loads (columns ow..ow+7) serve all K taps of one kernel row, without bounds
+// tests, and each tap leaves as one 128-bit store.
+template <int K>
+__global__ void __launch_bounds__(256) im2col_t_s1_kernel(const float* x, float* pt, ConvGeom g,
+                                                          int64_t Q, int TH, int bands) {
+    extern __shared__ __align__(16) float sx1[];
+    const int band = static_cast<int>(blockIdx.x % bands);
+    const int64_t nc = blockIdx.x / bands;
+    const int n = static_cast<int>(nc / g.C), c = static_cast<int>(nc - static_cast<int64_t>(n) * g.C);
+    const int oh0 = band * TH, th = min(TH, g.Ho - oh0);
+    const int rows_in = th + K - 1, Wp = g.Wo + 4;
+    const float* plane = x + nc * static_cast<int64_t>(g.H) * g.W;
+    const float rWp = 1.f / Wp;
+    for (int i = threadIdx.x; i < rows_in * Wp; i += blockDim.x) {
+        const int r = div_small(i, rWp), xc = i - r * Wp;
+        const int ih = oh0 - g.p_tl + r, iw = xc - g.p_tl;
+        sx1[i] = (static_cast<unsigned>(ih) < static_cast<unsigned>(g.H) &&
+                 static_cast<unsigned>(iw) < static_cast<unsigned>(g.W))
+                    ? __ldg(plane + static_cast<int64_t>(ih) * g.W + iw)
+                    : 0.f;
+    }
+    __syncthreads();
+    const int cnt = th * g.Wo;
+    const float rWo = 1.f / g.Wo;
+    float* base = pt + static_cast<int64_t>(c) * K * K * Q + static_cast<int64_t>(n) * g.Ho * g.Wo +
+                  static_cast<int64_t>(oh0) * g.Wo;
+    for (int j = 4 * threadIdx.x; j < cnt; j += 4 * blockDim.x) {
+        const int ol = div_small(j, rWo), ow = j - ol * g.Wo;
+        float* o = base + j;
+#pragma unroll
+        for (int kh = 0; kh < K; ++kh) {
+            const float* row = sx1 + (ol + kh) * Wp + ow;
+            const float4 a = *reinterpret_cast<const float4*>(row);
+            const float4 b = *reinterpret_cast<const float4*>(row + 4);
+            const float w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int kw = 0; kw < K; ++kw) {
+                *reinterpret_cast<float4*>(o) = make_float4(w[kw], w[kw + 1], w[kw + 2], w[kw + 3]);
+                o += Q;
+            }
+        }
+    }
+}
+
 // The same patches one element per thread, for images too wide to stage k rows
 // (grid row = patch row i).
 __global__ void im2col_t_kernel(const float* x, float* pt, ConvGeom g, int64_t Q) {
@@ -578,6 +626,26 @@ extern "C" int tagi_im2col_t(const float* x, float* pt, int64_t N, int64_t C, in
     TAGI_REQUIRE(x && pt, TAGI_E_BAD_ARG, "%s: null pointer", what);
     // band kernel: staged rows within 24 KB, band pixels (div_small) below 2^22
     constexpr int64_t kStage = 24 * 1024 / sizeof(float);
+    const bool al16 = (reinterpret_cast<uintptr_t>(pt) & 15) == 0;
+    const int64_t rows_s1 = kStage / (g.Wo + 4);
+    if (stride == 1 && (k == 1 || k == 3 || k == 5) && g.Wo % 4 == 0 && Q % 4 == 0 && al16 &&
+        rows_s1 >= k) {
+        const int64_t TH = std::min<int64_t>({static_cast<int64_t>(g.Ho), rows_s1 - k + 1,
+                                              ((int64_t(1) << 22) - 1) / g.Wo});
+        const int64_t bands = (g.Ho + TH - 1) / TH;
+        const size_t smem = static_cast<size_t>((TH + k - 1) * (g.Wo + 4)) * sizeof(float);
+        const int64_t blocks = N * C * bands;
+        TAGI_REQUIRE(blocks <= INT_MAX, TAGI_E_UNSUPPORTED, "%s: too many planes", what);
+        const unsigned nb = static_cast<unsigned>(blocks);
+        const int th = static_cast<int>(TH), nbands = static_cast<int>(bands);
+        if (k == 1)
+            im2col_t_s1_kernel<1><<<nb, 256, smem, as_stream(stream)>>>(x, pt, g, Q, th, nbands);
+        else if (k == 3)
+            im2col_t_s1_kernel<3><<<nb, 256, smem, as_stream(stream)>>>(x, pt, g, Q, th, nbands);
+        else
+            im2col_t_s1_kernel<5><<<nb, 256, smem, as_stream(stream)>>>(x, pt, g, Q, th, nbands);
+        return check_launch(what);
+    }
     const int64_t rows_max = kStage / W;
     if (rows_max >= k) {
         const int64_t TH = std::min<int64_t>({static_cast<int64_t>(g.Ho), (rows_max - k) / stride + 1,
