@@ -444,3 +444,34 @@ def test_param_grad_transposed_patches(C, H, W, k, s, p, pt, Co):
     assert_rel(outs[1][0], d(Sw) * (P.t() @ Dm), MEAN_RTOL, "delta_mw")
     assert_rel(outs[1][1], d(Sw) ** 2 * ((P * P).t() @ DS), VAR_RTOL, "delta_Sw")
     _ok()
+
+
+@pytest.mark.parametrize("C,Co,k,p,N", [(3, 64, 3, 1, 20), (3, 32, 5, 2, 16), (4, 24, 3, 1, 17)])
+def test_stem_weight_sums(C, Co, k, p, N):
+    """Weight deltas of stem convolutions: few weight rows (C*k*k + 1 <= 96)
+    over a reduction of >= 16384 output pixels, which run on the CUDA-core
+    kernel that keeps all outputs of a reduction slice in registers, against
+    the float64 oracle (bias included; a pixel count that is not a multiple of
+    the staged tile)."""
+    import oracle.net as ON
+    from triton_tagi import Conv2D
+
+    g = torch.Generator().manual_seed(C * Co + k)
+    H = W = 32
+    torch.manual_seed(5)
+    ref = ON.Conv2D(C, Co, k, 1, p, 1)
+    dev = Conv2D(C, Co, k, 1, p, 1, device=DEV)
+    for n in ("mw", "Sw", "mb", "Sb"):
+        setattr(dev, n, getattr(ref, n).to(DEV))
+    ma, Sa = _rnd(g, N, C, H, W), _rnd(g, N, C, H, W, u=True, scale=0.1)
+    rm, _ = ref.forward(ma, Sa)
+    dev.forward(ma.to(DEV), Sa.to(DEV))
+    dmz, dSz = _rnd(g, *rm.shape, scale=0.1), -_rnd(g, *rm.shape, u=True, scale=1e-2)
+    ref.backward(dmz, dSz)
+    dev._skip_input_delta = True
+    dev.backward(dmz.to(DEV), dSz.to(DEV))
+    assert_rel(dev.delta_mw, ref.delta_mw, MEAN_RTOL, "delta_mw")
+    assert_rel(dev.delta_Sw, ref.delta_Sw, VAR_RTOL, "delta_Sw")
+    assert_rel(dev.delta_mb, ref.delta_mb, MEAN_RTOL, "delta_mb")
+    assert_rel(dev.delta_Sb, ref.delta_Sb, VAR_RTOL, "delta_Sb")
+    _ok()

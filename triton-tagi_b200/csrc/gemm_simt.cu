@@ -191,6 +191,20 @@ __global__ void __launch_bounds__(NT) moment_gemm_kernel(const GemmArgs g) {
 }
 
 // Sums split-K partials in split order, then stores or applies the parameter epilogue.
+// Output idx (row-major over M x N) of a split reduction whose totals are g0, g1:
+// the parameter epilogue or the scaled, biased store.
+__device__ __forceinline__ void finish_one(const GemmArgs& g, int param, int64_t idx, float g0,
+                                           float g1) {
+    const int r = static_cast<int>(idx / g.N), c = static_cast<int>(idx % g.N);
+    if (param) {
+        param_epilogue(r, c, g0, g1, g.pe);
+    } else {
+        const int64_t o = g.orow.off(r) + static_cast<int64_t>(c) * g.on;
+        if (g.o0) g.o0[o] = g.scale0 * g0 + (g.bias0 ? g.bias0[c] : 0.f);
+        g.o1[o] = g.scale1 * g1 + (g.bias1 ? g.bias1[c] : 0.f);
+    }
+}
+
 __global__ void splitk_finish_kernel(const GemmArgs g, int param) {
     const int64_t mn = static_cast<int64_t>(g.M) * g.N;
     for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < mn;
@@ -200,14 +214,36 @@ __global__ void splitk_finish_kernel(const GemmArgs g, int param) {
             g0 += g.ws[(2 * s) * mn + idx];
             g1 += g.ws[(2 * s + 1) * mn + idx];
         }
-        const int r = static_cast<int>(idx / g.N), c = static_cast<int>(idx % g.N);
-        if (param) {
-            param_epilogue(r, c, g0, g1, g.pe);
-        } else {
-            const int64_t o = g.orow.off(r) + static_cast<int64_t>(c) * g.on;
-            if (g.o0) g.o0[o] = g.scale0 * g0 + (g.bias0 ? g.bias0[c] : 0.f);
-            g.o1[o] = g.scale1 * g1 + (g.bias1 ? g.bias1[c] : 0.f);
+        finish_one(g, param, idx, g0, g1);
+    }
+}
+
+// The same for hundreds of splits over few outputs: 16 outputs per CTA, the
+// splits dealt round-robin to 16 thread groups, then the 16 group totals added
+// in group order (a fixed order: deterministic).
+__global__ void __launch_bounds__(256) splitk_finish_wide_kernel(const GemmArgs g, int param) {
+    __shared__ float red[2][16][17];
+    const int64_t mn = static_cast<int64_t>(g.M) * g.N;
+    const int o = threadIdx.x & 15, grp = threadIdx.x >> 4;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * 16 + o;
+    float g0 = 0.f, g1 = 0.f;
+    if (idx < mn) {
+#pragma unroll 4
+        for (int s = grp; s < g.splits; s += 16) {
+            g0 += g.ws[(2 * static_cast<int64_t>(s)) * mn + idx];
+            g1 += g.ws[(2 * static_cast<int64_t>(s) + 1) * mn + idx];
         }
+    }
+    red[0][grp][o] = g0;
+    red[1][grp][o] = g1;
+    __syncthreads();
+    if (grp == 0 && idx < mn) {
+        float t0 = 0.f, t1 = 0.f;
+        for (int j = 0; j < 16; ++j) {
+            t0 += red[0][j][o];
+            t1 += red[1][j][o];
+        }
+        finish_one(g, param, idx, t0, t1);
     }
 }
 
@@ -288,6 +324,151 @@ size_t wgrad_pack_bytes(int Mo, int N, int Kr, int bn_tc) {
     return tc_pack_bytes(LSQ, N, Kr, bn_tc);
 }
 
+// ---- weight sums of few weight rows over long reductions ---------------------
+// A network's first convolution has few weight rows (C*k*k + 1: 28 for a 3x3
+// RGB stem, 76 for 5x5) against a reduction over every output pixel. A
+// tensor-core pair tile is 256 rows, so such a launch wastes 70-90 % of its
+// MMAs and runs at a fraction of the rate of the other layers. Here one CTA
+// owns a slice of the reduction and ALL Mo x N outputs in registers: thread
+// (rg, cg) accumulates rows 4rg..4rg+3 x columns 4cg..4cg+3 of both sums in
+// fp32 (sum a*u and sum a^2*v). Tiles of kSkTM reduction elements are staged
+// transposed in shared memory ([k][row] and [k][column], padded pitches), so
+// that each thread reads its 4 rows and 4 columns of one element as three
+// 128-bit loads for 36 floating-point operations. Slices write split partials
+// that splitk_finish_wide_kernel adds in a fixed order (deterministic) and
+// passes to the store or parameter epilogue.
+constexpr int kSkTM = 32;           // reduction elements per staged tile
+constexpr int kSkMaxRows = 96;      // weight rows (incl. the bias row)
+constexpr int kSkMaxCols = 64;      // output columns
+constexpr int kSkAP = kSkMaxRows + 4;  // pitches = 4 mod 8 (staging stores)
+constexpr int kSkBP = kSkMaxCols + 4;
+
+bool skinny_ok(int Mo, int N, int Kr) {
+    return Mo >= 1 && N >= 1 && Mo <= kSkMaxRows && N <= kSkMaxCols &&
+           cdiv(Mo, 4) * cdiv(N, 4) <= 256 && Kr >= 16384;
+}
+
+void skinny_plan(int Kr, int* splits, int* chunk) {
+    const int s = std::max(2, std::min(cdiv(Kr, 512), 4 * kNumSMs));
+    *chunk = cdiv(cdiv(Kr, s), kSkTM) * kSkTM;
+    *splits = cdiv(Kr, *chunk);
+}
+
+__global__ void __launch_bounds__(256) wgrad_skinny_kernel(const GemmArgs g) {
+    __shared__ __align__(16) float sa[kSkTM][kSkAP];
+    __shared__ __align__(16) float su[kSkTM][kSkBP];
+    __shared__ __align__(16) float sv[kSkTM][kSkBP];
+    constexpr int kNA = kSkMaxRows * kSkTM / 256;  // staged A elements per thread (max)
+    constexpr int kNB = kSkMaxCols * kSkTM / 256;  // staged elements per delta operand
+    const int Mo = g.M, N = g.N;
+    const int RG = (Mo + 3) >> 2, CG = (N + 3) >> 2;
+    const int nA = 4 * RG * kSkTM, nB = 4 * CG * kSkTM;
+    const int tid = threadIdx.x;
+    const bool active = tid < RG * CG;
+    const int rg = active ? tid / CG : 0, cg = active ? tid - rg * CG : 0;
+    const int kb = blockIdx.x * g.kchunk, ke = min(g.Kr, kb + g.kchunk);
+    float am[4][4] = {}, aS[4][4] = {};
+    // tile k0 .. k0+kSkTM-1 into registers: A rows up to 4*RG (zeros past Mo,
+    // ones on the bias row), delta columns up to 4*CG (zeros past N)
+    float ra[kNA], ru[kNB], rv[kNB];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int q = 0; q < kNA; ++q) {
+            const int i = tid + q * 256, r = i / kSkTM, k = k0 + (i - r * kSkTM);
+            float x = 0.f;
+            if (i < nA && k < ke && r < Mo)
+                x = r == g.ones_row ? 1.f
+                                    : __ldg(g.x + g.arow.off(r) + static_cast<int64_t>(k) * g.ak);
+            ra[q] = x;
+        }
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) {
+            const int i = tid + q * 256, c = i / kSkTM, k = k0 + (i - c * kSkTM);
+            float u = 0.f, v = 0.f;
+            if (i < nB && k < ke && c < N) {
+                const int64_t o = static_cast<int64_t>(c) * g.bn + g.brow.off(k);
+                u = __ldg(g.u + o);
+                v = __ldg(g.v + o);
+            }
+            ru[q] = u;
+            rv[q] = v;
+        }
+    };
+    auto put = [&]() {
+#pragma unroll
+        for (int q = 0; q < kNA; ++q) {
+            const int i = tid + q * 256, r = i / kSkTM;
+            if (i < nA) sa[i - r * kSkTM][r] = ra[q];
+        }
+#pragma unroll
+        for (int q = 0; q < kNB; ++q) {
+            const int i = tid + q * 256, c = i / kSkTM;
+            if (i < nB) {
+                su[i - c * kSkTM][c] = ru[q];
+                sv[i - c * kSkTM][c] = rv[q];
+            }
+        }
+    };
+    // double buffering through registers: the next tile's loads are in flight
+    // while this tile is summed
+    if (kb < ke) fetch(kb);
+    for (int k0 = kb; k0 < ke; k0 += kSkTM) {
+        __syncthreads();  // the previous tile has been read
+        put();
+        __syncthreads();
+        if (k0 + kSkTM < ke) fetch(k0 + kSkTM);
+        if (active) {
+            // elements past the slice end are staged as zeros and add nothing
+#pragma unroll 8
+            for (int ki = 0; ki < kSkTM; ++ki) {
+                const float4 a = *reinterpret_cast<const float4*>(&sa[ki][4 * rg]);
+                const float4 u = *reinterpret_cast<const float4*>(&su[ki][4 * cg]);
+                const float4 v = *reinterpret_cast<const float4*>(&sv[ki][4 * cg]);
+                const float ar[4] = {a.x, a.y, a.z, a.w}, ur[4] = {u.x, u.y, u.z, u.w};
+                const float vr[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float a2 = ar[i] * ar[i];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        am[i][j] = fmaf(ar[i], ur[j], am[i][j]);
+                        aS[i][j] = fmaf(a2, vr[j], aS[i][j]);
+                    }
+                }
+            }
+        }
+    }
+    if (!active) return;
+    const int64_t mn = static_cast<int64_t>(Mo) * N;
+    float* pm = g.ws + (2 * static_cast<int64_t>(blockIdx.x)) * mn;
+    float* pS = pm + mn;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 4 * rg + i;
+        if (r >= Mo) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = 4 * cg + j;
+            if (c < N) {
+                pm[static_cast<int64_t>(r) * N + c] = am[i][j];
+                pS[static_cast<int64_t>(r) * N + c] = aS[i][j];
+            }
+        }
+    }
+}
+
+// Split plan of the weight sums: the skinny kernel above, or tensor-core / CUDA-
+// core tiles (choose_splits). bn_tc = 0 for the skinny kernel.
+void plan_wgrad(int Mo, int N, int Kr, int* splits, int* chunk, int* bn_tc, bool* skinny) {
+    *skinny = skinny_ok(Mo, N, Kr);
+    if (*skinny) {
+        skinny_plan(Kr, splits, chunk);
+        *bn_tc = 0;
+        return;
+    }
+    choose_splits(Mo, N, Kr, 1, splits, chunk, bn_tc);
+}
+
 // Shared driver for the weight-gradient family (stores or parameter epilogue).
 // The workspace must hold the split-reduction partials when a split is planned;
 // room past them (256-byte aligned) takes the prepared B tiles (the deltas) of
@@ -295,8 +476,24 @@ size_t wgrad_pack_bytes(int Mo, int N, int Kr, int bn_tc) {
 int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
               const char* what) {
     int splits, chunk, bn_tc;
-    choose_splits(Mo, g.N, g.Kr, 1, &splits, &chunk, &bn_tc);
+    bool skinny;
+    plan_wgrad(Mo, g.N, g.Kr, &splits, &chunk, &bn_tc, &skinny);
     g.M = Mo;
+    if (skinny) {
+        const size_t part = sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N;
+        TAGI_REQUIRE(ws != nullptr && ws_bytes >= part, TAGI_E_WORKSPACE,
+                     "%s: workspace of %zu bytes required, %zu given", what, part, ws_bytes);
+        g.splits = splits;
+        g.kchunk = chunk;
+        g.ws = static_cast<float*>(ws);
+        wgrad_skinny_kernel<<<splits, 256, 0, st>>>(g);
+        int rc = check_launch(what);
+        if (rc) return rc;
+        const int64_t mn = static_cast<int64_t>(Mo) * g.N;  // <= 96 x 64
+        splitk_finish_wide_kernel<<<static_cast<unsigned>((mn + 15) / 16), 256, 0, st>>>(
+            g, param ? 1 : 0);
+        return check_launch(what);
+    }
     const size_t need = splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N : 0;
     const size_t pack_off = (need + 255) / 256 * 256;
     const size_t pack = wgrad_pack_bytes(Mo, g.N, g.Kr, bn_tc);
@@ -383,14 +580,16 @@ int run_store(GemmArgs& g, void* ws, size_t ws_bytes, cudaStream_t st, const cha
 // Split-reduction partials a weight-gradient call requires.
 size_t wgrad_ws_bytes(int Mo, int N, int Kr) {
     int splits, chunk, bn_tc;
-    choose_splits(Mo, N, Kr, 1, &splits, &chunk, &bn_tc);
-    return splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * N : 0;
+    bool skinny;
+    plan_wgrad(Mo, N, Kr, &splits, &chunk, &bn_tc, &skinny);
+    return (splits > 1 || skinny) ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * N : 0;
 }
 
 // The partials plus the optional prepared B tiles (what the size queries report).
 size_t wgrad_ws_total(int Mo, int N, int Kr) {
     int splits, chunk, bn_tc;
-    choose_splits(Mo, N, Kr, 1, &splits, &chunk, &bn_tc);
+    bool skinny;
+    plan_wgrad(Mo, N, Kr, &splits, &chunk, &bn_tc, &skinny);
     const size_t need = wgrad_ws_bytes(Mo, N, Kr);
     const size_t pack = wgrad_pack_bytes(Mo, N, Kr, bn_tc);
     return pack > 0 ? (need + 255) / 256 * 256 + pack : need;
