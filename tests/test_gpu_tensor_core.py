@@ -4,8 +4,11 @@ Shapes are chosen so that the library routes them to the tensor-core kernel
 (M ≥ 16, N ≥ 16, reduction ≥ 8 and M·N·K ≥ 4e6) and cover ragged tails in
 every dimension, operands narrower than one K-block or a quarter tile, the variance-only forward, row-split (NCHW) operand views,
 the split reduction of the weight sums, the fused capped update and batched
-attention products. Each test also checks that no bounded wait inside the
-kernel ran out (tagi_device_status).
+attention products. Weight sums of at most 96 rows and 64 columns over a
+reduction of 16384 or more (the narrow shapes of TC_SHAPES, stem convolutions)
+run on the CUDA-core slice kernel instead and are checked the same way. Each
+test also checks that no bounded wait inside the kernel ran out
+(tagi_device_status).
 """
 
 from __future__ import annotations
