@@ -362,7 +362,6 @@ __global__ void __launch_bounds__(256) wgrad_skinny_kernel(const GemmArgs g) {
     constexpr int kNB = kSkMaxCols * kSkTM / 256;  // staged elements per delta operand
     const int Mo = g.M, N = g.N;
     const int RG = (Mo + 3) >> 2, CG = (N + 3) >> 2;
-    const int nA = 4 * RG * kSkTM, nB = 4 * CG * kSkTM;
     const int tid = threadIdx.x;
     const bool active = tid < RG * CG;
     const int rg = active ? tid / CG : 0, cg = active ? tid - rg * CG : 0;
@@ -371,22 +370,30 @@ __global__ void __launch_bounds__(256) wgrad_skinny_kernel(const GemmArgs g) {
     // tile k0 .. k0+kSkTM-1 into registers: A rows up to 4*RG (zeros past Mo,
     // ones on the bias row), delta columns up to 4*CG (zeros past N)
     float ra[kNA], ru[kNB], rv[kNB];
+    // staged element i = tid + 256 q is (row or column i / 32, element i % 32):
+    // every element a thread stages lies at reduction index k0 + (tid % 32), rows
+    // (columns) tid / 32 + 8 q
+    const int ki_t = tid & (kSkTM - 1), rc0 = tid / kSkTM;
+    static_assert(256 % kSkTM == 0, "staging layout");
     auto fetch = [&](int k0) {
+        const int k = k0 + ki_t;
+        const bool kin = k < ke;
+        const int64_t ak = static_cast<int64_t>(k) * g.ak;
 #pragma unroll
         for (int q = 0; q < kNA; ++q) {
-            const int i = tid + q * 256, r = i / kSkTM, k = k0 + (i - r * kSkTM);
+            const int r = rc0 + q * (256 / kSkTM);
             float x = 0.f;
-            if (i < nA && k < ke && r < Mo)
-                x = r == g.ones_row ? 1.f
-                                    : __ldg(g.x + g.arow.off(r) + static_cast<int64_t>(k) * g.ak);
+            if (kin && r < Mo)
+                x = r == g.ones_row ? 1.f : __ldg(g.x + g.arow.off(r) + ak);
             ra[q] = x;
         }
+        const int64_t bo = kin ? g.brow.off(k) : 0;
 #pragma unroll
         for (int q = 0; q < kNB; ++q) {
-            const int i = tid + q * 256, c = i / kSkTM, k = k0 + (i - c * kSkTM);
+            const int c = rc0 + q * (256 / kSkTM);
             float u = 0.f, v = 0.f;
-            if (i < nB && k < ke && c < N) {
-                const int64_t o = static_cast<int64_t>(c) * g.bn + g.brow.off(k);
+            if (kin && c < N) {
+                const int64_t o = static_cast<int64_t>(c) * g.bn + bo;
                 u = __ldg(g.u + o);
                 v = __ldg(g.v + o);
             }
@@ -397,15 +404,15 @@ __global__ void __launch_bounds__(256) wgrad_skinny_kernel(const GemmArgs g) {
     auto put = [&]() {
 #pragma unroll
         for (int q = 0; q < kNA; ++q) {
-            const int i = tid + q * 256, r = i / kSkTM;
-            if (i < nA) sa[i - r * kSkTM][r] = ra[q];
+            const int r = rc0 + q * (256 / kSkTM);
+            if (r < 4 * RG) sa[ki_t][r] = ra[q];
         }
 #pragma unroll
         for (int q = 0; q < kNB; ++q) {
-            const int i = tid + q * 256, c = i / kSkTM;
-            if (i < nB) {
-                su[i - c * kSkTM][c] = ru[q];
-                sv[i - c * kSkTM][c] = rv[q];
+            const int c = rc0 + q * (256 / kSkTM);
+            if (c < 4 * CG) {
+                su[ki_t][c] = ru[q];
+                sv[ki_t][c] = rv[q];
             }
         }
     };
