@@ -200,14 +200,15 @@ ENTRY_BYTES = {
 
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# contraction families, from one ncu capture of this build: 114 consecutive
-# contraction launches of two ResNet-18 steps (after 3 warm-up steps), and one
+# contraction families, from one ncu capture of this build: 112 consecutive
+# tensor-core contraction launches of two ResNet-18 steps (after 3 warm-up
+# steps; the stem's weight sums run on CUDA cores and are not among them), and one
 # 4096 x 4096 x 4096 Linear forward scaled by M to the sweep's 8192-row headline
 # (A and the number of B re-reads both grow with M).
 MEASURED_TRAFFIC = {
     ("r18", "moment_forward"): 53.2e6,
-    ("r18", "backward_delta"): 43.6e6,
-    ("r18", "param_grad"): 150.8e6,
+    ("r18", "backward_delta"): 44.6e6,
+    ("r18", "param_grad"): 154.6e6,
     ("swp", "moment_forward"): 2 * 1.833e9,
 }
 
