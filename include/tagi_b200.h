@@ -280,6 +280,31 @@ int tagi_avgpool_backward(const float* dm, const float* dS, float* dm_out, float
                           int64_t N, int64_t C, int64_t H, int64_t W, int64_t k, float var_scale,
                           void* stream);
 
+/* Gaussian embedding lookup: token t (ids as floats, truncated toward zero as
+ * the reference's ma.long()) gets rows (mw[id], Sw[id]) of the (V x D)
+ * tables; ids outside [0, V) and padding_idx (-1: none) give zero rows.
+ * Replaces Embedding.forward, triton_tagi/layers/embedding.py:88-110. */
+int tagi_embedding_forward(const float* idx, const float* mw, const float* Sw, float* mz,
+                           float* Sz, int64_t n_tokens, int64_t V, int64_t D,
+                           int64_t padding_idx, void* stream);
+
+/* Per-row parameter sums of the embedding over its tokens, in token order
+ * (deterministic): mode TAGI_WGRAD_SUMS writes sum dmz, sum dSz (V x D, for an
+ * all-reduce); TAGI_WGRAD_DELTAS writes sum dmz*Sw[id] and sum dSz*Sw[id]^2
+ * (delta_mw, delta_Sw). Every row is written (zeros where no token maps to it);
+ * padding and out-of-range ids contribute nothing.
+ * Replaces Embedding.backward, triton_tagi/layers/embedding.py:112-151. */
+int tagi_embedding_backward(const float* idx, const float* dmz, const float* dSz,
+                            const float* Sw, int64_t n_tokens, int64_t V, int64_t D,
+                            int64_t padding_idx, int mode, float* out_m, float* out_S,
+                            void* stream);
+
+/* out[r][d] = ma[r][d] + pe[r % S][d] for the rows of a (B*S, D) tensor (the
+ * variances pass through unchanged). Replaces PositionalEncoding.forward,
+ * triton_tagi/layers/positional_encoding.py:113-118. */
+int tagi_positional_add(const float* ma, const float* pe, float* out, int64_t rows, int64_t S,
+                        int64_t D, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Convolution helpers (NCHW; padding_type 2 = right/bottom only)
  * ------------------------------------------------------------------------- */

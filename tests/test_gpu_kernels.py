@@ -469,3 +469,73 @@ def test_relu_jacobian_folded_into_batchnorm_backward(N, C, H, W):
              "delta_Sw", "delta_mb", "delta_Sb")
     for name, a, b in zip(names, *outs):
         torch.testing.assert_close(b, a, rtol=1e-6, atol=1e-9, msg=name)
+
+
+@pytest.mark.parametrize("V,D", [(64, 512), (37, 40), (5, 3)])
+def test_embedding_against_oracle(V, D):
+    """tagi_embedding_forward gathers the rows of every token id; the weight
+    deltas of tagi_embedding_backward add the tokens' products in token order,
+    the same float32 operations as the oracle's index_add."""
+    import oracle.net as ON
+    from triton_tagi.layers.embedding import Embedding
+
+    gen = torch.Generator().manual_seed(V * D)
+    torch.manual_seed(V)
+    ref = ON.Embedding(V, D, scale=0.5)
+    dev = Embedding(V, D, scale=0.5, device=DEV)
+    dev.mw, dev.Sw = g(ref.mw), g(ref.Sw)
+    ids = torch.randint(0, V, (3, 37), generator=gen).float()
+    rm, rS = ref.forward(ids, torch.zeros_like(ids))
+    mz, Sz = dev.forward(g(ids), g(torch.zeros_like(ids)))
+    assert torch.equal(mz.cpu(), rm) and torch.equal(Sz.cpu(), rS)
+    dm, dS = rnd(gen, 3, 37, D), -rnd(gen, 3, 37, D, kind="u")
+    ref.backward(dm, dS)
+    dev.backward(g(dm), g(dS))
+    torch.testing.assert_close(dev.delta_mw.cpu(), ref.delta_mw, rtol=1e-6, atol=1e-12)
+    torch.testing.assert_close(dev.delta_Sw.cpu(), ref.delta_Sw, rtol=1e-6, atol=1e-12)
+
+
+def test_embedding_padding_out_of_range_and_sums():
+    """Padding and out-of-range ids give zero rows and add nothing; the sums
+    mode returns the raw per-row sums (what data parallelism all-reduces)."""
+    from triton_tagi._lib import WGRAD_SUMS, lib, stream
+
+    gen = torch.Generator().manual_seed(11)
+    V, D, n = 16, 24, 300
+    mw, Sw = rnd(gen, V, D), rnd(gen, V, D, kind="u")
+    ids = torch.randint(-2, V + 2, (n,), generator=gen).float()
+    ids[::7] = 3.0  # padding id
+    ids[5] = 2.7    # truncates to 2, as .long()
+    dm, dS = rnd(gen, n, D), rnd(gen, n, D)
+    d_ids, d_mw, d_Sw, d_dm, d_dS = g(ids), g(mw), g(Sw), g(dm), g(dS)
+    mz, Sz = torch.full((n, D), 7.0, device=DEV), torch.full((n, D), 7.0, device=DEV)
+    lib()("tagi_embedding_forward", d_ids.data_ptr(), d_mw.data_ptr(), d_Sw.data_ptr(),
+          mz.data_ptr(), Sz.data_ptr(), n, V, D, 3, stream(mz))
+    cat = ids.long()
+    keep = (cat >= 0) & (cat < V) & (cat != 3)
+    safe = cat.clamp(0, V - 1)
+    ex_m = torch.where(keep[:, None], mw[safe], torch.zeros(()))
+    ex_S = torch.where(keep[:, None], Sw[safe], torch.zeros(()))
+    assert torch.equal(mz.cpu(), ex_m) and torch.equal(Sz.cpu(), ex_S)
+    gm, gS = torch.full((V, D), 7.0, device=DEV), torch.full((V, D), 7.0, device=DEV)
+    lib()("tagi_embedding_backward", d_ids.data_ptr(), d_dm.data_ptr(), d_dS.data_ptr(), None,
+          n, V, D, 3, WGRAD_SUMS, gm.data_ptr(), gS.data_ptr(), stream(gm))
+    w = keep[:, None].float()
+    ref_m = torch.zeros(V, D).index_add_(0, safe, dm * w)
+    ref_S = torch.zeros(V, D).index_add_(0, safe, dS * w)
+    torch.testing.assert_close(gm.cpu(), ref_m, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(gS.cpu(), ref_S, rtol=1e-6, atol=1e-6)
+
+
+def test_positional_encoding_add():
+    """tagi_positional_add adds the table row of each position to the means;
+    the variances pass through."""
+    from triton_tagi.layers.positional_encoding import PositionalEncoding
+
+    gen = torch.Generator().manual_seed(5)
+    pe = PositionalEncoding(48, max_seq_len=64, device=DEV)
+    ma, Sa = g(rnd(gen, 3, 20, 48)), g(rnd(gen, 3, 20, 48, kind="u"))
+    om, oS = pe.forward(ma, Sa)
+    assert torch.equal(om, ma + pe.pe_cache[:20]) and oS is Sa
+    with pytest.raises(ValueError):
+        pe.forward(g(rnd(gen, 2, 65, 48)), None)

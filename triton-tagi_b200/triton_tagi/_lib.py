@@ -47,6 +47,9 @@ _SIGS = {
     "tagi_jacobian_backward": "ppppp" + "i" + "p",
     "tagi_remax_forward": "ppppp" + "iii" + "p",
     "tagi_add_inplace": "pppp" + "i" + "p",
+    "tagi_embedding_forward": "ppppp" + "iiii" + "p",
+    "tagi_embedding_backward": "pppp" + "iiii" + "n" + "pp" + "p",
+    "tagi_positional_add": "ppp" + "iii" + "p",
     "tagi_avgpool_forward": "pppp" + "iiiii" + "f" + "p",
     "tagi_avgpool_backward": "pppp" + "iiiii" + "f" + "p",
     "tagi_im2col": "pppp" + "iiiiiiii" + "p",

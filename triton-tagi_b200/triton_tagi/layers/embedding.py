@@ -1,9 +1,11 @@
 """Gaussian embedding lookup (drop-in for triton_tagi/layers/embedding.py).
 
-Forward gathers rows (μ_w[cat], S_w[cat]); backward accumulates
-δμ·S_w[cat] and δS·S_w[cat]² into the rows with index_add (embedding.py:112-151).
-This layer is outside the fused moment path and runs as torch device ops;
-``padding_idx`` rows emit zeros and receive no update, as in the reference.
+Forward gathers rows (μ_w[cat], S_w[cat]) (tagi_embedding_forward); backward
+accumulates δμ·S_w[cat] and δS·S_w[cat]² per row in token order
+(tagi_embedding_backward: deterministic, the same additions as the reference's
+index_add on the CPU; embedding.py:112-151). ``padding_idx`` rows emit zeros and
+receive no update, as in the reference; ids outside the table do the same
+instead of aborting the device context.
 """
 
 from __future__ import annotations
@@ -11,6 +13,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
+from .._lib import WGRAD_DELTAS, WGRAD_SUMS, check_cuda_f32, lib, stream
 from ..base import LearnableLayer
 from ..param_init import gaussian_param_init
 from ..update.parameters import update_parameters
@@ -32,36 +35,39 @@ class Embedding(LearnableLayer):
     def forward(self, ma: Tensor, Sa: Tensor) -> tuple[Tensor, Tensor]:
         if ma.dim() == 3 and ma.shape[-1] == 1:
             ma = ma.squeeze(-1)
-        cat = ma.long()
-        self.cat_idx = cat
-        mz, Sz = self.mw[cat], self.Sw[cat]
-        if self.padding_idx >= 0:
-            mask = (cat == self.padding_idx).unsqueeze(-1)
-            mz, Sz = mz.masked_fill(mask, 0.0), Sz.masked_fill(mask, 0.0)
+        ids = ma.float().contiguous()
+        check_cuda_f32(ids)
+        self.mw, self.Sw = self.mw.contiguous(), self.Sw.contiguous()
+        self._ids = ids
+        self.cat_idx = ids.long()
+        D = self.embedding_dim
+        mz = torch.empty(*ids.shape, D, device=ids.device)
+        Sz = torch.empty_like(mz)
+        lib()("tagi_embedding_forward", ids.data_ptr(), self.mw.data_ptr(), self.Sw.data_ptr(),
+              mz.data_ptr(), Sz.data_ptr(), ids.numel(), self.num_embeddings, D,
+              self.padding_idx, stream(ids))
         return mz, Sz
 
-    def _sums(self, delta_mz: Tensor, delta_Sz: Tensor):
-        D = self.embedding_dim
-        idx = self.cat_idx.reshape(-1)
-        rows = self.Sw[idx]
-        dm = delta_mz.reshape(-1, D)
-        dS = delta_Sz.reshape(-1, D)
-        if self.padding_idx >= 0:
-            keep = (idx != self.padding_idx).unsqueeze(-1).to(dm.dtype)
-            dm, dS = dm * keep, dS * keep
-        return idx, dm, dS, rows
-
     def backward(self, delta_mz: Tensor, delta_Sz: Tensor) -> tuple[Tensor, Tensor]:
-        idx, dm, dS, rows = self._sums(delta_mz, delta_Sz)
+        check_cuda_f32(delta_mz, delta_Sz)
+        ids = self._ids
+        dm, dS = delta_mz.contiguous(), delta_Sz.contiguous()
+        if dm.numel() != ids.numel() * self.embedding_dim:
+            raise ValueError("Embedding.backward: deltas do not match the last forward")
+        V, D = self.num_embeddings, self.embedding_dim
+        args = (ids.data_ptr(), dm.data_ptr(), dS.data_ptr(), self.Sw.data_ptr(), ids.numel(),
+                V, D, self.padding_idx)
         if self._param_mode == "sums":
             buf = self._reducer.buffer(self, 2 * self.mw.numel(), torch.float32)
             g_m, g_S = buf.view(2, *self.mw.shape)
-            g_m.zero_().index_add_(0, idx, dm)
-            g_S.zero_().index_add_(0, idx, dS)
+            lib()("tagi_embedding_backward", *args, WGRAD_SUMS, g_m.data_ptr(), g_S.data_ptr(),
+                  stream(dm))
             self._reducer.ready(self)
         else:
-            self.delta_mw = torch.zeros_like(self.mw).index_add_(0, idx, dm * rows)
-            self.delta_Sw = torch.zeros_like(self.Sw).index_add_(0, idx, dS * rows * rows)
+            self.delta_mw = torch.empty_like(self.mw)
+            self.delta_Sw = torch.empty_like(self.Sw)
+            lib()("tagi_embedding_backward", *args, WGRAD_DELTAS, self.delta_mw.data_ptr(),
+                  self.delta_Sw.data_ptr(), stream(dm))
         z = torch.zeros(self.cat_idx.shape, dtype=delta_mz.dtype, device=delta_mz.device)
         return z, z.clone()
 

@@ -1,13 +1,15 @@
 """Fixed sinusoidal positional encoding (drop-in for
 triton_tagi/layers/positional_encoding.py): pe[t, d] = sin(t·f_d) for even d,
-cos(t·f_d) for odd d, f_d = 10000^(−d/E); added to the means only, identity
-backward. Runs as torch device ops (outside the fused moment path)."""
+cos(t·f_d) for odd d, f_d = 10000^(−d/E); added to the means only
+(tagi_positional_add), identity backward. The table is built once with torch
+device ops at construction."""
 
 from __future__ import annotations
 
 import torch
 from torch import Tensor
 
+from .._lib import check_cuda_f32, lib, stream
 from ..base import Layer
 
 
@@ -22,7 +24,16 @@ class PositionalEncoding(Layer):
         self.pe_cache = torch.where(even, torch.sin(angle), torch.cos(angle))
 
     def forward(self, ma: Tensor, Sa: Tensor) -> tuple[Tensor, Tensor]:
-        return ma + self.pe_cache[: ma.shape[-2]], Sa
+        check_cuda_f32(ma)
+        if ma.dim() < 2 or ma.shape[-1] != self.embed_dim or ma.shape[-2] > self.max_seq_len:
+            raise ValueError(f"PositionalEncoding: input {tuple(ma.shape)} does not fit "
+                             f"(S <= {self.max_seq_len}, E = {self.embed_dim})")
+        ma = ma.contiguous()
+        out = torch.empty_like(ma)
+        S, E = ma.shape[-2], self.embed_dim
+        lib()("tagi_positional_add", ma.data_ptr(), self.pe_cache.data_ptr(), out.data_ptr(),
+              ma.numel() // E, S, E, stream(ma))
+        return out, Sa
 
     def backward(self, delta_ma: Tensor, delta_Sa: Tensor) -> tuple[Tensor, Tensor]:
         return delta_ma, delta_Sa
