@@ -181,6 +181,9 @@ ENTRY_BYTES = {
     "tagi_add_inplace": lambda a: 24 * a[4],
     "tagi_capped_update": lambda a: 24 * a[4],
     "tagi_remax_forward": lambda a: 20 * a[5] * a[6],
+    # ids read, rows written (mean and variance)
+    "tagi_embedding_forward": lambda a: (4 + 8 * a[7]) * a[5],
+    "tagi_positional_add": lambda a: 8 * a[3] * a[5],
     "tagi_bn_channel_sums": lambda a: 8 * a[3] * a[4] * a[5],
     # reads mz, Sz; writes ma, Sa, m_hat
     "tagi_bn_train_forward": lambda a: (20 + 8 * _planes(a[13])) * a[15] * a[16] * a[17],
