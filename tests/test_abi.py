@@ -84,3 +84,8 @@ def test_workspace_queries_are_host_only():
     assert L.size("tagi_param_grad_workspace_size", 16, 30, 20, 1) == 0  # CUDA-core path
     big = L.size("tagi_param_grad_workspace_size", 128 * 1024, 576, 64, 1)
     assert big > 0 and big % 4 == 0
+    # few weight rows over a long reduction (a 3x3 RGB stem): the CUDA-core slice
+    # kernel, 256 slices of 512 pixels, partial sums for all 28 x 64 outputs
+    assert L.size("tagi_param_grad_workspace_size", 131072, 27, 64, 1) == 2 * 256 * 28 * 64 * 4
+    # 592 slices at most (4 per SM)
+    assert L.size("tagi_param_grad_workspace_size", 524288, 75, 32, 1) == 2 * 586 * 76 * 32 * 4
