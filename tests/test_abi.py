@@ -79,8 +79,12 @@ def test_workspace_queries_are_host_only():
     # A short reduction is never split; with 8 or more tiles of 256 weight rows
     # the workspace holds the optional prepared tiles of the deltas (8 K-blocks x
     # 4 tiles x 256 columns x 32 bytes); a long one over a small output is split.
+    # With K a multiple of 256 the bias sums are formed apart (their one slice of
+    # 2 x 256 column sums follows the weight rows' workspace).
     assert L.size("tagi_param_grad_workspace_size", 64, 784, 256, 1) == 0
-    assert L.size("tagi_param_grad_workspace_size", 64, 2048, 256, 1) == 8 * 4 * 256 * 32
+    assert L.size("tagi_param_grad_workspace_size", 64, 2048, 256, 0) == 8 * 4 * 256 * 32
+    assert (L.size("tagi_param_grad_workspace_size", 64, 2048, 256, 1)
+            == 8 * 4 * 256 * 32 + 2 * 256 * 4)
     assert L.size("tagi_param_grad_workspace_size", 16, 30, 20, 1) == 0  # CUDA-core path
     big = L.size("tagi_param_grad_workspace_size", 128 * 1024, 576, 64, 1)
     assert big > 0 and big % 4 == 0

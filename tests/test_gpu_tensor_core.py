@@ -478,3 +478,58 @@ def test_stem_weight_sums(C, Co, k, p, N):
     assert_rel(dev.delta_mb, ref.delta_mb, MEAN_RTOL, "delta_mb")
     assert_rel(dev.delta_Sb, ref.delta_Sb, VAR_RTOL, "delta_Sb")
     _ok()
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("M,K,N", [(3000, 512, 200), (20000, 256, 96), (4096, 512, 512)])
+def test_bias_sums_apart_equal_ones_row(M, K, N, mode):
+    """With K a multiple of 256 and a workspace of the size the query reports,
+    the bias sums are formed by a column-sum pass next to the K-row contraction;
+    with a smaller workspace that still holds the plan of K + 1 rows (sized by
+    the no-bias query for K + 1) the bias stays a row of ones in the contraction.
+    The two agree (sums, deltas and the capped update) and match float64."""
+    from triton_tagi._lib import lib, stream
+
+    L = lib()
+    g = torch.Generator().manual_seed(M + K + N + mode)
+    a = _rnd(g, M, K).to(DEV)
+    dmz = _rnd(g, M, N, scale=0.1).to(DEV)
+    dSz = -_rnd(g, M, N, u=True, scale=1e-2).to(DEV)
+    mw, Sw = _rnd(g, K, N, scale=0.1), _rnd(g, K, N, u=True, scale=1e-2, lo=1e-3)
+    mb, Sb = _rnd(g, 1, N, scale=0.1), _rnd(g, 1, N, u=True, scale=1e-2, lo=1e-3)
+    need = L.size("tagi_param_grad_workspace_size", M, K, N, 1)
+    ones = L.size("tagi_fused_weight_grad_workspace_size", M, K + 1, N)
+    assert 0 < ones < need
+    outs = []
+    for ws_bytes in (need, ones):
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+        p = [t.to(DEV).clone() for t in (mw, Sw, mb, Sb)]
+        o = [torch.zeros(K + 1, N, device=DEV), torch.zeros(K + 1, N, device=DEV),
+             torch.zeros(1, N, device=DEV), torch.zeros(1, N, device=DEV)]
+        if mode == 0:
+            args = (None, None, None, None, o[0].data_ptr(), o[1].data_ptr(), None, None)
+        elif mode == 1:
+            args = (None, p[1].data_ptr(), None, p[3].data_ptr(), o[0].data_ptr(),
+                    o[1].data_ptr(), o[2].data_ptr(), o[3].data_ptr())
+        else:
+            args = tuple(t.data_ptr() for t in p) + (None, None, None, None)
+        L("tagi_param_grad", a.data_ptr(), K, dmz.data_ptr(), dSz.data_ptr(), 0, 0, N, 1, M, K,
+          N, 1, mode, *args, 2.0, ws.data_ptr(), ws_bytes, stream(a))
+        outs.append((o, p))
+    (o1, p1), (o2, p2) = outs
+    if mode == 0:
+        gm = (a.double().t() @ dmz.double())
+        gS = ((a.double() ** 2).t() @ dSz.double())
+        for o in (o1, o2):
+            assert_rel(o[0][:K], gm, MEAN_RTOL, "weight sums")
+            assert_rel(o[1][:K], gS, VAR_RTOL, "weight var sums")
+            assert_rel(o[0][K], dmz.double().sum(0), MEAN_RTOL, "bias sums")
+            assert_rel(o[1][K], dSz.double().sum(0), VAR_RTOL, "bias var sums")
+    elif mode == 1:
+        for x, y in zip(o1, o2):
+            assert_rel(x, y.double(), MEAN_RTOL, "deltas")
+        assert_rel(o1[2], Sb.double().to(DEV) * dmz.double().sum(0), MEAN_RTOL, "bias delta")
+    else:
+        for x, y in zip(p1, p2):
+            assert_rel(x, y.double(), VAR_RTOL, "updated parameters")
+    _ok()

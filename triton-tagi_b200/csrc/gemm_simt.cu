@@ -476,12 +476,110 @@ void plan_wgrad(int Mo, int N, int Kr, int* splits, int* chunk, int* bn_tc, bool
     choose_splits(Mo, N, Kr, 1, splits, chunk, bn_tc);
 }
 
+// ---- bias sums apart from the weight rows -----------------------------------
+// The weight sums carry a bias as a row of ones after the K weight rows. When K
+// is a multiple of 256 that row alone would open another 256-row tensor-core
+// pair tile (513 rows: three tiles for the work of two), so the bias sums are
+// then formed by a column-sum pass and the contraction runs on the K weight rows.
+size_t wgrad_ws_total(int Mo, int N, int Kr);
+
+bool bias_apart(int Mo, int N, int Kr, bool bias_row) {
+    if (!bias_row || Mo < 2 || Kr < 1 || (Mo - 1) % 256 != 0) return false;
+    int splits, chunk, bn_tc;
+    bool skinny;
+    plan_wgrad(Mo - 1, N, Kr, &splits, &chunk, &bn_tc, &skinny);
+    return bn_tc > 0 && !skinny;
+}
+
+// Reduction slices of the column sums: enough CTAs of 32 columns to fill the
+// machine twice, slices of at least 256 rows.
+void bias_plan(int N, int Kr, int* slices, int* chunk) {
+    int s = std::max(1, std::min(64, cdiv(2 * kNumSMs, cdiv(N, 32))));
+    s = std::min(s, std::max(1, cdiv(Kr, 256)));
+    *chunk = cdiv(Kr, s);
+    *slices = cdiv(Kr, *chunk);
+}
+
+// Workspace of a weight-sum call with the bias apart: the weight rows' own
+// workspace, then (256-byte aligned) the column-sum slices.
+size_t bias_apart_bytes(int Mo, int N, int Kr, size_t* off) {
+    int slices, chunk;
+    bias_plan(N, Kr, &slices, &chunk);
+    *off = (wgrad_ws_total(Mo - 1, N, Kr) + 255) / 256 * 256;
+    return *off + sizeof(float) * 2ull * slices * static_cast<size_t>(N);
+}
+
+// CTA (32 columns, one reduction slice): thread (column c, row group r) adds
+// rows r, r+8, ... of the slice; the 8 group totals are added in group order.
+__global__ void __launch_bounds__(256) bias_sums_kernel(const GemmArgs g, int chunk, float* part) {
+    __shared__ float red[2][8][33];
+    const int c = threadIdx.x & 31, r = threadIdx.x >> 5;
+    const int n = blockIdx.x * 32 + c;
+    const int m0 = blockIdx.y * chunk, m1 = min(g.Kr, m0 + chunk);
+    float a = 0.f, b = 0.f;
+    if (n < g.N) {
+        for (int m = m0 + r; m < m1; m += 8) {
+            const int64_t o = static_cast<int64_t>(n) * g.bn + g.brow.off(m);
+            a += __ldg(g.u + o);
+            b += __ldg(g.v + o);
+        }
+    }
+    red[0][r][c] = a;
+    red[1][r][c] = b;
+    __syncthreads();
+    if (r == 0 && n < g.N) {
+        float ta = 0.f, tb = 0.f;
+        for (int j = 0; j < 8; ++j) {
+            ta += red[0][j][c];
+            tb += red[1][j][c];
+        }
+        part[(2 * static_cast<int64_t>(blockIdx.y)) * g.N + n] = ta;
+        part[(2 * static_cast<int64_t>(blockIdx.y) + 1) * g.N + n] = tb;
+    }
+}
+
+// Adds the slices in order and applies the epilogue to output row `row`.
+__global__ void bias_finish_kernel(const GemmArgs g, int slices, const float* part, int param,
+                                   int row) {
+    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < g.N; n += gridDim.x * blockDim.x) {
+        float ta = 0.f, tb = 0.f;
+        for (int s = 0; s < slices; ++s) {
+            ta += part[(2 * static_cast<int64_t>(s)) * g.N + n];
+            tb += part[(2 * static_cast<int64_t>(s) + 1) * g.N + n];
+        }
+        finish_one(g, param, static_cast<int64_t>(row) * g.N + n, ta, tb);
+    }
+}
+
 // Shared driver for the weight-gradient family (stores or parameter epilogue).
 // The workspace must hold the split-reduction partials when a split is planned;
 // room past them (256-byte aligned) takes the prepared B tiles (the deltas) of
 // the tensor-core kernel.
 int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
               const char* what) {
+    if (bias_apart(Mo, g.N, g.Kr, g.ones_row == Mo - 1)) {
+        size_t off = 0;
+        const size_t total = bias_apart_bytes(Mo, g.N, g.Kr, &off);
+        if (ws != nullptr && ws_bytes >= total) {  // else: the ones row, as below
+            int slices, chunk;
+            bias_plan(g.N, g.Kr, &slices, &chunk);
+            float* part = reinterpret_cast<float*>(static_cast<char*>(ws) + off);
+            const unsigned cols = static_cast<unsigned>(cdiv(g.N, 32));
+            bias_sums_kernel<<<dim3(cols, static_cast<unsigned>(slices)), 256, 0, st>>>(g, chunk,
+                                                                                       part);
+            int rc = check_launch(what);
+            if (rc) return rc;
+            bias_finish_kernel<<<grid_1d(g.N, 256), 256, 0, st>>>(g, slices, part, param ? 1 : 0,
+                                                                  Mo - 1);
+            rc = check_launch(what);
+            if (rc) return rc;
+            GemmArgs gw = g;
+            gw.ones_row = -1;
+            rc = run_wgrad(gw, Mo - 1, ws, off, param, st, what);
+            g.M = Mo;
+            return rc;
+        }
+    }
     int splits, chunk, bn_tc;
     bool skinny;
     plan_wgrad(Mo, g.N, g.Kr, &splits, &chunk, &bn_tc, &skinny);
@@ -851,7 +949,12 @@ extern "C" int tagi_fused_weight_grad(const float* a, const float* dmz, const fl
 
 extern "C" size_t tagi_param_grad_workspace_size(int64_t M, int64_t K, int64_t N, int has_bias) {
     if (bad_size(M) || bad_size(K) || bad_size(N)) return 0;
-    return wgrad_ws_total((int)K + (has_bias ? 1 : 0), (int)N, (int)M);
+    const int Mo = (int)K + (has_bias ? 1 : 0);
+    if (bias_apart(Mo, (int)N, (int)M, has_bias != 0)) {
+        size_t off = 0;
+        return bias_apart_bytes(Mo, (int)N, (int)M, &off);
+    }
+    return wgrad_ws_total(Mo, (int)N, (int)M);
 }
 
 namespace tagi {
