@@ -32,6 +32,12 @@ def test_cpu_tensors_are_rejected_not_computed():
     lin = tt.Linear(4, 3, device="cpu")
     with pytest.raises(ValueError, match="CUDA"):
         lin.forward(torch.zeros(2, 4), torch.zeros(2, 4))
+    emb = tt.Embedding(8, 6, device="cpu")
+    with pytest.raises(ValueError, match="CUDA"):
+        emb.forward(torch.zeros(2, 5), torch.zeros(2, 5))
+    pe = tt.PositionalEncoding(6, max_seq_len=16, device="cpu")
+    with pytest.raises(ValueError, match="CUDA"):
+        pe.forward(torch.zeros(2, 5, 6), torch.zeros(2, 5, 6))
 
 
 def test_unported_options_raise_like_reference():
