@@ -19,8 +19,17 @@ roofline   the dominant moment contraction, timed with CUDA events around
            FLOPs (6·M·N·K forward, 4·M·N·K backward/weight sums) ÷ time,
            against the 3xTF32-effective tensor peak (measured cuBLAS TF32 ÷ 3).
 cpu_baseline  the CPU oracle (float32 PyTorch restatement of the reference's
-           equations) on the host cores, rank 0 at N = 1, bounded sample.
---impl reference  times that CPU restatement as the reference arm.
+           equations) on the host cores, rank 0 at N = 1, at the workload's
+           own batch (5 timed steps after 1 warm-up).
+subrecords the MLP step at the same number of GPUs, and on one GPU the Linear
+           sweep's 8192 x 4096 x 4096 shape (forward, input deltas, weight
+           sums + capped update), from the same run.
+device_status  the tensor-core kernels' error word after the timed steps
+           (non-zero: a bounded wait ran out; the run then exits with an error).
+replicas_bit_identical  (N > 1) every rank's parameters after the run have the
+           same bits.
+--impl reference  times that CPU restatement as the reference arm, at the
+           workload's own batch.
 """
 
 from __future__ import annotations
@@ -271,25 +280,27 @@ class LaunchTimer:
 
 
 def tf32_peak_tflops(device) -> float:
-    """Burst cuBLAS TF32 throughput on an 8192³ GEMM (best of 5, CUDA events)."""
+    """Burst cuBLAS TF32 throughput on an 8192³ GEMM: the median of 9 single
+    launches timed with CUDA events after 3 warm-up launches (the best of a few
+    moved by ±5 % between runs)."""
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = True
     try:
         n = 8192
         a = torch.randn(n, n, device=device)
         b = torch.randn(n, n, device=device)
-        for _ in range(2):
+        for _ in range(3):
             torch.matmul(a, b)
-        best = float("inf")
-        for _ in range(5):
+        times = []
+        for _ in range(9):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             torch.matmul(a, b)
             e.record()
             e.synchronize()
-            best = min(best, s.elapsed_time(e) * 1e-3)
+            times.append(s.elapsed_time(e) * 1e-3)
         del a, b
-        return 2.0 * n**3 / best / 1e12
+        return 2.0 * n**3 / statistics.median(times) / 1e12
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
@@ -306,20 +317,23 @@ def measured_peaks():
 
 # ----------------------------------------------------------------------------- CPU arms
 def cpu_rate(workload: str, steps: int, warmup: int, budget_s: float) -> dict:
-    """Samples/s of the CPU oracle (float32 PyTorch on all host threads)."""
+    """Samples/s of the CPU oracle (float32 PyTorch on all host threads) at the
+    workload's own batch. Only if (steps + warmup) steps at that batch would
+    take much longer than ``budget_s`` (a slow host) is the batch reduced; the
+    sample string says which batch was timed."""
     import oracle.net as ON
 
     torch.set_num_threads(os.cpu_count() or 1)
-    # size the sample so that one step takes about budget_s / (steps + warmup)
-    probe_b = 2
+    full = WORKLOADS[workload]["batch"]
     torch.manual_seed(0)
     net = ON.Sequential(build_layers(workload, ON, "cpu"))
+    probe_b = min(full, 16)
     x, y = make_batch(workload, probe_b, 1)
     t0 = time.perf_counter()
     net.step(x, y, SIGMA_V)
     per_sample = (time.perf_counter() - t0) / probe_b
-    target = budget_s / max(1, steps + warmup)
-    batch = int(max(2, min(WORKLOADS[workload]["batch"], target / max(per_sample, 1e-6))))
+    target = 2.0 * budget_s / max(1, steps + warmup)
+    batch = full if per_sample * full <= target else int(max(2, target / max(per_sample, 1e-6)))
     x, y = make_batch(workload, batch, 2)
     for _ in range(warmup):
         net.step(x, y, SIGMA_V)
@@ -331,16 +345,16 @@ def cpu_rate(workload: str, steps: int, warmup: int, budget_s: float) -> dict:
     total = sum(times)
     return {"value": steps * batch / total, "unit": "samples/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{workload} Sequential.step at batch {batch} (of {WORKLOADS[workload]['batch']}),"
+            "sample": f"{workload} Sequential.step at batch {batch} (of {full}),"
                       f" {steps} timed steps after {warmup} warm-up, float32 oracle on "
                       f"{torch.get_num_threads()} threads",
-            "ms_per_step": 1e3 * total / steps}
+            "batch": batch, "ms_per_step": 1e3 * total / steps}
 
 
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    r = cpu_rate(args.workload, args.steps, args.warmup, budget_s=60.0)
+    r = cpu_rate(args.workload, args.steps, args.warmup, budget_s=150.0)
     line = {
         "impl": "reference", "metric": WORKLOADS[args.workload]["metric"], "value": r["value"],
         "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -361,7 +375,7 @@ def reference_arm(args, rank: int, world: int) -> None:
 # ----------------------------------------------------------------------------- GPU arm
 def our_arm(args, rank: int, world: int, local: int) -> None:
     import triton_tagi as TT
-    from triton_tagi._lib import kernel_launches, lib
+    from triton_tagi._lib import device_status, kernel_launches, lib
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -446,13 +460,31 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     barrier()
     e2e_s = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)) * 1e-3
 
+    # error word of the tensor-core kernels: a bounded wait that ran out inside
+    # the timed or end-to-end steps would have left outputs incomplete
+    status = device_status(reset=True)
+    replicas = replica_check(net, dev, world) if world > 1 else None
+
     if world > 1:
-        t = torch.tensor([step_s, e2e_s], device=dev, dtype=torch.float64)
+        t = torch.tensor([step_s, e2e_s, float(status != 0)], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_s, e2e_s = t.tolist()
+        step_s, e2e_s, bad = t.tolist()
+        status = status or int(bad)
+
+    # North-star sub-records from the same run: the MLP step at the same number
+    # of GPUs, and (one GPU) the Linear sweep's 8192 x 4096 x 4096 headline shape.
+    tf32 = tf32_peak_tflops(dev) if rank == 0 or world == 1 else None
+    sub = {}
+    if not args.no_subrecords:
+        if args.workload != "mlp":
+            sub["mlp"] = mlp_subrecord(dev, rank, world, args.steps, args.warmup, flush, barrier)
+        if world == 1:
+            row = sweep_rows([(8192, 4096)], dev, 5, 3, tf32)[0]
+            sub["sweep_8192x4096"] = {k: row[k] for k in ("forward", "backward", "update")}
+            sub["sweep_8192x4096"]["peak_3xtf32_tflops"] = tf32 / 3.0
+    status = status or device_status(reset=True)
 
     peaks = measured_peaks()
-    tf32 = tf32_peak_tflops(dev) if rank == 0 else None
     if rank != 0:
         return
     value = args.steps * B * world / step_s
@@ -493,81 +525,150 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
                            if v["bytes_known"] and v["bytes"] > 0 else {})}
                     for k, v in sorted(other.items(), key=lambda kv: -kv[1]["seconds"])},
         "clocks": clocks.summary(),
-        "peaks": {"tf32_cublas_tflops": tf32, "hbm_gbs": peaks.get("hbm_gbs"),
-                  "bf16_tflops": peaks.get("bf16_tflops")},
+        "peaks": {"tf32_cublas_tflops": tf32, "tf32_source": "cuBLAS 8192^3, median of 9",
+                  "hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops": peaks.get("bf16_tflops")},
+        "device_status": status,
+        **({"replicas_bit_identical": replicas} if replicas is not None else {}),
+        **({"subrecords": sub} if sub else {}),
     }
     if world == 1 and not args.no_cpu_baseline:
-        r = cpu_rate(args.workload, steps=3, warmup=1, budget_s=20.0)
+        r = cpu_rate(args.workload, steps=5, warmup=1, budget_s=30.0)
         line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line), flush=True)
+    if status != 0:
+        raise RuntimeError(f"a tensor-core kernel wait ran out during the run (code {status}); "
+                           "the numbers above are not valid")
+
+
+def replica_check(net, dev, world: int) -> bool:
+    """True if every rank holds bit-identical parameters (an integer checksum of
+    every parameter's bits, gathered from all ranks)."""
+    acc = torch.zeros(2, dtype=torch.int64, device=dev)
+    for leaf in net.leaves():
+        for name in ("mw", "Sw", "mb", "Sb", "running_mean", "running_var"):
+            t = getattr(leaf, name, None)
+            if t is not None:
+                bits = t.detach().contiguous().view(torch.int32).to(torch.int64)
+                acc[0] += bits.sum()
+                acc[1] += (bits * torch.arange(1, bits.numel() + 1, device=dev) % 1000003).sum()
+    allv = [torch.empty_like(acc) for _ in range(world)]
+    dist.all_gather(allv, acc)
+    return all(torch.equal(v, allv[0]) for v in allv)
+
+
+def mlp_subrecord(dev, rank: int, world: int, steps: int, warmup: int, flush, barrier) -> dict:
+    """MLP 784-256-128-10 Sequential.step, batch 256 per GPU, at the run's number
+    of GPUs (data parallel for N > 1), timed like the main workload."""
+    import triton_tagi as TT
+
+    B = WORKLOADS["mlp"]["batch"]
+    torch.manual_seed(4321)
+    net = TT.Sequential(build_layers("mlp", TT, dev), device=dev, cuda_graph=world == 1)
+    if world > 1:
+        from triton_tagi.distributed import DataParallel
+
+        DataParallel(net)
+    x, y = make_batch("mlp", B, 300 + rank, dev)
+    for _ in range(max(3, warmup)):
+        net.step(x, y, SIGMA_V)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        net.step(x, y, SIGMA_V)
+        ends[i].record()
+    torch.cuda.synchronize()
+    barrier()
+    t = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) * 1e-3
+    if world > 1:
+        tt = torch.tensor([t], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = tt.item()
+    return {"metric": WORKLOADS["mlp"]["metric"], "value": steps * B * world / t,
+            "unit": "samples/s", "ms_per_step": 1e3 * t / steps, "batch_per_gpu": B,
+            "global_batch": B * world, "steps": steps, "cuda_graph": world == 1,
+            "l2": "flushed between steps"}
+
+
+def sweep_rows(shapes, dev, steps: int, warmup: int, peak_tf32: float) -> list[dict]:
+    """Linear op sweep rows: forward (mean+var), backward delta and weight sums
+    with the capped update of each (M, K = N) shape, each launch timed with CUDA
+    events (L2 flushed before every launch), median over ``steps``."""
+    import triton_tagi as TT
+    from triton_tagi._lib import lib, stream
+    from triton_tagi.layers._params import weight_param_backward
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    L = lib()
+    rows = []
+    for M, K in shapes:
+        N = K
+        g = torch.Generator(device=dev).manual_seed(M + K)
+        ma = torch.randn(M, K, device=dev, generator=g)
+        Sa = torch.rand(M, K, device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
+        lin = TT.Linear(K, N, device=dev)
+        lin.mw = torch.randn(K, N, device=dev, generator=g) / K**0.5
+        lin.Sw = (torch.rand(K, N, device=dev, generator=g) + 0.5) / K
+        lin.mb = torch.zeros(1, N, device=dev)
+        lin.Sb = torch.full((1, N), 1e-3, device=dev)
+        dmz = torch.randn(M, N, device=dev, generator=g) * 0.1
+        dSz = -torch.rand(M, N, device=dev, generator=g) * 1e-2
+        d_ma = torch.empty(M, K, device=dev)
+        d_Sa = torch.empty(M, K, device=dev)
+        ws_n = L.size("tagi_store_workspace_size", M, K, N)
+        ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+
+        def fwd():
+            lin.forward(ma, Sa)
+
+        def bwd():
+            L("tagi_linear_backward_delta", dmz.data_ptr(), dSz.data_ptr(), lin.mw.data_ptr(),
+              d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, ws.data_ptr() if ws_n else None,
+              ws_n, stream(dmz))
+
+        def upd():
+            lin._set_param_mode("update", 3.0)
+            weight_param_backward(lin, ma, K, (dmz, dSz), (0, 0, N, 1), M, K, N, True)
+            lin._set_param_mode("deltas")
+
+        row = {"M": M, "K": K, "N": N}
+        for name, fn, flops in (("forward", fwd, 6.0 * M * N * K),
+                                ("backward", bwd, 4.0 * M * N * K),
+                                ("update", upd, 4.0 * M * N * K)):
+            for _ in range(warmup):
+                fn()
+            times = []
+            for _ in range(steps):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                b.synchronize()
+                times.append(a.elapsed_time(b) * 1e-3)
+            t = statistics.median(times)
+            row[name] = {"ms": 1e3 * t, "tflops": flops / t / 1e12,
+                         "frac": flops / t / 1e12 / (peak_tf32 / 3.0),
+                         "samples_per_s": M / t}
+        rows.append(row)
+        del ma, Sa, lin, dmz, dSz, d_ma, d_Sa, ws
+    return rows
 
 
 def sweep_arm(args, rank: int, world: int, local: int) -> None:
-    """Linear op sweep: forward (mean+var), backward delta and weight sums with the
-    capped update, each timed with CUDA events (L2 flushed before every launch)."""
-    import triton_tagi as TT
-    from triton_tagi._lib import kernel_launches, lib, stream
+    """Linear op sweep, every shape."""
+    from triton_tagi._lib import kernel_launches
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     shapes = [tuple(int(v) for v in args.shape.split(","))] if args.shape else SWEEP
-    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
-    L = lib()
-    rows, peak_tf32 = [], tf32_peak_tflops(dev)
+    peak_tf32 = tf32_peak_tflops(dev)
     launches0 = kernel_launches()
     with ClockSampler(dev.index or 0) as clocks:
-        for M, K in shapes:
-            N = K
-            g = torch.Generator(device=dev).manual_seed(M + K)
-            ma = torch.randn(M, K, device=dev, generator=g)
-            Sa = torch.rand(M, K, device=dev, generator=g) * (1e-2 - 1e-4) + 1e-4
-            lin = TT.Linear(K, N, device=dev)
-            lin.mw = torch.randn(K, N, device=dev, generator=g) / K**0.5
-            lin.Sw = (torch.rand(K, N, device=dev, generator=g) + 0.5) / K
-            lin.mb = torch.zeros(1, N, device=dev)
-            lin.Sb = torch.full((1, N), 1e-3, device=dev)
-            dmz = torch.randn(M, N, device=dev, generator=g) * 0.1
-            dSz = -torch.rand(M, N, device=dev, generator=g) * 1e-2
-            d_ma = torch.empty(M, K, device=dev)
-            d_Sa = torch.empty(M, K, device=dev)
-            ws_n = L.size("tagi_store_workspace_size", M, K, N)
-            ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
-
-            def fwd():
-                lin.forward(ma, Sa)
-
-            def bwd():
-                L("tagi_linear_backward_delta", dmz.data_ptr(), dSz.data_ptr(), lin.mw.data_ptr(),
-                  d_ma.data_ptr(), d_Sa.data_ptr(), M, K, N, ws.data_ptr() if ws_n else None,
-                  ws_n, stream(dmz))
-
-            def upd():
-                from triton_tagi.layers._params import weight_param_backward
-
-                lin._set_param_mode("update", 3.0)
-                weight_param_backward(lin, ma, K, (dmz, dSz), (0, 0, N, 1), M, K, N, True)
-                lin._set_param_mode("deltas")
-
-            row = {"M": M, "K": K, "N": N}
-            for name, fn, flops in (("forward", fwd, 6.0 * M * N * K),
-                                    ("backward", bwd, 4.0 * M * N * K),
-                                    ("update", upd, 4.0 * M * N * K)):
-                for _ in range(args.warmup):
-                    fn()
-                times = []
-                for _ in range(args.steps):
-                    flush.zero_()
-                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a.record()
-                    fn()
-                    b.record()
-                    b.synchronize()
-                    times.append(a.elapsed_time(b) * 1e-3)
-                t = statistics.median(times)
-                row[name] = {"ms": 1e3 * t, "tflops": flops / t / 1e12,
-                             "frac": flops / t / 1e12 / (peak_tf32 / 3.0),
-                             "samples_per_s": M / t}
-            rows.append(row)
+        rows = sweep_rows(shapes, dev, args.steps, args.warmup, peak_tf32)
     if rank != 0:
         return
     top = max(rows, key=lambda r: r["M"] * r["K"])
@@ -585,7 +686,8 @@ def sweep_arm(args, rank: int, world: int, local: int) -> None:
                      "traffic": MEASURED_TRAFFIC.get(("swp", "moment_forward"))
                      if (top["M"], top["K"]) == (8192, 4096) else None,
                      "traffic_unit": "bytes per launch (ncu)",
-                     "peak_source": f"measured cuBLAS TF32 burst {peak_tf32:.0f} TF/s / 3"},
+                     "peak_source": f"measured cuBLAS TF32 burst {peak_tf32:.0f} TF/s "
+                                    "(median of 9) / 3"},
         "sweep": rows, "gpu_launches": int(kernel_launches() - launches0),
         "clocks": clocks.summary(),
     }
@@ -603,6 +705,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true",
                     help="mlp/cnn: run the steps eagerly instead of replaying a CUDA graph")
     ap.add_argument("--shape", default=None, help="swp workload: one 'M,K' shape (K = N)")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="skip the MLP and sweep sub-records of the default line")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

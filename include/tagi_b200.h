@@ -48,6 +48,14 @@ uint64_t tagi_kernel_launches(void);     /* kernels this library has launched (p
  * the first bounded wait that ran out (the kernel then skipped its remaining work
  * and released its tensor memory). Synchronises the device; `reset` clears it. */
 int tagi_device_status(int reset);
+/* Limit, in nanoseconds, of the tensor-core kernels' waits that give up a tile
+ * when they run out (default 2 s; 0 restores it), on the current device. A
+ * diagnostic hook: a test sets a few nanoseconds to make those waits run out
+ * and checks that the kernel returns, that tagi_device_status reports it and
+ * that later calls with the default limit are correct. The waits for a CTA's
+ * own in-flight copies and MMAs keep the 2 s limit whatever this is. No
+ * reference counterpart (the reference's Triton kernels do not wait). */
+int tagi_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------------------
  * Dense moment contractions
@@ -161,8 +169,10 @@ int tagi_fused_weight_grad(const float* a, const float* dmz, const float* dSz, f
  * device memory is a fixed pool that a plugin may not grow. Instead of a caller
  * workspace, the split-reduction partial sums go to one array of
  * TAGI_STATIC_SCRATCH_BYTES that lives in the library's device image: every
- * GPU that loads the library holds it until the process exits. Shapes whose
- * split plan needs more than that return TAGI_E_WORKSPACE. The first call on a
+ * GPU that loads the library holds it until the process exits. When room is
+ * left after the partials, the tensor-core kernel's prepared delta tiles go
+ * there too (as they would into a large enough workspace). Shapes whose split
+ * partials alone need more than the array return TAGI_E_WORKSPACE. The first call on a
  * device looks up that device's copy of the array (cudaGetSymbolAddress on
  * the current device), so make the first call before any stream capture.
  * All calls share the array: calls that overlap on the GPU (e.g. on two
@@ -247,22 +257,22 @@ int tagi_capped_update(float* m, float* S, const float* delta_m, const float* de
 
 /* delta_mu = (y - mu)/(var + sv2), delta_var = -1/(var + sv2).
  * Replaces the dense branch of compute_innovation,
- * triton_tagi/update/observation.py:247-291. */
+ * triton_tagi/update/observation.py:119-163 (dense branch 149-161). */
 int tagi_innovation(const float* y, const float* mu, const float* var, float* delta_mu,
                     float* delta_var, int64_t n, float sigma_v_sq, void* stream);
 
 /* Rectified-Gaussian moments and Jacobian. Replaces bayesian_relu,
- * triton_tagi/layers/relu.py:275-303. */
+ * triton_tagi/layers/relu.py:94-122. */
 int tagi_relu_forward(const float* mz, const float* Sz, float* ma, float* Sa, float* J, int64_t n,
                       void* stream);
 
-/* out_m = dm * J, out_S = dS * J^2 (ReLU.backward relu.py:333-350,
- * Remax.backward remax.py:538-541). */
+/* out_m = dm * J, out_S = dS * J^2 (ReLU.backward relu.py:152-169,
+ * Remax.backward remax.py:185-188). */
 int tagi_jacobian_backward(const float* dm, const float* dS, const float* J, float* out_m,
                            float* out_S, int64_t n, void* stream);
 
 /* Row-wise Remax over K classes. Replaces triton_remax,
- * triton_tagi/layers/remax.py:475-512. */
+ * triton_tagi/layers/remax.py:122-164. */
 int tagi_remax_forward(const float* mz, const float* Sz, float* ma, float* Sa, float* J,
                        int64_t rows, int64_t K, int64_t row_stride, void* stream);
 
@@ -301,7 +311,7 @@ int tagi_embedding_backward(const float* idx, const float* dmz, const float* dSz
 
 /* out[r][d] = ma[r][d] + pe[r % S][d] for the rows of a (B*S, D) tensor (the
  * variances pass through unchanged). Replaces PositionalEncoding.forward,
- * triton_tagi/layers/positional_encoding.py:113-118. */
+ * triton_tagi/layers/positional_encoding.py:57-62. */
 int tagi_positional_add(const float* ma, const float* pe, float* out, int64_t rows, int64_t S,
                         int64_t D, void* stream);
 
@@ -380,7 +390,7 @@ int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* 
  * grads[0:C]=sum dma*m_hat, [C:2C]=sum dSa*m_hat^2, [2C:3C]=sum dma, [3C:4C]=sum dSa.
  * relu_J (NULL: none): Jacobian of a ReLU that produced this layer's input;
  * the outgoing deltas are then multiplied by J and J^2 as the ReLU's backward
- * (triton_tagi/layers/relu.py:333-350) would. cap_factor > 0: the capped update
+ * (triton_tagi/layers/relu.py:152-169) would. cap_factor > 0: the capped update
  * of gamma (mg, Sw) and beta (mb, Sb) is also applied from the sums, as
  * tagi_bn_apply_grads in update mode would (mg is updated in place after every
  * block has read it); cap_factor <= 0 leaves the parameters alone.
@@ -398,7 +408,7 @@ int tagi_bn_apply_grads(const double* grads, int64_t C, int mode, float* mw, flo
                         float cap_factor, void* stream);
 
 /* RMSNorm over the last dim (rows x ni). Replaces RMSNorm.forward/backward,
- * triton_tagi/layers/rms_norm.py:387-428. Backward writes propagated deltas
+ * triton_tagi/layers/rms_norm.py:93-137. Backward writes propagated deltas
  * and the raw gamma sums (float64) sum_mu[ni], sum_var[ni]. */
 int tagi_rmsnorm_forward(const float* ma, const float* Sa, const float* mw, const float* Sw,
                          float* mz, float* Sz, float* inv_rms, int64_t rows, int64_t ni,

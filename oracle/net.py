@@ -28,13 +28,13 @@ class Layer:
 
 
 def _gauss(scale, gain, shape):
-    """triton_tagi/param_init.py:447-468 (global torch RNG, as the reference)."""
+    """triton_tagi/param_init.py:57-84 (global torch RNG, as the reference)."""
     m = torch.randn(shape) * scale
     return m, torch.full(shape, (gain * scale) ** 2)
 
 
 def _scale(init_method, fan_in, fan_out):
-    """triton_tagi/param_init.py:412-439, 501-506."""
+    """triton_tagi/param_init.py:22-54."""
     if init_method.lower() == "he":
         return F.he_scale(fan_in)
     if init_method.lower() == "xavier":
@@ -169,7 +169,7 @@ class BatchNorm2D(Layer):
 
 
 class ReLU(Layer):
-    """triton_tagi/layers/relu.py:306-353."""
+    """triton_tagi/layers/relu.py:125-169."""
 
     def forward(self, mz, Sz):
         ma, Sa, self.J = F.relu_moments(mz, Sz)
@@ -180,7 +180,7 @@ class ReLU(Layer):
 
 
 class Remax(Layer):
-    """triton_tagi/layers/remax.py:160-191."""
+    """triton_tagi/layers/remax.py:167-191."""
 
     def forward(self, mz, Sz):
         ma, Sa, self.J = F.remax(mz, Sz)
@@ -263,7 +263,7 @@ class ResBlock(Layer):
 
 
 class RMSNorm(Layer):
-    """triton_tagi/layers/rms_norm.py:336-444."""
+    """triton_tagi/layers/rms_norm.py:42-150."""
 
     learnable = True
 

@@ -66,3 +66,44 @@ def assert_as_accurate(got, ref32, exact, factor=2.0, floor=1e-6, what=""):
     assert e_got <= factor * e_ref + floor, (
         f"{what}: error vs float64 {e_got:.3e} exceeds {factor}x the reference's "
         f"{e_ref:.3e} + {floor:.0e}")
+
+
+def elem_check(got, ref32, ref64, tol, floor=1e-6):
+    """Element-wise relative check of a sign-definite tensor (variances and
+    variance deltas) against the float32 reference, with the reference's own
+    float32 error as the allowance where that is larger.
+
+    Element i passes if |g − r32| ≤ tol·|r32|, or if |g − r64| ≤ 2·|r32 − r64|
+    + tol·|r64|: where the reference's float32 result is itself further than
+    the bar from the float64 evaluation (closed forms that cancel: the ReLU
+    variance, Remax), the result must be at least as close to float64 as the
+    reference is (twice its error). Elements smaller than ``floor``·max|r32| are
+    measured against floor·max|r32| (exact zeros of switched-off units).
+
+    Returns (worst, fallbacks, plain): worst ≤ 1 passes (the largest over
+    elements of the smaller of the two ratios to their bars), fallbacks counts
+    the elements that needed the second branch, plain is the largest
+    element-wise relative error against float32.
+    """
+    g, a, b = _arr(got), _arr(ref32), _arr(ref64)
+    assert g.shape == a.shape == b.shape, (g.shape, a.shape, b.shape)
+    if g.size == 0:
+        return 0.0, 0, 0.0
+    fl = floor * max(np.abs(a).max(), 1e-300)
+    den32 = np.maximum(np.abs(a), fl)
+    den64 = np.maximum(np.abs(b), fl)
+    e32 = np.abs(g - a) / den32
+    r1 = e32 / tol
+    r2 = np.abs(g - b) / (2.0 * np.abs(a - b) + tol * den64)
+    r = np.minimum(r1, r2)
+    return float(r.max()), int(((r1 > 1) & (r2 <= 1)).sum()), float(e32.max())
+
+
+def norm_check(got, ref32, ref64, tol):
+    """Normwise form of ``elem_check`` for means (which cross zero): passes if
+    rel_err(g, r32) ≤ tol, or if rel_err(g, r64) ≤ 2·rel_err(r32, r64) + tol.
+    Returns (worst, used_fallback, plain)."""
+    e32 = rel_err(got, ref32)
+    r1 = e32 / tol
+    r2 = rel_err(got, ref64) / (2.0 * rel_err(ref32, ref64) + tol)
+    return float(min(r1, r2)), bool(r1 > 1 and r2 <= 1), e32

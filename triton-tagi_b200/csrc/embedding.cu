@@ -1,5 +1,5 @@
 // Gaussian embedding lookup and its parameter sums, and the positional-encoding
-// add (triton_tagi/layers/embedding.py:88-151, positional_encoding.py:113-118).
+// add (triton_tagi/layers/embedding.py:88-151, positional_encoding.py:57-62).
 //
 // Token ids arrive as floats (the reference casts `ma.long()`, truncating toward
 // zero). Ids outside [0, V) and the padding id give zero rows in the forward and

@@ -50,6 +50,11 @@
 namespace tagi {
 
 __device__ int g_device_error = 0;  // 0 = ok, else the code of the first timeout
+// Limit of the waits that give up the tile (the producers', the MMA issuer's and
+// the accumulator warps'). tagi_set_wait_limit_ns changes it so that a test can
+// make those waits run out; the drains that must complete before a CTA exits
+// (its own bulk copies, its MMAs) keep the fixed kTimeoutNs.
+__device__ unsigned long long g_wait_limit_ns = 2000000000ull;
 
 namespace {
 
@@ -154,10 +159,11 @@ struct Abort {
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const Abort& ab,
                                             int code) {
     const unsigned long long t0 = globaltimer();
+    const unsigned long long limit = *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
     for (;;) {
         if (mbar_try(bar, parity)) return true;
         if (*ab.flag) return false;
-        if (globaltimer() - t0 > kTimeoutNs) {
+        if (globaltimer() - t0 > limit) {
             *ab.flag = 1;
             asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ab.peer), "r"(1) : "memory");
             atomicCAS(&g_device_error, 0, code);
@@ -1245,8 +1251,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     }
 
     if (warp == R::MMA_W) {
-        // the pair's MMAs read both CTAs' shared memory: wait until they are complete
-        if (!mbar_try(done, 0)) mbar_wait(done, 0, ab, 4);
+        // The pair's MMAs read both CTAs' shared memory and write both CTAs'
+        // tensor memory: wait until they are complete, also after an abort (the
+        // leader commits `done` on every path out of its issue loop).
+        if (!mbar_drain(done, 0) && lane == 0) atomicCAS(&g_device_error, 0, 4);
     }
     tc_fence_before();
     cluster_sync();  // no peer access (remote arrive, multicast commit) is still due
@@ -1426,6 +1434,17 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
 }
 
 }  // namespace tagi
+
+extern "C" int tagi_set_wait_limit_ns(uint64_t ns) {
+    const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : tagi::kTimeoutNs;
+    cudaError_t e = cudaMemcpyToSymbol(tagi::g_wait_limit_ns, &v, sizeof(v));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        tagi::set_error("tagi_set_wait_limit_ns: %s", cudaGetErrorString(e));
+        return TAGI_E_LAUNCH;
+    }
+    return TAGI_OK;
+}
 
 extern "C" int tagi_device_status(int reset) {
     int v = 0;

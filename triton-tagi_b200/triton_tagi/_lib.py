@@ -16,9 +16,9 @@ import torch
 
 LIB_PATH = Path(os.environ.get("TAGI_B200_LIB", Path(__file__).resolve().parent / "libtagi_b200.so"))
 
-_P, _I, _F, _D, _N, _Z = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_double,
-                          ctypes.c_int, ctypes.c_size_t)
-_CODES = {"p": _P, "i": _I, "f": _F, "d": _D, "n": _N, "z": _Z}
+_P, _I, _F, _D, _N, _Z, _U = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_double,
+                              ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64)
+_CODES = {"p": _P, "i": _I, "f": _F, "d": _D, "n": _N, "z": _Z, "u": _U}
 
 # name -> argument codes (stream last, always 'p'); returns int status unless listed in _RET.
 _SIGS = {
@@ -69,6 +69,7 @@ _SIGS = {
     "tagi_last_error": "",
     "tagi_kernel_launches": "",
     "tagi_device_status": "n",
+    "tagi_set_wait_limit_ns": "u",
 }
 _RET = {
     "tagi_fused_weight_grad_workspace_size": _Z,
@@ -130,6 +131,22 @@ def lib() -> _Lib:
 def device_status(reset: bool = False) -> int:
     """0, or the code of a tensor-core kernel wait that timed out (synchronises)."""
     return int(lib().fn["tagi_device_status"](1 if reset else 0))
+
+
+def check_device_status() -> None:
+    """Raise RuntimeError if a tensor-core kernel wait ran out since the last
+    check (its outputs are then incomplete); clears the error word."""
+    code = device_status(reset=True)
+    if code != 0:
+        raise RuntimeError(f"a tensor-core kernel gave up a tile (bounded wait {code} ran out); "
+                           "its outputs are incomplete")
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of the tensor-core kernels' abortable waits (0 restores 2 s); a test hook."""
+    rc = lib().fn["tagi_set_wait_limit_ns"](int(ns))
+    if rc != 0:
+        raise RuntimeError(lib().fn["tagi_last_error"]().decode(errors="replace"))
 
 
 def kernel_launches() -> int:

@@ -6,6 +6,10 @@ accumulates δμ·S_w[cat] and δS·S_w[cat]² per row in token order
 index_add on the CPU; embedding.py:112-151). ``padding_idx`` rows emit zeros and
 receive no update, as in the reference; ids outside the table do the same
 instead of aborting the device context.
+
+Token ids travel to the kernels as float32, which holds every integer up to
+2^24 exactly; larger vocabularies are refused at construction (an integer id
+tensor would otherwise be rounded to a neighbouring row without error).
 """
 
 from __future__ import annotations
@@ -22,6 +26,9 @@ from ..update.parameters import update_parameters
 class Embedding(LearnableLayer):
     def __init__(self, num_embeddings: int, embedding_dim: int, input_size: int = 0,
                  scale: float = 1.0, padding_idx: int = -1, device="cuda") -> None:
+        if num_embeddings > 2**24:
+            raise ValueError(f"Embedding: num_embeddings={num_embeddings} exceeds 2^24, the "
+                             "largest vocabulary whose ids float32 holds exactly")
         self.num_embeddings, self.embedding_dim = num_embeddings, embedding_dim
         self.input_size, self.scale, self.padding_idx = input_size, scale, padding_idx
         self.device = torch.device(device)

@@ -17,7 +17,7 @@ from ..base import Layer
 
 
 def bayesian_relu(mz: Tensor, Sz: Tensor):
-    """(ma, Sa, J) for any shape, processed flat (relu.py:275-303)."""
+    """(ma, Sa, J) for any shape, processed flat (relu.py:94-122)."""
     check_cuda_f32(mz, Sz)
     mz, Sz = mz.contiguous(), Sz.contiguous()
     ma = torch.empty_like(mz)

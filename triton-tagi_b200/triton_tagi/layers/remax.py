@@ -20,7 +20,7 @@ from .relu import jacobian_backward
 
 
 def triton_remax(mu_z: Tensor, var_z: Tensor):
-    """(mu_a, var_a, J) for (B, K) or (K,) inputs (remax.py:475-512)."""
+    """(mu_a, var_a, J) for (B, K) or (K,) inputs (remax.py:122-164)."""
     check_cuda_f32(mu_z, var_z)
     squeeze = mu_z.dim() == 1
     mz = mu_z.reshape(1, -1) if squeeze else mu_z.reshape(-1, mu_z.shape[-1])

@@ -20,15 +20,25 @@ new input shape (or σ_v) runs eagerly, the next one is captured on static input
 buffers and replayed, and later steps copy their inputs in and replay. A step
 of small layers is a few dozen short kernels, so launch overhead otherwise
 dominates it. The replayed kernels are the eager step's; returned predictions
-are copies. Not used under data parallelism (the step then runs eagerly).
+are copies. Not used under data parallelism (the step then runs eagerly). The
+captured graph is keyed on the input shapes, σ_v, ``fuse_update`` and every
+layer's training flag, so ``train()`` / ``eval()`` lead to a new capture.
+
+``check_device=True`` (or the environment variable ``TAGI_B200_CHECK=1``) reads
+the tensor-core kernels' error word after every step (this synchronises) and
+raises ``RuntimeError`` if a bounded wait inside a kernel ran out, in which case
+that kernel's outputs are incomplete.
 """
 
 from __future__ import annotations
+
+import os
 
 import torch
 from torch import Tensor
 
 from ._chain import backward_chain, forward_chain
+from ._lib import check_device_status
 from .base import LearnableLayer
 from .layers.multihead_attention import MultiheadAttentionV2
 from .layers.resblock import ResBlock
@@ -38,11 +48,14 @@ from .update.parameters import get_cap_factor
 
 class Sequential:
     def __init__(self, layers: list, device="cuda", fuse_update: bool = True,
-                 cuda_graph: bool = False) -> None:
+                 cuda_graph: bool = False, check_device: bool | None = None) -> None:
         self.device = torch.device(device)
         self.layers = layers
         self.fuse_update = fuse_update
         self.cuda_graph = cuda_graph
+        if check_device is None:
+            check_device = os.environ.get("TAGI_B200_CHECK", "0") == "1"
+        self.check_device = check_device
         self._graph = None  # (key, CUDAGraph or None, static x, static y, outputs)
         self.reducer = None  # set by triton_tagi.distributed.DataParallel
         for layer in self.layers:
@@ -85,12 +98,30 @@ class Sequential:
 
     def step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
         if self.cuda_graph and self.reducer is None and x_batch.is_cuda:
-            return self._graph_step(x_batch, y_batch, sigma_v)
-        return self._step(x_batch, y_batch, sigma_v)
+            out = self._graph_step(x_batch, y_batch, sigma_v)
+        else:
+            out = self._step(x_batch, y_batch, sigma_v)
+        if self.check_device:
+            check_device_status()
+        return out
+
+    def _modes(self) -> tuple:
+        """Training flags of every layer (and sub-layer), in network order."""
+        flags = []
+
+        def walk(layer):
+            flags.append(getattr(layer, "training", None))
+            for sub in getattr(layer, "_learnable", ()):
+                if sub is not layer:
+                    walk(sub)
+
+        for layer in self.layers:
+            walk(layer)
+        return tuple(flags)
 
     def _graph_step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
         key = (tuple(x_batch.shape), x_batch.dtype, tuple(y_batch.shape), y_batch.dtype,
-               float(sigma_v), x_batch.device)
+               float(sigma_v), x_batch.device, self.fuse_update, self._modes())
         if self._graph is None or self._graph[0] != key:
             # first step of this shape: eager (it also leaves every layer in its
             # steady state, e.g. BatchNorm's running statistics initialised)
@@ -141,11 +172,13 @@ class Sequential:
         for layer in self.layers:
             if hasattr(layer, "training"):
                 layer.train()
+        self._graph = None
 
     def eval(self) -> None:
         for layer in self.layers:
             if hasattr(layer, "training"):
                 layer.eval()
+        self._graph = None
 
     def __repr__(self):
         lines = ["Sequential("] + [f"  ({i}): {layer}" for i, layer in enumerate(self.layers)]

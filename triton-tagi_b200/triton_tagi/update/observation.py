@@ -12,7 +12,7 @@ from .._lib import check_cuda_f32, lib, stream
 
 
 def compute_innovation(y: Tensor, y_pred_mu: Tensor, y_pred_var: Tensor, sigma_v: float):
-    """Dense innovation (observation.py:247-291). The heteroscedastic branch
+    """Dense innovation (observation.py:119-163). The heteroscedastic branch
     (predictions twice as wide as y) is not part of this library."""
     if y_pred_mu.shape[-1] == 2 * y.shape[-1] and y.shape[-1] != 0:
         raise NotImplementedError("heteroscedastic (TAGI-V) innovation is not implemented")
