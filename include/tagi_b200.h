@@ -53,8 +53,10 @@ int tagi_device_status(int reset);
  * diagnostic hook: a test sets a few nanoseconds to make those waits run out
  * and checks that the kernel returns, that tagi_device_status reports it and
  * that later calls with the default limit are correct. The waits for a CTA's
- * own in-flight copies and MMAs keep the 2 s limit whatever this is. No
- * reference counterpart (the reference's Triton kernels do not wait). */
+ * own in-flight copies and MMAs keep the 2 s limit whatever this is. Values
+ * below 1 ms also shorten the suspend hint of every barrier test to the same
+ * value (default 1 ms), so that the limit is reached. No reference
+ * counterpart (the reference's Triton kernels do not wait). */
 int tagi_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------------------

@@ -44,25 +44,76 @@ __device__ __forceinline__ void capped_pair(float& m, float& S, float dm, float 
 }
 
 // Rectified-Gaussian moments of a = max(0, z), z ~ N(mz, Sz), and the Jacobian
-// J = Phi(alpha) (triton_tagi/layers/relu.py:63-86). Shared by the ReLU kernels
-// and the contraction epilogues that apply a following ReLU.
+// J = Phi(alpha), alpha = mz / sqrt(Sz) (triton_tagi/layers/relu.py:63-86).
+//
+// The reference evaluates
+//   mu = s phi + mz Phi,  var = -mu^2 + 2 mu mz - mz s phi + (Sz - mz^2) Phi
+// with Phi = (1 + erf(alpha/sqrt2))/2, and for alpha < -5 with the leading
+// asymptotic term Phi = phi/|alpha|. For negative alpha the terms of var cancel
+// (by a factor of ~1e3 near alpha = -4) and 1 + erf loses most of Phi's digits,
+// so two float32 evaluations of that form differ in the leading digits of
+// small variances. Here the same moments are written through the Mills ratio
+// R(t) = (1 - Phi(t)) / phi(t) of t = |alpha| and the two functions
+// u(t) = 1 - t R(t), w(t) = R(t) - t u(t), each positive on t >= 0:
+//   alpha < 0:  mu = s phi u,       var = Sz phi (w - phi u^2),            J = phi R
+//   alpha >= 0: mu = mz + s phi u,  var = Sz (1 - phi (w + 2 alpha u + phi u^2)),
+//               J = 1 - phi R
+// (substituting Phi = phi R or 1 - phi R into the reference's expressions), so
+// no term cancels. R, u and w are rational functions of degree (5, 5) in t on
+// [0, 8] (|t| beyond 8 only meets phi < 1e-14), fitted for this library to the
+// functions' definitions by weighted least squares (relative error below 1e-7;
+// below 3e-7 evaluated in float32). The reference's asymptotic branch is kept
+// for alpha < -5 and simplified exactly: with Phi = phi/|alpha| its mu is 0 and
+// its var is Sz phi / |alpha|.
+struct MillsRational {
+    float p[6], q[6];
+    __device__ __forceinline__ float operator()(float t) const {
+        float a = p[5], b = q[5];
+#pragma unroll
+        for (int i = 4; i >= 0; --i) {
+            a = fmaf(a, t, p[i]);
+            b = fmaf(b, t, q[i]);
+        }
+        return __fdividef(a, b);
+    }
+};
+
 __device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
     constexpr float kInvSqrt2Pi = 0.3989422804014327f;
-    constexpr float kInvSqrt2 = 0.7071067811865476f;
-    // The kernel is bound by instruction issue, so the square root, the two
-    // divisions and the exponential use the hardware approximations (a few
-    // ulp, as the reference's fast sqrt, division and exp).
+    constexpr MillsRational kR{{1.253314138e+00f, 1.005634046e+00f, 3.946390781e-01f,
+                                8.097509709e-02f, 7.426330130e-03f, -4.375365097e-08f},
+                               {1.0f, 1.600264494e+00f, 1.091702061e+00f, 4.014938611e-01f,
+                                8.101891127e-02f, 7.424280418e-03f}};
+    constexpr MillsRational kU{{1.000000011e+00f, 4.315312545e-01f, 1.080994959e-01f,
+                                1.094768367e-02f, 7.352854563e-06f, -1.571496301e-07f},
+                               {1.0f, 1.684846170e+00f, 1.219731834e+00f, 4.815096427e-01f,
+                                1.061304995e-01f, 1.110309952e-02f}};
+    constexpr MillsRational kW{{1.253314259e+00f, 2.230172686e-01f, 4.091967526e-02f,
+                                -5.645271322e-04f, 2.714108879e-05f, -5.835115929e-07f},
+                               {1.0f, 1.773717656e+00f, 1.363021453e+00f, 5.782114722e-01f,
+                                1.393231313e-01f, 1.699321488e-02f}};
     const float Ss = fmaxf(Sz, 1e-30f);
-    const float rs = rsqrtf(Ss);
-    const float sd = Ss * rs;
-    const float alpha = mz * rs;
-    const float pdf = __expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
-    // Below alpha = -5 the erf form cancels to 0 in fp32; the reference uses the
-    // leading asymptotic term phi(alpha)/|alpha| there.
-    const float cdf =
-        alpha < -5.0f ? __fdividef(pdf, -alpha) : 0.5f * (1.0f + erff(alpha * kInvSqrt2));
-    const float mu = sd * pdf + mz * cdf;
-    const float v = -mu * mu + 2.0f * mu * mz - mz * sd * pdf + (Ss - mz * mz) * cdf;
+    const float sd = sqrtf(Ss);
+    const float alpha = mz / sd;
+    const float pdf = expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
+    const float t = fminf(fabsf(alpha), 8.0f);
+    const float R = kR(t), u = kU(t), w = kW(t);
+    const float pu = pdf * u;
+    float mu, v, cdf;
+    if (alpha < 0.0f) {
+        cdf = pdf * R;
+        mu = sd * pu;
+        v = Ss * (pdf * fmaf(-pu, u, w));
+    } else {
+        cdf = fmaf(-pdf, R, 1.0f);
+        mu = fmaf(sd, pu, mz);
+        v = Ss * fmaf(-pdf, fmaf(pu, u, fmaf(2.0f * alpha, u, w)), 1.0f);
+    }
+    if (alpha < -5.0f) {
+        cdf = pdf / (-alpha);
+        mu = 0.0f;
+        v = Ss * cdf;
+    }
     ma = mu;
     Sa = fmaxf(v, 0.0f);
     J = cdf;

@@ -137,15 +137,18 @@ __device__ __forceinline__ void arrive_cluster(uint32_t addr) {
 
 // Test for completion of phase `parity` (default acquire semantics at CTA scope,
 // as for the other barriers of the pair); a waiting thread is suspended (it
-// takes no issue slots) until the phase completes or about kSuspendNs passed.
+// takes no issue slots) until the phase completes or about c_suspend_ns passed
+// (1 ms; tagi_set_wait_limit_ns shortens it together with the wait limit, so
+// that a test's short limit is reached).
 constexpr uint32_t kSuspendNs = 1000000;
+__constant__ uint32_t c_suspend_ns = kSuspendNs;
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(c_suspend_ns)
         : "memory");
     return ok != 0;
 }
@@ -1437,7 +1440,9 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
 
 extern "C" int tagi_set_wait_limit_ns(uint64_t ns) {
     const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : tagi::kTimeoutNs;
+    const uint32_t hint = static_cast<uint32_t>(v < tagi::kSuspendNs ? v : tagi::kSuspendNs);
     cudaError_t e = cudaMemcpyToSymbol(tagi::g_wait_limit_ns, &v, sizeof(v));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tagi::c_suspend_ns, &hint, sizeof(hint));
     if (e != cudaSuccess) {
         cudaGetLastError();
         tagi::set_error("tagi_set_wait_limit_ns: %s", cudaGetErrorString(e));

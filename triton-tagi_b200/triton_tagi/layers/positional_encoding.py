@@ -1,8 +1,12 @@
 """Fixed sinusoidal positional encoding (drop-in for
 triton_tagi/layers/positional_encoding.py): pe[t, d] = sin(t·f_d) for even d,
 cos(t·f_d) for odd d, f_d = 10000^(−d/E); added to the means only
-(tagi_positional_add), identity backward. The table is built once with torch
-device ops at construction."""
+(tagi_positional_add), identity backward. The table is built once at
+construction with the reference's torch operations on the host, in float32, and
+copied to the device: CUDA's pow, sin and cos differ from the host's in the last
+bit, and a one-bit difference of f_d becomes ~1e-5 in sin(t·f_d) at positions in
+the hundreds, so a device-built table would not reproduce the reference's
+host-built one."""
 
 from __future__ import annotations
 
@@ -17,11 +21,11 @@ class PositionalEncoding(Layer):
     def __init__(self, embed_dim: int, max_seq_len: int = 2048, device="cuda") -> None:
         self.embed_dim, self.max_seq_len = embed_dim, max_seq_len
         self.device = torch.device(device)
-        d = torch.arange(embed_dim, dtype=torch.float32, device=self.device)
-        pos = torch.arange(max_seq_len, dtype=torch.float32, device=self.device)
+        d = torch.arange(embed_dim, dtype=torch.float32)
+        pos = torch.arange(max_seq_len, dtype=torch.float32)
         angle = pos.unsqueeze(1) * (1.0 / torch.pow(10000.0, d / embed_dim)).unsqueeze(0)
-        even = (torch.arange(embed_dim, device=self.device) % 2 == 0).unsqueeze(0)
-        self.pe_cache = torch.where(even, torch.sin(angle), torch.cos(angle))
+        even = (torch.arange(embed_dim) % 2 == 0).unsqueeze(0)
+        self.pe_cache = torch.where(even, torch.sin(angle), torch.cos(angle)).to(self.device)
 
     def forward(self, ma: Tensor, Sa: Tensor) -> tuple[Tensor, Tensor]:
         check_cuda_f32(ma)
