@@ -705,9 +705,14 @@ def main():
     ap.add_argument("--no-graph", action="store_true",
                     help="mlp/cnn: run the steps eagerly instead of replaying a CUDA graph")
     ap.add_argument("--shape", default=None, help="swp workload: one 'M,K' shape (K = N)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch (default: the workload's configuration; smaller "
+                         "batches are for profiling captures only)")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="skip the MLP and sweep sub-records of the default line")
     args = ap.parse_args()
+    if args.batch is not None:
+        WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], batch=args.batch)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

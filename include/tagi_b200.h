@@ -55,7 +55,9 @@ int tagi_device_status(int reset);
  * that later calls with the default limit are correct. The waits for a CTA's
  * own in-flight copies and MMAs keep the 2 s limit whatever this is. Values
  * below 1 ms also shorten the suspend hint of every barrier test to the same
- * value (default 1 ms), so that the limit is reached. No reference
+ * value (default 1 ms), so that the limit is reached; values below 1000 also
+ * bound the number of failed tests of a wait (the device's global timer
+ * advances in steps coarser than a microsecond). No reference
  * counterpart (the reference's Triton kernels do not wait). */
 int tagi_set_wait_limit_ns(uint64_t ns);
 

@@ -42,7 +42,7 @@ def capped_update(m: Tensor, S: Tensor, dm: Tensor, dS: Tensor, cap: float):
 
 def innovation(y: Tensor, mu: Tensor, S: Tensor, sigma_v: float):
     """Dense output innovation — triton_tagi/update/observation.py:24-46 (kernel)
-    and 247-291 (wrapper; dense branch only)."""
+    and 119-163 (wrapper; dense branch only)."""
     Sy = S + sigma_v**2
     return (y - mu) / Sy, -1.0 / Sy
 
@@ -84,12 +84,20 @@ def relu_moments(mz: Tensor, Sz: Tensor):
     """Rectified-Gaussian moments and Jacobian — triton_tagi/layers/relu.py:63-86.
 
     Includes the reference's asymptotic branch Φ(α) ≈ φ(α)/|α| for α < −5.
+    The reference's moments jump at α = −5 (by ~α²/2 in the variance), so in a
+    float64 evaluation the branch is chosen where the reference's float32 α
+    falls (the inputs rounded to float32, α = μ/√S in correctly rounded float32
+    arithmetic, emulated in float64): elements within a rounding of the
+    threshold then take the reference's branch. Float32 inputs are unaffected
+    except that their branch test, too, uses the correctly rounded α.
     """
     Sz_safe = torch.clamp(Sz, min=1e-30)
     sd = torch.sqrt(Sz_safe)
     alpha = mz / sd
     pdf = torch.exp(-0.5 * alpha * alpha) * INV_SQRT_2PI
-    cdf = torch.where(alpha < -5.0, pdf / (-alpha), 0.5 * (1.0 + torch.erf(alpha * INV_SQRT_2)))
+    sd32 = torch.sqrt(torch.clamp(Sz.float(), min=1e-30).double()).float()
+    alpha32 = (mz.float().double() / sd32.double()).float()
+    cdf = torch.where(alpha32 < -5.0, pdf / (-alpha), 0.5 * (1.0 + torch.erf(alpha * INV_SQRT_2)))
     mu = sd * pdf + mz * cdf
     var = -mu * mu + 2.0 * mu * mz - mz * sd * pdf + (Sz_safe - mz * mz) * cdf
     return mu, torch.clamp(var, min=0.0), cdf

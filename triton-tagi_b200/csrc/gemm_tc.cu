@@ -163,10 +163,14 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, cons
                                             int code) {
     const unsigned long long t0 = globaltimer();
     const unsigned long long limit = *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
-    for (;;) {
+    // The global timer advances in steps of up to a microsecond or more, so a
+    // limit below 1 us (a test's) also counts failed tests: the wait gives up
+    // after `limit` of them.
+    const unsigned long long spins = limit < 1000ull ? limit : ~0ull;
+    for (unsigned long long spin = 0;; ++spin) {
         if (mbar_try(bar, parity)) return true;
         if (*ab.flag) return false;
-        if (globaltimer() - t0 > limit) {
+        if (globaltimer() - t0 > limit || spin >= spins) {
             *ab.flag = 1;
             asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ab.peer), "r"(1) : "memory");
             atomicCAS(&g_device_error, 0, code);
