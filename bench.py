@@ -53,6 +53,7 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 SIGMA_V = 0.05
+_NETS: list = []  # networks whose CUDA graphs are released before the process group
 WORKLOADS = {
     "r18": dict(batch=128, metric="TAGI ResNet-18 Sequential.step samples/sec"),
     "mlp": dict(batch=256, metric="TAGI MLP 784-256-128-10 Sequential.step samples/sec"),
@@ -279,6 +280,30 @@ class LaunchTimer:
         return fam, other
 
 
+class CollectiveTimer:
+    """CUDA events around the data-parallel reducer's collectives (its timer hook)."""
+
+    def __init__(self):
+        self.open, self.records = {}, []
+
+    def __call__(self, phase, what):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        if phase == "before":
+            self.open[what] = ev
+        else:
+            self.records.append((what, self.open.pop(what), ev))
+
+    def summary(self, steps: int) -> dict:
+        torch.cuda.synchronize()
+        out = {}
+        for what, a, b in self.records:
+            d = out.setdefault(what, {"calls_per_step": 0.0, "ms_per_step": 0.0})
+            d["calls_per_step"] += 1.0 / steps
+            d["ms_per_step"] += a.elapsed_time(b) / steps
+        return out
+
+
 def tf32_peak_tflops(device) -> float:
     """Burst cuBLAS TF32 throughput on an 8192³ GEMM: the median of 9 single
     launches timed with CUDA events after 3 warm-up launches (the best of a few
@@ -382,13 +407,16 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     B = WORKLOADS[args.workload]["batch"]
     torch.manual_seed(1234)
     # Steps of small networks are a few dozen short kernels: replay them from a
-    # CUDA graph (Sequential(cuda_graph=True); single GPU only).
-    graphed = args.workload in ("mlp", "cnn", "r18") and world == 1 and not args.no_graph
+    # CUDA graph (Sequential(cuda_graph=True)); with --dp-graph the data-parallel
+    # step, collectives included, is captured too.
+    graphed = args.workload in ("mlp", "cnn", "r18") and not args.no_graph and (
+        world == 1 or args.dp_graph)
     net = TT.Sequential(build_layers(args.workload, TT, dev), device=dev, cuda_graph=graphed)
+    _NETS.append(net)
     if world > 1:
         from triton_tagi.distributed import DataParallel
 
-        DataParallel(net)
+        DataParallel(net, capturable=args.dp_graph)
     x, y = make_batch(args.workload, B, 100 + rank, dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
 
@@ -428,15 +456,21 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     # every library call; the timed steps carry no events of their own).
     fam_steps = min(3, args.steps)
     net.cuda_graph = False
+    dp_timer = CollectiveTimer() if world > 1 else None
     for _ in range(fam_steps):
         flush.zero_()
         L.hook = timer
+        if dp_timer is not None:
+            net.reducer.timer = dp_timer
         net.step(x, y, SIGMA_V)
         L.hook = None
+        if dp_timer is not None:
+            net.reducer.timer = None
     net.cuda_graph = graphed
     torch.cuda.synchronize()
     barrier()
     fam, other = timer.summary()
+    dp_times = dp_timer.summary(fam_steps) if dp_timer is not None else None
 
     # end to end through the public API: pinned host inputs in, predictions out
     xh, yh = x.cpu().pin_memory(), y.cpu().pin_memory()
@@ -477,7 +511,8 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     sub = {}
     if not args.no_subrecords:
         if args.workload != "mlp":
-            sub["mlp"] = mlp_subrecord(dev, rank, world, args.steps, args.warmup, flush, barrier)
+            sub["mlp"] = mlp_subrecord(dev, rank, world, args.steps, args.warmup, flush, barrier,
+                                       args.dp_graph)
         if world == 1:
             row = sweep_rows([(8192, 4096)], dev, 5, 3, tf32)[0]
             sub["sweep_8192x4096"] = {k: row[k] for k in ("forward", "backward", "update")}
@@ -529,6 +564,12 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
                   "hbm_gbs": peaks.get("hbm_gbs"), "bf16_tflops": peaks.get("bf16_tflops")},
         "device_status": status,
         **({"replicas_bit_identical": replicas} if replicas is not None else {}),
+        # data-parallel collectives on the compute stream (CUDA events, rank 0,
+        # eager steps after the timed ones): SyncBN statistics all-reduces, the
+        # waits for the gradient buckets at the end of the backward (the part of
+        # their all-reduces not hidden behind the backward), the update from the
+        # reduced sums
+        **({"dp_collectives": dp_times} if dp_times is not None else {}),
         **({"subrecords": sub} if sub else {}),
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -556,18 +597,21 @@ def replica_check(net, dev, world: int) -> bool:
     return all(torch.equal(v, allv[0]) for v in allv)
 
 
-def mlp_subrecord(dev, rank: int, world: int, steps: int, warmup: int, flush, barrier) -> dict:
+def mlp_subrecord(dev, rank: int, world: int, steps: int, warmup: int, flush, barrier,
+                  dp_graph: bool = False) -> dict:
     """MLP 784-256-128-10 Sequential.step, batch 256 per GPU, at the run's number
     of GPUs (data parallel for N > 1), timed like the main workload."""
     import triton_tagi as TT
 
     B = WORKLOADS["mlp"]["batch"]
     torch.manual_seed(4321)
-    net = TT.Sequential(build_layers("mlp", TT, dev), device=dev, cuda_graph=world == 1)
+    graphed = world == 1 or dp_graph
+    net = TT.Sequential(build_layers("mlp", TT, dev), device=dev, cuda_graph=graphed)
+    _NETS.append(net)
     if world > 1:
         from triton_tagi.distributed import DataParallel
 
-        DataParallel(net)
+        DataParallel(net, capturable=dp_graph)
     x, y = make_batch("mlp", B, 300 + rank, dev)
     for _ in range(max(3, warmup)):
         net.step(x, y, SIGMA_V)
@@ -589,7 +633,7 @@ def mlp_subrecord(dev, rank: int, world: int, steps: int, warmup: int, flush, ba
         t = tt.item()
     return {"metric": WORKLOADS["mlp"]["metric"], "value": steps * B * world / t,
             "unit": "samples/s", "ms_per_step": 1e3 * t / steps, "batch_per_gpu": B,
-            "global_batch": B * world, "steps": steps, "cuda_graph": world == 1,
+            "global_batch": B * world, "steps": steps, "cuda_graph": graphed,
             "l2": "flushed between steps"}
 
 
@@ -708,6 +752,9 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch (default: the workload's configuration; smaller "
                          "batches are for profiling captures only)")
+    ap.add_argument("--dp-graph", action="store_true",
+                    help="N > 1: capture the data-parallel step (with its NCCL collectives) "
+                         "in a CUDA graph")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="skip the MLP and sweep sub-records of the default line")
     args = ap.parse_args()
@@ -730,6 +777,14 @@ def main():
     try:
         our_arm(args, rank, world, local)
     finally:
+        # graphs that hold NCCL calls go before the process group does
+        for n in _NETS:
+            n.release_graph()
+        _NETS.clear()
+        import gc
+
+        gc.collect()
+        torch.cuda.synchronize()
         if world > 1:
             dist.destroy_process_group()
 

@@ -143,7 +143,7 @@ def _data(batch=12):
     return x, y
 
 
-def _worker(rank, world, init, out_q):
+def _worker(rank, world, init, out_q, bucket_bytes=4 << 20, steps=2):
     import datetime
 
     dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world,
@@ -155,12 +155,14 @@ def _worker(rank, world, init, out_q):
         # Sequential.step calls the CUDA innovation kernel; use the oracle's on CPU.
         net_mod.compute_innovation = lambda y, mu, var, sv: F.innovation(y, mu, var, sv)
         net = net_mod.Sequential(_make_net(0), device="cpu")
-        dp = DataParallel(net, broadcast_from=0)
+        dp = DataParallel(net, broadcast_from=0, bucket_bytes=bucket_bytes)
         x, y = _data()
         shard = x.shape[0] // world
         sl = slice(rank * shard, (rank + 1) * shard)
-        for _ in range(2):
+        for _ in range(steps):
             dp.step(x[sl], y[sl], 0.05)
+        if steps > 1:  # buckets planned after the first step
+            assert dp._plan_ok and len(dp._buckets) >= 1
         # numpy arrays travel by value: a torch tensor would travel as a shared-memory
         # handle that is gone if this process exits before the parent receives it
         out_q.put((rank, [t.clone().numpy() for l in net.leaves() for t in (l.mw, l.Sw, l.mb, l.Sb)]))
@@ -168,8 +170,8 @@ def _worker(rank, world, init, out_q):
         dist.destroy_process_group()
 
 
-def _single_process_reference():
-    """Two full-batch steps with the plain oracle (same maths, no sharding)."""
+def _single_process_reference(steps=2):
+    """Full-batch steps with the plain oracle (same maths, no sharding)."""
     layers = _make_net(0)
     x, y = _data()
 
@@ -194,7 +196,7 @@ def _single_process_reference():
                 layer._apply_sums(self.bufs[id(layer)], cap)
 
     red = Red()
-    for _ in range(2):
+    for _ in range(steps):
         m, S = x, torch.zeros_like(x)
         for layer in layers:
             m, S = layer.forward(m, S)
@@ -210,11 +212,17 @@ def _single_process_reference():
     return [t for l in layers if hasattr(l, "_apply_sums") for t in (l.mw, l.Sw, l.mb, l.Sb)]
 
 
-def test_two_rank_step_equals_full_batch_step():
+@pytest.mark.parametrize("bucket_bytes,steps", [(4 << 20, 2), (600, 3)])
+def test_two_rank_step_equals_full_batch_step(bucket_bytes, steps):
+    """Two ranks, each half of the batch, equal the full-batch step; the first
+    step all-reduces every layer's buffer on its own, later steps go through
+    the buckets (one bucket per dtype, or with 600-byte buckets one per layer
+    group that fits)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     init = _rendezvous()
-    procs = [ctx.Process(target=_worker, args=(r, 2, init, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, init, q, bucket_bytes, steps))
+             for r in range(2)]
     for p in procs:
         p.start()
     results = {r: [torch.from_numpy(a) for a in arrs]
@@ -222,7 +230,7 @@ def test_two_rank_step_equals_full_batch_step():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    ref = _single_process_reference()
+    ref = _single_process_reference(steps)
     for r in (0, 1):
         for got, want in zip(results[r], ref):
             torch.testing.assert_close(got, want, rtol=2e-5, atol=1e-7)

@@ -15,6 +15,21 @@ data-parallel step only has to combine those sums:
   so all replicas stay bit-identical and equal the single-batch closed form
   up to float summation order.
 
+Buckets: the first step records the order (and dtype) in which the layers
+request their sum buffers, which is the order in which they become ready.
+From then on every buffer is a view into a flat bucket of at most
+``bucket_bytes`` (one dtype per bucket; a larger buffer is a bucket of its
+own), and one all-reduce is issued per bucket when its last layer is ready:
+the 20 BatchNorm γ/β buffers of a ResNet-18 (a few KB each, float64) travel
+as one message instead of twenty, and the small convolutions of the early
+stages are grouped the same way.
+
+``timer`` (optional): a callable ``timer(phase, what)`` with phase "before" /
+"after" around each SyncBN statistics all-reduce (what = "syncbn"), each wait
+for a bucket's all-reduce at the end of the backward ("grad_wait") and the
+application of the reduced sums ("apply"); the benchmark records CUDA events
+there.
+
 Only ``torch.distributed`` collectives are used, so the same code runs on
 ``nccl`` (GPU) and ``gloo`` (CPU tests).
 """
@@ -29,15 +44,30 @@ class DataParallel:
     """Attach to a ``Sequential``; ``net.step`` then runs data-parallel."""
 
     def __init__(self, net, process_group=None, sync_bn: bool = True,
-                 broadcast_from: int | None = 0) -> None:
+                 broadcast_from: int | None = 0, bucket_bytes: int = 4 << 20,
+                 capturable: bool = False) -> None:
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed must be initialised before DataParallel")
+        if capturable and dist.get_backend(process_group) != "nccl":
+            raise ValueError("DataParallel(capturable=True) needs the nccl backend")
+        # Sequential(cuda_graph=True) may capture the data-parallel step (with its
+        # collectives) into a CUDA graph; release it (net.release_graph()) before
+        # the process group is destroyed.
+        self.capturable = capturable
         self.net = net
         self.group = process_group
         self.world_size = dist.get_world_size(process_group)
         self.rank = dist.get_rank(process_group)
-        self._buffers: dict[int, torch.Tensor] = {}
-        self._pending: list[tuple[object, torch.Tensor, object]] = []
+        self.bucket_bytes = bucket_bytes
+        self.timer = None
+        self._buffers: dict[int, torch.Tensor] = {}  # layer -> its own buffer (first step)
+        self._order: list[tuple] = []                # (key, layer, numel, dtype, device)
+        self._views: dict[int, torch.Tensor] = {}    # layer -> view into a bucket
+        self._bucket_of: dict[int, int] = {}
+        self._buckets: list[dict] = []               # flat tensor + member layers
+        self._pending: list[tuple[list, torch.Tensor, object]] = []
+        self._left: list[int] = []
+        self._plan_ok = False
         net.reducer = self
         if sync_bn:
             for leaf in net.leaves():
@@ -59,33 +89,98 @@ class DataParallel:
                         setattr(leaf, name, t)
                     dist.broadcast(t, src=src, group=self.group)
 
+    def _time(self, phase: str, what: str) -> None:
+        if self.timer is not None:
+            self.timer(phase, what)
+
     def allreduce_now(self, t: torch.Tensor) -> None:
         """Blocking (stream-ordered) sum over ranks, used for SyncBN statistics."""
+        self._time("before", "syncbn")
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        self._time("after", "syncbn")
 
     # -- reducer protocol used by the layers and Sequential.step ----------------
     def begin_step(self) -> None:
         self._pending = []
+        self._order = []
+        self._left = [len(b["layers"]) for b in self._buckets]
 
     def buffer(self, layer, numel: int, dtype: torch.dtype) -> torch.Tensor:
         key = id(layer)
-        buf = self._buffers.get(key)
         device = layer.mw.device
+        self._order.append((key, layer, numel, dtype, device))
+        view = self._views.get(key) if self._plan_ok else None
+        if view is not None and view.numel() == numel and view.dtype == dtype \
+                and view.device == device:
+            return view
+        self._plan_ok = False  # a new layer or a new size: plan again after this step
+        buf = self._buffers.get(key)
         if buf is None or buf.numel() != numel or buf.dtype != dtype or buf.device != device:
             buf = torch.empty(numel, dtype=dtype, device=device)
             self._buffers[key] = buf
         return buf
 
+    def _issue(self, layers: list, flat: torch.Tensor) -> None:
+        work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        self._pending.append((layers, flat, work))
+
     def ready(self, layer) -> None:
-        buf = self._buffers[id(layer)]
-        work = dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
-        self._pending.append((layer, buf, work))
+        key = id(layer)
+        if self._plan_ok and key in self._bucket_of:
+            b = self._bucket_of[key]
+            self._left[b] -= 1
+            if self._left[b] == 0:
+                bucket = self._buckets[b]
+                self._issue(bucket["layers"], bucket["flat"])
+            return
+        self._issue([layer], self._buffers[key])
 
     def finish_step(self, cap: float) -> None:
-        for layer, buf, work in self._pending:
+        if self._plan_ok and any(n != 0 for n in self._left):
+            raise RuntimeError("DataParallel: a bucket's layers did not all report ready")
+        for _, _, work in self._pending:
+            self._time("before", "grad_wait")
             work.wait()
-            layer._apply_sums(buf, cap)
+            self._time("after", "grad_wait")
+        self._time("before", "apply")
+        for layers, _, _ in self._pending:
+            for layer in layers:
+                key = id(layer)
+                buf = self._views[key] if self._plan_ok and key in self._views \
+                    else self._buffers[key]
+                layer._apply_sums(buf, cap)
+        self._time("after", "apply")
         self._pending = []
+        if not self._plan_ok:
+            self._plan()
+
+    def _plan(self) -> None:
+        """Group this step's buffers, in the order they were requested, into
+        buckets of one dtype and at most ``bucket_bytes`` each; a bucket's
+        members keep the order in which they become ready."""
+        self._buckets, self._views, self._bucket_of = [], {}, {}
+        open_by: dict = {}
+        align = 64  # elements: every view starts 256-byte aligned
+        groups: list[dict] = []
+        for key, layer, numel, dtype, device in self._order:
+            esize = torch.empty((), dtype=dtype).element_size()
+            size = (numel + align - 1) // align * align
+            g = open_by.get((dtype, device))
+            if g is None or (g["elems"] + size) * esize > self.bucket_bytes:
+                g = {"dtype": dtype, "device": device, "members": [], "elems": 0}
+                groups.append(g)
+                open_by[(dtype, device)] = g
+            g["members"].append((key, layer, numel, g["elems"]))
+            g["elems"] += size
+        for i, g in enumerate(groups):
+            flat = torch.zeros(g["elems"], dtype=g["dtype"], device=g["device"])
+            self._buckets.append({"flat": flat,
+                                  "layers": [layer for _, layer, _, _ in g["members"]]})
+            for key, _, numel, off in g["members"]:
+                self._views[key] = flat[off:off + numel]
+                self._bucket_of[key] = i
+        self._buffers = {}
+        self._plan_ok = True
 
     def step(self, x, y, sigma_v):
         return self.net.step(x, y, sigma_v)

@@ -20,7 +20,11 @@ new input shape (or σ_v) runs eagerly, the next one is captured on static input
 buffers and replayed, and later steps copy their inputs in and replay. A step
 of small layers is a few dozen short kernels, so launch overhead otherwise
 dominates it. The replayed kernels are the eager step's; returned predictions
-are copies. Not used under data parallelism (the step then runs eagerly). The
+are copies. Under data parallelism the step is captured only if the reducer
+says its collectives can be (``DataParallel(capturable=True)``, NCCL): the
+graph then holds the SyncBN and gradient all-reduces too, every rank replays
+the same graph, and the capture is thread-local so that the communicator's
+watchdog thread may keep polling; otherwise the step runs eagerly. The
 captured graph is keyed on the input shapes, σ_v, ``fuse_update`` and every
 layer's training flag, so ``train()`` / ``eval()`` lead to a new capture.
 
@@ -97,7 +101,9 @@ class Sequential:
         return forward_chain(self.layers, x, torch.zeros_like(x))
 
     def step(self, x_batch: Tensor, y_batch: Tensor, sigma_v: float) -> tuple[Tensor, Tensor]:
-        if self.cuda_graph and self.reducer is None and x_batch.is_cuda:
+        red = self.reducer
+        if self.cuda_graph and x_batch.is_cuda and (
+                red is None or getattr(red, "capturable", False)):
             out = self._graph_step(x_batch, y_batch, sigma_v)
         else:
             out = self._step(x_batch, y_batch, sigma_v)
@@ -131,7 +137,8 @@ class Sequential:
         if graph is None:
             sx, sy = x_batch.clone(), y_batch.clone()
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            mode = "thread_local" if self.reducer is not None else "global"
+            with torch.cuda.graph(graph, capture_error_mode=mode):
                 out = self._step(sx, sy, sigma_v)
             self._graph = (key, graph, sx, sy, out)
         else:
@@ -167,6 +174,11 @@ class Sequential:
             for layer in learn:
                 layer._set_param_mode("deltas")
         return y_pred_mu, y_pred_var
+
+    def release_graph(self) -> None:
+        """Drop the captured step (a graph that holds NCCL calls must be released
+        before the process group is destroyed)."""
+        self._graph = None
 
     def train(self) -> None:
         for layer in self.layers:
