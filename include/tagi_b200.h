@@ -390,6 +390,19 @@ int tagi_bn_train_forward(const float* mz, const float* Sz, float* mean, float* 
                           int64_t HW, int first, int preserve_var, float momentum, float eps,
                           void* stream);
 
+/* Data-parallel training forward after the statistics exchange: from the
+ * all-reduced channel sums (tagi_bn_channel_sums layout, `count` elements over
+ * all ranks) every channel is finalised as tagi_bn_finalize does and
+ * normalised as tagi_bn_train_forward does (residual stream add_m, add_S
+ * optional), in one launch. Replaces, for SyncBN, batchnorm2d.py:336-355 and
+ * 388-431 together with the shortcut add of resblock.py:138-154. */
+int tagi_bn_sync_forward(const float* mz, const float* Sz, const double* sums, double count,
+                         float* mean, float* var, float* running_mean, float* running_var,
+                         float* mg, const float* Sg, const float* mb, const float* Sb, float* ma,
+                         float* Sa, float* m_hat, const float* add_m, const float* add_S,
+                         int64_t N, int64_t C, int64_t HW, int first, int preserve_var,
+                         float momentum, float eps, void* stream);
+
 /* Delta propagation plus per-channel raw sums (float64)
  * grads[0:C]=sum dma*m_hat, [C:2C]=sum dSa*m_hat^2, [2C:3C]=sum dma, [3C:4C]=sum dSa.
  * relu_J (NULL: none): Jacobian of a ReLU that produced this layer's input;

@@ -539,3 +539,68 @@ def test_positional_encoding_add():
     assert torch.equal(om, ma + pe.pe_cache[:20]) and oS is Sa
     with pytest.raises(ValueError):
         pe.forward(g(rnd(gen, 2, 65, 48)), None)
+
+
+@pytest.mark.parametrize("N,C,H,W,first,residual", [(16, 64, 8, 8, True, False),
+                                                      (12, 32, 5, 5, False, True),
+                                                      (8, 128, 4, 4, True, True)])
+def test_bn_sync_forward_two_shards(N, C, H, W, first, residual):
+    """SyncBN on one GPU with two emulated ranks: each half of the batch forms
+    its channel sums, the sums are added (the all-reduce), and
+    tagi_bn_sync_forward finalises and normalises each half (residual added);
+    both halves together equal the oracle's BatchNorm forward on the whole
+    batch, and the running statistics follow the reference's init / EMA."""
+    from triton_tagi._lib import lib, stream
+
+    L = lib()
+    g = torch.Generator().manual_seed(N * C + H)
+    mz, Sz = torch.randn(N, C, H, W, generator=g) * 2 + 0.5, torch.rand(N, C, H, W, generator=g)
+    rm, rv = torch.randn(C, generator=g), torch.rand(C, generator=g) + 0.5
+    mg, Sg = torch.rand(C, generator=g) + 0.5, torch.rand(C, generator=g) * 0.1
+    mb, Sb = torch.randn(C, generator=g) * 0.1, torch.rand(C, generator=g) * 0.1
+    add_m, add_S = torch.randn(N, C, H, W, generator=g), torch.rand(N, C, H, W, generator=g)
+    eps, mom = 1e-5, 0.1
+    halves = [slice(0, N // 2), slice(N // 2, N)]
+    d = {k: v.to(DEV) for k, v in dict(mz=mz, Sz=Sz, add_m=add_m, add_S=add_S).items()}
+    sums = torch.zeros(3 * C, dtype=torch.float64, device=DEV)
+    for h in halves:
+        part = torch.empty(3 * C, dtype=torch.float64, device=DEV)
+        m_h, S_h = d["mz"][h].contiguous(), d["Sz"][h].contiguous()
+        L("tagi_bn_channel_sums", m_h.data_ptr(), S_h.data_ptr(), part.data_ptr(), N // 2, C,
+          H * W, stream(m_h))
+        sums += part
+    outs = []
+    for h in halves:
+        prm = [t.clone().to(DEV) for t in (rm, rv, mg, Sg, mb, Sb)]
+        mean, var = torch.empty(C, device=DEV), torch.empty(C, device=DEV)
+        m_h, S_h = d["mz"][h].contiguous(), d["Sz"][h].contiguous()
+        a_m = d["add_m"][h].contiguous() if residual else None
+        a_S = d["add_S"][h].contiguous() if residual else None
+        ma, Sa, mh = (torch.empty_like(m_h) for _ in range(3))
+        L("tagi_bn_sync_forward", m_h.data_ptr(), S_h.data_ptr(), sums.data_ptr(),
+          float(N * H * W), mean.data_ptr(), var.data_ptr(), prm[0].data_ptr(), prm[1].data_ptr(),
+          prm[2].data_ptr(), prm[3].data_ptr(), prm[4].data_ptr(), prm[5].data_ptr(),
+          ma.data_ptr(), Sa.data_ptr(), mh.data_ptr(),
+          a_m.data_ptr() if residual else None, a_S.data_ptr() if residual else None,
+          N // 2, C, H * W, 1 if first else 0, 1, mom, eps, stream(m_h))
+        outs.append((ma, Sa, mean, var, prm))
+    torch.cuda.synchronize()
+    e_mean, e_var = F.bn_batch_stats(mz.double(), Sz.double())
+    g_ref = torch.sqrt(e_var + eps) if first else mg.double()
+    e_ma, e_Sa, _, _ = F.bn_forward(mz.double(), Sz.double(), e_mean, e_var, g_ref, Sg.double(),
+                                    mb.double(), Sb.double(), eps)
+    if residual:
+        e_ma, e_Sa = e_ma + add_m.double(), e_Sa + add_S.double()
+    got_m = torch.cat([o[0].cpu() for o in outs])
+    got_S = torch.cat([o[1].cpu() for o in outs])
+    assert_rel(got_m, e_ma, MEAN_RTOL, "ma")
+    assert_rel(got_S, e_Sa, VAR_RTOL, "Sa")
+    e_rm = e_mean if first else (1 - mom) * rm.double() + mom * e_mean
+    e_rv = e_var if first else (1 - mom) * rv.double() + mom * e_var
+    for ma, Sa, mean, var, prm in outs:  # every shard finalises the same statistics
+        assert_rel(mean, e_mean, MEAN_RTOL, "mean")
+        assert_rel(var, e_var, VAR_RTOL, "var")
+        assert_rel(prm[0], e_rm, MEAN_RTOL, "running mean")
+        assert_rel(prm[1], e_rv, VAR_RTOL, "running var")
+        assert_rel(prm[2], g_ref, MEAN_RTOL, "gamma")
+    assert torch.equal(outs[0][2], outs[1][2]) and torch.equal(outs[0][3], outs[1][3])

@@ -313,6 +313,76 @@ __global__ void bn_forward_v4_kernel(const float4* mz, const float4* Sz, const f
     }
 }
 
+// The normalised affine of the elements of one channel slab (batchnorm2d.py:
+// 59-126), 4 at a time when V4, with an optional residual stream added to the
+// outputs; mean mu, variance rs and scale g of the channel given.
+template <bool V4>
+__device__ __forceinline__ void bn_normalize(const ChanSlab& sl, const float* mz, const float* Sz,
+                                             float mu, float rs, float g, float sg, float b,
+                                             float sb, float* ma, float* Sa, float* mhat,
+                                             const float* add_m, const float* add_S, int total,
+                                             int HW4, int HW, float eps) {
+    const float inv_std = 1.0f / sqrtf(rs + eps);
+    const float inv_var = 1.0f / (rs + eps);
+    auto off4 = [&](int t) {
+        const int li = t / HW4;
+        return sl.offset(li, (t - li * HW4) * 4);
+    };
+    for (int t = threadIdx.x; V4 && t < total; t += 2 * blockDim.x) {
+        const int t1 = t + blockDim.x;
+        const bool two = t1 < total;
+        const int64_t o[2] = {off4(t), two ? off4(t1) : off4(t)};
+        float4 m[2], S[2], am[2], aS[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            m[u] = __ldg(reinterpret_cast<const float4*>(mz + o[u]));
+            S[u] = __ldg(reinterpret_cast<const float4*>(Sz + o[u]));
+            if (add_m) {  // a residual stream added to the outputs
+                am[u] = __ldg(reinterpret_cast<const float4*>(add_m + o[u]));
+                aS[u] = __ldg(reinterpret_cast<const float4*>(add_S + o[u]));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (u == 1 && !two) break;
+            const float mv[4] = {m[u].x, m[u].y, m[u].z, m[u].w};
+            const float Sv[4] = {S[u].x, S[u].y, S[u].z, S[u].w};
+            float om[4], oS[4], mh[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                mh[e] = (mv[e] - mu) * inv_std;
+                const float Sh = Sv[e] * inv_var;
+                om[e] = g * mh[e] + b;
+                oS[e] = g * g * Sh + sg * mh[e] * mh[e] + sg * Sh + sb;
+            }
+            if (add_m) {
+                om[0] += am[u].x; om[1] += am[u].y; om[2] += am[u].z; om[3] += am[u].w;
+                oS[0] += aS[u].x; oS[1] += aS[u].y; oS[2] += aS[u].z; oS[3] += aS[u].w;
+            }
+            *reinterpret_cast<float4*>(ma + o[u]) = make_float4(om[0], om[1], om[2], om[3]);
+            *reinterpret_cast<float4*>(Sa + o[u]) = make_float4(oS[0], oS[1], oS[2], oS[3]);
+            *reinterpret_cast<float4*>(mhat + o[u]) = make_float4(mh[0], mh[1], mh[2], mh[3]);
+        }
+    }
+    for (int t = threadIdx.x; !V4 && t < total; t += blockDim.x) {
+        {
+            const int li = t / HW;
+            const int64_t o = sl.offset(li, t - li * HW);
+            const float m_hat = (mz[o] - mu) * inv_std;
+            const float S_hat = Sz[o] * inv_var;
+            float om = g * m_hat + b;
+            float oS = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
+            if (add_m) {
+                om += add_m[o];
+                oS += add_S[o];
+            }
+            ma[o] = om;
+            Sa[o] = oS;
+            mhat[o] = m_hat;
+        }
+    }
+}
+
 // Training-mode forward in one launch (single process: no all-reduce between
 // the passes): each channel's cluster sums its planes as bn_sums_kernel, rank 0
 // finalises the statistics as bn_finalize_kernel (running statistics, the
@@ -400,63 +470,49 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     }
     cluster.sync();
     const int c = sl.c;
-    const float mu = stat[0], rs = stat[1], g = stat[2];
-    const float inv_std = 1.0f / sqrtf(rs + eps);
-    const float inv_var = 1.0f / (rs + eps);
-    const float sg = Sg[c], b = mb[c], sb = Sb[c];
-    for (int t = threadIdx.x; V4 && t < total; t += 2 * blockDim.x) {
-        const int t1 = t + blockDim.x;
-        const bool two = t1 < total;
-        const int64_t o[2] = {off4(t), two ? off4(t1) : off4(t)};
-        float4 m[2], S[2], am[2], aS[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            m[u] = __ldg(reinterpret_cast<const float4*>(mz + o[u]));
-            S[u] = __ldg(reinterpret_cast<const float4*>(Sz + o[u]));
-            if (add_m) {  // a residual stream added to the outputs
-                am[u] = __ldg(reinterpret_cast<const float4*>(add_m + o[u]));
-                aS[u] = __ldg(reinterpret_cast<const float4*>(add_S + o[u]));
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            if (u == 1 && !two) break;
-            const float mv[4] = {m[u].x, m[u].y, m[u].z, m[u].w};
-            const float Sv[4] = {S[u].x, S[u].y, S[u].z, S[u].w};
-            float om[4], oS[4], mh[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                mh[e] = (mv[e] - mu) * inv_std;
-                const float Sh = Sv[e] * inv_var;
-                om[e] = g * mh[e] + b;
-                oS[e] = g * g * Sh + sg * mh[e] * mh[e] + sg * Sh + sb;
-            }
-            if (add_m) {
-                om[0] += am[u].x; om[1] += am[u].y; om[2] += am[u].z; om[3] += am[u].w;
-                oS[0] += aS[u].x; oS[1] += aS[u].y; oS[2] += aS[u].z; oS[3] += aS[u].w;
-            }
-            *reinterpret_cast<float4*>(ma + o[u]) = make_float4(om[0], om[1], om[2], om[3]);
-            *reinterpret_cast<float4*>(Sa + o[u]) = make_float4(oS[0], oS[1], oS[2], oS[3]);
-            *reinterpret_cast<float4*>(mhat + o[u]) = make_float4(mh[0], mh[1], mh[2], mh[3]);
-        }
-    }
-    for (int t = threadIdx.x; !V4 && t < total; t += blockDim.x) {
-        {
-            const int li = t / HW;
-            const int64_t o = sl.offset(li, t - li * HW);
-            const float m_hat = (mz[o] - mu) * inv_std;
-            const float S_hat = Sz[o] * inv_var;
-            float om = g * m_hat + b;
-            float oS = g * g * S_hat + sg * m_hat * m_hat + sg * S_hat + sb;
-            if (add_m) {
-                om += add_m[o];
-                oS += add_S[o];
-            }
-            ma[o] = om;
-            Sa[o] = oS;
-            mhat[o] = m_hat;
+    bn_normalize<V4>(sl, mz, Sz, stat[0], stat[1], stat[2], Sg[c], mb[c], Sb[c], ma, Sa, mhat,
+                     add_m, add_S, total, HW4, HW, eps);
+}
+
+// Data-parallel training forward after the statistics exchange: `sums` holds
+// the all-reduced [sum mz, sum Sz, sum mz^2] of every channel (the layout of
+// bn_sums_kernel) over `count` elements. Every block finalises its channel with
+// the arithmetic of bn_finalize_kernel (block 0 of the channel also writes the
+// statistics, the running statistics and the first-call scale) and normalises
+// its slab as bn_train_forward_kernel does, residual stream included: one
+// launch in place of finalise, normalise and add.
+template <bool V4>
+__global__ void __launch_bounds__(kBnThreads) bn_sync_forward_kernel(
+    const float* mz, const float* Sz, const double* sums, double count, float* mean, float* var,
+    float* rmean, float* rvar, float* mg, const float* Sg, const float* mb, const float* Sb,
+    float* ma, float* Sa, float* mhat, const float* add_m, const float* add_S, int N, int C,
+    int HW, int first, int preserve_var, float momentum, float one_minus, float eps) {
+    const ChanSlab sl(N, C, HW, blockIdx.y);
+    const int c = sl.c;
+    const float m = static_cast<float>(sums[c] / count);
+    const float mS = static_cast<float>(sums[C + c] / count);
+    const float msq = static_cast<float>(sums[2 * C + c] / count);
+    const float bessel = static_cast<float>(count / (count - 1.0));
+    const float vv = (mS + msq - m * m) * bessel;
+    // the first call with preserve_var sets the scale; otherwise it is read
+    // (no block writes it then)
+    const float g = (first && preserve_var) ? sqrtf(vv + eps) : mg[c];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        mean[c] = m;
+        var[c] = vv;
+        if (first) {
+            rmean[c] = m;
+            rvar[c] = vv;
+            if (preserve_var) mg[c] = g;
+        } else {
+            rmean[c] = one_minus * rmean[c] + momentum * m;
+            rvar[c] = one_minus * rvar[c] + momentum * vv;
         }
     }
+    const int HW4 = HW / 4;
+    const int total = V4 ? sl.nimg * HW4 : sl.nimg * HW;
+    bn_normalize<V4>(sl, mz, Sz, m, vv, g, Sg[c], mb[c], Sb[c], ma, Sa, mhat, add_m, add_S,
+                     total, HW4, HW, eps);
 }
 
 __global__ void bn_apply_kernel(const double* grads, int C, int mode, float* mw, float* Sw,
@@ -635,6 +691,46 @@ extern "C" int tagi_bn_train_forward(const float* mz, const float* Sz, float* me
                                mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
                                Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
                                preserve_var, momentum, one_minus, eps);
+}
+
+extern "C" int tagi_bn_sync_forward(const float* mz, const float* Sz, const double* sums,
+                                    double count, float* mean, float* var, float* running_mean,
+                                    float* running_var, float* mg, const float* Sg,
+                                    const float* mb, const float* Sb, float* ma, float* Sa,
+                                    float* m_hat, const float* add_m, const float* add_S,
+                                    int64_t N, int64_t C, int64_t HW, int first,
+                                    int preserve_var, float momentum, float eps, void* stream) {
+    const char* what = "tagi_bn_sync_forward";
+    TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535, TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (C == 0 || N * HW == 0) return TAGI_OK;
+    TAGI_REQUIRE(count > 1.0, TAGI_E_BAD_ARG, "%s: need count > 1", what);
+    TAGI_REQUIRE(mz && Sz && sums && mean && var && running_mean && running_var && mg && Sg &&
+                     mb && Sb && ma && Sa && m_hat,
+                 TAGI_E_BAD_ARG, "%s: null pointer", what);
+    TAGI_REQUIRE((add_m == nullptr) == (add_S == nullptr), TAGI_E_BAD_ARG,
+                 "%s: give both residual planes or neither", what);
+    TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    // about 4 blocks per SM in all, each a run of whole images of one channel
+    int64_t S = (4 * kNumSMs + C - 1) / C;
+    S = S < 1 ? 1 : (S > N ? N : S);
+    const uintptr_t al = reinterpret_cast<uintptr_t>(mz) | reinterpret_cast<uintptr_t>(Sz) |
+                         reinterpret_cast<uintptr_t>(ma) | reinterpret_cast<uintptr_t>(Sa) |
+                         reinterpret_cast<uintptr_t>(m_hat) | reinterpret_cast<uintptr_t>(add_m) |
+                         reinterpret_cast<uintptr_t>(add_S);
+    const bool v4 = HW % 4 == 0 && (al & 15) == 0;
+    const float one_minus = static_cast<float>(1.0 - static_cast<double>(momentum));
+    const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(C));
+    if (v4)
+        bn_sync_forward_kernel<true><<<grid, kBnThreads, 0, as_stream(stream)>>>(
+            mz, Sz, sums, count, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma, Sa,
+            m_hat, add_m, add_S, (int)N, (int)C, (int)HW, first, preserve_var, momentum, one_minus,
+            eps);
+    else
+        bn_sync_forward_kernel<false><<<grid, kBnThreads, 0, as_stream(stream)>>>(
+            mz, Sz, sums, count, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma, Sa,
+            m_hat, add_m, add_S, (int)N, (int)C, (int)HW, first, preserve_var, momentum, one_minus,
+            eps);
+    return check_launch(what);
 }
 
 extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat,

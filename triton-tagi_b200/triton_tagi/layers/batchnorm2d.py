@@ -96,19 +96,29 @@ class BatchNorm2D(LearnableLayer):
             self._norm_mean, self._norm_var = mean, var
             return ma, Sa
         if self.training:
+            # SyncBN: channel sums, all-reduced, then one launch that finalises
+            # the statistics and normalises (residual added)
             sums = torch.empty(3 * C, device=dev, dtype=torch.float64)
             L("tagi_bn_channel_sums", mz.data_ptr(), Sz.data_ptr(), sums.data_ptr(), N, C, HW, st)
-            count = float(N * HW)
-            if self._stats_allreduce is not None:
-                self._stats_allreduce(sums)
-                count *= self._stats_world
+            self._stats_allreduce(sums)
+            count = float(N * HW) * self._stats_world
             mean = torch.empty(C, device=dev)
             var = torch.empty(C, device=dev)
-            L("tagi_bn_finalize", sums.data_ptr(), C, count, mean.data_ptr(), var.data_ptr(),
-              self.running_mean.data_ptr(), self.running_var.data_ptr(), self.mw.data_ptr(),
+            ma = torch.empty_like(mz)
+            Sa = torch.empty_like(Sz)
+            self.m_hat = torch.empty_like(mz)
+            self.S_hat = None
+            L("tagi_bn_sync_forward", mz.data_ptr(), Sz.data_ptr(), sums.data_ptr(), count,
+              mean.data_ptr(), var.data_ptr(), self.running_mean.data_ptr(),
+              self.running_var.data_ptr(), self.mw.data_ptr(), self.Sw.data_ptr(),
+              self.mb.data_ptr(), self.Sb.data_ptr(), ma.data_ptr(), Sa.data_ptr(),
+              self.m_hat.data_ptr(), residual[0].data_ptr() if residual is not None else None,
+              residual[1].data_ptr() if residual is not None else None, N, C, HW,
               0 if self._is_initialized else 1, 1 if self.preserve_var else 0,
               float(self.momentum), float(self.eps), st)
             self._is_initialized = True
+            self._norm_mean, self._norm_var = mean, var
+            return ma, Sa
         else:
             mean, var = self.running_mean, self.running_var
         self._norm_mean, self._norm_var = mean, var
