@@ -59,7 +59,7 @@ _SIGS = {
     "tagi_bn_finalize": "p" + "i" + "d" + "ppppp" + "nn" + "ff" + "p",
     "tagi_bn_forward": "pppppppppppp" + "iii" + "f" + "p",
     "tagi_bn_train_forward": "ppppppppppppp" + "pp" + "iii" + "nn" + "ff" + "p",
-    "tagi_bn_sync_forward": "ppp" + "d" + "pppppppppppppp" + "iii" + "nn" + "ff" + "p",
+    "tagi_bn_sync_forward": "ppp" + "d" + "p" * 13 + "iii" + "nn" + "ff" + "p",
     "tagi_bn_backward": "ppppppp" + "pp" + "iii" + "f" + "ppp" + "f" + "p",
     "tagi_bn_apply_grads": "p" + "i" + "n" + "pppppppp" + "f" + "p",
     "tagi_rmsnorm_forward": "ppppppp" + "ii" + "f" + "p",
