@@ -55,9 +55,10 @@ int tagi_device_status(int reset);
  * that later calls with the default limit are correct. The waits for a CTA's
  * own in-flight copies and MMAs keep the 2 s limit whatever this is. Values
  * below 1 ms also shorten the suspend hint of every barrier test to the same
- * value (default 1 ms), so that the limit is reached; values below 1000 also
- * bound the number of failed tests of a wait (the device's global timer
- * advances in steps coarser than a microsecond). No reference
+ * value (default 1 ms), so that the limit is reached; values below 1000 make
+ * the barrier tests non-suspending and also bound the number of failed tests
+ * of a wait (the device's global timer advances in steps coarser than a
+ * microsecond, and a suspended test may outlast a short hint). No reference
  * counterpart (the reference's Triton kernels do not wait). */
 int tagi_set_wait_limit_ns(uint64_t ns);
 
@@ -249,6 +250,17 @@ int tagi_bmm_shared_right(const float* a_mean, const float* a_var, const float* 
                           int64_t sa_n, int64_t sa_m, int64_t sa_k, int64_t sb_n, int64_t sb_k,
                           int64_t sb_l, int64_t so_n, int64_t so_m, int64_t so_l, float scale,
                           void* stream);
+
+/* mean = scale * a @ b_mean, var = scale^2 * (a*a) @ b_var, batched like
+ * tagi_bmm_shared_right, with the deterministic operand on the left (its
+ * squares taken in the contraction). Replaces bmm_shared_left,
+ * triton_tagi/kernels/attention.py:339-374, without its transpose identity:
+ * the value deltas of attention, a = scores^T (a transposed view), run with
+ * the score rows as the output rows (M = S) instead of the head dimension. */
+int tagi_bmm_shared_left(const float* a, const float* b_mean, const float* b_var, float* mean,
+                         float* var, int64_t batch, int64_t M, int64_t L, int64_t K, int64_t sa_n,
+                         int64_t sa_m, int64_t sa_k, int64_t sb_n, int64_t sb_k, int64_t sb_l,
+                         int64_t so_n, int64_t so_m, int64_t so_l, float scale, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Elementwise / row kernels

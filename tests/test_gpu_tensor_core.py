@@ -248,6 +248,11 @@ def test_batched_attention_products():
     rm, rv = F.bmm_shared_left(tr(dm.double()), mk.double(), Sk.double())
     assert_rel(m, rm, MEAN_RTOL, "shared left mean")
     assert_rel(v, rv, VAR_RTOL, "shared left var")
+    # left operand with contiguous rows: the 64-column tensor-memory tiles
+    m, v = bmm_shared_left(dm.to(DEV), mk.to(DEV), Sk.to(DEV), 0.5)
+    rm, rv = F.bmm_shared_left(dm.double(), mk.double(), Sk.double(), 0.5)
+    assert_rel(m, rm, MEAN_RTOL, "shared left mean (row-contiguous a)")
+    assert_rel(v, rv, VAR_RTOL, "shared left var (row-contiguous a)")
     _ok()
 
 

@@ -1079,6 +1079,32 @@ extern "C" int tagi_bmm_shared_right(const float* a_mean, const float* a_var, co
     return launch<RSQ, true, EPI_STORE>(g, (int)batch, as_stream(stream), what);
 }
 
+extern "C" int tagi_bmm_shared_left(const float* a, const float* b_mean, const float* b_var,
+                                    float* mean, float* var, int64_t batch, int64_t M, int64_t L,
+                                    int64_t K, int64_t sa_n, int64_t sa_m, int64_t sa_k,
+                                    int64_t sb_n, int64_t sb_k, int64_t sb_l, int64_t so_n,
+                                    int64_t so_m, int64_t so_l, float scale, void* stream) {
+    const char* what = "tagi_bmm_shared_left";
+    TAGI_REQUIRE(!bad_size(M) && !bad_size(L) && !bad_size(K) && batch >= 0 && batch <= 65535,
+                 TAGI_E_BAD_ARG, "%s: bad sizes", what);
+    if (batch == 0 || M == 0 || L == 0) return TAGI_OK;
+    TAGI_REQUIRE(mean && var && (K == 0 || (a && b_mean && b_var)), TAGI_E_BAD_ARG,
+                 "%s: null pointer", what);
+    GemmArgs g = blank();
+    g.x = a; g.arow = plain_rows(sa_m); g.ak = sa_k; g.a_bs = sa_n;
+    g.u = b_mean; g.v = b_var; g.brow = plain_rows(sb_k); g.bn = sb_l; g.b_bs = sb_n;
+    g.o0 = mean; g.o1 = var; g.orow = plain_rows(so_m); g.on = so_l; g.o_bs = so_n;
+    g.scale0 = scale; g.scale1 = scale * scale;
+    g.M = (int)M; g.N = (int)L; g.Kr = (int)K; g.kchunk = K > 0 ? (int)K : BK;
+    int bn = tc_pick(LSQ, g.M, g.N, g.Kr, (int)batch);
+    // Narrow tiles (<= 64 columns) stage A one row per thread in tensor memory,
+    // which needs each row's reduction elements contiguous; an A read down its
+    // columns (a transposed view, e.g. the attention scores in the value deltas)
+    // goes through 128-column tiles, whose producers stage MN-major A.
+    if (bn > 0 && bn <= 64 && sa_k != 1) bn = 128;
+    return launch<LSQ, true, EPI_STORE>(g, (int)batch, as_stream(stream), what, bn);
+}
+
 // ---- weight sums without a caller workspace ---------------------------------
 // The split-reduction partials of tagi_fused_weight_grad_static live in this
 // array of the device image (one copy per GPU that loads the library). Host code

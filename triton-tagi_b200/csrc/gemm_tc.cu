@@ -142,13 +142,25 @@ __device__ __forceinline__ void arrive_cluster(uint32_t addr) {
 // that a test's short limit is reached).
 constexpr uint32_t kSuspendNs = 1000000;
 __constant__ uint32_t c_suspend_ns = kSuspendNs;
+// A hint of 0 (set only by the test hook) tests without suspending at all: the
+// hardware may keep a suspended thread waiting longer than a short hint asks.
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
+    const uint32_t hint = c_suspend_ns;
+    if (hint == 0) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        return ok != 0;
+    }
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(c_suspend_ns)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint)
         : "memory");
     return ok != 0;
 }
@@ -1444,7 +1456,9 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
 
 extern "C" int tagi_set_wait_limit_ns(uint64_t ns) {
     const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : tagi::kTimeoutNs;
-    const uint32_t hint = static_cast<uint32_t>(v < tagi::kSuspendNs ? v : tagi::kSuspendNs);
+    // below 1 us: tests that do not suspend (see mbar_try)
+    const uint32_t hint =
+        v < 1000ull ? 0u : static_cast<uint32_t>(v < tagi::kSuspendNs ? v : tagi::kSuspendNs);
     cudaError_t e = cudaMemcpyToSymbol(tagi::g_wait_limit_ns, &v, sizeof(v));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(tagi::c_suspend_ns, &hint, sizeof(hint));
     if (e != cudaSuccess) {

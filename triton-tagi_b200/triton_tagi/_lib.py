@@ -41,6 +41,7 @@ _SIGS = {
     "tagi_apply_param_sums": "pp" + "ii" + "n" + "pppp" + "f" + "p",
     "tagi_bmm_tagi_var": "pppppp" + "iiii" + "iiiiiiiii" + "ff" + "p",
     "tagi_bmm_shared_right": "ppppp" + "iiii" + "iiiiiiiii" + "f" + "p",
+    "tagi_bmm_shared_left": "ppppp" + "iiii" + "iiiiiiiii" + "f" + "p",
     "tagi_capped_update": "pppp" + "i" + "f" + "p",
     "tagi_innovation": "ppppp" + "i" + "f" + "p",
     "tagi_relu_forward": "ppppp" + "i" + "p",

@@ -3,7 +3,8 @@
 Drop-in for triton_tagi/kernels/attention.py (bmm_tagi_var 149-201,
 bmm_shared_right 286-336, bmm_shared_left 339-374): same signatures, same
 stride rules (leading dims packed; ``transpose(-1, -2)`` views accepted
-without copies), computed by libtagi_b200.
+without copies), computed by libtagi_b200. ``bmm_shared_left`` returns
+contiguous tensors where the reference returns transposed views of them.
 """
 
 from __future__ import annotations
@@ -97,9 +98,26 @@ def bmm_shared_left(a: Tensor, b_mean: Tensor, b_var: Tensor,
                     scale: float = 1.0) -> tuple[Tensor, Tensor]:
     """mean = scale · a @ b_mean, var = scale² · a² @ b_var (a deterministic).
 
-    Same transpose identity as the reference (attention.py:364-374): the
-    shared-right kernel on (b_meanᵀ, b_varᵀ, aᵀ), outputs returned transposed.
+    The reference evaluates this through its shared-right kernel on
+    (b_meanᵀ, b_varᵀ, aᵀ) (attention.py:364-374); here one contraction squares
+    the left operand (tagi_bmm_shared_left), so the output rows are a's rows
+    (the S score rows of the attention value deltas, not the head dimension)
+    and the result comes back contiguous, not as a transposed view.
     """
-    mean_t, var_t = bmm_shared_right(b_mean.transpose(-1, -2), b_var.transpose(-1, -2),
-                                     a.transpose(-1, -2), scale=scale)
-    return mean_t.transpose(-1, -2), var_t.transpose(-1, -2)
+    check_cuda_f32(a, b_mean, b_var)
+    batch_shape = a.shape[:-2]
+    M, K = a.shape[-2:]
+    Kb, L = b_mean.shape[-2:]
+    if K != Kb:
+        raise ValueError(f"Reduction dims disagree: a has {K}, b has {Kb}")
+    a, b_mean, b_var = (_packed(t) for t in (a, b_mean, b_var))
+    if b_var.stride() != b_mean.stride():
+        b_mean, b_var = b_mean.contiguous(), b_var.contiguous()
+    N = _nbatch(batch_shape)
+    mean = torch.empty((*batch_shape, M, L), device=a.device, dtype=a.dtype)
+    var = torch.empty_like(mean)
+    lib()("tagi_bmm_shared_left", a.data_ptr(), b_mean.data_ptr(), b_var.data_ptr(),
+          mean.data_ptr(), var.data_ptr(), N, M, L, K, _batch_stride(a), a.stride(-2),
+          a.stride(-1), _batch_stride(b_mean), b_mean.stride(-2), b_mean.stride(-1),
+          _batch_stride(mean), mean.stride(-2), mean.stride(-1), scale, stream(a))
+    return mean, var
