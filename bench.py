@@ -589,7 +589,7 @@ def replica_check(net, dev, world: int) -> bool:
         for name in ("mw", "Sw", "mb", "Sb", "running_mean", "running_var"):
             t = getattr(leaf, name, None)
             if t is not None:
-                bits = t.detach().contiguous().view(torch.int32).to(torch.int64)
+                bits = t.detach().contiguous().view(torch.int32).reshape(-1).to(torch.int64)
                 acc[0] += bits.sum()
                 acc[1] += (bits * torch.arange(1, bits.numel() + 1, device=dev) % 1000003).sum()
     allv = [torch.empty_like(acc) for _ in range(world)]
