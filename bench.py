@@ -407,8 +407,8 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
     B = WORKLOADS[args.workload]["batch"]
     torch.manual_seed(1234)
     # Steps of small networks are a few dozen short kernels: replay them from a
-    # CUDA graph (Sequential(cuda_graph=True)); with --dp-graph the data-parallel
-    # step, collectives included, is captured too.
+    # CUDA graph (Sequential(cuda_graph=True)); the data-parallel step is captured
+    # with its NCCL collectives (--no-dp-graph: eager).
     graphed = args.workload in ("mlp", "cnn", "r18") and not args.no_graph and (
         world == 1 or args.dp_graph)
     net = TT.Sequential(build_layers(args.workload, TT, dev), device=dev, cuda_graph=graphed)
@@ -752,9 +752,9 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch (default: the workload's configuration; smaller "
                          "batches are for profiling captures only)")
-    ap.add_argument("--dp-graph", action="store_true",
-                    help="N > 1: capture the data-parallel step (with its NCCL collectives) "
-                         "in a CUDA graph")
+    ap.add_argument("--no-dp-graph", dest="dp_graph", action="store_false",
+                    help="N > 1: run the data-parallel step eagerly instead of replaying it "
+                         "(NCCL collectives included) from a CUDA graph")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="skip the MLP and sweep sub-records of the default line")
     args = ap.parse_args()
