@@ -780,6 +780,9 @@ def main():
         # graphs that hold NCCL calls go before the process group does
         for n in _NETS:
             n.release_graph()
+        for n in _NETS:  # peer exchange buffers (collective, same order on every rank)
+            if getattr(n, "reducer", None) is not None:
+                n.reducer.close()
         _NETS.clear()
         import gc
 

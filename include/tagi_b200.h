@@ -63,6 +63,35 @@ int tagi_device_status(int reset);
 int tagi_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------------------
+ * Small all-reduces over NVLink peer memory (data-parallel SyncBN statistics)
+ * ------------------------------------------------------------------------- */
+
+/* Bytes of one rank's exchange buffer for `world` ranks (at most 32) and
+ * vectors of at most max_elems doubles: 256 bytes of flags, then two parity
+ * sets of world slots. */
+size_t tagi_peer_buffer_bytes(int world, int64_t max_elems);
+/* Allocates and zeroes one rank's exchange buffer on the current device and
+ * writes its CUDA IPC handle (64 bytes) to ipc_handle; the other ranks open it
+ * with tagi_peer_buffer_open. */
+int tagi_peer_buffer_create(size_t bytes, void** ptr, void* ipc_handle);
+int tagi_peer_buffer_open(const void* ipc_handle, void** ptr);
+/* Frees an own buffer (own != 0) or unmaps a peer's. */
+int tagi_peer_buffer_close(void* ptr, int own);
+/* In place: data[0:n] <- the sum over ranks of every rank's data[0:n], added in
+ * rank order (bit-identical on every rank). peer_bufs: device array of the
+ * world buffer addresses as this rank sees them (its own at [rank]); counter:
+ * a device uint64 (zero at the start) that the kernel advances, so the launch
+ * may be replayed from a CUDA graph. Every rank must issue the same sequence
+ * of calls on buffers created together. Replaces, for the SyncBN statistics,
+ * the NCCL all-reduce of the host package (no reference counterpart: the
+ * reference is single-GPU). A wait that runs out (2 s, a rank that stopped)
+ * leaves data unreduced and sets the word read by tagi_peer_status. */
+int tagi_peer_allreduce_f64(double* data, int64_t n, void* const* peer_bufs, int rank, int world,
+                            int64_t max_elems, uint64_t* counter, void* stream);
+/* 0, or 1 if a peer exchange wait ran out; synchronises; `reset` clears it. */
+int tagi_peer_status(int reset);
+
+/* ---------------------------------------------------------------------------
  * Dense moment contractions
  * ------------------------------------------------------------------------- */
 

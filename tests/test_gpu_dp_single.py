@@ -4,7 +4,8 @@ With a single rank the all-reduces are identities, so a ``DataParallel``
 network must reproduce the plain single-GPU step: the parameter sums written
 for the reducer (bucketed after the first step) and applied after the
 backward, and BatchNorm's SyncBN path (channel sums, all-reduce,
-``tagi_bn_sync_forward``) instead of the one-launch cluster forward. The same
+``tagi_bn_sync_forward``, the sums exchanged through the NVLink peer-memory
+kernel, here with one rank) instead of the one-launch cluster forward. The same
 is checked with the data-parallel step captured in a CUDA graph
 (``capturable=True``), NCCL calls included. The graph is released before the
 process group is destroyed.
@@ -70,6 +71,11 @@ def test_one_rank_data_parallel_equals_plain_step(one_rank_group, graph):
                 else:
                     assert var_update_err(a, b, prev[i]) <= 1e-4, (step, i)
         assert dp._plan_ok and len(dp._buckets) > 1
+        assert dp.peer is not None  # the SyncBN sums went through the peer exchange
+        from triton_tagi._lib import lib
+
+        assert int(lib().fn["tagi_peer_status"](1)) == 0
     finally:
         net_d.release_graph()
         torch.cuda.synchronize()
+        dp.close()

@@ -72,8 +72,15 @@ _SIGS = {
     "tagi_kernel_launches": "",
     "tagi_device_status": "n",
     "tagi_set_wait_limit_ns": "u",
+    "tagi_peer_buffer_bytes": "ni",
+    "tagi_peer_buffer_create": "zpp",
+    "tagi_peer_buffer_open": "pp",
+    "tagi_peer_buffer_close": "pn",
+    "tagi_peer_allreduce_f64": "pipnnip" + "p",
+    "tagi_peer_status": "n",
 }
 _RET = {
+    "tagi_peer_buffer_bytes": _Z,
     "tagi_fused_weight_grad_workspace_size": _Z,
     "tagi_param_grad_workspace_size": _Z,
     "tagi_store_workspace_size": _Z,
@@ -136,12 +143,15 @@ def device_status(reset: bool = False) -> int:
 
 
 def check_device_status() -> None:
-    """Raise RuntimeError if a tensor-core kernel wait ran out since the last
-    check (its outputs are then incomplete); clears the error word."""
+    """Raise RuntimeError if a tensor-core kernel wait or a peer exchange wait ran
+    out since the last check (outputs are then incomplete); clears the words."""
     code = device_status(reset=True)
     if code != 0:
         raise RuntimeError(f"a tensor-core kernel gave up a tile (bounded wait {code} ran out); "
                            "its outputs are incomplete")
+    if int(lib().fn["tagi_peer_status"](1)) != 0:
+        raise RuntimeError("a peer-memory exchange wait ran out (a rank stopped?); the "
+                           "statistics it carried were not reduced")
 
 
 def set_wait_limit_ns(ns: int) -> None:
