@@ -59,45 +59,38 @@ __device__ __forceinline__ void capped_pair(float& m, float& S, float dm, float 
 //   alpha >= 0: mu = mz + s phi u,  var = Sz (1 - phi (w + 2 alpha u + phi u^2)),
 //               J = 1 - phi R
 // (substituting Phi = phi R or 1 - phi R into the reference's expressions), so
-// no term cancels. R, u and w are rational functions of degree (5, 5) in t on
-// [0, 8] (|t| beyond 8 only meets phi < 1e-14), fitted for this library to the
-// functions' definitions by weighted least squares (relative error below 1e-7;
-// below 3e-7 evaluated in float32). The reference's asymptotic branch is kept
+// no term cancels. R, u and w are evaluated as three numerators of degree 5 in
+// t over one common denominator of degree 5, on [0, 8] (|t| beyond 8 only
+// meets phi < 1e-14), fitted for this library to the functions' definitions by
+// weighted least squares (relative error below 4e-7, 5e-7 evaluated in
+// float32). The reference's asymptotic branch is kept
 // for alpha < -5 and simplified exactly: with Phi = phi/|alpha| its mu is 0 and
 // its var is Sz phi / |alpha|.
-struct MillsRational {
-    float p[6], q[6];
-    __device__ __forceinline__ float operator()(float t) const {
-        float a = p[5], b = q[5];
+__device__ __forceinline__ float poly5(const float (&c)[6], float t) {
+    float a = c[5];
 #pragma unroll
-        for (int i = 4; i >= 0; --i) {
-            a = fmaf(a, t, p[i]);
-            b = fmaf(b, t, q[i]);
-        }
-        return __fdividef(a, b);
-    }
-};
+    for (int i = 4; i >= 0; --i) a = fmaf(a, t, c[i]);
+    return a;
+}
 
 __device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
     constexpr float kInvSqrt2Pi = 0.3989422804014327f;
-    constexpr MillsRational kR{{1.253314138e+00f, 1.005634046e+00f, 3.946390781e-01f,
-                                8.097509709e-02f, 7.426330130e-03f, -4.375365097e-08f},
-                               {1.0f, 1.600264494e+00f, 1.091702061e+00f, 4.014938611e-01f,
-                                8.101891127e-02f, 7.424280418e-03f}};
-    constexpr MillsRational kU{{1.000000011e+00f, 4.315312545e-01f, 1.080994959e-01f,
-                                1.094768367e-02f, 7.352854563e-06f, -1.571496301e-07f},
-                               {1.0f, 1.684846170e+00f, 1.219731834e+00f, 4.815096427e-01f,
-                                1.061304995e-01f, 1.110309952e-02f}};
-    constexpr MillsRational kW{{1.253314259e+00f, 2.230172686e-01f, 4.091967526e-02f,
-                                -5.645271322e-04f, 2.714108879e-05f, -5.835115929e-07f},
-                               {1.0f, 1.773717656e+00f, 1.363021453e+00f, 5.782114722e-01f,
-                                1.393231313e-01f, 1.699321488e-02f}};
+    constexpr float kR[6] = {1.253314207e+00f, 1.188586252e+00f, 5.311839209e-01f,
+                             1.276814494e-01f, 1.468054771e-02f, -2.474966628e-08f};
+    constexpr float kU[6] = {9.999996599e-01f, 4.929401602e-01f, 1.284475416e-01f,
+                             1.464294732e-02f, 6.302450154e-07f, 1.128922133e-08f};
+    constexpr float kW[6] = {1.253314576e+00f, 1.885815760e-01f, 3.825437504e-02f,
+                             -7.732495484e-04f, 3.961302328e-05f, -9.044357008e-07f};
+    constexpr float kQ[6] = {1.0f, 1.746248240e+00f, 1.317049340e+00f,
+                             5.458146858e-01f, 1.276858994e-01f, 1.468004551e-02f};
     const float Ss = fmaxf(Sz, 1e-30f);
     const float sd = sqrtf(Ss);
-    const float alpha = mz / sd;
-    const float pdf = expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
+    const float alpha = mz / sd;  // correctly rounded: decides the reference's branch at -5
+    // exp by the hardware approximation: ~1e-6 relative for the arguments that matter
+    const float pdf = __expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
     const float t = fminf(fabsf(alpha), 8.0f);
-    const float R = kR(t), u = kU(t), w = kW(t);
+    const float iq = __frcp_rn(poly5(kQ, t));
+    const float R = poly5(kR, t) * iq, u = poly5(kU, t) * iq, w = poly5(kW, t) * iq;
     const float pu = pdf * u;
     float mu, v, cdf;
     if (alpha < 0.0f) {
@@ -110,7 +103,7 @@ __device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& S
         v = Ss * fmaf(-pdf, fmaf(pu, u, fmaf(2.0f * alpha, u, w)), 1.0f);
     }
     if (alpha < -5.0f) {
-        cdf = pdf / (-alpha);
+        cdf = __fdividef(pdf, -alpha);
         mu = 0.0f;
         v = Ss * cdf;
     }
