@@ -70,7 +70,7 @@ def build(jobs: int | None = None, force: bool = False, verbose: bool = False) -
     objs = [str(BUILD / (s.stem + ".o")) for s in srcs]
     if todo or not LIB.exists() or force:
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-lcuda"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr[-4000:]}")

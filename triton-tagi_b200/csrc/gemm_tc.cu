@@ -40,8 +40,11 @@
 // Every wait is bounded: on timeout a CTA records an error word
 // (tagi_device_status), tells its peer, stops issuing work, waits (bounded) for
 // its MMAs and frees its tensor memory before returning.
+#include <cuda.h>
+
 #include <climits>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -210,6 +213,11 @@ __device__ __noinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
+// Arrive on a barrier of this CTA.
+__device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Arrive on a local barrier and add `bytes` to the transactions its phase waits for.
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
@@ -227,6 +235,26 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
             "r"(dst),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Tensor-map tile copies into this CTA's shared memory (no multicast; the
+// source is this GPU's own memory), completing as transactions on `bar`. The
+// innermost coordinate x is a multiple of 8 fp32 elements (32 bytes).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
 
@@ -473,10 +501,37 @@ constexpr int stage_area() {
                : kEpiBytes;
 }
 
+// Weight sums of narrow tiles (LSQ, A in tensor memory) can take their raw
+// operands from tensor-map bulk copies (TMA): per producer group a ring of
+// kRawSlots K-blocks, each the A block (128 rows x 8 reduction elements) and
+// the two B blocks (NC rows x 8) as fp32, followed by the ring's barriers.
+constexpr int kRawSlots = 8;
+template <int VM, int BN>
+constexpr bool tma_capable() {
+    return VM == LSQ && Roles<BN>::TA;
+}
+template <int BN>
+constexpr int raw_slot_bytes() {
+    return 128 * 32 + 2 * (BN / 2) * 32;
+}
+template <int VM, int BN>
+constexpr int raw_area() {
+    return tma_capable<VM, BN>() ? 2 * kRawSlots * raw_slot_bytes<BN>() + 2 * 2 * kRawSlots * 8 : 0;
+}
+
 template <int VM, int BN>
 constexpr int smem_bytes() {
-    return stage_area<VM, BN>() + kBarrierBytes;
+    return stage_area<VM, BN>() + kBarrierBytes + raw_area<VM, BN>();
 }
+
+// Tensor maps of the raw-operand copies (host-encoded; `on` = 0: the producers
+// read global memory themselves). a: the A rows, 2-D (reduction innermost, row
+// stride given); b0, b1: the two B operands of an NCHW delta tensor, 3-D
+// (pixels of one image innermost, channels, images); L: pixels per image.
+struct TmaArgs {
+    CUtensorMap a, b0, b1;
+    int on, L;
+};
 
 // Issue the MMAs of accumulator Q of one K-block: A tiles at descriptor da
 // (shared memory) or, for TA tiles, at tensor-memory column da; B tiles at
@@ -785,7 +840,31 @@ struct ProdCtx {
     int t;    // thread index within the group's threads of this side
     int lane;
     uint32_t tmem;  // tensor-memory base (A stages of TA tiles)
+    // raw operands by tensor-map copies (tm != nullptr): this group's ring of
+    // kRawSlots K-blocks and its barriers; `issuer` = the thread that issues the
+    // copies; a_row0 / b_row0: the CTA's first A row and B row (column)
+    const TmaArgs* tm;
+    char* raw;
+    uint64_t* rfull;
+    uint64_t* rempty;
+    bool issuer;
+    int a_row0, b_row0;
 };
+
+// Tensor-map copies of the raw operands of K-block `it` into ring slot `slot`:
+// the A block (128 rows) and both B blocks (NC rows of one image's pixels).
+template <int BN>
+__device__ __forceinline__ void tma_issue(const ProdCtx& c, int it, int slot) {
+    constexpr int NC = BN / 2;
+    const uint32_t base = smem_u32(c.raw + slot * raw_slot_bytes<BN>());
+    uint64_t* bar = &c.rfull[slot];
+    mbar_expect_tx(bar, static_cast<uint32_t>(raw_slot_bytes<BN>()));
+    const int k0 = c.kbeg + it * kBK;
+    tma_load_2d(base, &c.tm->a, k0, c.a_row0, bar);
+    const int img = k0 / c.tm->L, px = k0 - img * c.tm->L;
+    tma_load_3d(base + 128 * 32, &c.tm->b0, px, c.b_row0, img, bar);
+    tma_load_3d(base + 128 * 32 + NC * 32, &c.tm->b1, px, c.b_row0, img, bar);
+}
 
 // One side's producer thread: K-blocks grp, grp+2, ... with prefetch_depth of them loaded
 // ahead into registers.
@@ -893,12 +972,76 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
         return true;
     };
 
+    bool alive = true;
+    if (tma_capable<VM, BN>() && c.tm != nullptr) {
+        // Raw operands arrive by tensor-map copies kRawSlots K-blocks ahead; each
+        // thread reads its row's 8 elements from the ring slot, the group's warps
+        // release the slot, and the issuer refills it with the group's K-block
+        // kRawSlots later.
+        const int nj = c.niter > c.grp ? (c.niter - c.grp + 1) / 2 : 0;
+        int issued = 0;
+        if (c.issuer) {
+            for (; issued < nj && issued < kRawSlots; ++issued)
+                if (c.lane == 0) tma_issue<BN>(c, c.grp + 2 * issued, issued);
+            __syncwarp();
+        }
+        for (int j = 0; j < nj && alive; ++j) {
+            const int it = c.grp + 2 * j;
+            if (c.issuer && j >= 1 && issued < nj) {
+                // slot of K-block j - 1: free once every warp of the group read it
+                const int pj = j - 1, ps = pj % kRawSlots;
+                if (!warp_wait(&c.rempty[ps], (pj / kRawSlots) & 1, c.ab, 7)) break;
+                if (c.lane == 0) tma_issue<BN>(c, c.grp + 2 * issued, issued % kRawSlots);
+                __syncwarp();
+                ++issued;
+            }
+            const int sl = j % kRawSlots;
+            if (!warp_wait(&c.rfull[sl], (j / kRawSlots) & 1, c.ab, 8)) break;
+            float v[2][8];
+            const float* src = reinterpret_cast<const float*>(c.raw + sl * raw_slot_bytes<BN>()) +
+                               (IS_A ? 0 : 128 * 8);
+            const int k0 = c.kbeg + it * kBK;
+            if (has_row) {
+                const float4* p0 = reinterpret_cast<const float4*>(src + c.t * 8);
+                const float4 a0 = p0[0], a1 = p0[1];
+                const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (!IS_A) {
+                    const float4* p1 = reinterpret_cast<const float4*>(src + ROWS * 8 + c.t * 8);
+                    const float4 b0 = p1[0], b1 = p1[1];
+                    y[0] = b0.x; y[1] = b0.y; y[2] = b0.z; y[3] = b0.w;
+                    y[4] = b1.x; y[5] = b1.y; y[6] = b1.z; y[7] = b1.w;
+                }
+                const bool one = IS_A && row == sd.ones_row;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const bool in = k0 + e < c.kend;  // past the split's end: zero
+                    v[0][e] = in ? (one ? 1.f : x[e]) : 0.f;
+                    v[1][e] = in ? y[e] : 0.f;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[0][e] = v[1][e] = 0.f;
+            }
+            __syncwarp();
+            if (c.lane == 0) mbar_arrive_local(&c.rempty[sl]);
+            alive = produce(it, v);
+        }
+        // copies issued but not consumed (after an abort) land before the CTA exits
+        if (c.issuer) {
+            const int first = issued > kRawSlots ? issued - kRawSlots : 0;
+            for (int j = first; j < issued; ++j)
+                mbar_drain(&c.rfull[j % kRawSlots], (j / kRawSlots) & 1);
+        }
+    }
     constexpr int kDepth = prefetch_depth<BN>();
     float buf[kDepth][2][8];
+    if (!(tma_capable<VM, BN>() && c.tm != nullptr)) {
 #pragma unroll
-    for (int d = 0; d < kDepth; ++d) load(c.grp + 2 * d, buf[d]);
-    bool alive = true;
-    for (int it0 = c.grp; it0 < c.niter && alive; it0 += 2 * kDepth) {
+        for (int d = 0; d < kDepth; ++d) load(c.grp + 2 * d, buf[d]);
+    }
+    for (int it0 = c.grp; it0 < c.niter && alive && !(tma_capable<VM, BN>() && c.tm != nullptr);
+         it0 += 2 * kDepth) {
 #pragma unroll
         for (int d = 0; d < kDepth; ++d) {
             const int it = it0 + 2 * d;
@@ -973,7 +1116,7 @@ __device__ __forceinline__ void packed_b(const GemmArgs& g, const ProdCtx& c, in
 // stride 1); operands that are not gathered ignore it.
 template <int VM, bool MEAN, int EPI, int BN, int GM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 1)
-    moment_tc_kernel(const GemmArgs g) {
+    moment_tc_kernel(const GemmArgs g, const __grid_constant__ TmaArgs tm) {
     using R = Roles<BN>;
     using T = TcTiles<VM>;
     constexpr int A_TILE = 128 * 32, B_TILE = R::NC * 32;
@@ -991,6 +1134,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     uint64_t* bfull = done + 1;  // [OPS], prepared-B copies
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bfull + kMaxStages);
     volatile int* abort_word = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // raw-operand rings (tensor-map copies), one per producer group
+    constexpr bool kTma = tma_capable<VM, BN>();
+    char* raw = smem + stage_area<VM, BN>() + kBarrierBytes;
+    uint64_t* rfull = reinterpret_cast<uint64_t*>(raw + 2 * kRawSlots * raw_slot_bytes<BN>());
+    uint64_t* rempty = rfull + 2 * kRawSlots;  // [grp * kRawSlots + slot]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_rank();
@@ -1004,6 +1152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
     const Abort ab{abort_word, map_to(smem_u32(const_cast<int*>(abort_word)), rank ^ 1u)};
     // Prepared B tiles (FULL and RSQ, unbatched): one arrival per CTA for the B side.
     const bool packed = g.bpk != nullptr && g.bpk_nc == R::NC;
+    const bool use_tma = kTma && tm.on != 0 && !packed;
 
     if (tid == 0) {
         for (int s = 0; s < OPS; ++s) {
@@ -1016,6 +1165,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
             mbar_init(&chunk_empty[i], 16);  // 8 accumulator warps in each CTA
         }
         mbar_init(done, 1);
+        if (use_tma) {
+            for (int i = 0; i < 2 * kRawSlots; ++i) {
+                mbar_init(&rfull[i], 1);
+                mbar_init(&rempty[i], 4 + R::BW);  // the group's A and B producer warps
+            }
+        }
         *abort_word = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1064,6 +1219,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
         c.kend = kend;
         c.lane = lane;
         c.tmem = tmem;
+        c.tm = nullptr;
+        if (use_tma) {
+            const int grp = is_a ? (warp >> 2) : (warp - R::B_W0) / R::BW;
+            c.tm = &tm;
+            c.raw = raw + grp * kRawSlots * raw_slot_bytes<BN>();
+            c.rfull = rfull + grp * kRawSlots;
+            c.rempty = rempty + grp * kRawSlots;
+            c.issuer = is_a && (warp & 3) == 0;
+            c.a_row0 = sa.row0;
+            c.b_row0 = sb.row0;
+        }
         if (is_a) {
             c.grp = warp >> 2;
             c.t = (warp & 3) * 32 + lane;
@@ -1293,6 +1459,89 @@ bool tc_enabled() {
     return v == 1;
 }
 
+bool tma_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = std::getenv("TAGI_B200_TMA");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+// Tensor maps for the raw-operand copies of a weight-sum launch whose A rows
+// are contiguous along the reduction (the transposed patches) and whose B
+// operands are NCHW delta planes (row map: L pixels per image, N channels, unit
+// pixel stride); false (maps off) for any other operand layout. The copies
+// read K-blocks of 8 reduction elements: the split reduction's chunks start on
+// multiples of 8 and an image's L pixels are a multiple of 8, so a block never
+// crosses an image.
+// The driver's tensor-map encoder, looked up through the runtime (the library
+// does not link the driver library itself); null if unavailable.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+bool make_tma(const GemmArgs& g, int nc, TmaArgs* t) {
+    t->on = 0;
+    if (!tma_enabled() || g.bpk != nullptr || g.ga.on || g.a_bs != 0 || g.b_bs != 0) return false;
+    const EncodeTiledFn encode = encode_tiled();
+    if (encode == nullptr) return false;
+    const int64_t L = g.brow.div;
+    const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!(g.arow.div <= 0 && g.ak == 1 && g.arow.stride > 0 && (g.arow.stride * 4) % 16 == 0 &&
+          al16(g.x)))
+        return false;
+    if (!(L > 0 && L % 8 == 0 && g.brow.stride == 1 && g.bn == L &&
+          g.brow.outer == static_cast<int64_t>(g.N) * L && g.Kr % L == 0 && al16(g.u) &&
+          al16(g.v) && g.kchunk % 8 == 0))
+        return false;
+    const int64_t rows_a = g.ones_row >= 0 ? g.ones_row : g.M;
+    if (rows_a < 1) return false;
+    const cuuint32_t es[3] = {1, 1, 1};
+    {
+        const cuuint64_t dim[2] = {static_cast<cuuint64_t>(g.Kr), static_cast<cuuint64_t>(rows_a)};
+        const cuuint64_t stride[1] = {static_cast<cuuint64_t>(g.arow.stride) * 4};
+        const cuuint32_t box[2] = {kBK, 128};
+        if (encode(&t->a, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                                   const_cast<float*>(g.x), dim, stride, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    const cuuint64_t dim[3] = {static_cast<cuuint64_t>(L), static_cast<cuuint64_t>(g.N),
+                               static_cast<cuuint64_t>(g.Kr / L)};
+    const cuuint64_t stride[2] = {static_cast<cuuint64_t>(L) * 4,
+                                  static_cast<cuuint64_t>(g.brow.outer) * 4};
+    const cuuint32_t box[3] = {kBK, static_cast<cuuint32_t>(nc), 1};
+    for (int i = 0; i < 2; ++i) {
+        if (encode(i ? &t->b1 : &t->b0, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                                   const_cast<float*>(i ? g.v : g.u), dim, stride, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    t->L = static_cast<int>(L);
+    t->on = 1;
+    return true;
+}
+
 template <int VM, bool MEAN, int EPI, int BN, int GM>
 int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
     static std::once_flag once;
@@ -1311,7 +1560,10 @@ int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
     dim3 grid(static_cast<unsigned>(2 * pairs), (g.N + BN - 1) / BN, batch * g.splits);
     TAGI_REQUIRE(grid.y <= 65535 && grid.z <= 65535, TAGI_E_UNSUPPORTED, "%s: grid too large",
                  what);
-    moment_tc_kernel<VM, MEAN, EPI, BN, GM><<<grid, Roles<BN>::THREADS, smem, st>>>(g);
+    TmaArgs tm;
+    memset(&tm, 0, sizeof(tm));
+    if (tma_capable<VM, BN>() && batch == 1) make_tma(g, Roles<BN>::NC, &tm);
+    moment_tc_kernel<VM, MEAN, EPI, BN, GM><<<grid, Roles<BN>::THREADS, smem, st>>>(g, tm);
     return check_launch(what);
 }
 
