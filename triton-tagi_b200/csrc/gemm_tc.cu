@@ -42,6 +42,7 @@
 // its MMAs and frees its tensor memory before returning.
 #include <cuda.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdlib>
 #include <cstring>
@@ -1496,6 +1497,8 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+std::atomic<uint64_t> g_tma_launches{0};
+
 bool make_tma(const GemmArgs& g, int nc, TmaArgs* t) {
     t->on = 0;
     if (!tma_enabled() || g.bpk != nullptr || g.ga.on || g.a_bs != 0 || g.b_bs != 0) return false;
@@ -1562,7 +1565,7 @@ int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
                  what);
     TmaArgs tm;
     memset(&tm, 0, sizeof(tm));
-    if (tma_capable<VM, BN>() && batch == 1) make_tma(g, Roles<BN>::NC, &tm);
+    if (tma_capable<VM, BN>() && batch == 1 && make_tma(g, Roles<BN>::NC, &tm)) ++g_tma_launches;
     moment_tc_kernel<VM, MEAN, EPI, BN, GM><<<grid, Roles<BN>::THREADS, smem, st>>>(g, tm);
     return check_launch(what);
 }
@@ -1705,6 +1708,8 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
 }
 
 }  // namespace tagi
+
+extern "C" uint64_t tagi_tma_launches(void) { return tagi::g_tma_launches.load(); }
 
 extern "C" int tagi_set_wait_limit_ns(uint64_t ns) {
     const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : tagi::kTimeoutNs;

@@ -70,6 +70,7 @@ _SIGS = {
     "tagi_device_arch": "n",
     "tagi_last_error": "",
     "tagi_kernel_launches": "",
+    "tagi_tma_launches": "",
     "tagi_device_status": "n",
     "tagi_set_wait_limit_ns": "u",
     "tagi_peer_buffer_bytes": "ni",
@@ -86,6 +87,7 @@ _RET = {
     "tagi_store_workspace_size": _Z,
     "tagi_last_error": ctypes.c_char_p,
     "tagi_kernel_launches": ctypes.c_uint64,
+    "tagi_tma_launches": ctypes.c_uint64,
 }
 
 # Status codes (include/tagi_b200.h)
