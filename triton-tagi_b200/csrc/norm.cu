@@ -3,7 +3,7 @@
 // Channel reductions accumulate in float64 in a fixed order (deterministic, no
 // atomics), so the sums can be all-reduced across data-parallel ranks before the
 // statistics are finalised on the device. Each channel is reduced by a
-// thread-block cluster of S = 1, 2, 4, 8 or 16 blocks (about 1024 blocks in all):
+// thread-block cluster of S = 1, 2, 4 or 8 blocks (about 512 blocks in all):
 // block j takes images j, j+S, ..., and the cluster's first block adds the S
 // partial sums from its peers' shared memory in rank order. No workspace, one
 // launch.
@@ -18,12 +18,9 @@ namespace {
 
 constexpr int kBnThreads = 256;
 
-// Blocks per channel: about 1024 blocks in all (7 of 256 threads per SM; with
-// 512 the kernels were latency-bound at 43 % of warps resident), clusters of up
-// to 16 blocks (the non-portable size, allowed per kernel at launch).
 int bn_split(int64_t C, int64_t N) {
     int s = 1;
-    while (s < 16 && C * s < 1024 && s < N) s *= 2;
+    while (s < 8 && C * s < 512 && s < N) s *= 2;
     return s;
 }
 
@@ -63,15 +60,6 @@ __device__ __forceinline__ void cluster_channel_sum(double (&v)[NV], double* red
 
 template <typename K, typename... Args>
 int launch_cluster(K kernel, int S, int C, cudaStream_t st, const char* what, Args... args) {
-    if (S > 8) {
-        // clusters above the portable 8 blocks: allowed per kernel; if the device
-        // refuses, the channel is split over 8 blocks instead
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
-            cudaSuccess) {
-            cudaGetLastError();
-            S = 8;
-        }
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(S), static_cast<unsigned>(C), 1);
     cfg.blockDim = dim3(kBnThreads, 1, 1);
