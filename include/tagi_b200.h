@@ -51,16 +51,12 @@ uint64_t tagi_tma_launches(void);        /* of those, weight sums fed by tensor-
 int tagi_device_status(int reset);
 /* Limit, in nanoseconds, of the tensor-core kernels' waits that give up a tile
  * when they run out (default 2 s; 0 restores it), on the current device. A
- * diagnostic hook: a test sets a few nanoseconds to make those waits run out
- * and checks that the kernel returns, that tagi_device_status reports it and
- * that later calls with the default limit are correct. The waits for a CTA's
- * own in-flight copies and MMAs keep the 2 s limit whatever this is. Values
- * below 1 ms also shorten the suspend hint of every barrier test to the same
- * value (default 1 ms), so that the limit is reached; values below 1000 make
- * the barrier tests non-suspending and also bound the number of failed tests
- * of a wait (the device's global timer advances in steps coarser than a
- * microsecond, and a suspended test may outlast a short hint). No reference
- * counterpart (the reference's Triton kernels do not wait). */
+ * diagnostic hook: values below 1000 (a test's) also make every tensor-core
+ * launch give up its tiles at the start, as a wait that ran out would (error
+ * word 2), so that the abort path runs: the other warps of both CTAs see the
+ * pair's abort flag, stop, the kernel waits for its own copies and MMAs in
+ * flight (those keep the fixed 2 s limit), frees its tensor memory and returns.
+ * No reference counterpart (the reference's Triton kernels do not wait). */
 int tagi_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------------------

@@ -1,15 +1,16 @@
-"""The tensor-core kernels' bounded waits, made to run out on purpose.
+"""The tensor-core kernels' abort path, taken on purpose.
 
 Every wait inside the tcgen05 contraction kernel is bounded; when one runs out
 the kernel records the error word read by ``tagi_device_status``, tells the
 other CTA of its pair, stops issuing work, waits for its own MMAs and copies in
-flight and frees its tensor memory before returning. This test sets the limit
-of the abortable waits to a few nanoseconds (``tagi_set_wait_limit_ns``), so
-that the first wait that does not succeed at once gives up, and checks that
-the call returns, that the error word reports it, and that after restoring the
-default limit the same contraction is correct again. No fault is involved: the
-waits are on barriers that would complete, and the drains that must finish
-before a CTA exits keep their fixed limit.
+flight and frees its tensor memory before returning. The test hook
+``tagi_set_wait_limit_ns`` with a value below one microsecond makes every
+launch take that path from its start (the MMA issuer gives up before its first
+stage; the producers and accumulator warps find the abort flag when their next
+wait does not complete). The test checks that the call returns, that the error
+word reports it, and that after restoring the default limit the same
+contraction is correct again. No fault is involved: nothing waits on a barrier
+that cannot complete except through the bounded, abort-aware waits.
 """
 
 from __future__ import annotations
@@ -44,7 +45,7 @@ def test_wait_limit_runs_out_then_recovers():
         code = device_status(reset=True)
     finally:
         set_wait_limit_ns(0)
-    assert code != 0, "no wait ran out with a 1 ns limit"
+    assert code != 0, "the forced abort was not reported"
     for _ in range(2):
         mz, Sz = lin.forward(a, s)
         torch.cuda.synchronize()

@@ -59,6 +59,9 @@ __device__ int g_device_error = 0;  // 0 = ok, else the code of the first timeou
 // make those waits run out; the drains that must complete before a CTA exits
 // (its own bulk copies, its MMAs) keep the fixed kTimeoutNs.
 __device__ unsigned long long g_wait_limit_ns = 2000000000ull;
+// Test hook: non-zero makes every launch give up its tiles at the start, as a
+// wait that ran out would (the abort, drain and release path then runs).
+__device__ int g_force_abort = 0;
 
 namespace {
 
@@ -141,30 +144,17 @@ __device__ __forceinline__ void arrive_cluster(uint32_t addr) {
 
 // Test for completion of phase `parity` (default acquire semantics at CTA scope,
 // as for the other barriers of the pair); a waiting thread is suspended (it
-// takes no issue slots) until the phase completes or about c_suspend_ns passed
-// (1 ms; tagi_set_wait_limit_ns shortens it together with the wait limit, so
-// that a test's short limit is reached).
+// takes no issue slots) until the phase completes or about kSuspendNs passed.
+// (The hint is an immediate: reading it from memory in every wait slowed the
+// contractions by 4 %.)
 constexpr uint32_t kSuspendNs = 1000000;
-__constant__ uint32_t c_suspend_ns = kSuspendNs;
-// A hint of 0 (set only by the test hook) tests without suspending at all: the
-// hardware may keep a suspended thread waiting longer than a short hint asks.
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-    const uint32_t hint = c_suspend_ns;
-    if (hint == 0) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        return ok != 0;
-    }
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(hint)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -179,14 +169,10 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, cons
                                             int code) {
     const unsigned long long t0 = globaltimer();
     const unsigned long long limit = *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
-    // The global timer advances in steps of up to a microsecond or more, so a
-    // limit below 1 us (a test's) also counts failed tests: the wait gives up
-    // after `limit` of them.
-    const unsigned long long spins = limit < 1000ull ? limit : ~0ull;
-    for (unsigned long long spin = 0;; ++spin) {
+    for (;;) {
         if (mbar_try(bar, parity)) return true;
         if (*ab.flag) return false;
-        if (globaltimer() - t0 > limit || spin >= spins) {
+        if (globaltimer() - t0 > limit) {
             *ab.flag = 1;
             asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ab.peer), "r"(1) : "memory");
             atomicCAS(&g_device_error, 0, code);
@@ -1263,6 +1249,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
             uint64_t da = da_first, db = db_first;
             int s = 0;
             uint32_t ph = 0;
+            int nit = niter;
+            if (*const_cast<volatile int*>(&g_force_abort)) {
+                // test hook: give up the tiles as a wait that ran out would
+                if (el) {
+                    *ab.flag = 1;
+                    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ab.peer), "r"(1) : "memory");
+                    atomicCAS(&g_device_error, 0, 2);
+                }
+                __syncwarp();
+                nit = 0;
+            }
             int pos0 = 0, pos1 = kOff1;  // (stage + shift) % kChunk of each accumulator
             int c0 = 0, c1 = 0;          // chunk index of each accumulator
             // An accumulator whose chunk buffer must first be drained by a fold
@@ -1272,7 +1269,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Roles<BN>::THREADS, 
                 tc_fence_after();
                 return true;
             };
-            for (int it0 = 0; it0 < niter; it0 += kBlocks) {
+            for (int it0 = 0; it0 < nit; it0 += kBlocks) {
                 if (!warp_wait(&full[s], ph, ab, 2)) break;
                 tc_fence_after();
                 bool ok = true;
@@ -1713,11 +1710,9 @@ extern "C" uint64_t tagi_tma_launches(void) { return tagi::g_tma_launches.load()
 
 extern "C" int tagi_set_wait_limit_ns(uint64_t ns) {
     const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : tagi::kTimeoutNs;
-    // below 1 us: tests that do not suspend (see mbar_try)
-    const uint32_t hint =
-        v < 1000ull ? 0u : static_cast<uint32_t>(v < tagi::kSuspendNs ? v : tagi::kSuspendNs);
+    const int force = (ns > 0 && ns < 1000) ? 1 : 0;
     cudaError_t e = cudaMemcpyToSymbol(tagi::g_wait_limit_ns, &v, sizeof(v));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tagi::c_suspend_ns, &hint, sizeof(hint));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(tagi::g_force_abort, &force, sizeof(force));
     if (e != cudaSuccess) {
         cudaGetLastError();
         tagi::set_error("tagi_set_wait_limit_ns: %s", cudaGetErrorString(e));
