@@ -772,6 +772,10 @@ def main():
     if world > 1:
         import datetime
 
+        # NCCL's gradient all-reduces run beside the backward contractions; with
+        # at most 8 channels they take fewer SMs from them (measured at two GPUs:
+        # 13.37 -> 13.18 ms per ResNet-18 step) and still finish inside the backward
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "8")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
