@@ -81,12 +81,7 @@ constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 template <int BN>
 struct Roles {
     static constexpr int NC = BN / 2;                  // B rows staged by each CTA
-    // B producer warps per group. 64-column tiles use two for their 32 rows (and
-    // 32-column tiles all 32 lanes of one for 16 rows): each thread then stages
-    // half of a row's 8 reduction elements. One warp per group staging whole rows
-    // bounded the stage-1 weight sums (~1100 clk per K-block against ~850 clk of
-    // MMA issue).
-    static constexpr int BW = BN == 64 ? 2 : (NC >= 32 ? NC / 32 : 1);
+    static constexpr int BW = NC >= 32 ? NC / 32 : 1;  // B producer warps per group
     static constexpr int B_W0 = 8;
     static constexpr int MMA_W = B_W0 + 2 * BW;
     static constexpr int ACC_W0 = MMA_W + 1;
@@ -876,14 +871,8 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
     constexpr int OFF = IS_A ? 0 : b_off<VM, BN>();  // the side's first tile
     constexpr bool TMEM_A = IS_A && R::TA;          // A rows go to tensor memory
     constexpr bool TWO = IS_A ? VM != LSQ : VM != RSQ;
-    // B with more threads than rows (row mode): thread t stages elements
-    // 4*(t / ROWS) .. +3 of row t % ROWS
-    constexpr int KSPLIT = (!IS_A && NTH > ROWS) ? NTH / ROWS : 1;
-    static_assert(KSPLIT == 1 || KSPLIT == 2, "B threads per row");
-    const int trow = KSPLIT > 1 ? c.t % ROWS : c.t;
-    const int khalf = KSPLIT > 1 ? c.t / ROWS : 0;
-    const bool has_row = trow < ROWS;
-    const int row = sd.row0 + trow;
+    const bool has_row = c.t < ROWS;
+    const int row = sd.row0 + c.t;
     const bool row_in = has_row && row < sd.nrows;
     const int64_t base =
         (row_in && !(IS_A && (row == sd.ones_row || sd.gather))) ? row_base<IS_A>(g, row) : 0;
@@ -960,13 +949,8 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
                 }
             }
         } else if (row_in) {
-            if (KSPLIT > 1) {
-                store_tiles<VM, IS_A>(st, TILE, tile_off_k(trow, 4 * khalf), &v[0][4 * khalf],
-                                      &v[1][4 * khalf]);
-            } else {
-                store_tiles<VM, IS_A>(st, TILE, tile_off_k(c.t, 0), &v[0][0], &v[1][0]);
-                store_tiles<VM, IS_A>(st, TILE, tile_off_k(c.t, 4), &v[0][4], &v[1][4]);
-            }
+            store_tiles<VM, IS_A>(st, TILE, tile_off_k(c.t, 0), &v[0][0], &v[1][0]);
+            store_tiles<VM, IS_A>(st, TILE, tile_off_k(c.t, 4), &v[0][4], &v[1][4]);
             wrote = true;
         }
         if (wrote) fence_proxy_async();
@@ -1005,12 +989,12 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
                                (IS_A ? 0 : 128 * 8);
             const int k0 = c.kbeg + it * kBK;
             if (has_row) {
-                const float4* p0 = reinterpret_cast<const float4*>(src + trow * 8);
+                const float4* p0 = reinterpret_cast<const float4*>(src + c.t * 8);
                 const float4 a0 = p0[0], a1 = p0[1];
                 const float x[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
                 float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 if (!IS_A) {
-                    const float4* p1 = reinterpret_cast<const float4*>(src + ROWS * 8 + trow * 8);
+                    const float4* p1 = reinterpret_cast<const float4*>(src + ROWS * 8 + c.t * 8);
                     const float4 b0 = p1[0], b1 = p1[1];
                     y[0] = b0.x; y[1] = b0.y; y[2] = b0.z; y[3] = b0.w;
                     y[4] = b1.x; y[5] = b1.y; y[6] = b1.z; y[7] = b1.w;
