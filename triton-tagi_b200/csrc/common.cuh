@@ -73,7 +73,16 @@ __device__ __forceinline__ float poly5(const float (&c)[6], float t) {
     return a;
 }
 
-__device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
+// The shared core: (mu, var, Phi) through the Mills-ratio forms above, without
+// the reference ReLU's alpha < -5 branch; returns alpha and phi(alpha).
+// EXACT_EXP evaluates phi with expf instead of the hardware approximation
+// (about 1e-6 relative near |alpha| = 8).
+struct RectGauss {
+    float mu, v, cdf, alpha, pdf, Ss;
+};
+
+template <bool EXACT_EXP>
+__device__ __forceinline__ RectGauss rect_gauss(float mz, float Sz) {
     constexpr float kInvSqrt2Pi = 0.3989422804014327f;
     constexpr float kR[6] = {1.253314207e+00f, 1.188586252e+00f, 5.311839209e-01f,
                              1.276814494e-01f, 1.468054771e-02f, -2.474966628e-08f};
@@ -83,33 +92,38 @@ __device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& S
                              -7.732495484e-04f, 3.961302328e-05f, -9.044357008e-07f};
     constexpr float kQ[6] = {1.0f, 1.746248240e+00f, 1.317049340e+00f,
                              5.458146858e-01f, 1.276858994e-01f, 1.468004551e-02f};
-    const float Ss = fmaxf(Sz, 1e-30f);
-    const float sd = sqrtf(Ss);
-    const float alpha = mz / sd;  // correctly rounded: decides the reference's branch at -5
-    // exp by the hardware approximation: ~1e-6 relative for the arguments that matter
-    const float pdf = __expf(-0.5f * alpha * alpha) * kInvSqrt2Pi;
-    const float t = fminf(fabsf(alpha), 8.0f);
+    RectGauss g;
+    g.Ss = fmaxf(Sz, 1e-30f);
+    const float sd = sqrtf(g.Ss);
+    g.alpha = mz / sd;  // correctly rounded: decides the reference ReLU's branch at -5
+    const float e = -0.5f * g.alpha * g.alpha;
+    g.pdf = (EXACT_EXP ? expf(e) : __expf(e)) * kInvSqrt2Pi;
+    const float t = fminf(fabsf(g.alpha), 8.0f);
     const float iq = __frcp_rn(poly5(kQ, t));
     const float R = poly5(kR, t) * iq, u = poly5(kU, t) * iq, w = poly5(kW, t) * iq;
-    const float pu = pdf * u;
-    float mu, v, cdf;
-    if (alpha < 0.0f) {
-        cdf = pdf * R;
-        mu = sd * pu;
-        v = Ss * (pdf * fmaf(-pu, u, w));
+    const float pu = g.pdf * u;
+    if (g.alpha < 0.0f) {
+        g.cdf = g.pdf * R;
+        g.mu = sd * pu;
+        g.v = g.Ss * (g.pdf * fmaf(-pu, u, w));
     } else {
-        cdf = fmaf(-pdf, R, 1.0f);
-        mu = fmaf(sd, pu, mz);
-        v = Ss * fmaf(-pdf, fmaf(pu, u, fmaf(2.0f * alpha, u, w)), 1.0f);
+        g.cdf = fmaf(-g.pdf, R, 1.0f);
+        g.mu = fmaf(sd, pu, mz);
+        g.v = g.Ss * fmaf(-g.pdf, fmaf(pu, u, fmaf(2.0f * g.alpha, u, w)), 1.0f);
     }
-    if (alpha < -5.0f) {
-        cdf = __fdividef(pdf, -alpha);
-        mu = 0.0f;
-        v = Ss * cdf;
+    return g;
+}
+
+__device__ __forceinline__ void relu_one(float mz, float Sz, float& ma, float& Sa, float& J) {
+    RectGauss g = rect_gauss<false>(mz, Sz);
+    if (g.alpha < -5.0f) {
+        g.cdf = __fdividef(g.pdf, -g.alpha);
+        g.mu = 0.0f;
+        g.v = g.Ss * g.cdf;
     }
-    ma = mu;
-    Sa = fmaxf(v, 0.0f);
-    J = cdf;
+    ma = g.mu;
+    Sa = fmaxf(g.v, 0.0f);
+    J = g.cdf;
 }
 
 constexpr int kNumSMs = 148;

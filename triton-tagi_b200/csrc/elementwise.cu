@@ -11,9 +11,6 @@
 namespace tagi {
 namespace {
 
-constexpr float kInvSqrt2Pi = 0.3989422804014327f;
-constexpr float kInvSqrt2 = 0.7071067811865476f;
-
 __host__ __device__ inline bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
@@ -169,61 +166,90 @@ __global__ void avgpool_bwd_kernel(const float* dm, const float* dS, float* om, 
 }
 
 // ---- Remax (remax.py:33-114) -------------------------------------------------
-// Inputs and outputs are float32; the arithmetic runs in float64. The Remax
-// closed form cancels heavily (log(1+x) of small ratios, a sum of three logs
-// that nearly vanishes, exp(x)-1), so float32 evaluations that round
-// differently (FMA contraction, another exp/log) disagree by up to ~1e-3 on
-// its variance and Jacobian, and that difference is amplified by training: an
-// MLP run whose only float64 part is Remax stays within ~1e-5 of a float64 run
-// after 100 steps, against ~3e-3 for float32 Remax. Evaluating in float64
-// keeps the output within the reference's own rounding error of the exact
-// moments.
-struct RemaxLocal {
-    double Sz, mu_m, var_m, cdf;
+// The reference evaluates, per row of K classes,
+//   mixture:   m = max(E[max(0,Z)], eps), v = max(Var-expression(m), eps)
+//   sums:      T = max(sum m, eps), V = max(sum v, eps)
+//   log-normal: r = log(1 + v/m^2), t = log(1 + V/T^2), c = log(1 + v/(m T)),
+//              mu_raw = max(exp(log m - r/2 - log T + t/2 + (r + t - 2c)/2), eps)
+//   finish:    mu_a = mu_raw / max(sum mu_raw, eps), var_a = (exp(r + t - 2c) - 1) mu_a^2,
+//              cov_am = (exp(r - c) - 1) mu_a m, J = min(sqrt(var_a S), cov_am / cdf) / S.
+// Those exp/log pairs cancel: r + t - 2c nearly vanishes for a dominant class,
+// exp(x) - 1 and log(1 + x) of small x, so float32 evaluations that round
+// differently disagree in the leading digits of var_a and J (up to ~1 relative
+// on attention rows). Exponentiating the logs gives exact rational forms with
+// no cancelling term. With D = T - m and E = V - v (the other classes' sums,
+// both >= 0) and den = m T + v:
+//   mu_raw = max(m^2 (1 + V/T^2) / den, eps)
+//   var_a  = mu_a^2 (v D^2 + E (m^2 + v)) / den^2
+//   cov_am = mu_a v D / den
+// (e.g. (1+r')(1+t')/(1+c')^2 - 1 = (v D^2 + E (m^2 + v)) / den^2 for the
+// arguments r' = v/m^2, t' = V/T^2, c' = v/(m T) of the logs). Every term is
+// a product or sum of non-negative factors, so float32 keeps a few ulps of
+// relative accuracy; T and V are summed in float64 so that D and E (which
+// subtract a class from its row's sum) keep theirs when one class dominates.
+// The mixture moments come from rect_gauss (no cancelling term either). The
+// reference clamps m at eps before its variance expression, which then equals
+// V_true + (mu - m)(mu + m - 2 mz); that correction is applied where the
+// clamp is active. The reference's clamp of the log-normal variance at 0 is
+// inactive here (the form is non-negative).
+struct RemaxMix {
+    float m, v, cdf;
 };
 
-__device__ __forceinline__ RemaxLocal remax_mixture(float mz_f, float Sz_f) {
-    constexpr double EPS = 1e-6;
-    const double mz = mz_f, Sz = Sz_f;
-    RemaxLocal r;
-    r.Sz = Sz;
-    const double sd = sqrt(Sz);
-    const double alpha = mz / sd;
-    const double pdf = 0.3989422804014327 * exp(-0.5 * alpha * alpha);
-    r.cdf = 0.5 + 0.5 * erf(alpha * 0.7071067811865476);
-    r.mu_m = fmax(mz * r.cdf + sd * pdf, EPS);
-    const double v = -r.mu_m * r.mu_m + 2.0 * r.mu_m * mz - mz * sd * pdf + (Sz - mz * mz) * r.cdf;
-    r.var_m = fmax(v, EPS);
+__device__ __forceinline__ RemaxMix remax_mixture(float mz, float Sz) {
+    constexpr float EPS = 1e-6f;
+    const RectGauss g = rect_gauss<true>(mz, Sz);
+    RemaxMix r;
+    r.m = fmaxf(g.mu, EPS);
+    const float v = r.m == g.mu ? g.v : fmaf(g.mu - r.m, g.mu + r.m - 2.0f * mz, g.v);
+    r.v = fmaxf(v, EPS);
+    r.cdf = g.cdf;
     return r;
 }
 
-struct RemaxStage2 {
-    double var_log_m, cov_log, var_log_a, mu_raw;
+// Row constants after the first pass.
+struct RemaxRow {
+    double T, V;  // sums of m and v (clamped at eps)
+    float Tf, one_t;  // T in float32 and 1 + V/T^2
 };
 
-__device__ __forceinline__ RemaxStage2 remax_lognormal(const RemaxLocal& l, double mu_t,
-                                                       double var_log_t, double mu_log_t) {
-    constexpr double EPS = 1e-6;
-    RemaxStage2 s;
-    s.var_log_m = log(1.0 + l.var_m / (l.mu_m * l.mu_m));
-    const double mu_log_m = log(l.mu_m) - 0.5 * s.var_log_m;
-    s.cov_log = log(1.0 + l.var_m / (l.mu_m * mu_t));
-    const double mu_log_a = mu_log_m - mu_log_t;
-    s.var_log_a = fmax(s.var_log_m + var_log_t - 2.0 * s.cov_log, 0.0);
-    s.mu_raw = fmax(exp(mu_log_a + 0.5 * s.var_log_a), EPS);
-    return s;
+__device__ __forceinline__ RemaxRow remax_row(double sm, double sv) {
+    RemaxRow w;
+    w.T = fmax(sm, 1e-6);
+    w.V = fmax(sv, 1e-6);
+    w.Tf = static_cast<float>(w.T);
+    w.one_t = static_cast<float>(1.0 + w.V / (w.T * w.T));
+    return w;
 }
 
-__device__ __forceinline__ void remax_finish(const RemaxLocal& l, const RemaxStage2& s,
-                                             double sum_raw, float& ma, float& Sa, float& J) {
-    constexpr double EPS = 1e-6;
-    const double mu_a = s.mu_raw / sum_raw;
-    const double var_a = (exp(s.var_log_a) - 1.0) * mu_a * mu_a;
-    const double cov_a_m = (exp(s.var_log_m - s.cov_log) - 1.0) * mu_a * l.mu_m;
-    const double cov_a_z = fmin(sqrt(var_a * l.Sz), cov_a_m / fmax(l.cdf, EPS));
-    ma = static_cast<float>(mu_a);
-    Sa = static_cast<float>(var_a);
-    J = static_cast<float>(cov_a_z / l.Sz);
+// Second pass of one class: mu_raw and the two factors of the finish that do
+// not depend on the row sum of mu_raw.
+struct RemaxFactors {
+    float raw, qv, qc;
+};
+
+__device__ __forceinline__ RemaxFactors remax_factors(const RemaxMix& x, const RemaxRow& w) {
+    constexpr float EPS = 1e-6f;
+    const float D = static_cast<float>(fmax(w.T - static_cast<double>(x.m), 0.0));
+    const float E = static_cast<float>(fmax(w.V - static_cast<double>(x.v), 0.0));
+    const float den = fmaf(x.m, w.Tf, x.v);  // >= eps (v >= eps)
+    const float rd = __frcp_rn(den);
+    RemaxFactors f;
+    f.raw = fmaxf(x.m * x.m * w.one_t * rd, EPS);
+    f.qv = fmaf(x.v * D, D, E * fmaf(x.m, x.m, x.v)) * rd * rd;
+    f.qc = (x.v * D) / (den * fmaxf(x.cdf, EPS));
+    return f;
+}
+
+// The finish of one class, with rsum = 1 / max(sum of mu_raw, eps).
+__device__ __forceinline__ void remax_out(const RemaxFactors& f, float rsum, float Sz, float& ma,
+                                          float& Sa, float& J) {
+    const float mu_a = f.raw * rsum;
+    const float var_a = mu_a * mu_a * f.qv;
+    const float cov = fminf(sqrtf(var_a * Sz), f.qc * mu_a);
+    ma = mu_a;
+    Sa = var_a;
+    J = cov * __frcp_rn(Sz);
 }
 
 __device__ __forceinline__ double warp_sum(double v) {
@@ -232,139 +258,152 @@ __device__ __forceinline__ double warp_sum(double v) {
     return v;
 }
 
-// One warp per row, up to PER*32 classes held in registers (PER = 0: any K,
-// the mixture moments are recomputed from global memory in each pass). The
-// log-normal stage is recomputed in the last pass rather than stored.
-template <int PER>
-__global__ void remax_warp_kernel(const float* mz, const float* Sz, float* ma, float* Sa,
-                                  float* J, int64_t rows, int K, int64_t stride) {
-    constexpr double EPS = 1e-6;
-    constexpr int R = PER > 0 ? PER : 1;
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-         row < rows; row += warps) {
-        const int64_t base = row * stride;
-        RemaxLocal loc[R];
-        double s_mu = 0.0, s_var = 0.0;
-        if (PER > 0) {
+// Sum of one float64 value over the G warps of a row group, in warp order
+// (deterministic). `red` holds G slots of this group; the barriers are
+// block-wide, so every thread of the block must call this the same number of
+// times.
+template <int G>
+__device__ __forceinline__ double group_sum(double v, double* red) {
+    v = warp_sum(v);
+    if (G == 1) return v;
+    const int w = (threadIdx.x >> 5) % G;
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    double s = 0.0;
 #pragma unroll
-            for (int p = 0; p < R; ++p) {
-                const int j = lane + 32 * p;
-                if (j < K) {
-                    loc[p] = remax_mixture(mz[base + j], Sz[base + j]);
-                    s_mu += loc[p].mu_m;
-                    s_var += loc[p].var_m;
-                }
-            }
-        } else {
-            for (int j = lane; j < K; j += 32) {
-                const RemaxLocal l = remax_mixture(mz[base + j], Sz[base + j]);
-                s_mu += l.mu_m;
-                s_var += l.var_m;
-            }
-        }
-        const double mu_t = fmax(warp_sum(s_mu), EPS);
-        const double var_t = fmax(warp_sum(s_var), EPS);
-        const double var_log_t = log(1.0 + var_t / (mu_t * mu_t));
-        const double mu_log_t = log(mu_t) - 0.5 * var_log_t;
-        double s_raw = 0.0;
-        if (PER > 0) {
-#pragma unroll
-            for (int p = 0; p < R; ++p) {
-                const int j = lane + 32 * p;
-                if (j < K) s_raw += remax_lognormal(loc[p], mu_t, var_log_t, mu_log_t).mu_raw;
-            }
-        } else {
-            for (int j = lane; j < K; j += 32)
-                s_raw += remax_lognormal(remax_mixture(mz[base + j], Sz[base + j]), mu_t,
-                                         var_log_t, mu_log_t).mu_raw;
-        }
-        const double sum_raw = fmax(warp_sum(s_raw), EPS);
-        if (PER > 0) {
-#pragma unroll
-            for (int p = 0; p < R; ++p) {
-                const int j = lane + 32 * p;
-                if (j < K) {
-                    const RemaxStage2 s2 = remax_lognormal(loc[p], mu_t, var_log_t, mu_log_t);
-                    remax_finish(loc[p], s2, sum_raw, ma[base + j], Sa[base + j], J[base + j]);
-                }
-            }
-        } else {
-            for (int j = lane; j < K; j += 32) {
-                const RemaxLocal l = remax_mixture(mz[base + j], Sz[base + j]);
-                const RemaxStage2 s2 = remax_lognormal(l, mu_t, var_log_t, mu_log_t);
-                remax_finish(l, s2, sum_raw, ma[base + j], Sa[base + j], J[base + j]);
-            }
-        }
-    }
+    for (int i = 0; i < G; ++i) s += red[i];
+    __syncthreads();  // the slots are written again by the next sum
+    return s;
 }
 
-// Rows of 128 < K <= kRemaxSmemK classes (attention scores): one warp per row;
-// each class's mixture moments (pass 1) are computed once and kept in shared
-// memory (float64), and pass 2 replaces them with the log-normal results that
-// the finish needs, so nothing is evaluated twice (remax_warp_kernel<0>
-// recomputes both stages from global memory). The kernel was bound by the
-// float64 divisions, square roots and conversions of the XU pipe; this cuts
-// the per-class transcendental work by about a quarter. A lane only touches
-// its own classes (j = lane mod 32) in a fixed order; the covariance term is
-// associated as ((e - 1) * mu_m / cdf) * mu_a instead of ((e - 1) * mu_a *
-// mu_m) / cdf, a float64 rounding difference.
-constexpr int kRemaxSmemK = 1024;
-constexpr int kRemaxSmemWarps = 8;
-// (two CTAs per SM fit the shared memory of K = 512; registers up to 128)
-__global__ void __launch_bounds__(32 * kRemaxSmemWarps, 2)
-    remax_smem_kernel(const float* mz, const float* Sz, float* ma, float* Sa, float* J,
-                      int64_t rows, int K, int64_t stride) {
-    constexpr double EPS = 1e-6;
-    extern __shared__ double remax_rs[];  // [warp][3][K]
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    double* mu_m = remax_rs + static_cast<size_t>(w) * 3 * K;
-    double* var_m = mu_m + K;
-    double* cdf = var_m + K;
-    const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-         row < rows; row += warps) {
-        const int64_t base = row * stride;
-        double s_mu = 0.0, s_var = 0.0;
-        for (int j = lane; j < K; j += 32) {
-            const RemaxLocal l = remax_mixture(mz[base + j], Sz[base + j]);
-            mu_m[j] = l.mu_m;
-            var_m[j] = l.var_m;
-            cdf[j] = l.cdf;
-            s_mu += l.mu_m;
-            s_var += l.var_m;
+// G warps per row. PER > 0: the row's classes stay in registers, class
+// j = (p * 32 G + t) * VEC + e for thread t < 32 G of the row's group, p < PER,
+// e < VEC (VEC = 4: 16-byte accesses; needs K and the row stride multiples of 4
+// and aligned pointers). PER = 0 (G = 1): any K, each pass re-reads the row
+// and recomputes the mixture. Rows are visited in block-uniform steps, so the
+// block barriers of group_sum are reached by every thread.
+template <int PER, int VEC, int G>
+__global__ void __launch_bounds__(256) remax_rows_kernel(const float* __restrict__ mz,
+                                                         const float* __restrict__ Sz,
+                                                         float* __restrict__ ma,
+                                                         float* __restrict__ Sa,
+                                                         float* __restrict__ J, int64_t rows,
+                                                         int K, int64_t stride) {
+    constexpr int R = PER > 0 ? PER * VEC : 1;
+    constexpr int GT = 32 * G;                 // threads of a row
+    constexpr int GROUPS = 256 / GT;           // rows per block step
+    __shared__ double red[GROUPS][G];
+    const int grp = threadIdx.x / GT, t = threadIdx.x % GT;
+    float nz[R], ns[R];  // the next row's inputs (PER > 0)
+    auto fetch = [&](int64_t r, float* z, float* s) {
+        if (PER == 0 || r >= rows) return;
+        const int64_t rb = r * stride;
+#pragma unroll
+        for (int p = 0; p < (PER > 0 ? PER : 1); ++p) {
+            const int j0 = (p * GT + t) * VEC;
+            if (j0 < K) {
+                if (VEC == 4) {
+                    const float4 a = *reinterpret_cast<const float4*>(mz + rb + j0);
+                    const float4 b = *reinterpret_cast<const float4*>(Sz + rb + j0);
+                    z[p * VEC] = a.x, z[p * VEC + 1] = a.y, z[p * VEC + 2] = a.z,
+                    z[p * VEC + 3] = a.w;
+                    s[p * VEC] = b.x, s[p * VEC + 1] = b.y, s[p * VEC + 2] = b.z,
+                    s[p * VEC + 3] = b.w;
+                } else {
+                    z[p] = mz[rb + j0];
+                    s[p] = Sz[rb + j0];
+                }
+            }
         }
-        const double mu_t = fmax(warp_sum(s_mu), EPS);
-        const double var_t = fmax(warp_sum(s_var), EPS);
-        const double var_log_t = log(1.0 + var_t / (mu_t * mu_t));
-        const double mu_log_t = log(mu_t) - 0.5 * var_log_t;
-        // pass 2: the log-normal stage of each class, its sum, and the factors of
-        // the finish that do not depend on that sum, stored over the class's
-        // three slots: mu_raw, exp(var_log_a) - 1 and
-        // (exp(var_log_m - cov_log) - 1) * mu_m / max(cdf, eps)
-        double s_raw = 0.0;
-        for (int j = lane; j < K; j += 32) {
-            RemaxLocal l;
-            l.mu_m = mu_m[j];
-            l.var_m = var_m[j];
-            const RemaxStage2 s2 = remax_lognormal(l, mu_t, var_log_t, mu_log_t);
-            s_raw += s2.mu_raw;
-            const double c = fmax(cdf[j], EPS);
-            mu_m[j] = s2.mu_raw;
-            var_m[j] = exp(s2.var_log_a) - 1.0;
-            cdf[j] = (exp(s2.var_log_m - s2.cov_log) - 1.0) * l.mu_m / c;
-        }
-        const double sum_raw = fmax(warp_sum(s_raw), EPS);
-        // pass 3: normalise (remax_finish with the stored factors)
-        for (int j = lane; j < K; j += 32) {
-            const double mu_a = mu_m[j] / sum_raw;
-            const double var_a = var_m[j] * mu_a * mu_a;
-            const double Szd = static_cast<double>(Sz[base + j]);
-            const double cov_a_z = fmin(sqrt(var_a * Szd), cdf[j] * mu_a);
-            ma[base + j] = static_cast<float>(mu_a);
-            Sa[base + j] = static_cast<float>(var_a);
-            J[base + j] = static_cast<float>(cov_a_z / Szd);
+    };
+    fetch(static_cast<int64_t>(blockIdx.x) * GROUPS + grp, nz, ns);
+    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * GROUPS; row0 < rows;
+         row0 += static_cast<int64_t>(gridDim.x) * GROUPS) {
+        const int64_t row = row0 + grp;
+        const bool live = row < rows;
+        const int64_t base = live ? row * stride : 0;
+        double sm = 0.0, sv = 0.0;
+        if (PER > 0) {
+            float cz[R], cs[R];
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                cz[i] = nz[i];
+                cs[i] = ns[i];
+            }
+            // the next row's loads are in flight while this row is computed
+            fetch(row + static_cast<int64_t>(gridDim.x) * GROUPS, nz, ns);
+            RemaxMix x[R];
+#pragma unroll
+            for (int p = 0; p < PER; ++p) {
+                if (live && (p * GT + t) * VEC < K) {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        x[p * VEC + e] = remax_mixture(cz[p * VEC + e], cs[p * VEC + e]);
+                        sm += x[p * VEC + e].m;
+                        sv += x[p * VEC + e].v;
+                    }
+                }
+            }
+            const double tm = group_sum<G>(sm, red[grp]);
+            const RemaxRow w = remax_row(tm, group_sum<G>(sv, red[grp]));
+            RemaxFactors f[R];
+            double sr = 0.0;
+#pragma unroll
+            for (int p = 0; p < PER; ++p) {
+                if (live && (p * GT + t) * VEC < K) {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) {
+                        f[p * VEC + e] = remax_factors(x[p * VEC + e], w);
+                        sr += f[p * VEC + e].raw;
+                    }
+                }
+            }
+            const float rsum =
+                1.0f / static_cast<float>(fmax(group_sum<G>(sr, red[grp]), 1e-6));
+#pragma unroll
+            for (int p = 0; p < PER; ++p) {
+                const int j0 = (p * GT + t) * VEC;
+                if (live && j0 < K) {
+                    float o[3][VEC];
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e)
+                        remax_out(f[p * VEC + e], rsum, cs[p * VEC + e], o[0][e], o[1][e],
+                                  o[2][e]);
+                    if (VEC == 4) {
+                        *reinterpret_cast<float4*>(ma + base + j0) =
+                            make_float4(o[0][0], o[0][1], o[0][2], o[0][3]);
+                        *reinterpret_cast<float4*>(Sa + base + j0) =
+                            make_float4(o[1][0], o[1][1], o[1][2], o[1][3]);
+                        *reinterpret_cast<float4*>(J + base + j0) =
+                            make_float4(o[2][0], o[2][1], o[2][2], o[2][3]);
+                    } else {
+                        ma[base + j0] = o[0][0];
+                        Sa[base + j0] = o[1][0];
+                        J[base + j0] = o[2][0];
+                    }
+                }
+            }
+        } else {
+            static_assert(PER > 0 || G == 1, "the re-reading form runs one warp per row");
+            const int lane = t;
+            if (live)
+                for (int j = lane; j < K; j += 32) {
+                    const RemaxMix x = remax_mixture(mz[base + j], Sz[base + j]);
+                    sm += x.m;
+                    sv += x.v;
+                }
+            const RemaxRow w = remax_row(warp_sum(sm), warp_sum(sv));
+            double sr = 0.0;
+            if (live)
+                for (int j = lane; j < K; j += 32)
+                    sr += remax_factors(remax_mixture(mz[base + j], Sz[base + j]), w).raw;
+            const float rsum = 1.0f / static_cast<float>(fmax(warp_sum(sr), 1e-6));
+            if (live)
+                for (int j = lane; j < K; j += 32) {
+                    const float s = Sz[base + j];
+                    remax_out(remax_factors(remax_mixture(mz[base + j], s), w), rsum, s,
+                              ma[base + j], Sa[base + j], J[base + j]);
+                }
         }
     }
 }
@@ -497,22 +536,23 @@ extern "C" int tagi_remax_forward(const float* mz, const float* Sz, float* ma, f
     if (rows == 0 || K == 0) return TAGI_OK;
     TAGI_REQUIRE(mz && Sz && ma && Sa && J, TAGI_E_BAD_ARG, "%s: null pointer", what);
     cudaStream_t st = as_stream(stream);
-    const unsigned grid = grid_1d(rows * 32, 256);
+    const int k = static_cast<int>(K);
+    const bool v4 = K % 4 == 0 && row_stride % 4 == 0 && all_aligned({mz, Sz, ma, Sa, J});
+#define TAGI_REMAX(P, V, G)                                                              \
+    remax_rows_kernel<P, V, G><<<grid_1d((rows + 256 / (32 * G) - 1) / (256 / (32 * G)), 1), \
+                                 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, k, row_stride)
+    // up to 128 classes one warp per row; above, four warps per row keep the
+    // registers per thread (and so the warps per SM) of a 128-class row
     if (K <= 32)
-        remax_warp_kernel<1><<<grid, 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
+        TAGI_REMAX(1, 1, 1);
     else if (K <= 128)
-        remax_warp_kernel<4><<<grid, 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
-    else if (K <= kRemaxSmemK) {
-        static bool attr = false;
-        const size_t smem = sizeof(double) * 3 * static_cast<size_t>(K) * kRemaxSmemWarps;
-        if (!attr) {
-            cudaFuncSetAttribute(remax_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(sizeof(double) * 3 * kRemaxSmemK * kRemaxSmemWarps));
-            attr = true;
-        }
-        remax_smem_kernel<<<grid_1d(rows * 32, 32 * kRemaxSmemWarps), 32 * kRemaxSmemWarps, smem,
-                            st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
-    } else
-        remax_warp_kernel<0><<<grid, 256, 0, st>>>(mz, Sz, ma, Sa, J, rows, (int)K, row_stride);
+        v4 ? TAGI_REMAX(1, 4, 1) : TAGI_REMAX(4, 1, 1);
+    else if (K <= 512)
+        v4 ? TAGI_REMAX(1, 4, 4) : TAGI_REMAX(4, 1, 4);
+    else if (K <= 1024)
+        v4 ? TAGI_REMAX(2, 4, 4) : TAGI_REMAX(8, 1, 4);
+    else
+        TAGI_REMAX(0, 1, 1);
+#undef TAGI_REMAX
     return check_launch(what);
 }
