@@ -198,7 +198,7 @@ ENTRY_BYTES = {
     # reads mz, Sz; writes ma, Sa, m_hat
     "tagi_bn_train_forward": lambda a: (20 + 8 * _planes(a[13])) * a[15] * a[16] * a[17],
     "tagi_bn_forward": lambda a: 4 * (5 + _planes(a[11])) * a[12] * a[13] * a[14],
-    "tagi_bn_backward": lambda a: (24 if a[7] else 20) * a[9] * a[10] * a[11],
+    "tagi_bn_backward": lambda a: (24 if a[7] else 20) * a[10] * a[11] * a[12],
     "tagi_avgpool_forward": lambda a: 8 * a[4] * a[5] * a[6] * a[7] * (1 + 1 / a[8] ** 2),
     "tagi_avgpool_backward": lambda a: 8 * a[4] * a[5] * a[6] * a[7] * (1 + 1 / a[8] ** 2),
     # patches written (mean, and variance if given) + image read
@@ -246,6 +246,7 @@ class LaunchTimer:
             "backward_delta", lambda a: 4.0 * a[5] * a[7] * a[8] * a[6] * a[9] * a[10] * a[10]),
         "tagi_param_grad": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
         "tagi_param_grad_t": ("param_grad", lambda a: 4.0 * a[8] * a[9] * a[10]),
+        "tagi_param_grad_bias_given": ("param_grad", lambda a: 4.0 * a[9] * a[10] * a[11]),
     }
 
     def __init__(self):

@@ -248,6 +248,21 @@ int tagi_param_grad_t(const float* at, int64_t ldat, const float* dmz, const flo
                       float* out_Sb, float cap_factor, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* tagi_param_grad (transposed = 0) or tagi_param_grad_t (transposed = 1) of a
+ * layer with a bias whose two column sums are already known: bias_sums holds
+ * 2*N float64 values, sum of dmz per column then sum of dSz (e.g. the
+ * delta_sums of tagi_bn_backward for the convolution feeding that BatchNorm).
+ * The bias row (row K) is taken from them (the same three modes), so the
+ * contraction covers the K weight rows only. Replaces the bias part of
+ * conv2d.py:344-354 (sum of the output deltas per channel). */
+int tagi_param_grad_bias_given(const float* a, int64_t lda, int transposed, const float* dmz,
+                               const float* dSz, int64_t d_div, int64_t d_outer,
+                               int64_t d_stride, int64_t d_nstride, int64_t M, int64_t K,
+                               int64_t N, const double* bias_sums, int mode, float* mw, float* Sw,
+                               float* mb, float* Sb, float* out_m, float* out_S, float* out_mb,
+                               float* out_Sb, float cap_factor, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Apply all-reduced raw sums (layout of TAGI_WGRAD_SUMS) as the capped update:
  * m += cap(S*g_m), S += cap(S^2*g_S), floor 1e-5 (parameters.py:77-96). */
 int tagi_apply_param_sums(const float* g_m, const float* g_S, int64_t K, int64_t N, int has_bias,
@@ -449,11 +464,15 @@ int tagi_bn_sync_forward(const float* mz, const float* Sz, const double* sums, d
  * of gamma (mg, Sw) and beta (mb, Sb) is also applied from the sums, as
  * tagi_bn_apply_grads in update mode would (mg is updated in place after every
  * block has read it); cap_factor <= 0 leaves the parameters alone.
+ * delta_sums (NULL: not computed; else 2*C float64): [0:C] = sum of the
+ * outgoing dmz, [C:2C] = sum of the outgoing dSz per channel, i.e. the bias
+ * sums of the convolution that produced this layer's input (through the ReLU
+ * given by relu_J, if any), for tagi_param_grad_bias_given.
  * Replaces batchnorm2d.py:436-513 (torch sums + _batchnorm_bwd_kernel). */
 int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat, const float* var,
                      float* mg, float* dmz, float* dSz, const float* relu_J, double* grads,
-                     int64_t N, int64_t C, int64_t HW, float eps, float* Sw, float* mb, float* Sb,
-                     float cap_factor, void* stream);
+                     double* delta_sums, int64_t N, int64_t C, int64_t HW, float eps, float* Sw,
+                     float* mb, float* Sb, float cap_factor, void* stream);
 
 /* Apply per-channel sums (tagi_bn_backward layout, possibly all-reduced):
  * mode TAGI_WGRAD_DELTAS writes the four delta vectors, TAGI_WGRAD_UPDATE

@@ -130,3 +130,48 @@ def test_mha_zero_deltas_leave_parameters():
     assert torch.count_nonzero(d_m) == 0 and torch.count_nonzero(d_S) == 0
     for a, b in zip(before, params([mha])):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,N,H", [
+    (64, 64, 3, 1, 8, 32),     # transposed patches, bias row inside the contraction
+    (256, 256, 3, 1, 16, 8),   # 2304 weight rows: the bias computed apart
+    (64, 128, 2, 2, 8, 16),    # 2x2 stride-2 projection (256 weight rows)
+    (3, 64, 3, 1, 4, 32),      # few weight rows
+])
+def test_conv_bias_sums_from_batchnorm(cin, cout, k, stride, N, H):
+    """Conv → ReLU → BatchNorm as a container runs it: the BatchNorm backward
+    sums its outgoing deltas per channel (tagi_bn_backward delta_sums) and the
+    convolution takes its bias sums from them (tagi_param_grad_bias_given).
+    The sums equal float64 sums of the deltas, and every parameter delta equals
+    that of the convolution's own backward (bias sums computed by itself)."""
+    from triton_tagi._chain import backward_chain
+
+    torch.manual_seed(cin + cout + k)
+    pad = 1 if k == 3 else 0
+    conv = TT.Conv2D(cin, cout, k, stride=stride, padding=pad, device=DEV)
+    relu, bn = TT.ReLU(), TT.BatchNorm2D(cout, device=DEV)
+    twin = TT.Conv2D(cin, cout, k, stride=stride, padding=pad, device=DEV)
+    for a, b in zip(params([twin]), params([conv])):
+        a.copy_(b)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(N, cin, H, H, generator=g).to(DEV)
+    Sx = (torch.rand(N, cin, H, H, generator=g) * 0.1).to(DEV)
+    mz, Sz = conv.forward(x, Sx)
+    twin.forward(x, Sx)
+    ma, Sa = relu.forward(mz, Sz)
+    bn.forward(ma, Sa)
+    dm = (torch.randn(mz.shape, generator=g) * 0.1).to(DEV)
+    dS = (-torch.rand(mz.shape, generator=g) * 1e-2).to(DEV)
+    d_in = backward_chain([conv, relu, bn], dm, dS)
+    # the deltas the convolution received: the BatchNorm+ReLU backward again
+    dmz, dSz = bn.backward(dm, dS, relu=relu, delta_sums=True)
+    sums = bn.delta_sums.cpu()
+    want = torch.cat([dmz.double().sum((0, 2, 3)), dSz.double().sum((0, 2, 3))]).cpu()
+    assert torch.allclose(sums, want, rtol=1e-9, atol=1e-12 * want.abs().max())
+    d_twin = twin.backward(dmz, dSz)
+    for a, b in zip(d_in, d_twin):
+        assert torch.equal(a, b)
+    for name in ("delta_mw", "delta_Sw", "delta_mb", "delta_Sb"):
+        got, ref = getattr(conv, name), getattr(twin, name)
+        err = ((got - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+        assert err <= 1e-6, (name, err)

@@ -551,12 +551,31 @@ __global__ void bias_finish_kernel(const GemmArgs g, int slices, const float* pa
     }
 }
 
+// The bias row from column sums computed elsewhere (float64 sums of the
+// deltas: sums[n] of the means, sums[N + n] of the variances).
+__global__ void bias_given_kernel(const GemmArgs g, const double* sums, int param, int row) {
+    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < g.N; n += gridDim.x * blockDim.x)
+        finish_one(g, param, static_cast<int64_t>(row) * g.N + n, static_cast<float>(sums[n]),
+                   static_cast<float>(sums[g.N + n]));
+}
+
 // Shared driver for the weight-gradient family (stores or parameter epilogue).
 // The workspace must hold the split-reduction partials when a split is planned;
 // room past them (256-byte aligned) takes the prepared B tiles (the deltas) of
 // the tensor-core kernel.
+// `bsums` (the bias row is the last of Mo): the bias row's sums are given.
 int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
-              const char* what) {
+              const char* what, const double* bsums = nullptr) {
+    if (bsums != nullptr) {
+        bias_given_kernel<<<grid_1d(g.N, 256), 256, 0, st>>>(g, bsums, param ? 1 : 0, Mo - 1);
+        int rc = check_launch(what);
+        if (rc) return rc;
+        GemmArgs gw = g;
+        gw.ones_row = -1;
+        rc = Mo > 1 ? run_wgrad(gw, Mo - 1, ws, ws_bytes, param, st, what) : TAGI_OK;
+        g.M = Mo;
+        return rc;
+    }
     if (bias_apart(Mo, g.N, g.Kr, g.ones_row == Mo - 1)) {
         size_t off = 0;
         const size_t total = bias_apart_bytes(Mo, g.N, g.Kr, &off);
@@ -967,9 +986,10 @@ int param_grad(const char* what, const float* a, int64_t a_rows, int64_t a_k, co
                int64_t d_nstride, int64_t M, int64_t K, int64_t N, int has_bias, int mode,
                float* mw, float* Sw, float* mb, float* Sb, float* out_m, float* out_S,
                float* out_mb, float* out_Sb, float cap_factor, void* workspace,
-               size_t workspace_bytes, void* stream) {
+               size_t workspace_bytes, void* stream, const double* bias_sums = nullptr) {
     TAGI_REQUIRE(!bad_size(M) && !bad_size(N) && !bad_size(K), TAGI_E_BAD_ARG, "%s: bad sizes",
                  what);
+    TAGI_REQUIRE(!bias_sums || has_bias, TAGI_E_BAD_ARG, "%s: bias sums without a bias", what);
     TAGI_REQUIRE(M == 0 || (a && dmz && dSz), TAGI_E_BAD_ARG, "%s: null input", what);
     if ((K + (has_bias ? 1 : 0)) == 0 || N == 0) return TAGI_OK;
     TAGI_REQUIRE(mode >= TAGI_WGRAD_SUMS && mode <= TAGI_WGRAD_UPDATE, TAGI_E_BAD_ARG,
@@ -993,7 +1013,7 @@ int param_grad(const char* what, const float* a, int64_t a_rows, int64_t a_k, co
     g.pe = ParamEpi{mode, (int)K, (int)N, mw, Sw, mb, Sb, out_m, out_S, out_mb, out_Sb,
                     cap_factor};
     return run_wgrad(g, (int)K + (has_bias ? 1 : 0), workspace, workspace_bytes, true,
-                     as_stream(stream), what);
+                     as_stream(stream), what, bias_sums);
 }
 }  // namespace
 }  // namespace tagi
@@ -1019,6 +1039,26 @@ extern "C" int tagi_param_grad_t(const float* at, int64_t ldat, const float* dmz
     return param_grad("tagi_param_grad_t", at, ldat, 1, dmz, dSz, d_div, d_outer, d_stride,
                       d_nstride, M, K, N, has_bias, mode, mw, Sw, mb, Sb, out_m, out_S, out_mb,
                       out_Sb, cap_factor, workspace, workspace_bytes, stream);
+}
+
+extern "C" int tagi_param_grad_bias_given(const float* a, int64_t lda, int transposed,
+                                          const float* dmz, const float* dSz, int64_t d_div,
+                                          int64_t d_outer, int64_t d_stride, int64_t d_nstride,
+                                          int64_t M, int64_t K, int64_t N,
+                                          const double* bias_sums, int mode, float* mw,
+                                          float* Sw, float* mb, float* Sb, float* out_m,
+                                          float* out_S, float* out_mb, float* out_Sb,
+                                          float cap_factor, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+    const char* what = "tagi_param_grad_bias_given";
+    TAGI_REQUIRE(bias_sums != nullptr, TAGI_E_BAD_ARG, "%s: null bias sums", what);
+    return transposed
+               ? param_grad(what, a, lda, 1, dmz, dSz, d_div, d_outer, d_stride, d_nstride, M, K,
+                            N, 1, mode, mw, Sw, mb, Sb, out_m, out_S, out_mb, out_Sb, cap_factor,
+                            workspace, workspace_bytes, stream, bias_sums)
+               : param_grad(what, a, 1, lda, dmz, dSz, d_div, d_outer, d_stride, d_nstride, M, K,
+                            N, 1, mode, mw, Sw, mb, Sb, out_m, out_S, out_mb, out_Sb, cap_factor,
+                            workspace, workspace_bytes, stream, bias_sums);
 }
 
 extern "C" int tagi_apply_param_sums(const float* g_m, const float* g_S, int64_t K, int64_t N,

@@ -202,19 +202,23 @@ __device__ __forceinline__ void vector_apply(int64_t i, double gm, double gS, in
 }
 
 // batchnorm2d.py:134-192 plus the gamma/beta sums of 465-482, one cluster per channel.
-template <bool V4>
+// SUMS: also the channel sums of the outgoing deltas (written to dsums[c] and
+// dsums[C + c]): the bias sums of a convolution whose outputs this layer
+// normalised (through a ReLU or not), which then need no pass of their own.
+template <bool V4, bool SUMS>
 __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     const float* dma, const float* dSa, const float* mhat, const float* var, float* mg,
-    float* dmz, float* dSz, const float* rj, double* grads, int N, int C, int HW, float eps,
-    float* Sw, float* mb, float* Sb, float cap) {
-    __shared__ double red[4 * 32];
-    __shared__ double part[4];
+    float* dmz, float* dSz, const float* rj, double* grads, double* dsums, int N, int C, int HW,
+    float eps, float* Sw, float* mb, float* Sb, float cap) {
+    constexpr int NV = SUMS ? 6 : 4;
+    __shared__ double red[NV * 32];
+    __shared__ double part[NV];
     const ChanSlab sl(N, C, HW, blockIdx.y);
     const float g = mg[sl.c];
     const float rs = var[sl.c];
     const float inv_std = 1.0f / sqrtf(rs + eps);
     const float inv_var = 1.0f / (rs + eps);
-    double v[4] = {0.0, 0.0, 0.0, 0.0};
+    double v[NV] = {};
     // rj: Jacobian of the ReLU that produced this layer's input (NULL: none);
     // applied to the outgoing deltas in the ReLU backward's own order.
     auto one = [&](float dm, float dS, float mh, float j, float& om, float& oS) {
@@ -227,6 +231,10 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
         if (rj) {
             om = om * j;
             oS = oS * j * j;
+        }
+        if (SUMS) {
+            v[NV - 2] += om;
+            v[NV - 1] += oS;
         }
     };
     if (V4) {
@@ -269,10 +277,14 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
             one(dma[o], dSa[o], mhat[o], rj ? rj[o] : 0.f, dmz[o], dSz[o]);
         }
     }
-    cluster_channel_sum<4>(v, red, part);
+    cluster_channel_sum<NV>(v, red, part);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) grads[j * C + sl.c] = v[j];
+        if (SUMS) {
+            dsums[sl.c] = v[4];
+            dsums[C + sl.c] = v[5];
+        }
         // cap > 0: the capped update of this channel's gamma/beta from the sums
         // (as tagi_bn_apply_grads); every block of the cluster read gamma before
         // the cluster-wide reduction above
@@ -735,9 +747,9 @@ extern "C" int tagi_bn_sync_forward(const float* mz, const float* Sz, const doub
 
 extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float* m_hat,
                                 const float* var, float* mg, float* dmz, float* dSz,
-                                const float* relu_J, double* grads, int64_t N, int64_t C,
-                                int64_t HW, float eps, float* Sw, float* mb, float* Sb,
-                                float cap_factor, void* stream) {
+                                const float* relu_J, double* grads, double* delta_sums,
+                                int64_t N, int64_t C, int64_t HW, float eps, float* Sw, float* mb,
+                                float* Sb, float cap_factor, void* stream) {
     const char* what = "tagi_bn_backward";
     TAGI_REQUIRE(N >= 0 && C >= 0 && HW >= 0 && C <= 65535, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     if (C == 0) return TAGI_OK;
@@ -751,12 +763,14 @@ extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float*
                          reinterpret_cast<uintptr_t>(m_hat) | reinterpret_cast<uintptr_t>(dmz) |
                          reinterpret_cast<uintptr_t>(dSz) | reinterpret_cast<uintptr_t>(relu_J);
     const bool v4 = HW % 4 == 0 && (al & 15) == 0;
-    return v4 ? launch_cluster(bn_backward_kernel<true>, S, (int)C, as_stream(stream), what, dma,
-                               dSa, m_hat, var, mg, dmz, dSz, relu_J, grads, (int)N, (int)C,
-                               (int)HW, eps, Sw, mb, Sb, cap_factor)
-              : launch_cluster(bn_backward_kernel<false>, S, (int)C, as_stream(stream), what, dma,
-                               dSa, m_hat, var, mg, dmz, dSz, relu_J, grads, (int)N, (int)C,
-                               (int)HW, eps, Sw, mb, Sb, cap_factor);
+#define TAGI_BN_BWD(V, SU)                                                                      \
+    launch_cluster(bn_backward_kernel<V, SU>, S, (int)C, as_stream(stream), what, dma, dSa, m_hat, \
+                   var, mg, dmz, dSz, relu_J, grads, delta_sums, (int)N, (int)C, (int)HW, eps, Sw, \
+                   mb, Sb, cap_factor)
+    const int rc = delta_sums ? (v4 ? TAGI_BN_BWD(true, true) : TAGI_BN_BWD(false, true))
+                              : (v4 ? TAGI_BN_BWD(true, false) : TAGI_BN_BWD(false, false));
+#undef TAGI_BN_BWD
+    return rc;
 }
 
 extern "C" int tagi_bn_apply_grads(const double* grads, int64_t C, int mode, float* mw, float* Sw,

@@ -38,6 +38,8 @@ _SIGS = {
     "tagi_param_grad_workspace_size": "iiin",
     "tagi_param_grad": "pipp" + "iiii" + "iii" + "nn" + "pppp" + "pppp" + "f" + "pz" + "p",
     "tagi_param_grad_t": "pipp" + "iiii" + "iii" + "nn" + "pppp" + "pppp" + "f" + "pz" + "p",
+    "tagi_param_grad_bias_given": "pin" + "pp" + "iiii" + "iii" + "pn" + "pppp" + "pppp" + "f"
+                                  + "pz" + "p",
     "tagi_apply_param_sums": "pp" + "ii" + "n" + "pppp" + "f" + "p",
     "tagi_bmm_tagi_var": "pppppp" + "iiii" + "iiiiiiiii" + "ff" + "p",
     "tagi_bmm_shared_right": "ppppp" + "iiii" + "iiiiiiiii" + "f" + "p",
@@ -61,7 +63,7 @@ _SIGS = {
     "tagi_bn_forward": "pppppppppppp" + "iii" + "f" + "p",
     "tagi_bn_train_forward": "ppppppppppppp" + "pp" + "iii" + "nn" + "ff" + "p",
     "tagi_bn_sync_forward": "ppp" + "d" + "p" * 13 + "iii" + "nn" + "ff" + "p",
-    "tagi_bn_backward": "ppppppp" + "pp" + "iii" + "f" + "ppp" + "f" + "p",
+    "tagi_bn_backward": "ppppppp" + "ppp" + "iii" + "f" + "ppp" + "f" + "p",
     "tagi_bn_apply_grads": "p" + "i" + "n" + "pppppppp" + "f" + "p",
     "tagi_rmsnorm_forward": "ppppppp" + "ii" + "f" + "p",
     "tagi_rmsnorm_backward": "pppppppp" + "ii" + "p",

@@ -28,20 +28,34 @@ def sums_numel(K: int, N: int, has_bias: bool) -> int:
 
 
 def weight_param_backward(layer, a, lda, dm, d_map, M, K, N, has_bias,
-                          transposed: bool = False) -> None:
+                          transposed: bool = False, bias_sums=None) -> None:
     """Parameter side of backward for a (K x N) weight and optional (1 x N) bias.
 
     a: activation matrix (M x K, row stride lda), or with ``transposed`` its
     transpose (K x M, row stride lda); dm = (dmz, dSz) with row map
-    d_map = (div, outer, stride, col_stride).
+    d_map = (div, outer, stride, col_stride). ``bias_sums``: the bias's two
+    column sums of (dmz, dSz), already computed (float64, 2 N values); the
+    contraction then covers the weight rows only.
     """
     contiguous_params(layer)
     dmz, dSz = dm
     mode = layer._param_mode
     L = lib()
-    entry = "tagi_param_grad_t" if transposed else "tagi_param_grad"
     hb = 1 if has_bias else 0
+    if bias_sums is not None and (not has_bias or bias_sums.numel() != 2 * N
+                                  or bias_sums.dtype != torch.float64):
+        raise ValueError("bias_sums must hold 2 * N float64 values of a layer with a bias")
     hold, wp, wn = workspace(L.size("tagi_param_grad_workspace_size", M, K, N, hb), a)
+    head = (dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N)
+
+    def run(code, params, outs, cap):
+        if bias_sums is None:
+            L("tagi_param_grad_t" if transposed else "tagi_param_grad", a.data_ptr(), lda, *head,
+              hb, code, *params, *outs, cap, wp, wn, stream(a))
+        else:
+            L("tagi_param_grad_bias_given", a.data_ptr(), lda, 1 if transposed else 0, *head,
+              bias_sums.data_ptr(), code, *params, *outs, cap, wp, wn, stream(a))
+
     null4 = (None, None, None, None)
     if mode == "deltas":
         dev = a.device
@@ -53,21 +67,17 @@ def weight_param_backward(layer, a, lda, dm, d_map, M, K, N, has_bias,
         outs = (layer.delta_mw.data_ptr(), layer.delta_Sw.data_ptr(),
                 layer.delta_mb.data_ptr() if has_bias else None,
                 layer.delta_Sb.data_ptr() if has_bias else None)
-        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
-          hb, WGRAD_DELTAS, None, layer.Sw.data_ptr(), None,
-          layer.Sb.data_ptr() if has_bias else None, *outs, 1.0, wp, wn, stream(a))
+        run(WGRAD_DELTAS, (None, layer.Sw.data_ptr(), None,
+                           layer.Sb.data_ptr() if has_bias else None), outs, 1.0)
     elif mode == "update":
-        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
-          hb, WGRAD_UPDATE, layer.mw.data_ptr(), layer.Sw.data_ptr(),
-          layer.mb.data_ptr() if has_bias else None, layer.Sb.data_ptr() if has_bias else None,
-          *null4, float(layer._cap), wp, wn, stream(a))
+        run(WGRAD_UPDATE, (layer.mw.data_ptr(), layer.Sw.data_ptr(),
+                           layer.mb.data_ptr() if has_bias else None,
+                           layer.Sb.data_ptr() if has_bias else None), null4, float(layer._cap))
         layer._updated_in_backward = True
     elif mode == "sums":
         buf = layer._reducer.buffer(layer, sums_numel(K, N, has_bias), torch.float32)
         half = buf.numel() // 2
-        L(entry, a.data_ptr(), lda, dmz.data_ptr(), dSz.data_ptr(), *d_map, M, K, N,
-          hb, WGRAD_SUMS, None, None, None, None, buf.data_ptr(), buf[half:].data_ptr(), None,
-          None, 1.0, wp, wn, stream(a))
+        run(WGRAD_SUMS, null4, (buf.data_ptr(), buf[half:].data_ptr(), None, None), 1.0)
         layer._reducer.ready(layer)
     else:
         raise ValueError(f"unknown parameter mode {mode!r}")

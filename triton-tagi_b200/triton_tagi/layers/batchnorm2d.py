@@ -136,10 +136,14 @@ class BatchNorm2D(LearnableLayer):
             triton_add_shortcut(residual[0], residual[1], ma, Sa)
         return ma, Sa
 
-    def backward(self, delta_ma: Tensor, delta_Sa: Tensor, relu=None) -> tuple[Tensor, Tensor]:
+    def backward(self, delta_ma: Tensor, delta_Sa: Tensor, relu=None,
+                 delta_sums: bool = False) -> tuple[Tensor, Tensor]:
         """Input deltas and the γ/β sums; with ``relu`` (the ReLU layer that feeds
         this one in a container) the deltas leave already multiplied by its
-        Jacobian, i.e. as ``relu.backward`` would return them."""
+        Jacobian, i.e. as ``relu.backward`` would return them. ``delta_sums``:
+        the same launch also sums the outgoing deltas per channel (float64,
+        means then variances) into ``self.delta_sums``: the bias sums of the
+        convolution before, which a container hands to its backward."""
         check_cuda_f32(delta_ma, delta_Sa)
         dma, dSa = delta_ma.contiguous(), delta_Sa.contiguous()
         N, C, H, W = self.input_shape
@@ -157,9 +161,12 @@ class BatchNorm2D(LearnableLayer):
                 raise ValueError("BatchNorm2D.backward: the ReLU has no Jacobian of this size")
             rj = relu.J.contiguous()
         upd = mode == "update"  # the capped update applied by the same launch
+        self.delta_sums = (torch.empty(2 * C, device=dev, dtype=torch.float64) if delta_sums
+                           else None)
         L("tagi_bn_backward", dma.data_ptr(), dSa.data_ptr(), self.m_hat.data_ptr(),
           self._norm_var.data_ptr(), self.mw.data_ptr(), dmz.data_ptr(), dSz.data_ptr(),
-          rj.data_ptr() if rj is not None else None, grads.data_ptr(), N, C, H * W,
+          rj.data_ptr() if rj is not None else None, grads.data_ptr(),
+          self.delta_sums.data_ptr() if delta_sums else None, N, C, H * W,
           float(self.eps), self.Sw.data_ptr() if upd else None,
           self.mb.data_ptr() if upd else None, self.Sb.data_ptr() if upd else None,
           float(self._cap) if upd else 0.0, st)

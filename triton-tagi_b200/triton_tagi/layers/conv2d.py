@@ -99,7 +99,12 @@ class Conv2D(LearnableLayer):
            self.padding_type, 1 if C % 8 == 0 else 0, wp, wn, stream(ma))
         return mz, Sz
 
-    def backward(self, delta_mz: Tensor, delta_Sz: Tensor) -> tuple[Tensor, Tensor]:
+    def backward(self, delta_mz: Tensor, delta_Sz: Tensor,
+                 bias_sums: Tensor | None = None) -> tuple[Tensor, Tensor]:
+        """Input deltas and the parameter side. ``bias_sums``: the per-channel
+        sums of (delta_mz, delta_Sz) when a container already has them (float64,
+        2·C_out values, e.g. from the BatchNorm backward that produced the
+        deltas); the bias then needs no pass over the deltas of its own."""
         check_cuda_f32(delta_mz, delta_Sz)
         dmz, dSz = delta_mz.contiguous(), delta_Sz.contiguous()
         N, C, H, W = self.input_shape
@@ -144,12 +149,13 @@ class Conv2D(LearnableLayer):
             lib()("tagi_im2col_t", self.input_ma.data_ptr(), pt.data_ptr(), N, C, H, W, k,
                   self.stride, p, self.padding_type, st)
             weight_param_backward(self, pt, N * L, (dmz, dSz), d_map, N * L, K, Co, True,
-                                  transposed=True)
+                                  transposed=True, bias_sums=bias_sums)
         else:
             pm = torch.empty(N * L, K, device=dev)
             lib()("tagi_im2col", self.input_ma.data_ptr(), None, pm.data_ptr(), None, N, C, H,
                   W, k, self.stride, p, self.padding_type, st)
-            weight_param_backward(self, pm, K, (dmz, dSz), d_map, N * L, K, Co, True)
+            weight_param_backward(self, pm, K, (dmz, dSz), d_map, N * L, K, Co, True,
+                                  bias_sums=bias_sums)
         return d_ma, d_Sa
 
     def update(self, cap_factor: float) -> None:
