@@ -231,6 +231,30 @@ def test_im2col_col2im_golden(golden, tag, k, s, p):
             np.testing.assert_allclose(out.cpu().numpy(), z[f"col2im_{tag}"], rtol=1e-6, atol=1e-5)
 
 
+@pytest.mark.parametrize("N,C,H,k,p,pt", [(4, 64, 32, 3, 1, 2), (4, 128, 16, 3, 1, 2),
+                                          (8, 256, 8, 3, 1, 2), (4, 64, 32, 2, 0, 1),
+                                          (3, 12, 20, 3, 1, 1), (2, 8, 12, 3, 1, 2)])
+def test_col2im_stride2_staged(N, C, H, k, p, pt):
+    """Stride-2 gathers of the ResNet downsampling layers (16-byte staged
+    kernel: C and W multiples of 4), both modes, against the oracle's gather
+    (same taps, same order)."""
+    from triton_tagi._lib import lib, stream
+
+    Ho, Wo = F.conv_out_hw(H, H, k, 2, p, pt)
+    gen = torch.Generator().manual_seed(C + H + k)
+    cm = rnd(gen, N * Ho * Wo, C * k * k)
+    cS = rnd(gen, N * Ho * Wo, C * k * k, kind="u")
+    dm, dS = g(cm), g(cS)
+    for mode, adjoint in ((0, False), (1, True)):
+        om = torch.empty(N, C, H, H, device=DEV)
+        oS = torch.empty_like(om)
+        lib()("tagi_col2im", dm.data_ptr(), dS.data_ptr(), om.data_ptr(), oS.data_ptr(),
+              N, C, H, H, k, 2, p, pt, mode, stream(om))
+        for got, src in ((om, cm), (oS, cS)):
+            ref = F.col2im(src, N, C, H, H, k, 2, p, pt, adjoint=adjoint)
+            np.testing.assert_allclose(got.cpu().numpy(), ref.numpy(), rtol=1e-6, atol=1e-6)
+
+
 @pytest.mark.parametrize("C,k,s,p,pt", [(4, 3, 1, 1, 1), (8, 3, 2, 1, 1), (4, 2, 2, 0, 1),
                                        (12, 5, 1, 2, 2), (16, 1, 1, 0, 1)])
 def test_im2col_vectorised_rows(C, k, s, p, pt):

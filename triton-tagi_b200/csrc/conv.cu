@@ -311,6 +311,96 @@ __global__ void col2im_img_kernel(const float* cm, const float* cS, float* dm, f
     }
 }
 
+// 16-byte asynchronous copy global -> shared (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+// Stride-2 gather with the kernel size known at compile time (KS = 2 or 3),
+// one CTA per (image, slice of cs channels): the slice's patch columns (cs*k*k
+// contiguous floats of each of the L patch rows, both planes) are staged with
+// 16-byte asynchronous copies (row stride rs = 4 mod 8 floats: a warp's reads
+// hit at most two rows per bank); then each thread sums 4 consecutive input
+// pixels of one row of one channel and stores them with one 16-byte store. A
+// warp covers one input row h of 32 / (W / 4) channels, so the taps kh that
+// reach the row are the same for the whole warp. Each pixel visits its taps in
+// (kh, kw) order, as col2im_kernel does, so the sums are bit-identical to it.
+template <int KS, bool ADJOINT>
+__global__ void __launch_bounds__(256) col2im_s2_kernel(const float* cm, const float* cS,
+                                                        float* dm, float* dS, ConvGeom g, int cs,
+                                                        int rs) {
+    extern __shared__ __align__(16) float stage[];  // [plane][L][rs]
+    constexpr int KK = KS * KS;
+    const int K = g.C * KK, L = g.Ho * g.Wo;
+    const int nslice = g.C / cs;
+    const int n = blockIdx.x / nslice, c0 = (blockIdx.x - n * nslice) * cs;
+    const int q4 = cs * KK / 4;  // 16-byte chunks of a patch row
+    const float rq4 = 1.f / q4;
+    const int64_t base = static_cast<int64_t>(n) * L * K + static_cast<int64_t>(c0) * KK;
+    for (int e = threadIdx.x; e < L * q4; e += blockDim.x) {
+        const int r = div_small(e, rq4), j = e - r * q4;
+        const int64_t src = base + static_cast<int64_t>(r) * K + 4 * j;
+        cp_async16(stage + r * rs + 4 * j, cm + src);
+        cp_async16(stage + (L + r) * rs + 4 * j, cS + src);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int W4 = g.W >> 2, units = cs * g.H * W4;
+    const float rW4 = 1.f / W4, rcs = 1.f / cs;
+    const int64_t plane = static_cast<int64_t>(g.H) * g.W;
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+        const int t = div_small(u, rW4), wg = u - t * W4;
+        const int h = div_small(t, rcs), cl = t - h * cs;
+        float am[4] = {0.f, 0.f, 0.f, 0.f}, aS[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kh = 0; kh < KS; ++kh) {
+            const int ohn = h + g.p_tl - kh;
+            // the reference's test (ohn % 2 == 0 with truncating division):
+            // odd numerators, negative ones included, never contribute
+            if (ohn & 1) continue;
+            const int oh = ohn / 2;
+            if (oh < 0 || oh >= g.Ho) continue;
+            const float* prow = stage + oh * g.Wo * rs + cl * KK + kh * KS;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int w = 4 * wg + e;
+#pragma unroll
+                for (int kw = 0; kw < KS; ++kw) {
+                    const int own = w + g.p_tl - kw;
+                    const int ow = own >= 0 ? (own >> 1) : -((-own) >> 1);  // truncating
+                    // the reference does not test own % 2 (conv2d.py:126); the adjoint does
+                    const bool ok = ow >= 0 && ow < g.Wo && (!ADJOINT || (own >= 0 && !(own & 1)));
+                    if (ok) {
+                        am[e] += prow[ow * rs + kw];
+                        aS[e] += prow[(L + ow) * rs + kw];
+                    }
+                }
+            }
+        }
+        const int64_t o = (static_cast<int64_t>(n) * g.C + c0 + cl) * plane +
+                          static_cast<int64_t>(h) * g.W + 4 * wg;
+        *reinterpret_cast<float4*>(dm + o) = make_float4(am[0], am[1], am[2], am[3]);
+        *reinterpret_cast<float4*>(dS + o) = make_float4(aS[0], aS[1], aS[2], aS[3]);
+    }
+}
+
+// Channel slice and shared row stride of col2im_s2_kernel (cs = 0: not
+// applicable): the largest power-of-two slice dividing C whose staging fits
+// 76 KB (three CTAs per SM), rows padded to 4 mod 8 floats.
+inline void col2im_s2_plan(const ConvGeom& g, int* cs_out, int* rs_out) {
+    *cs_out = 0;
+    const int kk = g.k * g.k, L = g.Ho * g.Wo;
+    if (g.s != 2 || (g.k != 2 && g.k != 3) || g.W % 4 != 0 || g.C % 4 != 0) return;
+    for (int cs = 1; cs <= g.C && cs <= 1024; cs *= 2) {
+        if (g.C % cs || (cs * kk) % 4) continue;
+        const int rs = (cs * kk) % 8 == 0 ? cs * kk + 4 : cs * kk;
+        if (2ll * L * rs * 4 > 76 * 1024) break;
+        *cs_out = cs;
+        *rs_out = rs;
+    }
+}
+
 // NCHW -> NHWC of one or two planes over the flattened pixel index q = n*HW + p:
 // 32 x 32 tiles of (channel, q) through shared memory (padded against bank
 // conflicts). Reads run along q (contiguous within each image plane, so small
@@ -555,6 +645,32 @@ extern "C" int tagi_col2im(const float* cm, const float* cS, float* dm, float* d
     const int64_t total = N * C * H * W;
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(cm && cS && dm && dS, TAGI_E_BAD_ARG, "%s: null pointer", what);
+    {
+        int cs = 0, rs = 0;
+        col2im_s2_plan(g, &cs, &rs);
+        const uintptr_t al = reinterpret_cast<uintptr_t>(cm) | reinterpret_cast<uintptr_t>(cS) |
+                             reinterpret_cast<uintptr_t>(dm) | reinterpret_cast<uintptr_t>(dS);
+        const int64_t ctas = cs > 0 ? N * (C / cs) : 0;
+        if (cs > 0 && (al & 15) == 0 && ctas <= INT_MAX &&
+            static_cast<int64_t>(g.Ho) * g.Wo * C * k * k < (int64_t(1) << 22)) {
+            static bool attr_set[4] = {false, false, false, false};
+            const size_t smem = 2ull * g.Ho * g.Wo * rs * sizeof(float);
+            cudaStream_t st = as_stream(stream);
+            auto run = [&](auto kernel, int which) {
+                if (!attr_set[which]) {
+                    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         76 * 1024);
+                    attr_set[which] = true;
+                }
+                kernel<<<static_cast<unsigned>(ctas), 256, smem, st>>>(cm, cS, dm, dS, g, cs, rs);
+            };
+            if (k == 3)
+                mode == 0 ? run(col2im_s2_kernel<3, false>, 0) : run(col2im_s2_kernel<3, true>, 1);
+            else
+                mode == 0 ? run(col2im_s2_kernel<2, false>, 2) : run(col2im_s2_kernel<2, true>, 3);
+            return check_launch(what);
+        }
+    }
     // Staged per (image, channel slice) when one channel's patch columns for the
     // image fit: both planes of L rows x cslice*k*k columns within 48 KB.
     const int64_t L = static_cast<int64_t>(g.Ho) * g.Wo, kk = k * k;
