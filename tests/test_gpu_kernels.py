@@ -279,6 +279,32 @@ def test_im2col_vectorised_rows(C, k, s, p, pt):
     np.testing.assert_array_equal(only.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
 
 
+@pytest.mark.parametrize("C,H,k,s,p,pt", [(128, 16, 3, 1, 1, 1), (64, 32, 3, 2, 1, 2),
+                                          (64, 32, 2, 2, 0, 1), (512, 4, 3, 1, 1, 1),
+                                          (12, 20, 3, 2, 1, 1), (6, 8, 2, 1, 0, 1)])
+def test_im2col_row_staged(C, H, k, s, p, pt):
+    """ResNet shapes (W and C*k*k multiples of 4: every channel's input lines
+    staged at once, 16-byte stores), both planes and the mean alone, bit-exact
+    against the oracle's unfold."""
+    from triton_tagi._lib import lib, stream
+
+    gen = torch.Generator().manual_seed(C + H + k)
+    N = 3
+    xm, xS = rnd(gen, N, C, H, H), rnd(gen, N, C, H, H, kind="u")
+    Ho, Wo = F.conv_out_hw(H, H, k, s, p, pt)
+    dm, dS = g(xm), g(xS)
+    pm = torch.empty(N * Ho * Wo, C * k * k, device=DEV)
+    pS = torch.empty_like(pm)
+    lib()("tagi_im2col", dm.data_ptr(), dS.data_ptr(), pm.data_ptr(), pS.data_ptr(), N, C, H, H,
+          k, s, p, pt, stream(pm))
+    np.testing.assert_array_equal(pm.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
+    np.testing.assert_array_equal(pS.cpu().numpy(), F.im2col(xS, k, s, p, pt).numpy())
+    only = torch.full_like(pm, 7.0)
+    lib()("tagi_im2col", dm.data_ptr(), None, only.data_ptr(), None, N, C, H, H, k, s, p, pt,
+          stream(pm))
+    np.testing.assert_array_equal(only.cpu().numpy(), F.im2col(xm, k, s, p, pt).numpy())
+
+
 @pytest.mark.parametrize("C,H,W,k,s,p,pt", [(24, 6, 300, 3, 1, 1, 1), (10, 5, 700, 5, 2, 2, 2),
                                              (64, 9, 9, 3, 1, 1, 1), (3, 33, 31, 7, 2, 3, 1)])
 def test_im2col_channel_slices(C, H, W, k, s, p, pt):

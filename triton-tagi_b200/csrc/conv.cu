@@ -401,6 +401,79 @@ inline void col2im_s2_plan(const ConvGeom& g, int* cs_out, int* rs_out) {
     }
 }
 
+// 16-byte asynchronous copy global -> shared, zero-filled when !ok (the
+// source is then not read).
+__device__ __forceinline__ void cp_async16_zfill(float* dst, const float* src, bool ok) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src),
+                 "r"(ok ? 16 : 0)
+                 : "memory");
+}
+
+// Patches of one output image row (image n, output row oh) per CTA with the
+// kernel size known at compile time (KS = 2 or 3) and every channel staged at
+// once: the C*KS input lines (oh*s - p + kh, W columns each; zeros for lines
+// outside the image) arrive by 16-byte asynchronous copies (line stride W + 4
+// floats), then the CTA's Wo*K contiguous patch floats are written four at a
+// time, consecutive threads storing consecutive 16-byte pieces. Needs W and
+// K = C*KS*KS multiples of 4 and 16-byte aligned pointers.
+template <int KS, int PLANES>
+__global__ void __launch_bounds__(256) im2col_row4_kernel(const float* xm, const float* xS,
+                                                          float* pm, float* pS, ConvGeom g) {
+    extern __shared__ __align__(16) float lines[];  // [plane][C * KS lines][W + 4]
+    constexpr int KK = KS * KS;
+    const int ls = g.W + 4, W4 = g.W >> 2;
+    const int n = blockIdx.x / g.Ho, oh = blockIdx.x - n * g.Ho;
+    const int K = g.C * KK, nlines = g.C * KS, pstride = nlines * ls;
+    const int ih0 = oh * g.s - g.p_tl;
+    const int64_t img = static_cast<int64_t>(n) * g.C * g.H * g.W;
+    const float rW4 = 1.f / W4;
+    for (int e = threadIdx.x; e < PLANES * nlines * W4; e += blockDim.x) {
+        int li = div_small(e, rW4);
+        const int q = e - li * W4;
+        const int pl = (PLANES == 2 && li >= nlines) ? 1 : 0;
+        li -= pl * nlines;
+        const int c = li / KS, ih = ih0 + (li - c * KS);
+        const bool in = static_cast<unsigned>(ih) < static_cast<unsigned>(g.H);
+        const float* src =
+            (pl ? xS : xm) + img + (static_cast<int64_t>(c) * g.H + (in ? ih : 0)) * g.W + 4 * q;
+        cp_async16_zfill(lines + pl * pstride + li * ls + 4 * q, src, in);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int64_t out0 = static_cast<int64_t>(blockIdx.x) * g.Wo * K;  // patch row (n, oh, 0)
+    const int total4 = g.Wo * K / 4;
+    const float rK = 1.f / K;
+    for (int e4 = threadIdx.x; e4 < total4; e4 += blockDim.x) {
+        const int e = 4 * e4;
+        const int ow = div_small(e, rK), j = e - ow * K;
+        int c = j / KK;
+        const int t = j - c * KK;
+        int kh = t / KS, kw = t - kh * KS;
+        const int iw0 = ow * g.s - g.p_tl;
+        float v[PLANES][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int iw = iw0 + kw;
+            const bool in = static_cast<unsigned>(iw) < static_cast<unsigned>(g.W);
+            const int a = (c * KS + kh) * ls + (in ? iw : 0);
+            v[0][u] = in ? lines[a] : 0.f;
+            if (PLANES == 2) v[PLANES - 1][u] = in ? lines[pstride + a] : 0.f;
+            if (++kw == KS) {
+                kw = 0;
+                if (++kh == KS) {
+                    kh = 0;
+                    ++c;
+                }
+            }
+        }
+        *reinterpret_cast<float4*>(pm + out0 + e) = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
+        if (PLANES == 2)
+            *reinterpret_cast<float4*>(pS + out0 + e) =
+                make_float4(v[PLANES - 1][0], v[PLANES - 1][1], v[PLANES - 1][2], v[PLANES - 1][3]);
+    }
+}
+
 // NCHW -> NHWC of one or two planes over the flattened pixel index q = n*HW + p:
 // 32 x 32 tiles of (channel, q) through shared memory (padded against bank
 // conflicts). Reads run along q (contiguous within each image plane, so small
@@ -612,6 +685,32 @@ extern "C" int tagi_im2col(const float* xm, const float* xS, float* pm, float* p
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(xm && pm && (xS == nullptr) == (pS == nullptr), TAGI_E_BAD_ARG,
                  "%s: null pointer", what);
+    {
+        // every channel's lines staged at once, 16-byte copies and stores
+        const int64_t smem = (xS ? 2 : 1) * C * k * (W + 4) * static_cast<int64_t>(sizeof(float));
+        const uintptr_t a16 = reinterpret_cast<uintptr_t>(xm) | reinterpret_cast<uintptr_t>(xS) |
+                              reinterpret_cast<uintptr_t>(pm) | reinterpret_cast<uintptr_t>(pS);
+        if ((k == 2 || k == 3) && W % 4 == 0 && (C * k * k) % 4 == 0 && (a16 & 15) == 0 &&
+            smem <= 96 * 1024 && N * g.Ho <= INT_MAX &&
+            static_cast<int64_t>(g.Wo) * C * k * k < (int64_t(1) << 22)) {
+            static bool attr_set[4] = {false, false, false, false};
+            const unsigned grid = static_cast<unsigned>(N * g.Ho);
+            cudaStream_t st = as_stream(stream);
+            auto run = [&](auto kernel, int which) {
+                if (!attr_set[which]) {
+                    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         96 * 1024);
+                    attr_set[which] = true;
+                }
+                kernel<<<grid, 256, static_cast<size_t>(smem), st>>>(xm, xS, pm, pS, g);
+            };
+            if (k == 3)
+                xS ? run(im2col_row4_kernel<3, 2>, 0) : run(im2col_row4_kernel<3, 1>, 1);
+            else
+                xS ? run(im2col_row4_kernel<2, 2>, 2) : run(im2col_row4_kernel<2, 1>, 3);
+            return check_launch(what);
+        }
+    }
     // staged lines of a channel slice within 32 KB of shared memory
     const int64_t line_bytes = (xS ? 2 : 1) * k * (W | 1) * static_cast<int64_t>(sizeof(float));
     const int64_t cslice = std::min<int64_t>(C, (32 * 1024) / line_bytes);
