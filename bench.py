@@ -218,10 +218,12 @@ ENTRY_BYTES = {
 # steps; the stem's weight sums run on CUDA cores and are not among them), and one
 # 4096 x 4096 x 4096 Linear forward scaled by M to the sweep's 8192-row headline
 # (A and the number of B re-reads both grow with M).
+# DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum), family
+# averages; r18: a batch-64 capture of one step's 59 tensor-core launches, doubled
 MEASURED_TRAFFIC = {
-    ("r18", "moment_forward"): 53.2e6,
-    ("r18", "backward_delta"): 44.6e6,
-    ("r18", "param_grad"): 154.6e6,
+    ("r18", "moment_forward"): 63.1e6,
+    ("r18", "backward_delta"): 37.4e6,
+    ("r18", "param_grad"): 157.2e6,
     ("swp", "moment_forward"): 2 * 1.833e9,
 }
 
