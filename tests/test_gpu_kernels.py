@@ -459,20 +459,23 @@ def test_avgpool_and_add():
     assert torch.equal(a, 2 * a2) and torch.equal(b, 2 * b2)
 
 
-def test_rmsnorm_against_oracle():
+@pytest.mark.parametrize("B,S,E", [(3, 50, 96), (2, 9, 50), (8, 512, 512)])
+def test_rmsnorm_against_oracle(B, S, E):
+    """Rows of 4-column groups (16-byte path) and not, and the transformer's
+    width (column sums by clusters of row slices)."""
     import oracle.net as ON
     from triton_tagi import RMSNorm
 
     gen = torch.Generator().manual_seed(12)
-    ref, dev = ON.RMSNorm(96), RMSNorm(96, device=DEV)
-    ref.mw = ref.mw + rnd(gen, 96, scale=0.1)
+    ref, dev = ON.RMSNorm(E), RMSNorm(E, device=DEV)
+    ref.mw = ref.mw + rnd(gen, E, scale=0.1)
     dev.mw = g(ref.mw)
-    ma, Sa = rnd(gen, 3, 50, 96), rnd(gen, 3, 50, 96, kind="u", scale=0.1)
+    ma, Sa = rnd(gen, B, S, E), rnd(gen, B, S, E, kind="u", scale=0.1)
     rm, rS = ref.forward(ma, Sa)
     gm, gS = dev.forward(g(ma), g(Sa))
     assert_rel(gm, rm, 1e-5, "rms mz")
     assert_rel(gS, rS, 1e-4, "rms Sz")
-    dm, dS = rnd(gen, 3, 50, 96, scale=0.1), -rnd(gen, 3, 50, 96, kind="u", scale=0.01)
+    dm, dS = rnd(gen, B, S, E, scale=0.1), -rnd(gen, B, S, E, kind="u", scale=0.01)
     r = ref.backward(dm, dS)
     d = dev.backward(g(dm), g(dS))
     assert_rel(d[0], r[0], 1e-5, "rms dma")

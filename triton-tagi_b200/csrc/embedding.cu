@@ -10,7 +10,8 @@
 // the token ids in order and adds the matching delta rows in token order, so a
 // row's sum is the same sequence of fp32 additions as the reference's CPU
 // index_add (product rounded, then added). The scan is O(V x tokens) id compares
-// (cheap for the vocabularies of this path: 64 rows x 16384 tokens).
+// (cheap for the vocabularies of this path: 64 rows x 16384 tokens); the loads of
+// the matching rows are issued ahead of the ordered adds.
 
 #include <cstdint>
 
@@ -55,37 +56,86 @@ __global__ void embedding_fwd_kernel(const float* idx, const float* mw, const fl
 
 constexpr int kEmbIds = 1024;  // token ids staged per pass
 constexpr int kEmbCols = 256;  // columns per CTA (one per thread)
+constexpr int kEmbAhead = 8;   // delta rows loaded ahead of the ordered adds
 
 // CTA (v, slice): columns slice*256 .. +255 of vocabulary row v. Sums mode
 // (Sw == nullptr): out = sum dm, sum dS over the row's tokens; deltas mode:
 // out_m = sum dm*Sw[v], out_S = sum (dS*Sw[v])*Sw[v] (the reference's product
-// order; each product rounded, then added, in token order).
+// order; each product rounded, then added, in token order). Per pass of
+// kEmbIds token ids, the positions of the row's tokens are compacted in token
+// order (warp ballots, then the warps' counts in warp order); each thread then
+// loads kEmbAhead delta rows at a time before adding them in that order.
 __global__ void __launch_bounds__(kEmbCols) embedding_bwd_kernel(
     const float* idx, const float* dm, const float* dS, const float* Sw, int64_t n, int64_t V,
     int64_t D, int64_t pad, float* out_m, float* out_S) {
-    __shared__ int ids[kEmbIds];
+    __shared__ int pos[kEmbIds];
+    __shared__ int wcount[kEmbCols / 32 + 1];
     const int v = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kWarps = kEmbCols / 32;
     const int64_t col = static_cast<int64_t>(blockIdx.y) * kEmbCols + threadIdx.x;
     const bool on = col < D;
     const float w = (Sw && on) ? Sw[v * D + col] : 1.f;
     float am = 0.f, aS = 0.f;
     for (int64_t t0 = 0; t0 < n; t0 += kEmbIds) {
         const int cnt = static_cast<int>(n - t0 < kEmbIds ? n - t0 : kEmbIds);
+        // each warp owns kEmbIds / kWarps consecutive ids of the pass
+        constexpr int kPer = kEmbIds / kWarps;
+        const int base = warp * kPer;
+        int mine = 0;
+        for (int j = 0; j < kPer; j += 32) {
+            const int i = base + j + lane;
+            const bool hit = i < cnt && token_id(idx[t0 + i], V, pad) == v;
+            mine += __popc(__ballot_sync(0xffffffffu, hit));
+        }
+        if (lane == 0) wcount[warp] = mine;
         __syncthreads();
-        for (int i = threadIdx.x; i < cnt; i += blockDim.x) ids[i] = token_id(idx[t0 + i], V, pad);
+        if (threadIdx.x == 0) {
+            int run = 0;
+            for (int k = 0; k < kWarps; ++k) {
+                const int c = wcount[k];
+                wcount[k] = run;
+                run += c;
+            }
+            wcount[kWarps] = run;
+        }
         __syncthreads();
-        if (!on) continue;
-        for (int i = 0; i < cnt; ++i) {
-            if (ids[i] != v) continue;  // warp-uniform: every lane reads the same id
-            const int64_t o = (t0 + i) * D + col;
-            if (Sw) {
-                am = __fadd_rn(am, __fmul_rn(dm[o], w));
-                aS = __fadd_rn(aS, __fmul_rn(__fmul_rn(dS[o], w), w));
-            } else {
-                am = __fadd_rn(am, dm[o]);
-                aS = __fadd_rn(aS, dS[o]);
+        int at = wcount[warp];
+        for (int j = 0; j < kPer; j += 32) {
+            const int i = base + j + lane;
+            const bool hit = i < cnt && token_id(idx[t0 + i], V, pad) == v;
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (hit) pos[at + __popc(m & ((1u << lane) - 1u))] = i;
+            at += __popc(m);
+        }
+        __syncthreads();
+        const int total = wcount[kWarps];
+        if (on) {
+            for (int k0 = 0; k0 < total; k0 += kEmbAhead) {
+                float xm[kEmbAhead], xs[kEmbAhead];
+#pragma unroll
+                for (int u = 0; u < kEmbAhead; ++u) {
+                    if (k0 + u < total) {
+                        const int64_t o = (t0 + pos[k0 + u]) * D + col;
+                        xm[u] = dm[o];
+                        xs[u] = dS[o];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kEmbAhead; ++u) {
+                    if (k0 + u < total) {
+                        if (Sw) {
+                            am = __fadd_rn(am, __fmul_rn(xm[u], w));
+                            aS = __fadd_rn(aS, __fmul_rn(__fmul_rn(xs[u], w), w));
+                        } else {
+                            am = __fadd_rn(am, xm[u]);
+                            aS = __fadd_rn(aS, xs[u]);
+                        }
+                    }
+                }
             }
         }
+        __syncthreads();  // pos and wcount are rewritten by the next pass
     }
     if (on) {
         out_m[v * D + col] = am;

@@ -578,15 +578,43 @@ __global__ void rmsnorm_bwd_prop_kernel(const float* dmz, const float* dSz, cons
     }
 }
 
-// Column sums over rows: block = 32 columns x 32 row-lanes.
-__global__ void rmsnorm_bwd_sums_kernel(const float* dmz, const float* dSz, const float* ma,
-                                        const float* inv_rms, double* sums, int64_t rows,
-                                        int ni) {
-    __shared__ double sm[2][32][33];
-    const int col = blockIdx.x * 32 + threadIdx.x;
+// The same, 4 columns per thread (ni a multiple of 4, 16-byte aligned rows):
+// thread t of a block keeps column group t % q (q = ni / 4 <= blockDim.x) and
+// its gamma values and walks rows blockDim.x / q apart.
+__global__ void rmsnorm_bwd_prop_v4_kernel(const float4* dmz, const float4* dSz,
+                                           const float* inv_rms, const float4* mw, float4* dma,
+                                           float4* dSa, int64_t rows, int q) {
+    const int per = blockDim.x / q;
+    if (static_cast<int>(threadIdx.x) >= per * q) return;
+    const int c4 = threadIdx.x % q;
+    const float4 w = mw[c4];
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * per + threadIdx.x / q; r < rows;
+         r += static_cast<int64_t>(gridDim.x) * per) {
+        const float inv = inv_rms[r];
+        const int64_t o = r * q + c4;
+        const float4 m = dmz[o], S = dSz[o];
+        const float tx = inv * w.x, ty = inv * w.y, tz = inv * w.z, tw = inv * w.w;
+        dma[o] = make_float4(tx * m.x, ty * m.y, tz * m.z, tw * m.w);
+        dSa[o] = make_float4(tx * tx * S.x, ty * ty * S.y, tz * tz * S.z, tw * tw * S.w);
+    }
+}
+
+// Column sums over rows: one cluster of S blocks per 32 columns (gridDim.y =
+// column blocks); block j of a cluster takes rows j*R + ly, stepping S*R (R =
+// blockDim.x / 32 row lanes, lane = column); the block's lanes are added in
+// row-lane order, then the cluster's blocks in rank order (deterministic).
+__global__ void __launch_bounds__(kBnThreads) rmsnorm_bwd_sums_kernel(
+    const float* dmz, const float* dSz, const float* ma, const float* inv_rms, double* sums,
+    int64_t rows, int ni) {
+    constexpr int R = kBnThreads / 32;
+    __shared__ double sm[2][R][33];
+    __shared__ double part[2][32];
+    const int lx = threadIdx.x & 31, ly = threadIdx.x >> 5;
+    const int col = blockIdx.y * 32 + lx;
     double s_mu = 0.0, s_var = 0.0;
     if (col < ni) {
-        for (int64_t r = threadIdx.y; r < rows; r += blockDim.y) {
+        for (int64_t r = static_cast<int64_t>(blockIdx.x) * R + ly; r < rows;
+             r += static_cast<int64_t>(gridDim.x) * R) {
             const float inv = inv_rms[r];
             const int64_t o = r * ni + col;
             const float x = ma[o];
@@ -594,18 +622,31 @@ __global__ void rmsnorm_bwd_sums_kernel(const float* dmz, const float* dSz, cons
             s_var += static_cast<double>(inv * inv * x * x * dSz[o]);
         }
     }
-    sm[0][threadIdx.y][threadIdx.x] = s_mu;
-    sm[1][threadIdx.y][threadIdx.x] = s_var;
+    sm[0][ly][lx] = s_mu;
+    sm[1][ly][lx] = s_var;
     __syncthreads();
-    if (threadIdx.y == 0 && col < ni) {
+    if (ly == 0) {
         double a = 0.0, b = 0.0;
-        for (int y = 0; y < static_cast<int>(blockDim.y); ++y) {
-            a += sm[0][y][threadIdx.x];
-            b += sm[1][y][threadIdx.x];
+        for (int y = 0; y < R; ++y) {
+            a += sm[0][y][lx];
+            b += sm[1][y][lx];
+        }
+        part[0][lx] = a;
+        part[1][lx] = b;
+    }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0 && ly == 0 && col < ni) {
+        double a = 0.0, b = 0.0;
+        for (unsigned rk = 0; rk < cluster.num_blocks(); ++rk) {
+            const double* peer = cluster.map_shared_rank(&part[0][0], rk);
+            a += peer[lx];
+            b += peer[32 + lx];
         }
         sums[col] = a;
         sums[ni + col] = b;
     }
+    cluster.sync();  // peers keep their shared memory until it has been read
 }
 
 }  // namespace
@@ -832,14 +873,28 @@ extern "C" int tagi_rmsnorm_backward(const float* dmz, const float* dSz, const f
                  "%s: null pointer", what);
     cudaStream_t st = as_stream(stream);
     if (rows > 0) {
-        rmsnorm_bwd_prop_kernel<<<grid_1d(rows * ni, 256), 256, 0, st>>>(dmz, dSz, inv_rms, mw,
-                                                                         dma, dSa, rows * ni,
-                                                                         (int)ni);
+        const int q = static_cast<int>(ni / 4);
+        const uintptr_t al = reinterpret_cast<uintptr_t>(dmz) | reinterpret_cast<uintptr_t>(dSz) |
+                             reinterpret_cast<uintptr_t>(mw) | reinterpret_cast<uintptr_t>(dma) |
+                             reinterpret_cast<uintptr_t>(dSa);
+        if (ni % 4 == 0 && q <= 256 && (al & 15) == 0) {
+            const int per = 256 / q;
+            rmsnorm_bwd_prop_v4_kernel<<<grid_1d((rows + per - 1) / per, 1), 256, 0, st>>>(
+                reinterpret_cast<const float4*>(dmz), reinterpret_cast<const float4*>(dSz),
+                inv_rms, reinterpret_cast<const float4*>(mw), reinterpret_cast<float4*>(dma),
+                reinterpret_cast<float4*>(dSa), rows, q);
+        } else {
+            rmsnorm_bwd_prop_kernel<<<grid_1d(rows * ni, 256), 256, 0, st>>>(
+                dmz, dSz, inv_rms, mw, dma, dSa, rows * ni, (int)ni);
+        }
         int rc = check_launch(what);
         if (rc) return rc;
     }
-    dim3 blk(32, 32);
-    rmsnorm_bwd_sums_kernel<<<(unsigned)((ni + 31) / 32), blk, 0, st>>>(dmz, dSz, ma, inv_rms, sums,
-                                                                        rows, (int)ni);
-    return check_launch(what);
+    // clusters of up to 8 blocks along the rows, enough to fill the SMs
+    const int64_t cblocks = (ni + 31) / 32;
+    int S = 1;
+    while (S < 8 && cblocks * S < 2 * kNumSMs && S * (kBnThreads / 32) < rows) S *= 2;
+    TAGI_REQUIRE(cblocks <= 65535, TAGI_E_UNSUPPORTED, "%s: too many columns", what);
+    return launch_cluster(rmsnorm_bwd_sums_kernel, S, static_cast<int>(cblocks), st, what, dmz,
+                          dSz, ma, inv_rms, sums, rows, static_cast<int>(ni));
 }
