@@ -331,8 +331,9 @@ int tagi_jacobian_backward(const float* dm, const float* dS, const float* J, flo
 /* Row-wise Remax over K classes. Replaces triton_remax,
  * triton_tagi/layers/remax.py:122-164. The same moments as the reference's
  * log-normal closed form, evaluated through exact rational forms without its
- * cancelling exp/log pairs (float32 with float64 row sums): within a few 1e-6
- * relative of a float64 evaluation of the reference's formulas. */
+ * cancelling exp/log pairs (float32 with float64 row sums, hardware
+ * approximations for exp, sqrt and divisions): within ~1e-5 relative of a
+ * float64 evaluation of the reference's formulas. */
 int tagi_remax_forward(const float* mz, const float* Sz, float* ma, float* Sa, float* J,
                        int64_t rows, int64_t K, int64_t row_stride, void* stream);
 

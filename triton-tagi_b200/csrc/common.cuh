@@ -76,12 +76,14 @@ __device__ __forceinline__ float poly5(const float (&c)[6], float t) {
 // The shared core: (mu, var, Phi) through the Mills-ratio forms above, without
 // the reference ReLU's alpha < -5 branch; returns alpha and phi(alpha).
 // EXACT_EXP evaluates phi with expf instead of the hardware approximation
-// (about 1e-6 relative near |alpha| = 8).
+// (about 1e-6 relative near |alpha| = 8); FAST_ALPHA forms alpha and sd from
+// the hardware reciprocal square root instead of a correctly rounded sqrt and
+// division.
 struct RectGauss {
     float mu, v, cdf, alpha, pdf, Ss;
 };
 
-template <bool EXACT_EXP>
+template <bool EXACT_EXP, bool FAST_ALPHA = false>
 __device__ __forceinline__ RectGauss rect_gauss(float mz, float Sz) {
     constexpr float kInvSqrt2Pi = 0.3989422804014327f;
     constexpr float kR[6] = {1.253314207e+00f, 1.188586252e+00f, 5.311839209e-01f,
@@ -94,8 +96,17 @@ __device__ __forceinline__ RectGauss rect_gauss(float mz, float Sz) {
                              5.458146858e-01f, 1.276858994e-01f, 1.468004551e-02f};
     RectGauss g;
     g.Ss = fmaxf(Sz, 1e-30f);
-    const float sd = sqrtf(g.Ss);
-    g.alpha = mz / sd;  // correctly rounded: decides the reference ReLU's branch at -5
+    float sd;
+    if (FAST_ALPHA) {
+        // callers without a branch on alpha: the hardware reciprocal square root
+        // (a few ulp on alpha and sd)
+        const float rs = rsqrtf(g.Ss);
+        sd = g.Ss * rs;
+        g.alpha = mz * rs;
+    } else {
+        sd = sqrtf(g.Ss);
+        g.alpha = mz / sd;  // correctly rounded: decides the reference ReLU's branch at -5
+    }
     const float e = -0.5f * g.alpha * g.alpha;
     g.pdf = (EXACT_EXP ? expf(e) : __expf(e)) * kInvSqrt2Pi;
     const float t = fminf(fabsf(g.alpha), 8.0f);

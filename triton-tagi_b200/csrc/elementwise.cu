@@ -188,6 +188,9 @@ __global__ void avgpool_bwd_kernel(const float* dm, const float* dS, float* om, 
 // relative accuracy; T and V are summed in float64 so that D and E (which
 // subtract a class from its row's sum) keep theirs when one class dominates.
 // The mixture moments come from rect_gauss (no cancelling term either). The
+// kernel is issue-bound at attention sizes, so alpha, the exponential, the
+// square roots and the divisions use the hardware approximations (a few ulp;
+// the forms above keep that from growing). The
 // reference clamps m at eps before its variance expression, which then equals
 // V_true + (mu - m)(mu + m - 2 mz); that correction is applied where the
 // clamp is active. The reference's clamp of the log-normal variance at 0 is
@@ -198,7 +201,7 @@ struct RemaxMix {
 
 __device__ __forceinline__ RemaxMix remax_mixture(float mz, float Sz) {
     constexpr float EPS = 1e-6f;
-    const RectGauss g = rect_gauss<true>(mz, Sz);
+    const RectGauss g = rect_gauss<false, true>(mz, Sz);
     RemaxMix r;
     r.m = fmaxf(g.mu, EPS);
     const float v = r.m == g.mu ? g.v : fmaf(g.mu - r.m, g.mu + r.m - 2.0f * mz, g.v);
@@ -233,11 +236,11 @@ __device__ __forceinline__ RemaxFactors remax_factors(const RemaxMix& x, const R
     const float D = static_cast<float>(fmax(w.T - static_cast<double>(x.m), 0.0));
     const float E = static_cast<float>(fmax(w.V - static_cast<double>(x.v), 0.0));
     const float den = fmaf(x.m, w.Tf, x.v);  // >= eps (v >= eps)
-    const float rd = __frcp_rn(den);
+    const float rd = __fdividef(1.0f, den);
     RemaxFactors f;
     f.raw = fmaxf(x.m * x.m * w.one_t * rd, EPS);
     f.qv = fmaf(x.v * D, D, E * fmaf(x.m, x.m, x.v)) * rd * rd;
-    f.qc = (x.v * D) / (den * fmaxf(x.cdf, EPS));
+    f.qc = __fdividef(x.v * D * rd, fmaxf(x.cdf, EPS));
     return f;
 }
 
@@ -246,10 +249,11 @@ __device__ __forceinline__ void remax_out(const RemaxFactors& f, float rsum, flo
                                           float& Sa, float& J) {
     const float mu_a = f.raw * rsum;
     const float var_a = mu_a * mu_a * f.qv;
-    const float cov = fminf(sqrtf(var_a * Sz), f.qc * mu_a);
+    const float p = var_a * Sz;
+    const float cov = fminf(p > 0.f ? p * rsqrtf(p) : 0.f, f.qc * mu_a);
     ma = mu_a;
     Sa = var_a;
-    J = cov * __frcp_rn(Sz);
+    J = __fdividef(cov, Sz);
 }
 
 __device__ __forceinline__ double warp_sum(double v) {
