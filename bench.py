@@ -741,6 +741,68 @@ def sweep_arm(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+MICRO = ("remax", "col2im", "im2col")
+
+
+def micro_arm(which: str) -> None:
+    """Profiling drivers: one library entry on the benchmark shapes, 3 warm-up
+    and 10 timed calls per shape (CUDA events), one line per shape. remax: the
+    transformer's score rows (32768 x 512, a quarter of one layer's);
+    col2im / im2col: the ResNet-18 (batch 128) stride-2 gathers and the patches
+    of the weight sums."""
+    import triton_tagi  # noqa: F401  (loads the library)
+    from triton_tagi._lib import lib
+    from triton_tagi.layers.remax import triton_remax
+
+    L = lib()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def timed(fn, n=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return 1e3 * e0.elapsed_time(e1) / n
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    N = 128
+    if which == "remax":
+        mz = torch.randn(32768, 512, device="cuda", generator=g) * 2
+        Sz = torch.rand(32768, 512, device="cuda", generator=g) * 2 + 1e-3
+        us = timed(lambda: triton_remax(mz, Sz))
+        print(f"remax 32768x512: {us:.1f} us, {20 * mz.numel() / us / 1e3:.0f} GB/s")
+        return
+    shapes = {"col2im": ((64, 32, 3, 1, 2), (128, 16, 3, 1, 2), (256, 8, 3, 1, 2),
+                         (64, 32, 2, 0, 1), (128, 16, 2, 0, 1), (256, 8, 2, 0, 1)),
+              "im2col": ((64, 32, 3, 1, 2), (128, 16, 3, 1, 1), (128, 16, 3, 1, 2),
+                         (256, 8, 3, 1, 1), (256, 8, 3, 1, 2), (512, 4, 3, 1, 1),
+                         (64, 32, 2, 0, 1))}[which]
+    for C, H, k, p, pt in shapes:
+        s = 2 if (which == "col2im" or pt == 2 or k == 2) else 1
+        Ho = (H + (p if pt == 2 else 2 * p) - k) // s + 1
+        K = C * k * k
+        if which == "col2im":
+            cm = torch.randn(N * Ho * Ho, K, device="cuda", generator=g)
+            cS = torch.rand(N * Ho * Ho, K, device="cuda", generator=g)
+            dm = torch.empty(N, C, H, H, device="cuda")
+            dS = torch.empty_like(dm)
+            us = timed(lambda: L("tagi_col2im", cm.data_ptr(), cS.data_ptr(), dm.data_ptr(),
+                                 dS.data_ptr(), N, C, H, H, k, s, p, pt, 0, st))
+            nbytes = 8 * (cm.numel() + dm.numel())
+        else:
+            x = torch.randn(N, C, H, H, device="cuda", generator=g)
+            pm = torch.empty(N * Ho * Ho, K, device="cuda")
+            us = timed(lambda: L("tagi_im2col", x.data_ptr(), None, pm.data_ptr(), None, N, C,
+                                 H, H, k, s, p, pt, st))
+            nbytes = 4 * (x.numel() + pm.numel())
+        print(f"{which} C{C} H{H} k{k} s{s}: {us:.1f} us, {nbytes / us / 1e3:.0f} GB/s")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -760,7 +822,13 @@ def main():
                          "(NCCL collectives included) from a CUDA graph")
     ap.add_argument("--no-subrecords", action="store_true",
                     help="skip the MLP and sweep sub-records of the default line")
+    ap.add_argument("--micro", choices=MICRO, default=None,
+                    help="profiling driver: time one library entry on the benchmark shapes "
+                         "instead of a workload step (no JSON line)")
     args = ap.parse_args()
+    if args.micro is not None:
+        micro_arm(args.micro)
+        return
     if args.batch is not None:
         WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], batch=args.batch)
     world = int(os.environ.get("WORLD_SIZE", "1"))
