@@ -414,9 +414,10 @@ __device__ __forceinline__ void cp_async16_zfill(float* dst, const float* src, b
 // kernel size known at compile time (KS = 2 or 3) and every channel staged at
 // once: the C*KS input lines (oh*s - p + kh, W columns each; zeros for lines
 // outside the image) arrive by 16-byte asynchronous copies (line stride W + 4
-// floats), then the CTA's Wo*K contiguous patch floats are written four at a
-// time, consecutive threads storing consecutive 16-byte pieces. Needs W and
-// K = C*KS*KS multiples of 4 and 16-byte aligned pointers.
+// floats), then each thread owns patch columns and walks the row's pixels
+// (index decoding once per column; a warp stores 32 consecutive columns of one
+// patch row per step). Needs W and K = C*KS*KS multiples of 4 and 16-byte
+// aligned pointers.
 template <int KS, int PLANES>
 __global__ void __launch_bounds__(256) im2col_row4_kernel(const float* xm, const float* xS,
                                                           float* pm, float* pS, ConvGeom g) {
@@ -441,36 +442,26 @@ __global__ void __launch_bounds__(256) im2col_row4_kernel(const float* xm, const
     }
     cp_async_wait_all();
     __syncthreads();
+    // thread t owns patch columns j = t, t + blockDim.x, ... and walks the row's
+    // Wo pixels: a warp stores 32 consecutive columns of one patch row per step
     const int64_t out0 = static_cast<int64_t>(blockIdx.x) * g.Wo * K;  // patch row (n, oh, 0)
-    const int total4 = g.Wo * K / 4;
-    const float rK = 1.f / K;
-    for (int e4 = threadIdx.x; e4 < total4; e4 += blockDim.x) {
-        const int e = 4 * e4;
-        const int ow = div_small(e, rK), j = e - ow * K;
-        int c = j / KK;
-        const int t = j - c * KK;
-        int kh = t / KS, kw = t - kh * KS;
-        const int iw0 = ow * g.s - g.p_tl;
-        float v[PLANES][4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int iw = iw0 + kw;
+    for (int j = threadIdx.x; j < K; j += blockDim.x) {
+        const int c = j / KK, t = j - c * KK;
+        const int kh = t / KS, kw = t - kh * KS;
+        const float* line = lines + (c * KS + kh) * ls;
+        float* om = pm + out0 + j;
+        float* oS = PLANES == 2 ? pS + out0 + j : nullptr;
+        int iw = kw - g.p_tl;
+#pragma unroll 4
+        for (int ow = 0; ow < g.Wo; ++ow, iw += g.s, om += K) {
             const bool in = static_cast<unsigned>(iw) < static_cast<unsigned>(g.W);
-            const int a = (c * KS + kh) * ls + (in ? iw : 0);
-            v[0][u] = in ? lines[a] : 0.f;
-            if (PLANES == 2) v[PLANES - 1][u] = in ? lines[pstride + a] : 0.f;
-            if (++kw == KS) {
-                kw = 0;
-                if (++kh == KS) {
-                    kh = 0;
-                    ++c;
-                }
+            const int a = in ? iw : 0;
+            *om = in ? line[a] : 0.f;
+            if (PLANES == 2) {
+                *oS = in ? line[pstride + a] : 0.f;
+                oS += K;
             }
         }
-        *reinterpret_cast<float4*>(pm + out0 + e) = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
-        if (PLANES == 2)
-            *reinterpret_cast<float4*>(pS + out0 + e) =
-                make_float4(v[PLANES - 1][0], v[PLANES - 1][1], v[PLANES - 1][2], v[PLANES - 1][3]);
     }
 }
 
