@@ -44,6 +44,7 @@ int tagi_version(void);                  /* (major << 16) | (minor << 8) | patch
 const char* tagi_last_error(void);       /* message of the last failing call (this thread) */
 int tagi_device_arch(int device);        /* SM version of `device` (e.g. 100), <0 on error */
 uint64_t tagi_kernel_launches(void);     /* kernels this library has launched (process-wide) */
+uint64_t tagi_tc_launches(void);         /* of those, tcgen05 tensor-core contractions */
 uint64_t tagi_tma_launches(void);        /* of those, weight sums fed by tensor-map copies */
 /* Error word of the tensor-core kernels on the current device: 0, or the code of
  * the first bounded wait that ran out (the kernel then skipped its remaining work

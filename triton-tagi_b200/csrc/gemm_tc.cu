@@ -1495,6 +1495,7 @@ EncodeTiledFn encode_tiled() {
 }
 
 std::atomic<uint64_t> g_tma_launches{0};
+std::atomic<uint64_t> g_tc_launches{0};
 
 bool make_tma(const GemmArgs& g, int nc, TmaArgs* t) {
     t->on = 0;
@@ -1563,6 +1564,7 @@ int launch_tc(const GemmArgs& g, int batch, cudaStream_t st, const char* what) {
     TmaArgs tm;
     memset(&tm, 0, sizeof(tm));
     if (tma_capable<VM, BN>() && batch == 1 && make_tma(g, Roles<BN>::NC, &tm)) ++g_tma_launches;
+    ++g_tc_launches;
     moment_tc_kernel<VM, MEAN, EPI, BN, GM><<<grid, Roles<BN>::THREADS, smem, st>>>(g, tm);
     return check_launch(what);
 }
@@ -1707,6 +1709,7 @@ int tc_launch(const GemmArgs& g, int vm, bool mean, int epi, int bn, int batch, 
 }  // namespace tagi
 
 extern "C" uint64_t tagi_tma_launches(void) { return tagi::g_tma_launches.load(); }
+extern "C" uint64_t tagi_tc_launches(void) { return tagi::g_tc_launches.load(); }
 
 extern "C" int tagi_set_wait_limit_ns(uint64_t ns) {
     const unsigned long long v = ns ? static_cast<unsigned long long>(ns) : tagi::kTimeoutNs;

@@ -73,6 +73,7 @@ _SIGS = {
     "tagi_last_error": "",
     "tagi_kernel_launches": "",
     "tagi_tma_launches": "",
+    "tagi_tc_launches": "",
     "tagi_device_status": "n",
     "tagi_set_wait_limit_ns": "u",
     "tagi_peer_buffer_bytes": "ni",
@@ -90,6 +91,7 @@ _RET = {
     "tagi_last_error": ctypes.c_char_p,
     "tagi_kernel_launches": ctypes.c_uint64,
     "tagi_tma_launches": ctypes.c_uint64,
+    "tagi_tc_launches": ctypes.c_uint64,
 }
 
 # Status codes (include/tagi_b200.h)
@@ -168,6 +170,11 @@ def set_wait_limit_ns(ns: int) -> None:
 def kernel_launches() -> int:
     """Kernels launched by libtagi_b200 so far in this process."""
     return int(lib().fn["tagi_kernel_launches"]())
+
+
+def tc_launches() -> int:
+    """Of those, launches of the tcgen05 tensor-core contraction kernel."""
+    return int(lib().fn["tagi_tc_launches"]())
 
 
 def stream(t: torch.Tensor) -> int:
