@@ -911,15 +911,16 @@ __device__ __forceinline__ void producer(const GemmArgs& g, const ProdCtx& c, co
             const uint32_t col = R::A0 + static_cast<uint32_t>(
                                              (s * kBlocks + it % kBlocks) * a_cols<VM>());
             const uint32_t ta = c.tmem + (static_cast<uint32_t>(c.t & ~31) << 16) + col;
-            float hi[8], lo[8], sq[8];
+            float sq[8];
+            // a tile's hi and lo parts are 16 consecutive columns: one 16-column store
             auto put = [&](int t, const float (&x)[8]) {
+                float hl[16];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    hi[e] = tf32_rna(x[e]);
-                    lo[e] = tf32_rna(x[e] - hi[e]);
+                    hl[e] = tf32_rna(x[e]);
+                    hl[8 + e] = tf32_rna(x[e] - hl[e]);
                 }
-                tmem_st8(ta + t * 16, hi);
-                tmem_st8(ta + t * 16 + 8, lo);
+                tmem_st16(ta + t * 16, hl);
             };
             put(0, v[0]);
             if (VM == FULL || VM == LSQ) {
