@@ -208,10 +208,16 @@ __device__ __forceinline__ void finish_one(const GemmArgs& g, int param, int64_t
 // Partials of eight splits are loaded before they are added (in split order,
 // so the sums are the same as one at a time): one load latency per eight
 // splits instead of one per split.
-__global__ void splitk_finish_kernel(const GemmArgs g, int param) {
+// bsums (optional): the bias row `brow` from column sums computed elsewhere,
+// as bias_given_kernel writes it.
+__global__ void splitk_finish_kernel(const GemmArgs g, int param, const double* bsums, int brow) {
     constexpr int kAhead = 8;
     const int64_t mn = static_cast<int64_t>(g.M) * g.N;
     const float* ws = g.ws;
+    if (bsums != nullptr)
+        for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < g.N; n += gridDim.x * blockDim.x)
+            finish_one(g, param, static_cast<int64_t>(brow) * g.N + n,
+                       static_cast<float>(bsums[n]), static_cast<float>(bsums[g.N + n]));
     for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < mn;
          idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         float g0 = 0.f, g1 = 0.f;
@@ -583,18 +589,29 @@ __global__ void bias_given_kernel(const GemmArgs g, const double* sums, int para
 // room past them (256-byte aligned) takes the prepared B tiles (the deltas) of
 // the tensor-core kernel.
 // `bsums` (the bias row is the last of Mo): the bias row's sums are given.
+// `brow_sums` (internal): the sums of the bias row Mo, which follows these Mo
+// rows; the split finish writes it, else bias_given_kernel.
 int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaStream_t st,
-              const char* what, const double* bsums = nullptr) {
+              const char* what, const double* bsums = nullptr,
+              const double* brow_sums = nullptr) {
     if (bsums != nullptr) {
-        bias_given_kernel<<<grid_1d(g.N, 256), 256, 0, st>>>(g, bsums, param ? 1 : 0, Mo - 1);
-        int rc = check_launch(what);
-        if (rc) return rc;
         GemmArgs gw = g;
         gw.ones_row = -1;
-        rc = Mo > 1 ? run_wgrad(gw, Mo - 1, ws, ws_bytes, param, st, what) : TAGI_OK;
+        int rc = TAGI_OK;
+        if (Mo > 1) {
+            rc = run_wgrad(gw, Mo - 1, ws, ws_bytes, param, st, what, nullptr, bsums);
+        } else {
+            bias_given_kernel<<<grid_1d(g.N, 256), 256, 0, st>>>(g, bsums, param ? 1 : 0, Mo - 1);
+            rc = check_launch(what);
+        }
         g.M = Mo;
         return rc;
     }
+    auto bias_row = [&]() -> int {  // the given bias row, where no finish pass writes it
+        if (brow_sums == nullptr) return TAGI_OK;
+        bias_given_kernel<<<grid_1d(g.N, 256), 256, 0, st>>>(g, brow_sums, param ? 1 : 0, Mo);
+        return check_launch(what);
+    };
     if (bias_apart(Mo, g.N, g.Kr, g.ones_row == Mo - 1)) {
         size_t off = 0;
         const size_t total = bias_apart_bytes(Mo, g.N, g.Kr, &off);
@@ -635,7 +652,8 @@ int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaSt
         const int64_t mn = static_cast<int64_t>(Mo) * g.N;  // <= 96 x 64
         splitk_finish_wide_kernel<<<static_cast<unsigned>((mn + 15) / 16), 256, 0, st>>>(
             g, param ? 1 : 0);
-        return check_launch(what);
+        rc = check_launch(what);
+        return rc ? rc : bias_row();
     }
     const size_t need = splits > 1 ? sizeof(float) * 2ull * splits * static_cast<size_t>(Mo) * g.N : 0;
     const size_t pack_off = (need + 255) / 256 * 256;
@@ -653,13 +671,14 @@ int run_wgrad(GemmArgs& g, int Mo, void* ws, size_t ws_bytes, bool param, cudaSt
         int rc = launch<LSQ, true, EPI_PARTIAL>(g, 1, st, what, bn_tc);
         if (rc) return rc;
         splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(Mo) * g.N, 256), 256, 0, st>>>(
-            g, param ? 1 : 0);
+            g, param ? 1 : 0, brow_sums, Mo);
         return check_launch(what);
     }
     g.splits = 1;
     g.kchunk = g.Kr > 0 ? g.Kr : BK;
-    return param ? launch<LSQ, true, EPI_PARAM>(g, 1, st, what, bn_tc)
-                 : launch<LSQ, true, EPI_STORE>(g, 1, st, what, bn_tc);
+    const int rc = param ? launch<LSQ, true, EPI_PARAM>(g, 1, st, what, bn_tc)
+                         : launch<LSQ, true, EPI_STORE>(g, 1, st, what, bn_tc);
+    return rc ? rc : bias_row();
 }
 
 // Workspace of a store-epilogue contraction: split-reduction partials (when the
@@ -712,7 +731,8 @@ int run_store(GemmArgs& g, void* ws, size_t ws_bytes, cudaStream_t st, const cha
         g.ws = reinterpret_cast<float*>(w);
         int rc = launch<VM, true, EPI_PARTIAL>(g, 1, st, what, p.bn_split);
         if (rc) return rc;
-        splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(g.M) * g.N, 256), 256, 0, st>>>(g, 0);
+        splitk_finish_kernel<<<grid_1d(static_cast<int64_t>(g.M) * g.N, 256), 256, 0, st>>>(
+            g, 0, nullptr, 0);
         return check_launch(what);
     }
     g.splits = 1;
