@@ -535,16 +535,34 @@ size_t bias_apart_bytes(int Mo, int N, int Kr, size_t* off) {
 }
 
 // CTA (32 columns, one reduction slice): thread (column c, row group r) adds
-// rows r, r+8, ... of the slice; the 8 group totals are added in group order.
+// rows r, r+8, ... of the slice, eight rows' loads in flight before their adds
+// (the same order of additions); the 8 group totals are added in group order.
 __global__ void __launch_bounds__(256) bias_sums_kernel(const GemmArgs g, int chunk, float* part) {
+    constexpr int kAhead = 8;
     __shared__ float red[2][8][33];
     const int c = threadIdx.x & 31, r = threadIdx.x >> 5;
     const int n = blockIdx.x * 32 + c;
     const int m0 = blockIdx.y * chunk, m1 = min(g.Kr, m0 + chunk);
     float a = 0.f, b = 0.f;
     if (n < g.N) {
-        for (int m = m0 + r; m < m1; m += 8) {
-            const int64_t o = static_cast<int64_t>(n) * g.bn + g.brow.off(m);
+        const int64_t col = static_cast<int64_t>(n) * g.bn;
+        int m = m0 + r;
+        for (; m + 8 * (kAhead - 1) < m1; m += 8 * kAhead) {
+            float xa[kAhead], xb[kAhead];
+#pragma unroll
+            for (int u = 0; u < kAhead; ++u) {
+                const int64_t o = col + g.brow.off(m + 8 * u);
+                xa[u] = __ldg(g.u + o);
+                xb[u] = __ldg(g.v + o);
+            }
+#pragma unroll
+            for (int u = 0; u < kAhead; ++u) {
+                a += xa[u];
+                b += xb[u];
+            }
+        }
+        for (; m < m1; m += 8) {
+            const int64_t o = col + g.brow.off(m);
             a += __ldg(g.u + o);
             b += __ldg(g.v + o);
         }
