@@ -13,6 +13,7 @@
 // of convolutions) are split over the reduction and finished by a fixed-order
 // reduce kernel, so results are deterministic.
 #include <algorithm>
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -776,10 +777,21 @@ size_t wgrad_ws_total(int Mo, int N, int Kr) {
     return pack > 0 ? (need + 255) / 256 * 256 + pack : need;
 }
 
+// Element i of the (K + bias) x N sums: param_epilogue needs its row only to
+// tell the bias row (r == K) and to form r * N + c = i, so (when K N fits an
+// int) the weight rows go as (0, i) and the bias row as (K, i - K N): no
+// division per element.
 __global__ void apply_sums_kernel(const float* gm, const float* gS, ParamEpi p, int64_t total) {
+    const int64_t kn = static_cast<int64_t>(p.K) * p.N;
+    const bool flat = kn + p.N <= INT_MAX;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        param_epilogue(static_cast<int>(i / p.N), static_cast<int>(i % p.N), gm[i], gS[i], p);
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const bool bias = i >= kn;
+        if (flat)
+            param_epilogue(bias ? p.K : 0, static_cast<int>(bias ? i - kn : i), gm[i], gS[i], p);
+        else
+            param_epilogue(static_cast<int>(i / p.N), static_cast<int>(i % p.N), gm[i], gS[i], p);
+    }
 }
 
 }  // namespace

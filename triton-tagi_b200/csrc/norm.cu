@@ -104,19 +104,34 @@ __global__ void __launch_bounds__(kBnThreads) bn_sums_kernel(const float* mz, co
     const ChanSlab sl(N, C, HW, blockIdx.y);
     double v[3] = {0.0, 0.0, 0.0};
     if (V4) {
+        // four float4 runs per thread and iteration, loaded before any is summed
+        // (the same summation order as one at a time)
+        constexpr int kRuns = 4;
         const int HW4 = HW / 4, total = sl.nimg * HW4;
-        for (int t = threadIdx.x; t < total; t += blockDim.x) {
-            const int li = t / HW4, h = (t - li * HW4) * 4;
-            const int64_t o = sl.offset(li, h);
-            const float4 m = __ldg(reinterpret_cast<const float4*>(mz + o));
-            const float4 S = __ldg(reinterpret_cast<const float4*>(Sz + o));
-            const float mm[4] = {m.x, m.y, m.z, m.w}, ss[4] = {S.x, S.y, S.z, S.w};
+        for (int t = threadIdx.x; t < total; t += kRuns * blockDim.x) {
+            float4 m[kRuns], S[kRuns];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const double x = mm[e];
-                v[0] += x;
-                v[1] += ss[e];
-                v[2] += x * x;
+            for (int u = 0; u < kRuns; ++u) {
+                const int tu = t + u * blockDim.x;
+                if (tu < total) {
+                    const int li = tu / HW4, h = (tu - li * HW4) * 4;
+                    const int64_t o = sl.offset(li, h);
+                    m[u] = __ldg(reinterpret_cast<const float4*>(mz + o));
+                    S[u] = __ldg(reinterpret_cast<const float4*>(Sz + o));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kRuns; ++u) {
+                if (t + u * static_cast<int>(blockDim.x) >= total) break;
+                const float mm[4] = {m[u].x, m[u].y, m[u].z, m[u].w};
+                const float ss[4] = {S[u].x, S[u].y, S[u].z, S[u].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const double x = mm[e];
+                    v[0] += x;
+                    v[1] += ss[e];
+                    v[2] += x * x;
+                }
             }
         }
     } else {
