@@ -441,7 +441,9 @@ def test_avgpool_and_add():
     from triton_tagi.layers.resblock import triton_add_shortcut
 
     gen = torch.Generator().manual_seed(4)
-    for k, sc, shape in ((2, False, (3, 5, 8, 8)), (4, False, (2, 7, 4, 4)), (2, True, (2, 3, 7, 9))):
+    # 2 x 2 pools of rows with W a multiple of 4 take the 16-byte kernels (odd H too)
+    for k, sc, shape in ((2, False, (3, 5, 8, 8)), (4, False, (2, 7, 4, 4)), (2, True, (2, 3, 7, 9)),
+                         (2, False, (2, 4, 7, 12)), (2, True, (4, 32, 32, 32))):
         ma, Sa = rnd(gen, *shape), rnd(gen, *shape, kind="u")
         pool = AvgPool2D(k, spatial_correlation=sc)
         om, oS = pool.forward(g(ma), g(Sa))

@@ -165,6 +165,48 @@ __global__ void avgpool_bwd_kernel(const float* dm, const float* dS, float* om, 
     }
 }
 
+// 2 x 2 pooling of images with W a multiple of 4 (16-byte rows): per thread
+// one pair of output pixels from two float4 runs of the input rows (the same
+// additions, in the same order, as avgpool_fwd_kernel); 32-bit indices.
+__global__ void avgpool2_fwd_v4(const float4* ma, const float4* Sa, float2* om, float2* oS,
+                                uint32_t orows, uint32_t Ho, uint32_t H, uint32_t W4,
+                                float inv_k2, float var_scale) {
+    const uint32_t total = orows * W4;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += gridDim.x * blockDim.x) {
+        const uint32_t orow = i / W4, q = i - orow * W4;  // orow = nc * Ho + oh
+        const uint32_t nc = orow / Ho, oh = orow - nc * Ho;
+        const uint32_t r0 = (nc * H + 2 * oh) * W4 + q;
+        const float4 a = ma[r0], b = ma[r0 + W4], c = Sa[r0], d = Sa[r0 + W4];
+        om[i] = make_float2((((a.x + a.y) + b.x) + b.y) * inv_k2,
+                            (((a.z + a.w) + b.z) + b.w) * inv_k2);
+        oS[i] = make_float2((((c.x + c.y) + d.x) + d.y) * var_scale,
+                            (((c.z + c.w) + d.z) + d.w) * var_scale);
+    }
+}
+
+// Its backward: each thread writes 4 input pixels of one row from a pair of
+// output pixels (rows past 2 Ho get zeros, as avgpool_bwd_kernel).
+__global__ void avgpool2_bwd_v4(const float2* dm, const float2* dS, float4* om, float4* oS,
+                                uint32_t rows, uint32_t H, uint32_t Ho, uint32_t W4,
+                                float inv_k2, float var_scale) {
+    const uint32_t total = rows * W4;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += gridDim.x * blockDim.x) {
+        const uint32_t row = i / W4, q = i - row * W4;  // row = nc * H + h
+        const uint32_t nc = row / H, h = row - nc * H, oh = h >> 1;
+        float4 m = make_float4(0.f, 0.f, 0.f, 0.f), S = m;
+        if (oh < Ho) {
+            const uint32_t o = (nc * Ho + oh) * W4 + q;  // output pairs: Wo / 2 = W4 per row
+            const float2 a = dm[o], b = dS[o];
+            m = make_float4(a.x * inv_k2, a.x * inv_k2, a.y * inv_k2, a.y * inv_k2);
+            S = make_float4(b.x * var_scale, b.x * var_scale, b.y * var_scale, b.y * var_scale);
+        }
+        om[i] = m;
+        oS[i] = S;
+    }
+}
+
 // ---- Remax (remax.py:33-114) -------------------------------------------------
 // The reference evaluates, per row of K classes,
 //   mixture:   m = max(E[max(0,Z)], eps), v = max(Var-expression(m), eps)
@@ -513,6 +555,17 @@ extern "C" int tagi_avgpool_forward(const float* ma, const float* Sa, float* ma_
     const int64_t total = N * C * (H / k) * (W / k);
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(ma && Sa && ma_out && Sa_out, TAGI_E_BAD_ARG, "%s: null pointer", what);
+    if (k == 2 && W % 4 == 0 && N * C * H * W < (int64_t(1) << 31) &&
+        all_aligned({ma, Sa}) && ((reinterpret_cast<uintptr_t>(ma_out) |
+                                    reinterpret_cast<uintptr_t>(Sa_out)) & 7) == 0) {
+        const uint32_t orows = static_cast<uint32_t>(N * C * (H / 2)), W4 = static_cast<uint32_t>(W / 4);
+        avgpool2_fwd_v4<<<grid_1d(static_cast<int64_t>(orows) * W4, 256), 256, 0,
+                          as_stream(stream)>>>(
+            reinterpret_cast<const float4*>(ma), reinterpret_cast<const float4*>(Sa),
+            reinterpret_cast<float2*>(ma_out), reinterpret_cast<float2*>(Sa_out), orows,
+            static_cast<uint32_t>(H / 2), static_cast<uint32_t>(H), W4, 0.25f, var_scale);
+        return check_launch(what);
+    }
     avgpool_fwd_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
         ma, Sa, ma_out, Sa_out, N * C, (int)H, (int)W, (int)k, 1.0f / (float)(k * k), var_scale);
     return check_launch(what);
@@ -527,6 +580,16 @@ extern "C" int tagi_avgpool_backward(const float* dm, const float* dS, float* dm
     const int64_t total = N * C * H * W;
     if (total == 0) return TAGI_OK;
     TAGI_REQUIRE(dm && dS && dm_out && dS_out, TAGI_E_BAD_ARG, "%s: null pointer", what);
+    if (k == 2 && W % 4 == 0 && total < (int64_t(1) << 31) && all_aligned({dm_out, dS_out}) &&
+        ((reinterpret_cast<uintptr_t>(dm) | reinterpret_cast<uintptr_t>(dS)) & 7) == 0) {
+        const uint32_t rows = static_cast<uint32_t>(N * C * H), W4 = static_cast<uint32_t>(W / 4);
+        avgpool2_bwd_v4<<<grid_1d(static_cast<int64_t>(rows) * W4, 256), 256, 0,
+                          as_stream(stream)>>>(
+            reinterpret_cast<const float2*>(dm), reinterpret_cast<const float2*>(dS),
+            reinterpret_cast<float4*>(dm_out), reinterpret_cast<float4*>(dS_out), rows,
+            static_cast<uint32_t>(H), static_cast<uint32_t>(H / 2), W4, 0.25f, var_scale);
+        return check_launch(what);
+    }
     avgpool_bwd_kernel<<<grid_1d(total, 256), 256, 0, as_stream(stream)>>>(
         dm, dS, dm_out, dS_out, N * C, (int)H, (int)W, (int)k, 1.0f / (float)(k * k), var_scale);
     return check_launch(what);
