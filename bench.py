@@ -24,6 +24,8 @@ cpu_baseline  the CPU oracle (float32 PyTorch restatement of the reference's
 subrecords the MLP step at the same number of GPUs, and on one GPU the Linear
            sweep's 8192 x 4096 x 4096 shape (forward, input deltas, weight
            sums + capped update), from the same run.
+clocks     SM clock (median, min) and the clock-event reasons seen, read
+           through NVML every 10 ms during the timed steps (read-only).
 device_status  the tensor-core kernels' error word after the timed steps
            (non-zero: a bounded wait ran out; the run then exits with an error).
 replicas_bit_identical  (N > 1) every rank's parameters after the run have the
@@ -38,7 +40,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -111,56 +112,87 @@ def make_batch(name: str, batch: int, seed: int, device="cpu"):
 
 # ----------------------------------------------------------------------------- helpers
 class ClockSampler:
-    """nvidia-smi clock and throttle-reason samples while the timed region runs."""
+    """SM clock and clock-event (throttle) reasons read through NVML every
+    ``period`` seconds while the timed region runs. Read-only: no setting of the
+    GPU is touched. The first sample is taken before ``__enter__`` returns, so a
+    timed region of a few hundred milliseconds still carries tens of samples."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits reported (nvmlClocksEventReason*)
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
 
-    def __init__(self, index: int):
-        self.index, self.lines, self.proc = index, [], None
+    def __init__(self, index: int, period: float = 0.01):
+        self.index, self.period = index, period
+        self.sm, self.power, self.max_sm, self.mask = [], [], None, 0
+        self.error, self._nvml, self._thread = None, None, None
+        self._stop = threading.Event()
+
+    def _handle(self, nv):
+        try:  # CUDA and NVML may order devices differently: match the PCI address
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample(self):
+        nv, h = self._nvml, self._h
+        self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+        self.mask |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+        try:
+            self.power.append(nv.nvmlDeviceGetPowerUsage(h) / 1e3)
+        except Exception:
+            pass
+
+    def _loop(self):
+        while not self._stop.wait(self.period):
+            try:
+                self._sample()
+            except Exception as e:  # keep what was sampled so far
+                self.error = repr(e)
+                return
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = self._handle(pynvml)
+            self.max_sm = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+            self._sample()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+        except Exception as e:
+            self.error = repr(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2.0)
+            try:  # a region shorter than the period is still bracketed by two samples
+                self._sample()
+            except Exception as e:
+                self.error = repr(e)
+        if self._nvml is not None:
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[3:7]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        d = {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_sm,
+             "samples": len(self.sm),
+             "reasons": sorted(n for n, bit in self.REASONS if self.mask & bit),
+             "source": "nvml", "period_ms": 1e3 * self.period}
+        if self.sm:
+            d["sm_mhz_min"] = min(self.sm)
+        if self.power:
+            d["power_w_median"] = round(statistics.median(self.power), 1)
+        if self.error:
+            d["error"] = self.error
+        return d
 
 
 def _conv_pixels(a) -> int:
