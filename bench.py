@@ -15,9 +15,12 @@ value      samples/s over all ranks: K·B·N / (max over ranks of the summed
 e2e        the same metric through the public API with pinned host buffers:
            H2D of x, y and D2H of (μ, S) inside the timed events.
 roofline   the dominant moment contraction, timed with CUDA events around
-           each of its launches during the timed steps; achieved = algorithmic
-           FLOPs (6·M·N·K forward, 4·M·N·K backward/weight sums) ÷ time,
-           against the 3xTF32-effective tensor peak (measured cuBLAS TF32 ÷ 3).
+           each of its launches in up to 3 steps after the timed ones; achieved
+           = algorithmic FLOPs (6·M·N·K forward, 4·M·N·K backward/weight sums)
+           ÷ time, against the 3xTF32-effective tensor peak (measured cuBLAS
+           TF32 ÷ 3). One GPU with a captured step: the events are nodes of a
+           second capture of the step, replayed (no host launch gaps inside the
+           intervals); otherwise eager steps (`entry_timing` says which).
 cpu_baseline  the CPU oracle (float32 PyTorch restatement of the reference's
            equations) on the host cores, rank 0 at N = 1, at the workload's
            own batch (5 timed steps after 1 warm-up).
@@ -283,11 +286,14 @@ class LaunchTimer:
         "tagi_param_grad_bias_given": ("param_grad", lambda a: 4.0 * a[9] * a[10] * a[11]),
     }
 
-    def __init__(self):
-        self.records, self._open = [], None
+    def __init__(self, external: bool = False):
+        # external: the events become event-record nodes of a CUDA graph being
+        # captured, so every replay times the same calls again
+        self.records, self._open, self.external = [], None, external
+        self.seconds, self.reps = None, 0
 
     def __call__(self, phase, name, args):
-        ev = torch.cuda.Event(enable_timing=True)
+        ev = torch.cuda.Event(enable_timing=True, external=self.external)
         ev.record()
         if phase == "before":
             self._open = ev
@@ -299,17 +305,27 @@ class LaunchTimer:
             nb = ENTRY_BYTES.get(name)
             self.records.append((name, None, nb(args) if nb else None, self._open, ev))
 
+    def harvest(self):
+        """Adds every recorded call's event interval (after a synchronize): once
+        after eager steps, or after each replay of a captured step."""
+        if self.seconds is None:
+            self.seconds = [0.0] * len(self.records)
+        for i, (_, _, _, a, b) in enumerate(self.records):
+            self.seconds[i] += a.elapsed_time(b) * 1e-3
+        self.reps += 1
+
     def summary(self):
-        """(contraction families, other entries)."""
+        """(contraction families, other entries), over every harvested pass."""
+        if self.seconds is None:
+            self.harvest()
         fam, other = {}, {}
-        for name, flops, nbytes, a, b in self.records:
-            t = a.elapsed_time(b) * 1e-3
+        for (name, flops, nbytes, _, _), t in zip(self.records, self.seconds):
             d = fam if flops is not None else other
             f = d.setdefault(name, {"launches": 0, "flops": 0.0, "bytes": 0.0, "seconds": 0.0,
                                     "bytes_known": True})
-            f["launches"] += 1
-            f["flops"] += flops or 0.0
-            f["bytes"] += nbytes or 0.0
+            f["launches"] += self.reps
+            f["flops"] += self.reps * (flops or 0.0)
+            f["bytes"] += self.reps * (nbytes or 0.0)
             f["bytes_known"] &= nbytes is not None
             f["seconds"] += t
         return fam, other
@@ -467,7 +483,6 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
             per_step = kernel_launches() - l0  # the captured (or eager) step's launches
     torch.cuda.synchronize()
 
-    timer = LaunchTimer()
     L = lib()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -487,21 +502,38 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
         # replays launch without passing through the library's host calls
         launches = per_step * args.steps
     step_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) * 1e-3
-    # Per-entry timing of eager steps after the timed region (CUDA events around
-    # every library call; the timed steps carry no events of their own).
+    # Per-entry timing after the timed region (the timed steps carry no events
+    # of their own): CUDA events around every library call. One GPU with a
+    # captured step: the step is captured once more with the events as graph
+    # nodes and replayed, so each interval holds the call's kernels without the
+    # host's launch gaps. Otherwise eager steps (host gaps included).
     fam_steps = min(3, args.steps)
-    net.cuda_graph = False
     dp_timer = CollectiveTimer() if world > 1 else None
-    for _ in range(fam_steps):
-        flush.zero_()
-        L.hook = timer
-        if dp_timer is not None:
-            net.reducer.timer = dp_timer
-        net.step(x, y, SIGMA_V)
-        L.hook = None
-        if dp_timer is not None:
-            net.reducer.timer = None
-    net.cuda_graph = graphed
+    captured = graphed and world == 1
+    timer = LaunchTimer(external=captured)
+    if captured:
+        timed_graph = net._graph
+        net._graph = (timed_graph[0], None, None, None, None)  # capture again, hook on
+        for i in range(fam_steps):
+            flush.zero_()
+            L.hook = timer if i == 0 else None
+            net.step(x, y, SIGMA_V)
+            L.hook = None
+            torch.cuda.synchronize()
+            timer.harvest()
+        net._graph = timed_graph
+    else:
+        net.cuda_graph = False
+        for _ in range(fam_steps):
+            flush.zero_()
+            L.hook = timer
+            if dp_timer is not None:
+                net.reducer.timer = dp_timer
+            net.step(x, y, SIGMA_V)
+            L.hook = None
+            if dp_timer is not None:
+                net.reducer.timer = None
+        net.cuda_graph = graphed
     torch.cuda.synchronize()
     barrier()
     fam, other = timer.summary()
@@ -584,6 +616,8 @@ def our_arm(args, rank: int, world: int, local: int) -> None:
                 "d2h_bytes_per_step": (mu_h.numel() + var_h.numel()) * 4},
         "gpu_launches": int(launches),
         "roofline": roof,
+        "entry_timing": ("events as nodes of a captured step, replayed" if captured
+                         else "events around eager calls (host launch gaps included)"),
         "kernels": {k: {"launches": v["launches"], "ms_per_step": 1e3 * v["seconds"] / fam_steps,
                         "tflops": v["flops"] / v["seconds"] / 1e12} for k, v in fam.items()},
         # every other library entry of the step (CUDA events around each call);
