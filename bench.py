@@ -807,7 +807,7 @@ def sweep_arm(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-MICRO = ("remax", "col2im", "im2col")
+MICRO = ("remax", "col2im", "im2col", "bn")
 
 
 def micro_arm(which: str) -> None:
@@ -815,7 +815,8 @@ def micro_arm(which: str) -> None:
     and 10 timed calls per shape (CUDA events), one line per shape. remax: the
     transformer's score rows (32768 x 512, a quarter of one layer's);
     col2im / im2col: the ResNet-18 (batch 128) stride-2 gathers and the patches
-    of the weight sums."""
+    of the weight sums; bn: the BatchNorm training forward (with and without the
+    residual stream) and backward on the four ResNet-18 stage shapes."""
     import triton_tagi  # noqa: F401  (loads the library)
     from triton_tagi._lib import lib
     from triton_tagi.layers.remax import triton_remax
@@ -837,6 +838,38 @@ def micro_arm(which: str) -> None:
 
     g = torch.Generator(device="cuda").manual_seed(0)
     N = 128
+    if which == "bn":
+        # training forward (with and without the residual stream) and backward
+        # (ReLU Jacobian, delta sums, capped update) on the four stage shapes
+        for C, H in ((64, 32), (128, 16), (256, 8), (512, 4)):
+            mz = torch.randn(N, C, H, H, device="cuda", generator=g)
+            Sz = torch.rand(N, C, H, H, device="cuda", generator=g) + 0.1
+            rm, rS = torch.randn_like(mz), torch.rand_like(Sz)
+            prm = [torch.rand(C, device="cuda", generator=g) + 0.5 for _ in range(8)]
+            mean, var, rmean, rvar, mg, Sg, mb, Sb = prm
+            ma, Sa, mh = torch.empty_like(mz), torch.empty_like(mz), torch.empty_like(mz)
+            outs = [torch.empty_like(mz) for _ in range(2)]
+            grads = torch.empty(4 * C, device="cuda", dtype=torch.float64)
+            dsums = torch.empty(2 * C, device="cuda", dtype=torch.float64)
+            n = mz.numel()
+            for add in (False, True):
+                us = timed(lambda: L("tagi_bn_train_forward", mz.data_ptr(), Sz.data_ptr(),
+                                     mean.data_ptr(), var.data_ptr(), rmean.data_ptr(),
+                                     rvar.data_ptr(), mg.data_ptr(), Sg.data_ptr(), mb.data_ptr(),
+                                     Sb.data_ptr(), ma.data_ptr(), Sa.data_ptr(), mh.data_ptr(),
+                                     rm.data_ptr() if add else None,
+                                     rS.data_ptr() if add else None, N, C, H * H, 0, 0, 0.1,
+                                     1e-5, st))
+                nbytes = (28 if add else 20) * n
+                print(f"bn_train_forward C{C} H{H}{' +add' if add else ''}: {us:.1f} us, "
+                      f"{nbytes / us / 1e3:.0f} GB/s")
+            us = timed(lambda: L("tagi_bn_backward", ma.data_ptr(), Sa.data_ptr(), mh.data_ptr(),
+                                 var.data_ptr(), mg.data_ptr(), outs[0].data_ptr(),
+                                 outs[1].data_ptr(), rS.data_ptr(), grads.data_ptr(),
+                                 dsums.data_ptr(), N, C, H * H, 1e-5, Sg.data_ptr(),
+                                 mb.data_ptr(), Sb.data_ptr(), 2.0, st))
+            print(f"bn_backward C{C} H{H}: {us:.1f} us, {24 * n / us / 1e3:.0f} GB/s")
+        return
     if which == "remax":
         mz = torch.randn(32768, 512, device="cuda", generator=g) * 2
         Sz = torch.rand(32768, 512, device="cuda", generator=g) * 2 + 1e-3

@@ -216,6 +216,18 @@ __device__ __forceinline__ void vector_apply(int64_t i, double gm, double gS, in
     }
 }
 
+// vector_apply's update with the parameter's current mean m and variance s
+// already in registers.
+__device__ __forceinline__ void update_from(int64_t i, double gm, double gS, float m, float s,
+                                            float* pm, float* pS, float cap) {
+    const float dm = s * static_cast<float>(gm);
+    const float dS = (s * s) * static_cast<float>(gS);
+    float mm = m, ss = s;
+    capped_pair(mm, ss, dm, dS, cap);
+    pm[i] = mm;
+    pS[i] = ss;
+}
+
 // batchnorm2d.py:134-192 plus the gamma/beta sums of 465-482, one cluster per channel.
 // SUMS: also the channel sums of the outgoing deltas (written to dsums[c] and
 // dsums[C + c]): the bias sums of a convolution whose outputs this layer
@@ -231,6 +243,15 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     const ChanSlab sl(N, C, HW, blockIdx.y);
     const float g = mg[sl.c];
     const float rs = var[sl.c];
+    // the parameters the capped update reads, loaded before the pass (only the
+    // finalising thread writes them, after the cluster barriers)
+    const bool fin = blockIdx.x == 0 && threadIdx.x == 0;  // cluster rank 0, thread 0
+    float sw0 = 0.f, mb0 = 0.f, sb0 = 0.f;
+    if (fin && cap > 0.f) {
+        sw0 = Sw[sl.c];
+        mb0 = mb[sl.c];
+        sb0 = Sb[sl.c];
+    }
     const float inv_std = 1.0f / sqrtf(rs + eps);
     const float inv_var = 1.0f / (rs + eps);
     double v[NV] = {};
@@ -293,7 +314,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
         }
     }
     cluster_channel_sum<NV>(v, red, part);
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (fin) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) grads[j * C + sl.c] = v[j];
         if (SUMS) {
@@ -304,8 +325,8 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
         // (as tagi_bn_apply_grads); every block of the cluster read gamma before
         // the cluster-wide reduction above
         if (cap > 0.f) {
-            vector_apply(sl.c, v[0], v[1], TAGI_WGRAD_UPDATE, mg, Sw, nullptr, nullptr, cap);
-            vector_apply(sl.c, v[2], v[3], TAGI_WGRAD_UPDATE, mb, Sb, nullptr, nullptr, cap);
+            update_from(sl.c, v[0], v[1], g, sw0, mg, Sw, cap);
+            update_from(sl.c, v[2], v[3], mb0, sb0, mb, Sb, cap);
         }
     }
 }
@@ -426,6 +447,19 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     __shared__ double part[3];
     __shared__ float stat[3];  // mean, variance, scale of the channel
     const ChanSlab sl(N, C, HW, blockIdx.y);
+    // the channel's parameters, loaded before the first pass so that their
+    // latency is not added after the cluster barriers (no launch writes them
+    // but the finalising thread, which reads them first)
+    const float sg = Sg[sl.c], b = mb[sl.c], sb = Sb[sl.c];
+    const bool fin = blockIdx.x == 0 && threadIdx.x == 0;  // cluster rank 0, thread 0
+    float g0 = 0.f, rm0 = 0.f, rv0 = 0.f;
+    if (fin) {
+        g0 = mg[sl.c];
+        if (!first) {
+            rm0 = rmean[sl.c];
+            rv0 = rvar[sl.c];
+        }
+    }
     double v[3] = {0.0, 0.0, 0.0};
     const int HW4 = HW / 4;
     const int total = V4 ? sl.nimg * HW4 : sl.nimg * HW;
@@ -470,7 +504,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     }
     cluster_channel_sum<3>(v, red, part);
     cg::cluster_group cluster = cg::this_cluster();
-    if (cluster.block_rank() == 0 && threadIdx.x == 0) {
+    if (fin) {
         const int c = sl.c;
         const float m = static_cast<float>(v[0] / count);
         const float mS = static_cast<float>(v[1] / count);
@@ -479,15 +513,18 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
         const float vv = (mS + msq - m * m) * bessel;
         mean[c] = m;
         var[c] = vv;
+        float g = g0;
         if (first) {
             rmean[c] = m;
             rvar[c] = vv;
-            if (preserve_var) mg[c] = sqrtf(vv + eps);
+            if (preserve_var) {
+                g = sqrtf(vv + eps);
+                mg[c] = g;
+            }
         } else {
-            rmean[c] = one_minus * rmean[c] + momentum * m;
-            rvar[c] = one_minus * rvar[c] + momentum * vv;
+            rmean[c] = one_minus * rm0 + momentum * m;
+            rvar[c] = one_minus * rv0 + momentum * vv;
         }
-        const float g = mg[c];
         for (unsigned r = 0; r < cluster.num_blocks(); ++r) {
             float* peer = cluster.map_shared_rank(stat, r);
             peer[0] = m;
@@ -496,9 +533,8 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
         }
     }
     cluster.sync();
-    const int c = sl.c;
-    bn_normalize<V4>(sl, mz, Sz, stat[0], stat[1], stat[2], Sg[c], mb[c], Sb[c], ma, Sa, mhat,
-                     add_m, add_S, total, HW4, HW, eps);
+    bn_normalize<V4>(sl, mz, Sz, stat[0], stat[1], stat[2], sg, b, sb, ma, Sa, mhat, add_m,
+                     add_S, total, HW4, HW, eps);
 }
 
 // Data-parallel training forward after the statistics exchange: `sums` holds
