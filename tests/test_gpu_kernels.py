@@ -408,10 +408,12 @@ def test_conv_layer_against_oracle(shape, k, s, p, pt):
             assert_rel(getattr(dev, n), getattr(ref, n), 1e-4, n)
 
 
-@pytest.mark.parametrize("N,C,H,W", [(8, 16, 6, 6), (3, 5, 7, 5), (1, 600, 2, 2), (64, 4, 16, 16)])
+@pytest.mark.parametrize("N,C,H,W", [(8, 16, 6, 6), (3, 5, 7, 5), (1, 600, 2, 2), (64, 4, 16, 16),
+                                     (8, 512, 4, 4)])
 def test_batchnorm_layer_against_oracle(N, C, H, W):
-    """Covers 16-byte and element-wise channel slabs, clusters of 1 to 8 blocks per
-    channel, and fewer images than blocks in a cluster."""
+    """Covers 16-byte and element-wise channel slabs, clusters of 2 to 8 blocks per
+    channel, one block per channel (512 or more channels, or one image: a launch
+    without clusters), and fewer images than blocks in a cluster."""
     import oracle.net as ON
     from triton_tagi import BatchNorm2D
 
@@ -497,7 +499,7 @@ def test_empty_inputs_are_no_ops():
     update_parameters(e, e, e, e, 2.0)
 
 
-@pytest.mark.parametrize("N,C,H,W", [(8, 16, 6, 6), (3, 5, 7, 5), (16, 64, 8, 8)])
+@pytest.mark.parametrize("N,C,H,W", [(8, 16, 6, 6), (3, 5, 7, 5), (16, 64, 8, 8), (16, 512, 4, 4)])
 def test_relu_jacobian_folded_into_batchnorm_backward(N, C, H, W):
     """A ReLU feeding a BatchNorm2D, as containers run its backward (the ReLU's
     Jacobian applied by the BatchNorm's backward), against the two layers' own

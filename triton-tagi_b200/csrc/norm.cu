@@ -25,8 +25,10 @@ int bn_split(int64_t C, int64_t N) {
 }
 
 // Sums v over the block (fixed order), then over the cluster's blocks in rank
-// order; the totals are valid in thread 0 of cluster rank 0.
-template <int NV>
+// order; the totals are valid in thread 0 of cluster rank 0. CL = false: a
+// launch without clusters (one block per channel); the same sums, 0 + the
+// block's total as a one-block cluster gives, with no cluster barriers.
+template <int NV, bool CL = true>
 __device__ __forceinline__ void cluster_channel_sum(double (&v)[NV], double* red, double* part) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
@@ -42,8 +44,10 @@ __device__ __forceinline__ void cluster_channel_sum(double (&v)[NV], double* red
             double t = 0.0;
             for (int w = 0; w < nw; ++w) t += red[j * 32 + w];
             part[j] = t;
+            if (!CL) v[j] = 0.0 + t;
         }
     }
+    if constexpr (!CL) return;
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     if (cluster.block_rank() == 0 && threadIdx.x == 0) {
@@ -78,6 +82,16 @@ int launch_cluster(K kernel, int S, int C, cudaStream_t st, const char* what, Ar
         set_error("%s: launch failed (%s)", what, cudaGetErrorString(e));
         return TAGI_E_LAUNCH;
     }
+    return check_launch(what);
+}
+
+// S > 1: the cluster launch of `clustered`; S == 1 (one block per channel): a
+// plain launch of `single`, the same kernel built without cluster barriers.
+template <typename K, typename... Args>
+int launch_split(K clustered, K single, int S, int C, cudaStream_t st, const char* what,
+                 Args... args) {
+    if (S > 1) return launch_cluster(clustered, S, C, st, what, args...);
+    single<<<dim3(1u, static_cast<unsigned>(C), 1u), kBnThreads, 0, st>>>(args...);
     return check_launch(what);
 }
 
@@ -232,7 +246,7 @@ __device__ __forceinline__ void update_from(int64_t i, double gm, double gS, flo
 // SUMS: also the channel sums of the outgoing deltas (written to dsums[c] and
 // dsums[C + c]): the bias sums of a convolution whose outputs this layer
 // normalised (through a ReLU or not), which then need no pass of their own.
-template <bool V4, bool SUMS>
+template <bool V4, bool SUMS, bool CL>
 __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
     const float* dma, const float* dSa, const float* mhat, const float* var, float* mg,
     float* dmz, float* dSz, const float* rj, double* grads, double* dsums, int N, int C, int HW,
@@ -313,7 +327,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_backward_kernel(
             one(dma[o], dSa[o], mhat[o], rj ? rj[o] : 0.f, dmz[o], dSz[o]);
         }
     }
-    cluster_channel_sum<NV>(v, red, part);
+    cluster_channel_sum<NV, CL>(v, red, part);
     if (fin) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) grads[j * C + sl.c] = v[j];
@@ -437,7 +451,7 @@ __device__ __forceinline__ void bn_normalize(const ChanSlab& sl, const float* mz
 // first-call scale) and hands mean, variance and scale to every rank through
 // distributed shared memory, and each block normalises the elements it summed
 // (read again from L2) as bn_forward_v4_kernel / bn_forward_kernel.
-template <bool V4>
+template <bool V4, bool CL>
 __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
     const float* mz, const float* Sz, float* mean, float* var, float* rmean, float* rvar,
     float* mg, const float* Sg, const float* mb, const float* Sb, float* ma, float* Sa,
@@ -502,8 +516,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
             v[2] += x * x;
         }
     }
-    cluster_channel_sum<3>(v, red, part);
-    cg::cluster_group cluster = cg::this_cluster();
+    cluster_channel_sum<3, CL>(v, red, part);
     if (fin) {
         const int c = sl.c;
         const float m = static_cast<float>(v[0] / count);
@@ -525,14 +538,24 @@ __global__ void __launch_bounds__(kBnThreads) bn_train_forward_kernel(
             rmean[c] = one_minus * rm0 + momentum * m;
             rvar[c] = one_minus * rv0 + momentum * vv;
         }
-        for (unsigned r = 0; r < cluster.num_blocks(); ++r) {
-            float* peer = cluster.map_shared_rank(stat, r);
-            peer[0] = m;
-            peer[1] = vv;
-            peer[2] = g;
+        if constexpr (CL) {
+            cg::cluster_group cluster = cg::this_cluster();
+            for (unsigned r = 0; r < cluster.num_blocks(); ++r) {
+                float* peer = cluster.map_shared_rank(stat, r);
+                peer[0] = m;
+                peer[1] = vv;
+                peer[2] = g;
+            }
+        } else {
+            stat[0] = m;
+            stat[1] = vv;
+            stat[2] = g;
         }
     }
-    cluster.sync();
+    if constexpr (CL)
+        cg::this_cluster().sync();
+    else
+        __syncthreads();
     bn_normalize<V4>(sl, mz, Sz, stat[0], stat[1], stat[2], sg, b, sb, ma, Sa, mhat, add_m,
                      add_S, total, HW4, HW, eps);
 }
@@ -787,14 +810,16 @@ extern "C" int tagi_bn_train_forward(const float* mz, const float* Sz, float* me
                          reinterpret_cast<uintptr_t>(add_S);
     const bool v4 = HW % 4 == 0 && (al & 15) == 0;
     const float one_minus = static_cast<float>(1.0 - static_cast<double>(momentum));
-    return v4 ? launch_cluster(bn_train_forward_kernel<true>, S, (int)C, as_stream(stream), what,
-                               mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
-                               Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
-                               preserve_var, momentum, one_minus, eps)
-              : launch_cluster(bn_train_forward_kernel<false>, S, (int)C, as_stream(stream), what,
-                               mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb, ma,
-                               Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
-                               preserve_var, momentum, one_minus, eps);
+    return v4 ? launch_split(bn_train_forward_kernel<true, true>,
+                             bn_train_forward_kernel<true, false>, S, (int)C, as_stream(stream),
+                             what, mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb,
+                             ma, Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
+                             preserve_var, momentum, one_minus, eps)
+              : launch_split(bn_train_forward_kernel<false, true>,
+                             bn_train_forward_kernel<false, false>, S, (int)C, as_stream(stream),
+                             what, mz, Sz, mean, var, running_mean, running_var, mg, Sg, mb, Sb,
+                             ma, Sa, m_hat, add_m, add_S, (int)N, (int)C, (int)HW, count, first,
+                             preserve_var, momentum, one_minus, eps);
 }
 
 extern "C" int tagi_bn_sync_forward(const float* mz, const float* Sz, const double* sums,
@@ -856,7 +881,8 @@ extern "C" int tagi_bn_backward(const float* dma, const float* dSa, const float*
                          reinterpret_cast<uintptr_t>(dSz) | reinterpret_cast<uintptr_t>(relu_J);
     const bool v4 = HW % 4 == 0 && (al & 15) == 0;
 #define TAGI_BN_BWD(V, SU)                                                                      \
-    launch_cluster(bn_backward_kernel<V, SU>, S, (int)C, as_stream(stream), what, dma, dSa, m_hat, \
+    launch_split(bn_backward_kernel<V, SU, true>, bn_backward_kernel<V, SU, false>, S, (int)C,    \
+                 as_stream(stream), what, dma, dSa, m_hat,                                          \
                    var, mg, dmz, dSz, relu_J, grads, delta_sums, (int)N, (int)C, (int)HW, eps, Sw, \
                    mb, Sb, cap_factor)
     const int rc = delta_sums ? (v4 ? TAGI_BN_BWD(true, true) : TAGI_BN_BWD(false, true))
