@@ -18,7 +18,12 @@ namespace {
 
 constexpr int kBnThreads = 256;
 
+// Blocks per channel: about 512 blocks in all, at most 8 and at most one per
+// image; one (no cluster) from 256 channels up, where a second block per channel
+// saved less than the cluster barriers cost (backward at 256 channels of 8 x 8,
+// batch 128: 12.9 -> 11.3 us with one block).
 int bn_split(int64_t C, int64_t N) {
+    if (C >= 256) return 1;
     int s = 1;
     while (s < 8 && C * s < 512 && s < N) s *= 2;
     return s;
