@@ -600,7 +600,9 @@ def test_positional_encoding_add():
 
 @pytest.mark.parametrize("N,C,H,W,first,residual", [(16, 64, 8, 8, True, False),
                                                       (12, 32, 5, 5, False, True),
-                                                      (8, 128, 4, 4, True, True)])
+                                                      (8, 128, 4, 4, True, True),
+                                                      (8, 256, 4, 4, False, True),
+                                                      (4, 300, 3, 3, True, False)])
 def test_bn_sync_forward_two_shards(N, C, H, W, first, residual):
     """SyncBN on one GPU with two emulated ranks: each half of the batch forms
     its channel sums, the sums are added (the all-reduce), and

@@ -115,7 +115,7 @@ struct ChanSlab {
 };
 
 // sums[c] = sum mz, sums[C+c] = sum Sz, sums[2C+c] = sum mz^2 over (n, hw).
-template <bool V4>
+template <bool V4, bool CL>
 __global__ void __launch_bounds__(kBnThreads) bn_sums_kernel(const float* mz, const float* Sz,
                                                              double* sums, int N, int C, int HW) {
     __shared__ double red[3 * 32];
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_sums_kernel(const float* mz, co
             v[2] += x * x;
         }
     }
-    cluster_channel_sum<3>(v, red, part);
+    cluster_channel_sum<3, CL>(v, red, part);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         sums[sl.c] = v[0];
         sums[C + sl.c] = v[1];
@@ -742,10 +742,11 @@ extern "C" int tagi_bn_channel_sums(const float* mz, const float* Sz, double* su
     TAGI_REQUIRE(N * HW <= (int64_t(1) << 31) - 1, TAGI_E_BAD_ARG, "%s: bad sizes", what);
     const int S = bn_split(C, N);
     const bool v4 = HW % 4 == 0 && ((reinterpret_cast<uintptr_t>(mz) | reinterpret_cast<uintptr_t>(Sz)) & 15) == 0;
-    return v4 ? launch_cluster(bn_sums_kernel<true>, S, (int)C, as_stream(stream), what, mz, Sz,
-                               sums, (int)N, (int)C, (int)HW)
-              : launch_cluster(bn_sums_kernel<false>, S, (int)C, as_stream(stream), what, mz, Sz,
-                               sums, (int)N, (int)C, (int)HW);
+    return v4 ? launch_split(bn_sums_kernel<true, true>, bn_sums_kernel<true, false>, S, (int)C,
+                             as_stream(stream), what, mz, Sz, sums, (int)N, (int)C, (int)HW)
+              : launch_split(bn_sums_kernel<false, true>, bn_sums_kernel<false, false>, S,
+                             (int)C, as_stream(stream), what, mz, Sz, sums, (int)N, (int)C,
+                             (int)HW);
 }
 
 extern "C" int tagi_bn_finalize(const double* sums, int64_t C, double count, float* mean,
