@@ -247,14 +247,14 @@ ENTRY_BYTES = {
 }
 
 
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# contraction families, from one ncu capture of this build: 112 consecutive
-# tensor-core contraction launches of two ResNet-18 steps (after 3 warm-up
-# steps; the stem's weight sums run on CUDA cores and are not among them), and one
-# 4096 x 4096 x 4096 Linear forward scaled by M to the sweep's 8192-row headline
-# (A and the number of B re-reads both grow with M).
-# DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum), family
-# averages; r18: a batch-64 capture of one step's 59 tensor-core launches, doubled
+# DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum) of the
+# contraction families. r18: the family averages of a batch-64 capture of one
+# step's 59 tensor-core launches (the stem's weight sums and the classifier run
+# on CUDA cores), doubled for batch 128; a later single-launch full capture of
+# the forward family's stage-2 convolution gave 32.2 MB at batch 64 (64.4 MB
+# doubled), in line with the forward average. swp: one 4096 x 4096 x 4096 Linear
+# forward scaled by M to the sweep's 8192-row headline (A and the number of B
+# re-reads both grow with M).
 MEASURED_TRAFFIC = {
     ("r18", "moment_forward"): 63.1e6,
     ("r18", "backward_delta"): 37.4e6,
